@@ -1,0 +1,175 @@
+/*
+ * nq8.h -- C ABI of the B200 (sm_100a) GGUF Q8_0 contraction library, libnq8.so.
+ *
+ * Drop-in boundary for nspeech's Q8_0 matmul path.  Every entry point lists
+ * the reference interface it replaces (paths relative to the dropbox/nspeech
+ * source tree).  Plain C types only: device pointers are `void*`/`float*`,
+ * a CUDA stream is passed as `void*` (NULL = legacy default stream).
+ *
+ * Conventions
+ *   - Every function returns NQ_OK (0) or a negative NQ_ERR_* code; the
+ *     message of the last failure on the calling thread is kept for
+ *     nq_last_error().  No entry point falls back to a CPU path.
+ *   - Weights are opaque handles owned by the library (device memory,
+ *     immutable after creation, safe to share across threads/streams).
+ *   - Activations x, outputs y and bias live in caller-owned device memory
+ *     (the `enc_*` convention of src/triton_kernels.rs:862-1397).
+ *   - The library owns a per-(device, stream) workspace (activation split
+ *     planes, split-K partial sums, arrival counters).  It grows on demand,
+ *     so the first call of a given size on a stream may cudaMalloc; make that
+ *     call once before capturing the stream into a CUDA graph.
+ *   - Calls on different streams may run concurrently; calls on one stream
+ *     are ordered by the stream.
+ *
+ * Numerics: y = act(x . bf16(dequant(W))^T + bias) with f32 accumulation, the
+ * FbgemmBf16Op semantics of src/fast_matmul.rs:138-167 (weights rounded to
+ * bf16 after Q8_0 dequantization).  f32 activations are carried at f32
+ * precision (split into two bf16 planes); bf16 activations are used as is.
+ */
+#ifndef NQ8_H
+#define NQ8_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define NQ_OK 0
+#define NQ_ERR_ARG (-1)         /* null pointer, unknown enum value */
+#define NQ_ERR_SHAPE (-2)       /* K % 32 != 0, last dim != K, GLU with odd N, ... */
+#define NQ_ERR_ALIGN (-3)       /* pointer or leading dimension misaligned */
+#define NQ_ERR_DTYPE (-4)       /* unsupported dtype (GGUF tensor not Q8_0, ...) */
+#define NQ_ERR_CUDA (-5)        /* a CUDA runtime call failed */
+#define NQ_ERR_TIMEOUT (-6)     /* a kernel's bounded wait ran out (device status) */
+#define NQ_ERR_FORMAT (-7)      /* malformed GGUF file */
+#define NQ_ERR_IO (-8)          /* file open / mmap failure */
+#define NQ_ERR_NOT_INIT (-9)    /* nq_init was not called on this thread's device */
+#define NQ_ERR_UNSUPPORTED (-10)/* e.g. GLU epilogue on a weight not packed for it */
+#define NQ_ERR_DEVICE (-11)     /* device status word reported a kernel-side error */
+
+/* ---- element types of activations / outputs ---------------------------- */
+#define NQ_F32 0
+#define NQ_BF16 1
+
+/* ---- fused epilogues (applied after the bias add) ----------------------- */
+#define NQ_EPI_NONE 0
+#define NQ_EPI_SILU 1        /* Parakeet FFN w1 (src/parakeet/fast_conformer.rs:207) */
+#define NQ_EPI_GELU_ERF 2    /* Moonshine encoder fc1 (src/moonshine/encoder.rs:105) */
+#define NQ_EPI_GLU_SIGMOID 3 /* pointwise_conv1: a*sigmoid(b) (fast_conformer.rs:479-484) */
+#define NQ_EPI_GLU_SILU 4    /* Moonshine decoder fc1: x*silu(gate) (moonshine/decoder.rs:403-410) */
+
+/* ---- weight packing flags ----------------------------------------------- */
+#define NQ_PACK_DEFAULT 0
+/* Rows [0, N/2) are the value half and [N/2, N) the gate half of a GLU
+ * projection; they are interleaved per 128-row tile so that the GLU epilogues
+ * fuse into the matmul.  Required for NQ_EPI_GLU_*; output width is N/2. */
+#define NQ_PACK_GLU 1
+
+/* ---- device status bits (nq_status) -------------------------------------- */
+#define NQ_DEV_TIMEOUT_PRODUCER 0x1
+#define NQ_DEV_TIMEOUT_CONSUMER 0x2
+#define NQ_DEV_TIMEOUT_MMA 0x4
+#define NQ_DEV_TIMEOUT_EPILOGUE 0x8
+#define NQ_DEV_TIMEOUT_DRAIN 0x10
+
+typedef struct nq_weight nq_weight;
+
+/* Bind the calling thread to a device and create its context (status word,
+ * tensor-map entry point).  Per process, per GPU.  Replaces the device probe
+ * of src/parakeet/mod.rs:309-325 (get_device). */
+int nq_init(int device_ordinal);
+
+/* Library version string, e.g. "nq8 0.1 sm_100a". */
+const char *nq_version(void);
+
+/* Upload a GGUF Q8_0 weight of logical shape [n, k] (GGUF ne0 = k): n*k/32
+ * blocks of 34 bytes (f16 d, 32 x int8), host memory or an mmap.  Repacks once
+ * into the tiled HBM layout.  Replaces MatMul::from_qtensor
+ * (src/fast_matmul.rs:184) and EncoderBackend::upload_matmul_weight
+ * (src/moonshine/gpu_encoder.rs:33-35). */
+int nq_weight_from_q8_0(const void *blocks, int64_t n, int64_t k, int flags, nq_weight **out);
+
+/* Upload a dequantized f32 [n, k] weight.  It is re-quantized to Q8_0 with
+ * ggml semantics, which is lossless for tensors that came from Q8_0 (the only
+ * way the reference calls it: new_mm, src/moonshine/encoder.rs:29-39).
+ * Replaces MatMul::from_tensor (src/fast_matmul.rs:191-208). */
+int nq_weight_from_f32(const float *w, int64_t n, int64_t k, int flags, nq_weight **out);
+
+/* mmap a GGUF v2/v3 file, find `tensor_name`, check it is Q8_0 and 2-D, and
+ * upload it.  Replaces the mmap GGUF loader + QTensor path of
+ * src/parakeet/transducer.rs:1759-1865. */
+int nq_weight_from_gguf(const char *path, const char *tensor_name, int flags, nq_weight **out);
+
+/* Host-only: parse a GGUF file and report tensor `tensor_name`'s ggml type
+ * id (Q8_0 = 8) and its 2-D shape [n, k] (k = ne0).  No device work. */
+int nq_gguf_tensor_info(const char *path, const char *tensor_name, int *ggml_type, int64_t *n, int64_t *k);
+
+/* Concatenate weights along N (fused QKV [q;k;v], or [value; gate] with
+ * NQ_PACK_GLU) into a new handle; all must share K.  Mirrors the fused QKV
+ * upload of src/moonshine/gpu_encoder.rs:276-292. */
+int nq_weights_fuse(const nq_weight *const *ws, int count, int flags, nq_weight **out);
+
+/* Copy a weight back to GGUF Q8_0 blocks (n*k/32*34 bytes of host memory). */
+int nq_weight_to_q8_0(const nq_weight *w, void *blocks_out);
+
+int nq_weight_shape(const nq_weight *w, int64_t *n, int64_t *k, int *flags);
+void nq_weight_free(nq_weight *w);
+
+/* y[m, :] = act(x[m, :K] . W^T + bias), m in [0, M).
+ *   x: device, x_dtype NQ_F32 | NQ_BF16, row stride ldx elements (>= K).
+ *   bias: device f32 [N] or NULL.  epilogue: NQ_EPI_*.
+ *   y: device, y_dtype NQ_F32 | NQ_BF16, row stride ldy (>= N_out; N_out = N/2
+ *      for GLU epilogues).  M = 0 is a no-op.
+ * M <= 16 runs the split-K GEMV kernel, larger M the tcgen05 GEMM.
+ * Replaces MatMul::forward / FbgemmBf16Op::cpu_fwd (src/fast_matmul.rs:
+ * 138-167, 210-226) and QLinear::forward (src/parakeet/quantized_layers.rs:
+ * 31-38). */
+int nq_linear(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx,
+              const float *bias, int epilogue, void *y, int y_dtype, int64_t ldy, void *stream);
+
+/* Named dispatch entry points of src/triton_kernels.rs (contiguous rows). */
+/* triton_matmul :170-211 / enc_matmul :1205-1231: c = a . W^T */
+int nq_matmul(const nq_weight *w, const void *a, int a_dtype, void *c, int c_dtype, int64_t m,
+              void *stream);
+/* triton_matmul_bias :217-260 / enc_matmul_bias :1233-1260 */
+int nq_matmul_bias(const nq_weight *w, const void *a, int a_dtype, const float *bias, void *c,
+                   int c_dtype, int64_t m, void *stream);
+/* triton_matmul_bias_gelu :266-309 / enc_matmul_bias_gelu :1262-1289 */
+int nq_matmul_bias_gelu(const nq_weight *w, const void *a, int a_dtype, const float *bias,
+                        void *c, int c_dtype, int64_t m, void *stream);
+/* enc_gemv_splitk :1077-1115 and enc_gemv_splitk_bias :1036-1075 (bias may be
+ * NULL); x is one row. */
+int nq_gemv_splitk(const nq_weight *w, const void *x, int x_dtype, const float *bias, void *out,
+                   int out_dtype, void *stream);
+/* enc_gemv_glu_splitk :1163-1202: out = silu(gate) * value, W packed NQ_PACK_GLU */
+int nq_gemv_glu_splitk(const nq_weight *w, const void *x, int x_dtype, const float *bias,
+                       void *out, int out_dtype, void *stream);
+/* enc_gemv_qkv_splitk :1117-1161: three projections of one row in one launch
+ * sequence; weights must share K.  Outputs q, k, v are separate buffers. */
+int nq_gemv_qkv_splitk(const nq_weight *wq, const nq_weight *wk, const nq_weight *wv,
+                       const void *x, int x_dtype, void *q, void *k, void *v, int out_dtype,
+                       void *stream);
+
+/* Thread-local message of the last failure ("" if none); returns its length. */
+int nq_last_error(char *buf, int len);
+
+/* Synchronize `stream`, then read and clear this device's status word.
+ * Returns NQ_OK, or NQ_ERR_TIMEOUT with the NQ_DEV_* bits in *bits. */
+int nq_status(void *stream, int *bits);
+
+/* Cycle budget of every bounded wait in the kernels (default ~2^31 cycles,
+ * about one second).  Lowered only by tests. */
+int nq_set_wait_limit(int64_t cycles);
+
+/* Test hook for failure detection: launches a kernel that waits on an
+ * mbarrier nothing arrives on, bounded by the wait limit; the kernel records
+ * NQ_DEV_TIMEOUT_CONSUMER and returns, leaving the context usable. */
+int nq_debug_wait_timeout(void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NQ8_H */

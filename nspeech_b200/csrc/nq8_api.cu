@@ -1,0 +1,589 @@
+// nq8_api.cu -- the C ABI of libnq8.so (declared in include/nq8.h).
+//
+// Host runtime around the kernels: per-device contexts (status word, driver
+// entry point for tensor maps), immutable weight handles, a per-(device,
+// stream) workspace, shape/alignment validation and the GEMV / GEMM dispatch.
+// There is no CPU compute path: if a kernel cannot run, the call fails.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/nq8.h"
+#include "nq8_host.h"
+#include "nq8_kernels.h"
+
+struct nq_weight {
+  int device = 0;
+  int64_t n = 0, k = 0;
+  int flags = 0;
+  int n_tiles = 0, kc = 0;
+  uint8_t *dev = nullptr;
+  size_t bytes = 0;
+};
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kSmCountB200 = 148;
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+struct Workspace {
+  uint8_t *buf = nullptr;
+  size_t bytes = 0;
+  int *counters = nullptr;  // kCounterSlots ints, zero between calls
+};
+constexpr size_t kCounterSlots = 1 << 16;
+
+struct DeviceCtx {
+  bool ready = false;
+  int *status = nullptr;
+  int sm_count = kSmCountB200;
+  EncodeTiledFn encode = nullptr;
+  std::mutex mu;
+  std::map<cudaStream_t, Workspace> ws;
+};
+
+DeviceCtx g_ctx[kMaxDevices];
+std::mutex g_init_mu;
+long long g_wait_limit = 1LL << 31;
+thread_local std::string t_err;
+
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_err = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+  return fail(NQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+int current_ctx(DeviceCtx **out, int *dev_out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices || !g_ctx[dev].ready)
+    return fail(NQ_ERR_NOT_INIT, "nq_init(%d) was not called", dev);
+  *out = &g_ctx[dev];
+  if (dev_out) *dev_out = dev;
+  return NQ_OK;
+}
+
+// Grow-only workspace for `stream`; counters are zeroed once at allocation
+// and re-armed by the kernels.
+int get_workspace(DeviceCtx *ctx, cudaStream_t stream, size_t bytes, Workspace **out) {
+  std::lock_guard<std::mutex> lk(ctx->mu);
+  Workspace &w = ctx->ws[stream];
+  if (!w.counters) {
+    cudaError_t e = cudaMalloc(&w.counters, kCounterSlots * sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace counters)");
+    e = cudaMemset(w.counters, 0, kCounterSlots * sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(workspace counters)");
+  }
+  if (w.bytes < bytes) {
+    if (w.buf) {
+      cudaError_t e = cudaStreamSynchronize(stream);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize(workspace growth)");
+      cudaFree(w.buf);
+      w.buf = nullptr;
+      w.bytes = 0;
+    }
+    size_t sz = std::max(bytes, static_cast<size_t>(16) << 20);
+    cudaError_t e = cudaMalloc(&w.buf, sz);
+    if (e != cudaSuccess) return fail(NQ_ERR_CUDA, "cudaMalloc(workspace %zu bytes): %s", sz, cudaGetErrorString(e));
+    w.bytes = sz;
+  }
+  *out = &w;
+  return NQ_OK;
+}
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+int upload_packed(const uint8_t *blocks, int64_t n, int64_t k, int flags, nq_weight **out) {
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  int rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  std::unique_ptr<nq_weight> w(new nq_weight);
+  w->device = dev;
+  w->n = n;
+  w->k = k;
+  w->flags = flags;
+  w->n_tiles = nq::pack_n_tiles(n, flags);
+  w->kc = nq::pack_k_chunks(k);
+  w->bytes = static_cast<size_t>(w->n_tiles) * w->kc * nq::kTileBytes;
+  std::vector<uint8_t> host(w->bytes);
+  nq::pack_q8_0(blocks, n, k, flags, host.data());
+  cudaError_t e = cudaMalloc(&w->dev, w->bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(weight)");
+  e = cudaMemcpy(w->dev, host.data(), w->bytes, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(w->dev);
+    return cuda_fail(e, "cudaMemcpy(weight)");
+  }
+  *out = w.release();
+  return NQ_OK;
+}
+
+int check_weight_shape(int64_t n, int64_t k, int flags) {
+  if (n <= 0 || k <= 0) return fail(NQ_ERR_SHAPE, "weight shape [%lld, %lld] must be positive", (long long)n, (long long)k);
+  if (k % 32) return fail(NQ_ERR_SHAPE, "K=%lld is not a multiple of the Q8_0 block (32)", (long long)k);
+  if (flags & ~NQ_PACK_GLU) return fail(NQ_ERR_ARG, "unknown pack flags 0x%x", flags);
+  if ((flags & NQ_PACK_GLU) && (n % 2)) return fail(NQ_ERR_SHAPE, "GLU weight needs an even N (got %lld)", (long long)n);
+  if (n > (1LL << 31) || k > (1LL << 31)) return fail(NQ_ERR_SHAPE, "weight too large");
+  return NQ_OK;
+}
+
+int make_tmap(DeviceCtx *ctx, CUtensorMap *map, const void *ptr, int64_t kdim, int64_t rows, int64_t ld_elems) {
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kdim), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_elems) * 2};
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = ctx->encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
+                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(NQ_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return NQ_OK;
+}
+
+struct LinearArgs {
+  const nq_weight *w;
+  const float *bias;
+  void *y;
+  int64_t ldy;
+};
+
+int64_t out_width(const nq_weight *w) { return (w->flags & NQ_PACK_GLU) ? w->n / 2 : w->n; }
+
+int validate(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx, int epilogue, const void *y,
+             int y_dtype, int64_t ldy) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  if (m < 0) return fail(NQ_ERR_SHAPE, "negative M");
+  if (x_dtype != NQ_F32 && x_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "x dtype %d unsupported", x_dtype);
+  if (y_dtype != NQ_F32 && y_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "y dtype %d unsupported", y_dtype);
+  if (epilogue < NQ_EPI_NONE || epilogue > NQ_EPI_GLU_SILU) return fail(NQ_ERR_ARG, "unknown epilogue %d", epilogue);
+  const bool glu_epi = epilogue == NQ_EPI_GLU_SIGMOID || epilogue == NQ_EPI_GLU_SILU;
+  const bool glu_w = (w->flags & NQ_PACK_GLU) != 0;
+  if (glu_epi && !glu_w) return fail(NQ_ERR_UNSUPPORTED, "GLU epilogue needs a weight packed with NQ_PACK_GLU");
+  if (!glu_epi && glu_w) return fail(NQ_ERR_UNSUPPORTED, "weight packed with NQ_PACK_GLU needs a GLU epilogue");
+  if (m == 0) return NQ_OK;
+  if (!x || !y) return fail(NQ_ERR_ARG, "null activation or output pointer");
+  if (ldx < w->k) return fail(NQ_ERR_SHAPE, "ldx=%lld < K=%lld", (long long)ldx, (long long)w->k);
+  if (ldy < out_width(w)) return fail(NQ_ERR_SHAPE, "ldy=%lld < output width %lld", (long long)ldy, (long long)out_width(w));
+  if (m > (1LL << 30)) return fail(NQ_ERR_SHAPE, "M too large");
+  return NQ_OK;
+}
+
+// ------------------------------------------------------------------ GEMV
+int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
+             int epilogue, int y_dtype, cudaStream_t stream) {
+  const nq_weight *w0 = args[0].w;
+  int max_tiles = 0;
+  for (int i = 0; i < nprob; ++i) max_tiles = std::max(max_tiles, args[i].w->n_tiles);
+  const int kc = w0->kc;
+  const int target = 2 * ctx->sm_count;
+  int splits = std::max(1, std::min(kc, (target + max_tiles * nprob - 1) / (max_tiles * nprob)));
+  int cps = (kc + splits - 1) / splits;
+  cps = std::min(cps, 8);  // bounds the activation slice staged in shared memory
+  splits = (kc + cps - 1) / cps;
+  const int mrows = m <= 8 ? 8 : 16;
+
+  size_t part_bytes = 0;
+  if (splits > 1)
+    for (int i = 0; i < nprob; ++i)
+      part_bytes += align_up(static_cast<size_t>(splits) * args[i].w->n_tiles * 16 * nq::kPackRows * sizeof(float), 256);
+  Workspace *ws = nullptr;
+  int rc = get_workspace(ctx, stream, part_bytes, &ws);
+  if (rc) return rc;
+
+  nq::GemvParams p;
+  std::memset(&p, 0, sizeof(p));
+  size_t part_off = 0, ctr_off = 0;
+  for (int i = 0; i < nprob; ++i) {
+    const nq_weight *w = args[i].w;
+    nq::GemvProblem &pr = p.prob[i];
+    pr.w = w->dev;
+    pr.n_tiles = w->n_tiles;
+    pr.kc_total = w->kc;
+    pr.N = w->n;
+    pr.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
+    pr.n_out = out_width(w);
+    pr.bias = args[i].bias;
+    pr.y = args[i].y;
+    pr.ldy = args[i].ldy;
+    if (splits > 1) {
+      pr.partials = reinterpret_cast<float *>(ws->buf + part_off);
+      part_off += align_up(static_cast<size_t>(splits) * w->n_tiles * 16 * nq::kPackRows * sizeof(float), 256);
+      if (ctr_off + w->n_tiles > kCounterSlots) return fail(NQ_ERR_SHAPE, "too many tiles for the counter pool");
+      pr.counters = ws->counters + ctr_off;
+      ctr_off += w->n_tiles;
+    }
+  }
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.ldx = ldx;
+  p.M = static_cast<int>(m);
+  p.K = w0->k;
+  p.epi = epilogue;
+  p.y_dtype = y_dtype;
+  p.splits = splits;
+  p.cps = cps;
+  p.ctl.status = ctx->status;
+  p.ctl.wait_limit = g_wait_limit;
+  (void)mrows;
+  cudaError_t e = nq::launch_gemv(p, nprob, max_tiles, x_dtype == NQ_F32, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+  return NQ_OK;
+}
+
+// ------------------------------------------------------------------ GEMM
+int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, int64_t m, int64_t ldx, int epilogue,
+             int y_dtype, cudaStream_t stream) {
+  const nq_weight *w = a.w;
+  const int kc = w->kc;
+  const int64_t k_pad = static_cast<int64_t>(kc) * nq::kPackK;
+  const bool splitx = x_dtype == NQ_F32;
+  const bool direct = !splitx && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 8 == 0);
+  const int grid_m = static_cast<int>((m + 127) / 128);
+
+  nq::GemmVariant var;
+  if (splitx) {
+    var = nq::kGemmBn128SplitX;
+  } else {
+    const int tiles256 = grid_m * ((w->n_tiles + 1) / 2);
+    var = tiles256 >= ctx->sm_count ? nq::kGemmBn256 : nq::kGemmBn128;
+  }
+  const int bn = nq::gemm_block_n(var);
+  const int grid_n = (w->n_tiles * nq::kPackRows + bn - 1) / bn;
+  const int tiles = grid_m * grid_n;
+  int splits = 1;
+  if (tiles < ctx->sm_count) {
+    splits = std::min((ctx->sm_count + tiles - 1) / tiles, std::max(1, kc / 4));
+    splits = std::max(splits, 1);
+  }
+  int cps = (kc + splits - 1) / splits;
+  splits = (kc + cps - 1) / cps;
+
+  size_t xbytes = 0;
+  if (!direct) xbytes = align_up(static_cast<size_t>(m) * k_pad * 2, 1024) * (splitx ? 2 : 1);
+  size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * tiles * 128 * bn * sizeof(float) : 0;
+  Workspace *ws = nullptr;
+  int rc = get_workspace(ctx, stream, xbytes + part_bytes, &ws);
+  if (rc) return rc;
+  if (splits > 1 && static_cast<size_t>(tiles) > kCounterSlots) return fail(NQ_ERR_SHAPE, "too many tiles for the counter pool");
+
+  const void *a_ptr = x;
+  int64_t a_k = w->k, a_ld = ldx;
+  __nv_bfloat16 *hi = nullptr, *lo = nullptr;
+  if (!direct) {
+    hi = reinterpret_cast<__nv_bfloat16 *>(ws->buf);
+    if (splitx) lo = reinterpret_cast<__nv_bfloat16 *>(ws->buf + xbytes / 2);
+    cudaError_t e = nq::launch_split_x(x, x_dtype, ldx, m, w->k, k_pad, hi, lo, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "activation split launch");
+    a_ptr = hi;
+    a_k = k_pad;
+    a_ld = k_pad;
+  }
+  CUtensorMap tm_a, tm_alo;
+  rc = make_tmap(ctx, &tm_a, a_ptr, a_k, m, a_ld);
+  if (rc) return rc;
+  if (splitx) {
+    rc = make_tmap(ctx, &tm_alo, lo, a_k, m, a_ld);
+    if (rc) return rc;
+  } else {
+    tm_alo = tm_a;
+  }
+
+  nq::GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.w = w->dev;
+  p.n_tiles = w->n_tiles;
+  p.kc_total = kc;
+  p.N = w->n;
+  p.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
+  p.n_out = out_width(w);
+  p.M = static_cast<int>(m);
+  p.bias = a.bias;
+  p.epi = epilogue;
+  p.y = a.y;
+  p.y_dtype = y_dtype;
+  p.ldy = a.ldy;
+  p.splits = splits;
+  p.cps = cps;
+  p.grid_n = grid_n;
+  p.grid_m = grid_m;
+  p.partials = splits > 1 ? reinterpret_cast<float *>(ws->buf + xbytes) : nullptr;
+  p.counters = ws->counters;
+  p.ctl.status = ctx->status;
+  p.ctl.wait_limit = g_wait_limit;
+  cudaError_t e = nq::launch_gemm(var, tm_a, tm_alo, p, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  return NQ_OK;
+}
+
+int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx, int epilogue,
+                int y_dtype, void *stream) {
+  for (int i = 0; i < nprob; ++i) {
+    int rc = validate(args[i].w, x, x_dtype, m, ldx, epilogue, args[i].y, y_dtype, args[i].ldy);
+    if (rc) return rc;
+  }
+  if (m == 0) return NQ_OK;
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  int rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  for (int i = 0; i < nprob; ++i)
+    if (args[i].w->device != dev)
+      return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", args[i].w->device, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (m <= 16) return run_gemv(ctx, args, nprob, x, x_dtype, m, ldx, epilogue, y_dtype, s);
+  for (int i = 0; i < nprob; ++i) {
+    rc = run_gemm(ctx, args[i], x, x_dtype, m, ldx, epilogue, y_dtype, s);
+    if (rc) return rc;
+  }
+  return NQ_OK;
+}
+
+}  // namespace
+
+// ======================================================================= ABI
+extern "C" {
+
+const char *nq_version(void) { return "nq8 0.1 sm_100a"; }
+
+int nq_init(int device_ordinal) {
+  if (device_ordinal < 0 || device_ordinal >= kMaxDevices) return fail(NQ_ERR_ARG, "bad device %d", device_ordinal);
+  cudaError_t e = cudaSetDevice(device_ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+  std::lock_guard<std::mutex> lk(g_init_mu);
+  DeviceCtx &c = g_ctx[device_ordinal];
+  if (c.ready) return NQ_OK;
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, device_ordinal);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+  if (prop.major != 10 || prop.minor != 0)
+    return fail(NQ_ERR_UNSUPPORTED, "device %d is sm_%d%d; libnq8 is built for sm_100a (B200)", device_ordinal,
+                prop.major, prop.minor);
+  c.sm_count = prop.multiProcessorCount;
+  void *fn = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+  if (e != cudaSuccess || !fn || q != cudaDriverEntryPointSuccess)
+    return fail(NQ_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  c.encode = reinterpret_cast<EncodeTiledFn>(fn);
+  e = cudaMalloc(&c.status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(status)");
+  e = cudaMemset(c.status, 0, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(status)");
+  c.ready = true;
+  return NQ_OK;
+}
+
+int nq_weight_from_q8_0(const void *blocks, int64_t n, int64_t k, int flags, nq_weight **out) {
+  if (!blocks || !out) return fail(NQ_ERR_ARG, "null argument");
+  int rc = check_weight_shape(n, k, flags);
+  if (rc) return rc;
+  return upload_packed(static_cast<const uint8_t *>(blocks), n, k, flags, out);
+}
+
+int nq_weight_from_f32(const float *wf, int64_t n, int64_t k, int flags, nq_weight **out) {
+  if (!wf || !out) return fail(NQ_ERR_ARG, "null argument");
+  int rc = check_weight_shape(n, k, flags);
+  if (rc) return rc;
+  std::vector<uint8_t> blocks(static_cast<size_t>(n) * (k / 32) * 34);
+  nq::quantize_q8_0(wf, n, k, blocks.data());
+  return upload_packed(blocks.data(), n, k, flags, out);
+}
+
+int nq_weight_from_gguf(const char *path, const char *tensor_name, int flags, nq_weight **out) {
+  if (!path || !tensor_name || !out) return fail(NQ_ERR_ARG, "null argument");
+  nq::GgufFile f;
+  std::string err;
+  int rc = f.open(path, &err);
+  if (rc) return fail(rc, "%s", err.c_str());
+  const nq::GgufTensor *t = f.find(tensor_name);
+  if (!t) return fail(NQ_ERR_ARG, "tensor '%s' not found in %s", tensor_name, path);
+  if (t->type != 8) return fail(NQ_ERR_DTYPE, "tensor '%s' has ggml type %u, expected Q8_0 (8)", tensor_name, t->type);
+  if (t->dims.size() != 2) return fail(NQ_ERR_SHAPE, "tensor '%s' is %zu-D, expected 2-D", tensor_name, t->dims.size());
+  const int64_t k = static_cast<int64_t>(t->dims[0]);
+  const int64_t n = static_cast<int64_t>(t->dims[1]);
+  rc = check_weight_shape(n, k, flags);
+  if (rc) return rc;
+  const size_t bytes = static_cast<size_t>(n) * (k / 32) * 34;
+  const uint8_t *p = f.data(*t, bytes);
+  if (!p) return fail(NQ_ERR_FORMAT, "tensor '%s' data lies beyond the end of the file", tensor_name);
+  return upload_packed(p, n, k, flags, out);
+}
+
+int nq_gguf_tensor_info(const char *path, const char *tensor_name, int *ggml_type, int64_t *n, int64_t *k) {
+  if (!path || !tensor_name) return fail(NQ_ERR_ARG, "null argument");
+  nq::GgufFile f;
+  std::string err;
+  int rc = f.open(path, &err);
+  if (rc) return fail(rc, "%s", err.c_str());
+  const nq::GgufTensor *t = f.find(tensor_name);
+  if (!t) return fail(NQ_ERR_ARG, "tensor '%s' not found in %s", tensor_name, path);
+  if (ggml_type) *ggml_type = static_cast<int>(t->type);
+  if (t->dims.size() != 2) return fail(NQ_ERR_SHAPE, "tensor '%s' is %zu-D, expected 2-D", tensor_name, t->dims.size());
+  if (k) *k = static_cast<int64_t>(t->dims[0]);
+  if (n) *n = static_cast<int64_t>(t->dims[1]);
+  return NQ_OK;
+}
+
+int nq_weight_to_q8_0(const nq_weight *w, void *blocks_out) {
+  if (!w || !blocks_out) return fail(NQ_ERR_ARG, "null argument");
+  std::vector<uint8_t> host(w->bytes);
+  cudaError_t e = cudaMemcpy(host.data(), w->dev, w->bytes, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(weight readback)");
+  nq::unpack_q8_0(host.data(), w->n, w->k, w->flags, static_cast<uint8_t *>(blocks_out));
+  return NQ_OK;
+}
+
+int nq_weights_fuse(const nq_weight *const *ws, int count, int flags, nq_weight **out) {
+  if (!ws || count <= 0 || !out) return fail(NQ_ERR_ARG, "null argument");
+  int64_t k = -1, n_total = 0;
+  for (int i = 0; i < count; ++i) {
+    if (!ws[i]) return fail(NQ_ERR_ARG, "null weight %d", i);
+    if (ws[i]->flags & NQ_PACK_GLU) return fail(NQ_ERR_UNSUPPORTED, "cannot fuse GLU-packed weights");
+    if (k < 0) k = ws[i]->k;
+    if (ws[i]->k != k) return fail(NQ_ERR_SHAPE, "fused weights must share K");
+    n_total += ws[i]->n;
+  }
+  int rc = check_weight_shape(n_total, k, flags);
+  if (rc) return rc;
+  const size_t row_bytes = static_cast<size_t>(k / 32) * 34;
+  std::vector<uint8_t> blocks(static_cast<size_t>(n_total) * row_bytes);
+  size_t off = 0;
+  for (int i = 0; i < count; ++i) {
+    rc = nq_weight_to_q8_0(ws[i], blocks.data() + off);
+    if (rc) return rc;
+    off += static_cast<size_t>(ws[i]->n) * row_bytes;
+  }
+  return upload_packed(blocks.data(), n_total, k, flags, out);
+}
+
+int nq_weight_shape(const nq_weight *w, int64_t *n, int64_t *k, int *flags) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  if (n) *n = w->n;
+  if (k) *k = w->k;
+  if (flags) *flags = w->flags;
+  return NQ_OK;
+}
+
+void nq_weight_free(nq_weight *w) {
+  if (!w) return;
+  int cur = 0;
+  cudaGetDevice(&cur);
+  if (cur != w->device) cudaSetDevice(w->device);
+  cudaFree(w->dev);
+  if (cur != w->device) cudaSetDevice(cur);
+  delete w;
+}
+
+int nq_linear(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx, const float *bias, int epilogue,
+              void *y, int y_dtype, int64_t ldy, void *stream) {
+  LinearArgs a{w, bias, y, ldy};
+  return linear_impl(&a, 1, x, x_dtype, m, ldx, epilogue, y_dtype, stream);
+}
+
+int nq_matmul(const nq_weight *w, const void *a, int a_dtype, void *c, int c_dtype, int64_t m, void *stream) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  return nq_linear(w, a, a_dtype, m, w->k, nullptr, NQ_EPI_NONE, c, c_dtype, w->n, stream);
+}
+
+int nq_matmul_bias(const nq_weight *w, const void *a, int a_dtype, const float *bias, void *c, int c_dtype, int64_t m,
+                   void *stream) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  return nq_linear(w, a, a_dtype, m, w->k, bias, NQ_EPI_NONE, c, c_dtype, w->n, stream);
+}
+
+int nq_matmul_bias_gelu(const nq_weight *w, const void *a, int a_dtype, const float *bias, void *c, int c_dtype,
+                        int64_t m, void *stream) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  return nq_linear(w, a, a_dtype, m, w->k, bias, NQ_EPI_GELU_ERF, c, c_dtype, w->n, stream);
+}
+
+int nq_gemv_splitk(const nq_weight *w, const void *x, int x_dtype, const float *bias, void *out, int out_dtype,
+                   void *stream) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  return nq_linear(w, x, x_dtype, 1, w->k, bias, NQ_EPI_NONE, out, out_dtype, w->n, stream);
+}
+
+int nq_gemv_glu_splitk(const nq_weight *w, const void *x, int x_dtype, const float *bias, void *out, int out_dtype,
+                       void *stream) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  return nq_linear(w, x, x_dtype, 1, w->k, bias, NQ_EPI_GLU_SILU, out, out_dtype, w->n / 2, stream);
+}
+
+int nq_gemv_qkv_splitk(const nq_weight *wq, const nq_weight *wk, const nq_weight *wv, const void *x, int x_dtype,
+                       void *q, void *k, void *v, int out_dtype, void *stream) {
+  if (!wq || !wk || !wv) return fail(NQ_ERR_ARG, "null weight");
+  if (wq->k != wk->k || wq->k != wv->k) return fail(NQ_ERR_SHAPE, "Q/K/V weights must share K");
+  LinearArgs a[3] = {{wq, nullptr, q, wq->n}, {wk, nullptr, k, wk->n}, {wv, nullptr, v, wv->n}};
+  return linear_impl(a, 3, x, x_dtype, 1, wq->k, NQ_EPI_NONE, out_dtype, stream);
+}
+
+int nq_last_error(char *buf, int len) {
+  const int n = static_cast<int>(t_err.size());
+  if (buf && len > 0) {
+    const int c = std::min(n, len - 1);
+    std::memcpy(buf, t_err.data(), c);
+    buf[c] = 0;
+  }
+  return n;
+}
+
+int nq_status(void *stream, int *bits) {
+  DeviceCtx *ctx = nullptr;
+  int rc = current_ctx(&ctx, nullptr);
+  if (rc) return rc;
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  int v = 0;
+  e = cudaMemcpy(&v, ctx->status, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(status)");
+  if (bits) *bits = v;
+  if (v) {
+    cudaMemset(ctx->status, 0, sizeof(int));
+    // A kernel that gave up may have left split-K counters armed: re-zero them.
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    for (auto &kv : ctx->ws)
+      if (kv.second.counters) cudaMemset(kv.second.counters, 0, kCounterSlots * sizeof(int));
+    return fail(NQ_ERR_TIMEOUT, "device status 0x%x: a bounded wait in a kernel ran out", v);
+  }
+  return NQ_OK;
+}
+
+int nq_set_wait_limit(int64_t cycles) {
+  if (cycles <= 0) return fail(NQ_ERR_ARG, "wait limit must be positive");
+  g_wait_limit = cycles;
+  return NQ_OK;
+}
+
+int nq_debug_wait_timeout(void *stream) {
+  DeviceCtx *ctx = nullptr;
+  int rc = current_ctx(&ctx, nullptr);
+  if (rc) return rc;
+  nq::DevCtl ctl{ctx->status, g_wait_limit};
+  cudaError_t e = nq::launch_wait_timeout_probe(ctl, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "probe launch");
+  return NQ_OK;
+}
+
+}  // extern "C"

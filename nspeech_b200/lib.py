@@ -1,0 +1,129 @@
+"""ctypes binding of libnq8.so (the C ABI declared in include/nq8.h).
+
+The shared library is built in-tree (``nspeech_b200/_lib/libnq8.so``) by
+``make -C nspeech_b200/csrc`` or ``__graft_entry__.build()``.  Loading fails
+loudly when it is missing: there is no CPU fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "_lib", "libnq8.so")
+HEADER_PATH = os.path.join(os.path.dirname(_HERE), "include", "nq8.h")
+
+# status codes
+NQ_OK = 0
+NQ_ERR_ARG = -1
+NQ_ERR_SHAPE = -2
+NQ_ERR_ALIGN = -3
+NQ_ERR_DTYPE = -4
+NQ_ERR_CUDA = -5
+NQ_ERR_TIMEOUT = -6
+NQ_ERR_FORMAT = -7
+NQ_ERR_IO = -8
+NQ_ERR_NOT_INIT = -9
+NQ_ERR_UNSUPPORTED = -10
+NQ_ERR_DEVICE = -11
+
+NQ_F32 = 0
+NQ_BF16 = 1
+
+NQ_EPI_NONE = 0
+NQ_EPI_SILU = 1
+NQ_EPI_GELU_ERF = 2
+NQ_EPI_GLU_SIGMOID = 3
+NQ_EPI_GLU_SILU = 4
+
+NQ_PACK_DEFAULT = 0
+NQ_PACK_GLU = 1
+
+
+class NqError(RuntimeError):
+    """A non-zero status from libnq8 (carries the code and the library message)."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"libnq8 error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+_lock = threading.Lock()
+_inited: set[int] = set()
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I = ctypes.c_int
+
+# name -> (restype, argtypes); every function declared in include/nq8.h.
+SIGNATURES = {
+    "nq_init": (_I, [_I]),
+    "nq_version": (ctypes.c_char_p, []),
+    "nq_weight_from_q8_0": (_I, [_P, _I64, _I64, _I, ctypes.POINTER(_P)]),
+    "nq_weight_from_f32": (_I, [_P, _I64, _I64, _I, ctypes.POINTER(_P)]),
+    "nq_weight_from_gguf": (_I, [ctypes.c_char_p, ctypes.c_char_p, _I, ctypes.POINTER(_P)]),
+    "nq_gguf_tensor_info": (_I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(_I), ctypes.POINTER(_I64),
+                                 ctypes.POINTER(_I64)]),
+    "nq_weights_fuse": (_I, [ctypes.POINTER(_P), _I, _I, ctypes.POINTER(_P)]),
+    "nq_weight_to_q8_0": (_I, [_P, _P]),
+    "nq_weight_shape": (_I, [_P, ctypes.POINTER(_I64), ctypes.POINTER(_I64), ctypes.POINTER(_I)]),
+    "nq_weight_free": (None, [_P]),
+    "nq_linear": (_I, [_P, _P, _I, _I64, _I64, _P, _I, _P, _I, _I64, _P]),
+    "nq_matmul": (_I, [_P, _P, _I, _P, _I, _I64, _P]),
+    "nq_matmul_bias": (_I, [_P, _P, _I, _P, _P, _I, _I64, _P]),
+    "nq_matmul_bias_gelu": (_I, [_P, _P, _I, _P, _P, _I, _I64, _P]),
+    "nq_gemv_splitk": (_I, [_P, _P, _I, _P, _P, _I, _P]),
+    "nq_gemv_glu_splitk": (_I, [_P, _P, _I, _P, _P, _I, _P]),
+    "nq_gemv_qkv_splitk": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _I, _P]),
+    "nq_last_error": (_I, [ctypes.c_char_p, _I]),
+    "nq_status": (_I, [_P, ctypes.POINTER(_I)]),
+    "nq_set_wait_limit": (_I, [_I64]),
+    "nq_debug_wait_timeout": (_I, [_P]),
+}
+
+
+def load() -> ctypes.CDLL:
+    """Load libnq8.so and bind every exported symbol (no CUDA work)."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise ImportError(
+                    f"{LIB_PATH} is missing: build it with `make -C nspeech_b200/csrc` "
+                    "(there is no CPU fallback)")
+            L = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    load().nq_last_error(buf, len(buf))
+    return buf.value.decode(errors="replace")
+
+
+def check(rc: int) -> None:
+    if rc != NQ_OK:
+        raise NqError(rc, last_error())
+
+
+def init(device: int = 0) -> None:
+    """nq_init for `device` on the calling thread (idempotent)."""
+    L = load()
+    check(L.nq_init(device))
+    _inited.add(device)
+
+
+def status(stream_ptr: int = 0) -> int:
+    """Synchronize the stream and return the device status bits (0 = clean)."""
+    bits = ctypes.c_int(0)
+    rc = load().nq_status(_P(stream_ptr), ctypes.byref(bits))
+    if rc not in (NQ_OK, NQ_ERR_TIMEOUT):
+        check(rc)
+    return bits.value
