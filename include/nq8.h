@@ -59,6 +59,7 @@ extern "C" {
 #define NQ_EPI_GELU_ERF 2    /* Moonshine encoder fc1 (src/moonshine/encoder.rs:105) */
 #define NQ_EPI_GLU_SIGMOID 3 /* pointwise_conv1: a*sigmoid(b) (fast_conformer.rs:479-484) */
 #define NQ_EPI_GLU_SILU 4    /* Moonshine decoder fc1: x*silu(gate) (moonshine/decoder.rs:403-410) */
+#define NQ_EPI_RELU 5        /* subsampling pointwise convs (fast_conformer.rs:180-183) */
 
 /* ---- weight packing flags ----------------------------------------------- */
 #define NQ_PACK_DEFAULT 0
@@ -151,6 +152,84 @@ int nq_gemv_glu_splitk(const nq_weight *w, const void *x, int x_dtype, const flo
 int nq_gemv_qkv_splitk(const nq_weight *wq, const nq_weight *wk, const nq_weight *wv,
                        const void *x, int x_dtype, void *q, void *k, void *v, int out_dtype,
                        void *stream);
+
+/* ---- FastConformer encoder (the caller of the Q8_0 path for configs 2/5) ---
+ * Mirrors FastConformerConfig (src/parakeet/fast_conformer.rs:31-45) and
+ * FastConformerEncoder::forward (:1072-1104, blocks :967-999): dw-striding
+ * 8x subsampling, x*sqrt(d), relative positions, then per layer macaron FFN
+ * (x0.5), rel-pos MHSA, conv module (pw1+GLU, depthwise, BN, SiLU, pw2),
+ * FFN, norm_out.  Every contraction with a rank-2 / pointwise weight runs on
+ * the Q8_0 kernels with bf16 activations; the residual stream is f32.
+ * Batches of padded segments reproduce per-segment results (masks). */
+typedef struct nq_encoder_config {
+  int feat_in;      /* log-mel bins (128) */
+  int d_model;      /* 1024 (512 also supported); head dim must be 128 */
+  int n_heads;      /* 8 */
+  int ff_mult;      /* 4 */
+  int n_layers;     /* 24 */
+  int conv_kernel;  /* 9 (odd, <= 31) */
+  int sub_channels; /* 256 */
+  int scale_input;  /* 1: multiply the subsampled input by sqrt(d_model) */
+} nq_encoder_config;
+
+typedef struct nq_encoder nq_encoder;
+
+/* Empty encoder bound to the current device; fill with nq_encoder_set_tensor
+ * or nq_encoder_load_gguf, then nq_encoder_finalize. */
+int nq_encoder_create(const nq_encoder_config *cfg, nq_encoder **out);
+
+/* Stage one tensor by its reference name (e.g.
+ * "encoder.layers.3.self_attn.q_proj.weight", the names produced by
+ * remap_nemo_tensor_name, src/parakeet/transducer.rs:1279-1302).
+ * ggml_type 0 = F32 data, 8 = Q8_0 blocks; dims outermost first (candle
+ * order, e.g. a linear weight is [out, in]).  Q8_0 matrices given as F32 are
+ * quantized with ggml semantics.  Host memory; copied. */
+int nq_encoder_set_tensor(nq_encoder *enc, const char *name, int ggml_type, const void *data,
+                          const int64_t *dims, int n_dims);
+
+/* Stage every "encoder.*" tensor of a GGUF file (Q8_0 or F32). */
+int nq_encoder_load_gguf(nq_encoder *enc, const char *path);
+
+/* Check completeness, fill the defaults the reference loader adds (zero
+ * biases, BN running mean 0 / var 1: src/parakeet/transducer.rs:1955-1996),
+ * fuse Q/K/V, pack the pointwise_conv1 weight for the fused GLU, upload. */
+int nq_encoder_finalize(nq_encoder *enc);
+
+/* Encoder frames produced from t_mel input frames (three stride-2 stages). */
+int nq_encoder_out_frames(int t_mel);
+
+/* mel: device f32 [batch, t_mel, feat_in]; lengths: host int32 [batch] valid
+ * mel frames per segment (<= t_mel; NULL = all t_mel).  out: device f32
+ * [batch, T, d_model] with T = nq_encoder_out_frames(t_mel), frames beyond a
+ * segment's own length zeroed; out_lengths (host, may be NULL) receives the
+ * per-segment encoder lengths.  Replaces TransducerModel::run_encoder
+ * (src/parakeet/transducer.rs:387-404) for a batch of VAD segments. */
+int nq_encoder_forward(nq_encoder *enc, const float *mel, const int32_t *lengths, int batch, int t_mel,
+                       float *out, int32_t *out_lengths, void *stream);
+
+/* Same with host buffers: copies mel in and the output back on `stream`
+ * (pinned host memory recommended) and synchronizes it. */
+int nq_encoder_forward_host(nq_encoder *enc, const float *mel_host, const int32_t *lengths, int batch,
+                            int t_mel, float *out_host, int32_t *out_lengths, void *stream);
+
+/* Number of kernels nq_encoder_forward launches for (batch, t_mel). */
+int nq_encoder_launch_count(const nq_encoder *enc, int batch, int t_mel);
+
+void nq_encoder_free(nq_encoder *enc);
+
+/* ---- per-kernel timing --------------------------------------------------
+ * When enabled, every Q8_0 kernel launch of this process is bracketed by CUDA
+ * events on its own stream (the per-op timing of the reference's
+ * TRITON_ENCODER_PROFILE / forward_profile, src/moonshine/gpu_encoder.rs:
+ * 367-369,508).  Kernel classes: */
+#define NQ_KCLASS_GEMM 0 /* tcgen05 GEMM (M > 16) */
+#define NQ_KCLASS_GEMV 1 /* split-K GEMV (M <= 16) */
+int nq_profile_enable(int on);
+/* Synchronizes the recorded events and reports for one class: launches,
+ * summed device ms, summed algorithmic FLOPs (2MNK) and bytes
+ * (N*K*34/32 + M*K*sx + M*N*sy + 4N).  reset != 0 clears the record. */
+int nq_profile_read(int kernel_class, int64_t *launches, double *total_ms, double *flops, double *bytes,
+                    int reset);
 
 /* Thread-local message of the last failure ("" if none); returns its length. */
 int nq_last_error(char *buf, int len);

@@ -177,7 +177,7 @@ int validate(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t 
   if (m < 0) return fail(NQ_ERR_SHAPE, "negative M");
   if (x_dtype != NQ_F32 && x_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "x dtype %d unsupported", x_dtype);
   if (y_dtype != NQ_F32 && y_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "y dtype %d unsupported", y_dtype);
-  if (epilogue < NQ_EPI_NONE || epilogue > NQ_EPI_GLU_SILU) return fail(NQ_ERR_ARG, "unknown epilogue %d", epilogue);
+  if (epilogue < NQ_EPI_NONE || epilogue > NQ_EPI_RELU) return fail(NQ_ERR_ARG, "unknown epilogue %d", epilogue);
   const bool glu_epi = epilogue == NQ_EPI_GLU_SIGMOID || epilogue == NQ_EPI_GLU_SILU;
   const bool glu_w = (w->flags & NQ_PACK_GLU) != 0;
   if (glu_epi && !glu_w) return fail(NQ_ERR_UNSUPPORTED, "GLU epilogue needs a weight packed with NQ_PACK_GLU");
@@ -189,6 +189,51 @@ int validate(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t 
   if (m > (1LL << 30)) return fail(NQ_ERR_SHAPE, "M too large");
   return NQ_OK;
 }
+
+// ------------------------------------------------------------ profiling
+// Event pairs around each kernel launch while profiling is on; read back
+// (synchronizing the events) by nq_profile_read.
+struct ProfRecord {
+  int kclass;
+  cudaEvent_t start, stop;
+  double flops, bytes;
+};
+struct Profiler {
+  std::mutex mu;
+  bool on = false;
+  std::vector<ProfRecord> records;
+  std::vector<cudaEvent_t> pool;
+  cudaEvent_t take() {
+    if (!pool.empty()) {
+      cudaEvent_t e = pool.back();
+      pool.pop_back();
+      return e;
+    }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+  }
+};
+Profiler g_prof;
+
+struct ProfScope {
+  ProfRecord rec{};
+  cudaStream_t stream;
+  bool active = false;
+  ProfScope(int kclass, cudaStream_t s, double flops, double bytes) : stream(s) {
+    std::lock_guard<std::mutex> lk(g_prof.mu);
+    if (!g_prof.on) return;
+    rec = ProfRecord{kclass, g_prof.take(), g_prof.take(), flops, bytes};
+    active = rec.start && rec.stop;
+    if (active) cudaEventRecord(rec.start, stream);
+  }
+  ~ProfScope() {
+    if (!active) return;
+    cudaEventRecord(rec.stop, stream);
+    std::lock_guard<std::mutex> lk(g_prof.mu);
+    g_prof.records.push_back(rec);
+  }
+};
 
 // ------------------------------------------------------------------ GEMV
 int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
@@ -247,6 +292,14 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
   (void)mrows;
+  double flops = 0, bytes = 0;
+  for (int i = 0; i < nprob; ++i) {
+    const nq_weight *w = args[i].w;
+    flops += 2.0 * m * w->n * w->k;
+    bytes += w->n * (w->k / 32) * 34.0 + m * w->k * (x_dtype == NQ_F32 ? 4.0 : 2.0) +
+             m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (args[i].bias ? 4.0 * w->n : 0.0);
+  }
+  ProfScope ps(NQ_KCLASS_GEMV, stream, flops, bytes);
   cudaError_t e = nq::launch_gemv(p, nprob, max_tiles, x_dtype == NQ_F32, stream);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return NQ_OK;
@@ -332,6 +385,10 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
   p.counters = ws->counters;
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
+  const double flops = 2.0 * m * w->n * w->k;
+  const double bytes = w->n * (w->k / 32) * 34.0 + m * w->k * (x_dtype == NQ_F32 ? 4.0 : 2.0) +
+                       m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (a.bias ? 4.0 * w->n : 0.0);
+  ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
   cudaError_t e = nq::launch_gemm(var, tm_a, tm_alo, p, stream);
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return NQ_OK;
@@ -361,6 +418,10 @@ int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, i
 }
 
 }  // namespace
+
+namespace nq {
+int api_fail(int code, const std::string &msg) { return fail(code, "%s", msg.c_str()); }
+}  // namespace nq
 
 // ======================================================================= ABI
 extern "C" {
@@ -566,6 +627,43 @@ int nq_status(void *stream, int *bits) {
     for (auto &kv : ctx->ws)
       if (kv.second.counters) cudaMemset(kv.second.counters, 0, kCounterSlots * sizeof(int));
     return fail(NQ_ERR_TIMEOUT, "device status 0x%x: a bounded wait in a kernel ran out", v);
+  }
+  return NQ_OK;
+}
+
+int nq_profile_enable(int on) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  g_prof.on = on != 0;
+  return NQ_OK;
+}
+
+int nq_profile_read(int kernel_class, int64_t *launches, double *total_ms, double *flops, double *bytes, int reset) {
+  std::lock_guard<std::mutex> lk(g_prof.mu);
+  int64_t n = 0;
+  double ms = 0, fl = 0, by = 0;
+  for (const auto &r : g_prof.records) {
+    if (r.kclass != kernel_class) continue;
+    cudaError_t e = cudaEventSynchronize(r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize(profile)");
+    float t = 0.f;
+    e = cudaEventElapsedTime(&t, r.start, r.stop);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime(profile)");
+    ++n;
+    ms += t;
+    fl += r.flops;
+    by += r.bytes;
+  }
+  if (launches) *launches = n;
+  if (total_ms) *total_ms = ms;
+  if (flops) *flops = fl;
+  if (bytes) *bytes = by;
+  if (reset) {
+    for (const auto &r : g_prof.records) {
+      cudaEventSynchronize(r.stop);
+      g_prof.pool.push_back(r.start);
+      g_prof.pool.push_back(r.stop);
+    }
+    g_prof.records.clear();
   }
   return NQ_OK;
 }

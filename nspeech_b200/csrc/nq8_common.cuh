@@ -239,7 +239,7 @@ __device__ __forceinline__ void mma_16816_bf16(float (&d)[4], const uint32_t (&a
 }
 
 // ----------------------------------------------------------- epilogue math
-enum Epi : int { kEpiNone = 0, kEpiSilu = 1, kEpiGeluErf = 2, kEpiGluSigmoid = 3, kEpiGluSilu = 4 };
+enum Epi : int { kEpiNone = 0, kEpiSilu = 1, kEpiGeluErf = 2, kEpiGluSigmoid = 3, kEpiGluSilu = 4, kEpiRelu = 5 };
 
 __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + __expf(-v)); }
 
@@ -247,6 +247,7 @@ __device__ __forceinline__ float sigmoidf_(float v) { return 1.0f / (1.0f + __ex
 __device__ __forceinline__ float act_single(int epi, float v) {
   if (epi == kEpiSilu) return v * sigmoidf_(v);
   if (epi == kEpiGeluErf) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  if (epi == kEpiRelu) return fmaxf(v, 0.0f);
   return v;
 }
 // GLU: value * act(gate).

@@ -1,0 +1,33 @@
+// nq8_encoder.h -- launch interfaces of the encoder glue kernels (internal).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+
+namespace nq {
+namespace enc {
+
+constexpr int kLnScale = 0;      // x = alpha * u (f32); h = LN1(x)
+constexpr int kLnResAdd = 1;     // x += alpha * u (bf16); h = LN1(x)
+constexpr int kLnResAddOut = 2;  // x = LN1(x + alpha * u); h = LN2(x) if LN2 given
+
+cudaError_t conv0_relu(const float *mel, const int *len0, int B, int T, int F, int T1, int F1, int C, const float *w,
+                       const float *bias, __nv_bfloat16 *out, cudaStream_t s);
+cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int Tin, int Fin, int Tout, int Fout, int C,
+                        const float *w, const float *bias, __nv_bfloat16 *out, cudaStream_t s);
+cudaError_t flatten_cf(const __nv_bfloat16 *in, int rows, int F, int C, __nv_bfloat16 *out, cudaStream_t s);
+cudaError_t ln_rows(int mode, float *x, const void *u, float alpha, int rows, int D, const float *g1, const float *b1,
+                    const float *g2, const float *b2, __nv_bfloat16 *h, float eps, cudaStream_t s);
+cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int Tp, int D, int K, const float *w,
+                             const float *bias, const float *bn_scale, const float *bn_shift, __nv_bfloat16 *out,
+                             cudaStream_t s);
+cudaError_t relpos(int T, int D, __nv_bfloat16 *pos, cudaStream_t s);
+cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, const float *bias_u,
+                             const float *bias_v, const int *len, int B, int Tp, int H, int D, __nv_bfloat16 *out,
+                             cudaStream_t s);
+// out[b, t, :] = x[b, t, :] for t < len[b], else 0 (f32 rows of D).
+cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, float *out, cudaStream_t s);
+
+}  // namespace enc
+}  // namespace nq

@@ -373,8 +373,14 @@ static cudaError_t launch_gemm_t(const CUtensorMap &a_hi, const CUtensorMap &a_l
                                  cudaStream_t stream) {
   using C = GemmCfg<BN, STAGES, SPLITX>;
   auto kern = gemm_q8_sm100_kernel<BN, STAGES, SPLITX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-  if (e != cudaSuccess) return e;
+  static bool attr_set[64] = {false};  // once per device (the attribute is per-context state)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) attr_set[dev] = true;
+  }
   dim3 grid(p.grid_n, p.grid_m, p.splits);
   kern<<<grid, kGemmThreads, C::kSmemBytes, stream>>>(a_hi, a_lo, p);
   return cudaGetLastError();

@@ -28,6 +28,7 @@ constexpr int kGemvStages = 6;
 constexpr int kGemvConsumerWarps = 8;
 constexpr int kGemvThreads = 32 * (1 + kGemvConsumerWarps);
 constexpr int kAccPitch = 132;  // floats per row of the staged accumulator tile
+constexpr int kGemvMaxCps = 8;  // k chunks per split (bounds the staged activation slice)
 
 static __host__ __device__ inline int gemv_x_pitch(int cps) { return cps * kPackK * 2 + 8; }
 
@@ -255,8 +256,16 @@ template <int MT, bool SPLITX>
 static cudaError_t launch_gemv_t(const GemvParams &p, int nprob, int grid_x, cudaStream_t stream) {
   const size_t smem = gemv_smem_bytes(8 * MT, SPLITX, p.cps);
   auto kern = gemv_q8_kernel<MT, SPLITX>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
+  static bool attr_set[64] = {false};  // once per device, sized for the largest split (cps = 8)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(gemv_smem_bytes(8 * MT, SPLITX, kGemvMaxCps)));
+    if (e != cudaSuccess) return e;
+    if (dev < 64) attr_set[dev] = true;
+  }
+  if (p.cps > kGemvMaxCps) return cudaErrorInvalidValue;
   dim3 grid(grid_x, p.splits, nprob);
   kern<<<grid, kGemvThreads, smem, stream>>>(p);
   return cudaGetLastError();

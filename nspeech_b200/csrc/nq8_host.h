@@ -15,6 +15,9 @@ constexpr int kPackGlu = 1;
 constexpr int kErrIo = -8;
 constexpr int kErrFormat = -7;
 
+// Record `msg` as the calling thread's last error (nq_last_error) and return code.
+int api_fail(int code, const std::string &msg);
+
 int pack_n_tiles(int64_t n, int flags);
 int pack_k_chunks(int64_t k);
 // GGUF Q8_0 blocks [n][k/32] x 34 B  <->  tiles [n_tiles][kc] x 8704 B.

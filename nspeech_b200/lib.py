@@ -36,6 +36,7 @@ NQ_EPI_SILU = 1
 NQ_EPI_GELU_ERF = 2
 NQ_EPI_GLU_SIGMOID = 3
 NQ_EPI_GLU_SILU = 4
+NQ_EPI_RELU = 5
 
 NQ_PACK_DEFAULT = 0
 NQ_PACK_GLU = 1
@@ -47,6 +48,14 @@ class NqError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"libnq8 error {code}: {msg}")
         self.code = code
+
+
+class EncoderConfig(ctypes.Structure):
+    """nq_encoder_config (mirrors FastConformerConfig, src/parakeet/fast_conformer.rs:31-45)."""
+
+    _fields_ = [("feat_in", ctypes.c_int), ("d_model", ctypes.c_int), ("n_heads", ctypes.c_int),
+                ("ff_mult", ctypes.c_int), ("n_layers", ctypes.c_int), ("conv_kernel", ctypes.c_int),
+                ("sub_channels", ctypes.c_int), ("scale_input", ctypes.c_int)]
 
 
 _lib = None
@@ -77,6 +86,19 @@ SIGNATURES = {
     "nq_gemv_splitk": (_I, [_P, _P, _I, _P, _P, _I, _P]),
     "nq_gemv_glu_splitk": (_I, [_P, _P, _I, _P, _P, _I, _P]),
     "nq_gemv_qkv_splitk": (_I, [_P, _P, _P, _P, _I, _P, _P, _P, _I, _P]),
+    "nq_encoder_create": (_I, [_P, ctypes.POINTER(_P)]),
+    "nq_encoder_set_tensor": (_I, [_P, ctypes.c_char_p, _I, _P, ctypes.POINTER(_I64), _I]),
+    "nq_encoder_load_gguf": (_I, [_P, ctypes.c_char_p]),
+    "nq_encoder_finalize": (_I, [_P]),
+    "nq_encoder_out_frames": (_I, [_I]),
+    "nq_encoder_forward": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int32), _I, _I, _P, ctypes.POINTER(ctypes.c_int32), _P]),
+    "nq_encoder_forward_host": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int32), _I, _I, _P,
+                                     ctypes.POINTER(ctypes.c_int32), _P]),
+    "nq_encoder_launch_count": (_I, [_P, _I, _I]),
+    "nq_encoder_free": (None, [_P]),
+    "nq_profile_enable": (_I, [_I]),
+    "nq_profile_read": (_I, [_I, ctypes.POINTER(_I64), ctypes.POINTER(ctypes.c_double),
+                             ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _I]),
     "nq_last_error": (_I, [ctypes.c_char_p, _I]),
     "nq_status": (_I, [_P, ctypes.POINTER(_I)]),
     "nq_set_wait_limit": (_I, [_I64]),
@@ -127,3 +149,20 @@ def status(stream_ptr: int = 0) -> int:
     if rc not in (NQ_OK, NQ_ERR_TIMEOUT):
         check(rc)
     return bits.value
+
+
+NQ_KCLASS_GEMM = 0
+NQ_KCLASS_GEMV = 1
+
+
+def profile_enable(on: bool) -> None:
+    check(load().nq_profile_enable(1 if on else 0))
+
+
+def profile_read(kclass: int, reset: bool = True) -> dict:
+    """Per-kernel-class launch count, device ms, algorithmic FLOPs and bytes."""
+    n = ctypes.c_int64()
+    ms, fl, by = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+    check(load().nq_profile_read(kclass, ctypes.byref(n), ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(by),
+                                 1 if reset else 0))
+    return {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}

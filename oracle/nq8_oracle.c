@@ -182,6 +182,7 @@ enum {
     OQ_EPI_GELU_ERF = 2,
     OQ_EPI_GLU_SIGMOID = 3,
     OQ_EPI_GLU_SILU = 4,
+    OQ_EPI_RELU = 5,
 };
 
 static double sigmoid_d(double v) { return 1.0 / (1.0 + exp(-v)); }
@@ -201,6 +202,7 @@ void oq_epilogue_f64(const double *y, int64_t m, int64_t n, const float *bias, i
             if (!glu) {
                 if (epi == OQ_EPI_SILU) a = a * sigmoid_d(a);
                 else if (epi == OQ_EPI_GELU_ERF) a = 0.5 * a * (1.0 + erf(a / sqrt(2.0)));
+                else if (epi == OQ_EPI_RELU) a = a > 0.0 ? a : 0.0;
                 orow[j] = a;
             } else {
                 double g = yr[j + n_out] + (bias ? (double)bias[j + n_out] : 0.0);

@@ -22,7 +22,7 @@ _lib = None
 QK = 32
 BLOCK_BYTES = 34
 
-EPI_NONE, EPI_SILU, EPI_GELU_ERF, EPI_GLU_SIGMOID, EPI_GLU_SILU = range(5)
+EPI_NONE, EPI_SILU, EPI_GELU_ERF, EPI_GLU_SIGMOID, EPI_GLU_SILU, EPI_RELU = range(6)
 
 _f32p = np.ctypeslib.ndpointer(dtype=np.float32, flags="C_CONTIGUOUS")
 _f64p = np.ctypeslib.ndpointer(dtype=np.float64, flags="C_CONTIGUOUS")
@@ -33,8 +33,8 @@ _i64 = ctypes.c_int64
 
 def build() -> str:
     """Compile the oracle with its Makefile (gcc) if it is missing or stale."""
-    src = os.path.join(_HERE, "nq8_oracle.c")
-    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+    srcs = [os.path.join(_HERE, s) for s in ("nq8_oracle.c", "encoder_oracle.c", "Makefile")]
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(os.path.getmtime(s) for s in srcs):
         subprocess.run(["make", "-s", "-C", _HERE], check=True)
     return _LIB_PATH
 
@@ -177,3 +177,104 @@ def max_rel_err(y: np.ndarray, yref: np.ndarray, tau: float = 1e-3) -> float:
     m = y.shape[0] if y.ndim > 1 else 1
     n = y.shape[-1]
     return float(lib().oq_max_rel_err(y.reshape(-1), yref.reshape(-1), m, n, tau))
+
+
+# ---------------------------------------------------------------- encoder
+class _EncCfg(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("feat_in", "d_model", "n_heads", "ff_mult", "n_layers",
+                                             "conv_kernel", "sub_channels", "scale_input")]
+
+
+_U8P = ctypes.POINTER(ctypes.c_uint8)
+_F32P = ctypes.POINTER(ctypes.c_float)
+
+
+class _EncLayer(ctypes.Structure):
+    _fields_ = ([(n, _U8P) for n in ("ff1_w1", "ff1_w2", "ff2_w1", "ff2_w2", "q", "k", "v", "o", "rel", "pw1", "pw2")]
+                + [(n, _F32P) for n in ("ff1_b1", "ff1_b2", "ff2_b1", "ff2_b2", "q_b", "k_b", "v_b", "o_b", "pw1_b",
+                                        "pw2_b", "bias_u", "bias_v", "dw_w", "dw_b", "bn_g", "bn_b", "bn_mean",
+                                        "bn_var")]
+                + [("ln_g", _F32P * 5), ("ln_b", _F32P * 5)])
+
+
+class _EncWeights(ctypes.Structure):
+    _fields_ = ([(n, _F32P) for n in ("c0_w", "c0_b", "dw2_w", "dw2_b", "dw5_w", "dw5_b", "pw3_b", "pw6_b", "lin_b")]
+                + [(n, _U8P) for n in ("pw3", "pw6", "lin")] + [("layers", ctypes.POINTER(_EncLayer))])
+
+
+def encoder_forward(cfg: dict, tensors: dict, mel: np.ndarray, weight_mode: int = 0) -> np.ndarray:
+    """Batch-1 FastConformer encoder forward (encoder_oracle.c) -> [T3, d_model].
+
+    ``tensors``: name -> f32 array for vectors, uint8 Q8_0 blocks [n, k/32*34]
+    for the rank-2 / pointwise matrices (the names of remap_nemo_tensor_name).
+    weight_mode 0: bf16-rounded dequantized weights (fast_matmul semantics);
+    1: exact dequantized f32 weights (candle Linear).
+    """
+    L = lib()
+    L.oq_encoder_forward.argtypes = [ctypes.POINTER(_EncCfg), ctypes.POINTER(_EncWeights), _f32p, ctypes.c_int, _f32p]
+    L.oq_encoder_forward.restype = ctypes.c_int
+    L.oq_encoder_set_weight_mode.argtypes = [ctypes.c_int]
+    keep = []
+
+    def f(name, default=None):
+        a = tensors.get(name)
+        if a is None:
+            a = default
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        keep.append(a)
+        return a.ctypes.data_as(_F32P)
+
+    def q(name):
+        a = np.ascontiguousarray(tensors[name], dtype=np.uint8)
+        keep.append(a)
+        return a.ctypes.data_as(_U8P)
+
+    d = cfg["d_model"]
+    ones, zeros = np.ones(d, np.float32), np.zeros(d, np.float32)
+    c = _EncCfg(**{n: int(cfg[n]) for n, _ in _EncCfg._fields_})
+    layers = (_EncLayer * cfg["n_layers"])()
+    for i in range(cfg["n_layers"]):
+        p = f"encoder.layers.{i}."
+        Ly = layers[i]
+        Ly.ff1_w1, Ly.ff1_w2 = q(p + "feed_forward1.linear1.weight"), q(p + "feed_forward1.linear2.weight")
+        Ly.ff2_w1, Ly.ff2_w2 = q(p + "feed_forward2.linear1.weight"), q(p + "feed_forward2.linear2.weight")
+        Ly.q, Ly.k = q(p + "self_attn.q_proj.weight"), q(p + "self_attn.k_proj.weight")
+        Ly.v, Ly.o = q(p + "self_attn.v_proj.weight"), q(p + "self_attn.o_proj.weight")
+        Ly.rel = q(p + "self_attn.relative_k_proj.weight")
+        Ly.pw1, Ly.pw2 = q(p + "conv.pointwise_conv1.weight"), q(p + "conv.pointwise_conv2.weight")
+        ff = d * cfg["ff_mult"]
+        Ly.ff1_b1 = f(p + "feed_forward1.linear1.bias", np.zeros(ff, np.float32))
+        Ly.ff1_b2 = f(p + "feed_forward1.linear2.bias", zeros)
+        Ly.ff2_b1 = f(p + "feed_forward2.linear1.bias", np.zeros(ff, np.float32))
+        Ly.ff2_b2 = f(p + "feed_forward2.linear2.bias", zeros)
+        Ly.q_b, Ly.k_b = f(p + "self_attn.q_proj.bias", zeros), f(p + "self_attn.k_proj.bias", zeros)
+        Ly.v_b, Ly.o_b = f(p + "self_attn.v_proj.bias", zeros), f(p + "self_attn.o_proj.bias", zeros)
+        Ly.pw1_b = f(p + "conv.pointwise_conv1.bias", np.zeros(2 * d, np.float32))
+        Ly.pw2_b = f(p + "conv.pointwise_conv2.bias", zeros)
+        Ly.bias_u, Ly.bias_v = f(p + "self_attn.bias_u"), f(p + "self_attn.bias_v")
+        Ly.dw_w, Ly.dw_b = f(p + "conv.depthwise_conv.weight"), f(p + "conv.depthwise_conv.bias", zeros)
+        Ly.bn_g, Ly.bn_b = f(p + "conv.norm.weight", ones), f(p + "conv.norm.bias", zeros)
+        Ly.bn_mean, Ly.bn_var = f(p + "conv.norm.running_mean", zeros), f(p + "conv.norm.running_var", ones)
+        for j, nm in enumerate(("norm_feed_forward1", "norm_self_att", "norm_conv", "norm_feed_forward2", "norm_out")):
+            Ly.ln_g[j] = f(p + nm + ".weight", ones)
+            Ly.ln_b[j] = f(p + nm + ".bias", zeros)
+    sp = "encoder.subsampling."
+    C = cfg["sub_channels"]
+    zc = np.zeros(C, np.float32)
+    W = _EncWeights(c0_w=f(sp + "layers.0.weight"), c0_b=f(sp + "layers.0.bias", zc),
+                    dw2_w=f(sp + "layers.2.weight"), dw2_b=f(sp + "layers.2.bias", zc),
+                    dw5_w=f(sp + "layers.5.weight"), dw5_b=f(sp + "layers.5.bias", zc),
+                    pw3_b=f(sp + "layers.3.bias", zc), pw6_b=f(sp + "layers.6.bias", zc),
+                    lin_b=f(sp + "linear.bias", zeros), pw3=q(sp + "layers.3.weight"), pw6=q(sp + "layers.6.weight"),
+                    lin=q(sp + "linear.weight"), layers=layers)
+    mel = _f32(mel)
+    t_mel = mel.shape[0]
+    t3 = t_mel
+    for _ in range(3):
+        t3 = (t3 - 1) // 2 + 1
+    out = np.empty((t3, d), np.float32)
+    L.oq_encoder_set_weight_mode(weight_mode)
+    got = L.oq_encoder_forward(ctypes.byref(c), ctypes.byref(W), mel.reshape(-1), t_mel, out.reshape(-1))
+    assert got == t3
+    del keep
+    return out

@@ -1,0 +1,159 @@
+"""GPU FastConformer encoder (libnq8 nq_encoder_*) against the CPU oracle.
+
+The GPU runs bf16 activations into every Q8_0 contraction (config 2 says
+"bf16 activations"); the oracle keeps f32 activations with the same
+bf16-rounded weights (fast_matmul semantics).  Contract per config:
+  * max |y - y_ref| / max(|y_ref|, rms(row)) <= ENC_TOL (stated per case),
+  * per-frame argmax over channels identical on every frame whose top-2
+    margin in the oracle exceeds 4x the observed max abs error.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def nq():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from nspeech_b200 import lib
+    lib.init(0)
+    return lib
+
+
+def _model(oracle, spec, seed=1):
+    from nspeech_b200 import synthetic as S
+    t = S.encoder_tensors(spec, seed)
+    q = {}
+    for k, (v, is_q8) in t.items():
+        q[k] = (oracle.quantize_q8_0(v.reshape(v.shape[0], -1)), v.shape) if is_q8 else (v, None)
+    return q
+
+
+def _gpu_encoder(spec, q):
+    from nspeech_b200.encoder import ParakeetEncoder
+    enc = ParakeetEncoder(spec)
+    for name, (arr, dims) in q.items():
+        enc.set_tensor(name, arr, q8_0_dims=dims)
+    return enc.finalize()
+
+
+def _oracle_tensors(q):
+    return {k: v for k, (v, _d) in q.items()}
+
+
+def _record(tag, **kv):
+    path = os.environ.get("NQ8_TEST_METRICS")
+    if path:
+        with open(path, "a") as f:
+            f.write(json.dumps({"test": tag, **kv}) + "\n")
+
+
+def _compare(oracle, got, ref, tag, tol):
+    err = oracle.max_rel_err(got, ref.astype(np.float64), 1.0)
+    abs_err = float(np.abs(got - ref).max())
+    srt = np.sort(ref, axis=1)
+    margin = srt[:, -1] - srt[:, -2]
+    confident = margin > 4 * abs_err
+    agree = (got.argmax(1) == ref.argmax(1))
+    _record(tag, rel_err=err, max_abs=abs_err, frames=int(len(ref)), confident=int(confident.sum()),
+            argmax_agree_all=float(agree.mean()), argmax_agree_confident=float(agree[confident].mean()) if confident.any() else 1.0)
+    assert np.isfinite(got).all(), tag
+    assert err <= tol, f"{tag}: rel err {err:.3e} > {tol}"
+    assert agree[confident].all(), f"{tag}: argmax differs on a confident frame"
+    return err
+
+
+@pytest.mark.parametrize("d_model,heads,layers,t_mel,tol", [(512, 4, 2, 400, 0.05), (1024, 8, 2, 800, 0.05)])
+def test_encoder_matches_oracle(nq, oracle, d_model, heads, layers, t_mel, tol):
+    from nspeech_b200 import synthetic as S
+    spec = S.EncoderSpec(d_model=d_model, n_heads=heads, n_layers=layers, sub_channels=64 if d_model == 512 else 256)
+    q = _model(oracle, spec)
+    enc = _gpu_encoder(spec, q)
+    mel = oracle.normal(1, (t_mel, 128))
+    out, lens = enc.forward(torch.from_numpy(mel)[None].cuda())
+    torch.cuda.synchronize()
+    ref = oracle.encoder_forward(spec.as_dict(), _oracle_tensors(q), mel)
+    assert lens == [ref.shape[0]]
+    _compare(oracle, out[0].cpu().numpy(), ref, f"encoder d{d_model} L{layers} T{t_mel}", tol)
+
+
+def test_batched_segments_equal_single(nq, oracle):
+    """A padded batch of segments reproduces each segment's own forward."""
+    from nspeech_b200 import synthetic as S
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=2, sub_channels=64)
+    q = _model(oracle, spec, seed=3)
+    enc = _gpu_encoder(spec, q)
+    lens = [611, 200, 433, 97]
+    T = max(lens)
+    mel = np.zeros((len(lens), T, 128), np.float32)
+    for i, L in enumerate(lens):
+        mel[i, :L] = oracle.normal(10 + i, (L, 128))
+    out, olens = enc.forward(torch.from_numpy(mel).cuda(), lens)
+    out = out.cpu().numpy()
+    from nspeech_b200.encoder import out_frames
+    for i, L in enumerate(lens):
+        single, sl = enc.forward(torch.from_numpy(mel[i:i + 1, :L]).cuda().contiguous())
+        single = single[0].cpu().numpy()
+        assert olens[i] == sl[0] == out_frames(L)
+        np.testing.assert_allclose(out[i, :olens[i]], single, rtol=2e-2, atol=2e-2)
+        assert oracle.max_rel_err(out[i, :olens[i]], single.astype(np.float64), 1.0) < 2e-2
+        assert not out[i, olens[i]:].any()  # padded frames are zeroed
+        ref = oracle.encoder_forward(spec.as_dict(), _oracle_tensors(q), mel[i, :L])
+        _compare(oracle, out[i, :olens[i]], ref, f"batched seg {i} len {L}", 0.05)
+
+
+def test_forward_host_matches_device(nq, oracle):
+    from nspeech_b200 import synthetic as S
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=1, sub_channels=64)
+    q = _model(oracle, spec, seed=5)
+    enc = _gpu_encoder(spec, q)
+    mel = oracle.normal(2, (2, 300, 128))
+    d_out, _ = enc.forward(torch.from_numpy(mel).cuda())
+    h_out, lens = enc.forward_host(mel, [300, 250])
+    d_out2, _ = enc.forward(torch.from_numpy(mel).cuda(), [300, 250])
+    assert lens == [38, 32]
+    np.testing.assert_array_equal(h_out, d_out2.cpu().numpy())
+    np.testing.assert_array_equal(h_out[0], d_out[0].cpu().numpy())
+
+
+def test_encoder_from_gguf(nq, oracle, tmp_path):
+    gguf = pytest.importorskip("gguf")
+    from nspeech_b200 import synthetic as S
+    from nspeech_b200.encoder import ParakeetEncoder
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=1, sub_channels=64)
+    q = _model(oracle, spec, seed=7)
+    p = tmp_path / "enc.gguf"
+    w = gguf.GGUFWriter(str(p), arch="parakeet")
+    for name, (arr, dims) in q.items():
+        if dims is not None:
+            w.add_tensor(name, arr, raw_dtype=gguf.GGMLQuantizationType.Q8_0)  # byte shape -> [n, k]
+        else:
+            w.add_tensor(name, arr)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()
+    a = ParakeetEncoder(spec).load_gguf(str(p)).finalize()
+    b = _gpu_encoder(spec, q)
+    mel = torch.from_numpy(oracle.normal(3, (1, 256, 128))).cuda()
+    ya, _ = a.forward(mel)
+    yb, _ = b.forward(mel)
+    assert torch.equal(ya, yb)
+
+
+def test_encoder_rejects_bad_config(nq):
+    from nspeech_b200 import lib, synthetic as S
+    from nspeech_b200.encoder import ParakeetEncoder
+    with pytest.raises(lib.NqError) as e:
+        ParakeetEncoder(S.EncoderSpec(d_model=768, n_heads=8))
+    assert e.value.code == lib.NQ_ERR_UNSUPPORTED
+    enc = ParakeetEncoder(S.EncoderSpec(d_model=512, n_heads=4, n_layers=1, sub_channels=64))
+    with pytest.raises(lib.NqError) as e:
+        enc.finalize()  # nothing staged
+    assert "missing tensor" in str(e.value)
