@@ -150,10 +150,11 @@ int check_weight_shape(int64_t n, int64_t k, int flags) {
   return NQ_OK;
 }
 
-int make_tmap(DeviceCtx *ctx, CUtensorMap *map, const void *ptr, int64_t kdim, int64_t rows, int64_t ld_elems) {
+int make_tmap(DeviceCtx *ctx, CUtensorMap *map, const void *ptr, int64_t kdim, int64_t rows, int64_t ld_elems,
+              int box_rows) {
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(kdim), static_cast<cuuint64_t>(rows)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld_elems) * 2};
-  cuuint32_t box[2] = {64, 128};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = ctx->encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(ptr), dims, strides, box,
                            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -313,17 +314,12 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
   const int64_t k_pad = static_cast<int64_t>(kc) * nq::kPackK;
   const bool splitx = x_dtype == NQ_F32;
   const bool direct = !splitx && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 8 == 0);
-  const int grid_m = static_cast<int>((m + 127) / 128);
 
-  nq::GemmVariant var;
-  if (splitx) {
-    var = nq::kGemmBn128SplitX;
-  } else {
-    const int tiles256 = grid_m * ((w->n_tiles + 1) / 2);
-    var = tiles256 >= ctx->sm_count ? nq::kGemmBn256 : nq::kGemmBn128;
-  }
-  const int bn = nq::gemm_block_n(var);
-  const int grid_n = (w->n_tiles * nq::kPackRows + bn - 1) / bn;
+  const nq::GemmVariant var = splitx ? nq::kGemmBt128SplitX : nq::kGemmBt128;
+  const int bt = nq::gemm_block_t(var);
+  const int grid_m = static_cast<int>((m + bt - 1) / bt);
+  const int grid_n = w->n_tiles;
+  const int bn = bt;  // partial tile is [128][BT]
   const int tiles = grid_m * grid_n;
   int splits = 1;
   if (tiles < ctx->sm_count) {
@@ -354,10 +350,10 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     a_ld = k_pad;
   }
   CUtensorMap tm_a, tm_alo;
-  rc = make_tmap(ctx, &tm_a, a_ptr, a_k, m, a_ld);
+  rc = make_tmap(ctx, &tm_a, a_ptr, a_k, m, a_ld, bt);
   if (rc) return rc;
   if (splitx) {
-    rc = make_tmap(ctx, &tm_alo, lo, a_k, m, a_ld);
+    rc = make_tmap(ctx, &tm_alo, lo, a_k, m, a_ld, bt);
     if (rc) return rc;
   } else {
     tm_alo = tm_a;
@@ -389,7 +385,9 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
   const double bytes = w->n * (w->k / 32) * 34.0 + m * w->k * (x_dtype == NQ_F32 ? 4.0 : 2.0) +
                        m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (a.bias ? 4.0 * w->n : 0.0);
   ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
-  cudaError_t e = nq::launch_gemm(var, tm_a, tm_alo, p, stream);
+  const int units = tiles * splits;
+  const int grid = std::min(units, ctx->sm_count);
+  cudaError_t e = nq::launch_gemm(var, tm_a, tm_alo, p, grid, stream);
   if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   return NQ_OK;
 }

@@ -152,10 +152,10 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_cons
         break;
       }
       const uint8_t *st = ring + s * kTileBytes;
-      const uint4 qa = *reinterpret_cast<const uint4 *>(st + row_a * kPackK + c * 16);
-      const uint4 qb = *reinterpret_cast<const uint4 *>(st + row_b * kPackK + c * 16);
-      const float da = __half2float(*reinterpret_cast<const __half *>(st + kTileQsBytes + row_a * 4 + (c >> 1) * 2));
-      const float db = __half2float(*reinterpret_cast<const __half *>(st + kTileQsBytes + row_b * 4 + (c >> 1) * 2));
+      const uint4 qa = *reinterpret_cast<const uint4 *>(st + qs_offset(row_a, c));
+      const uint4 qb = *reinterpret_cast<const uint4 *>(st + qs_offset(row_b, c));
+      const float da = __half2float(*reinterpret_cast<const __half *>(st + scale_offset(row_a, c >> 1)));
+      const float db = __half2float(*reinterpret_cast<const __half *>(st + scale_offset(row_b, c >> 1)));
       __syncwarp();
       if (lane == 0) mbar_arrive(empty_bar(s));
 

@@ -49,8 +49,9 @@ void pack_q8_0(const uint8_t *blocks, int64_t n, int64_t k, int flags, uint8_t *
           const int64_t b = static_cast<int64_t>(c) * 2 + h;
           if (b >= kb) continue;
           const uint8_t *blk = srow + b * 34;
-          std::memcpy(tile + r * kPackK + h * 32, blk + 2, 32);
-          std::memcpy(tile + kTileQsBytes + r * 4 + h * 2, blk, 2);
+          std::memcpy(tile + qs_offset(r, 2 * h), blk + 2, 16);
+          std::memcpy(tile + qs_offset(r, 2 * h + 1), blk + 2 + 16, 16);
+          std::memcpy(tile + scale_offset(r, h), blk, 2);
         }
       }
     }
@@ -71,8 +72,9 @@ void unpack_q8_0(const uint8_t *packed, int64_t n, int64_t k, int flags, uint8_t
           const int64_t b = static_cast<int64_t>(c) * 2 + h;
           if (b >= kb) continue;
           uint8_t *blk = drow + b * 34;
-          std::memcpy(blk + 2, tile + r * kPackK + h * 32, 32);
-          std::memcpy(blk, tile + kTileQsBytes + r * 4 + h * 2, 2);
+          std::memcpy(blk + 2, tile + qs_offset(r, 2 * h), 16);
+          std::memcpy(blk + 2 + 16, tile + qs_offset(r, 2 * h + 1), 16);
+          std::memcpy(blk, tile + scale_offset(r, h), 2);
         }
       }
     }

@@ -58,19 +58,21 @@ struct GemmParams {
   int64_t ldy;
   int splits;
   int cps;
-  int grid_n;
-  int grid_m;
-  float *partials;  // [splits][grid_m][grid_n][128][BN] f32 (split-K only)
+  int grid_n;       // 128-row weight tiles (= n_tiles)
+  int grid_m;       // token tiles of BT rows
+  float *partials;  // [splits][grid_m][grid_n][128][BT] f32 (split-K only)
   int *counters;    // [grid_m * grid_n]
   DevCtl ctl;
 };
 
-// Which compiled tile configuration to launch.
-enum GemmVariant : int { kGemmBn256 = 0, kGemmBn128 = 1, kGemmBn128SplitX = 2 };
-int gemm_block_n(GemmVariant v);
+// Which compiled token-tile configuration to launch.
+enum GemmVariant : int { kGemmBt256 = 0, kGemmBt128 = 1, kGemmBt64 = 2, kGemmBt128SplitX = 3 };
+int gemm_block_t(GemmVariant v);
 size_t gemm_smem_bytes(GemmVariant v);
+// Persistent launch: `grid` CTAs (<= one per SM) walk grid_n * grid_m * splits
+// work units.
 cudaError_t launch_gemm(GemmVariant v, const CUtensorMap &a_hi, const CUtensorMap &a_lo,
-                        const GemmParams &p, cudaStream_t stream);
+                        const GemmParams &p, int grid, cudaStream_t stream);
 
 // f32 -> bf16 planes: hi = bf16(x), lo = bf16(x - hi) (lo may be null); rows
 // of k_pad elements, zero beyond K.  Also used for bf16 -> bf16 copies when a
