@@ -16,31 +16,42 @@ __device__ __forceinline__ float bf(const __nv_bfloat16 v) { return __bfloat162f
 // conv2d(1 -> C, 3x3, stride 2, pad 1) + bias + ReLU on the log-mel
 // [B, T, F] (f32), output NHWC [B, T1, F1, C] bf16 (fast_conformer.rs:103-107,
 // 176-177).  Frames t >= len0[b] read as zero.
+// One block per output row (b, t1): the three input mel rows it needs are
+// staged in shared memory (zero-padded on both axes, frames >= len0[b] zero),
+// thread c computes channel c for every output frequency; each output row
+// position is one contiguous C-wide store across the block.
+constexpr int kMaxFeat = 512;
 __global__ void conv0_relu_kernel(const float *__restrict__ mel, const int *__restrict__ len0, int T, int F,
                                   int T1, int F1, int C, const float *__restrict__ w, const float *__restrict__ bias,
                                   __nv_bfloat16 *__restrict__ out) {
-  const int b = blockIdx.z;
-  const int t1 = blockIdx.y;
-  const int c = threadIdx.x;  // blockDim.x == C
+  __shared__ float rows[3][kMaxFeat + 2];  // column j holds frequency j - 1
+  const int b = blockIdx.y;
+  const int t1 = blockIdx.x;
   const int L = len0[b];
-  float wr[9];
+  for (int idx = threadIdx.x; idx < 3 * (F + 2); idx += blockDim.x) {
+    const int dt = idx / (F + 2);
+    const int j = idx - dt * (F + 2);
+    const int t = 2 * t1 - 1 + dt;
+    const int f = j - 1;
+    float v = 0.f;
+    if (t >= 0 && t < T && t < L && f >= 0 && f < F) v = mel[(static_cast<int64_t>(b) * T + t) * F + f];
+    rows[dt][j] = v;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float wr[9];
 #pragma unroll
-  for (int i = 0; i < 9; ++i) wr[i] = w[c * 9 + i];
-  const float bc = bias[c];
-  for (int f1 = blockIdx.x * 8; f1 < min(F1, blockIdx.x * 8 + 8); ++f1) {
-    float acc = bc;
+    for (int i = 0; i < 9; ++i) wr[i] = w[c * 9 + i];
+    const float bc = bias[c];
+    __nv_bfloat16 *o = out + (static_cast<int64_t>(b) * T1 + t1) * F1 * C + c;
+    for (int f1 = 0; f1 < F1; ++f1) {
+      float acc = bc;
 #pragma unroll
-    for (int dt = 0; dt < 3; ++dt) {
-      const int t = 2 * t1 - 1 + dt;
-      if (t < 0 || t >= T || t >= L) continue;
+      for (int dt = 0; dt < 3; ++dt)
 #pragma unroll
-      for (int df = 0; df < 3; ++df) {
-        const int f = 2 * f1 - 1 + df;
-        if (f < 0 || f >= F) continue;
-        acc += wr[dt * 3 + df] * mel[(static_cast<int64_t>(b) * T + t) * F + f];
-      }
+        for (int df = 0; df < 3; ++df) acc += wr[dt * 3 + df] * rows[dt][2 * f1 + df];
+      o[static_cast<int64_t>(f1) * C] = __float2bfloat16_rn(fmaxf(acc, 0.f));
     }
-    out[((static_cast<int64_t>(b) * T1 + t1) * F1 + f1) * C + c] = __float2bfloat16_rn(fmaxf(acc, 0.f));
   }
 }
 
@@ -493,8 +504,9 @@ size_t attention_smem_bytes() {
 // ------------------------------------------------------------------ launches
 cudaError_t conv0_relu(const float *mel, const int *len0, int B, int T, int F, int T1, int F1, int C, const float *w,
                        const float *bias, __nv_bfloat16 *out, cudaStream_t s) {
-  dim3 grid((F1 + 7) / 8, T1, B);
-  conv0_relu_kernel<<<grid, C, 0, s>>>(mel, len0, T, F, T1, F1, C, w, bias, out);
+  if (F > kMaxFeat || 2 * (F1 - 1) + 2 > F + 1) return cudaErrorInvalidValue;
+  dim3 grid(T1, B);
+  conv0_relu_kernel<<<grid, C <= 1024 ? C : 1024, 0, s>>>(mel, len0, T, F, T1, F1, C, w, bias, out);
   return cudaGetLastError();
 }
 
