@@ -222,14 +222,22 @@ void nq_encoder_free(nq_encoder *enc);
  * events on its own stream (the per-op timing of the reference's
  * TRITON_ENCODER_PROFILE / forward_profile, src/moonshine/gpu_encoder.rs:
  * 367-369,508).  Kernel classes: */
-#define NQ_KCLASS_GEMM 0 /* tcgen05 GEMM (M > 16) */
-#define NQ_KCLASS_GEMV 1 /* split-K GEMV (M <= 16) */
+#define NQ_KCLASS_GEMM 0    /* tcgen05 GEMM (M > 16) */
+#define NQ_KCLASS_GEMV 1    /* split-K GEMV (M <= 16) */
+#define NQ_KCLASS_DEQUANT 2 /* Q8_0 -> bf16 weight pass of the large-M GEMM */
+#define NQ_KCLASS_REDUCE 3  /* split-K reduction after a split GEMM */
 int nq_profile_enable(int on);
 /* Synchronizes the recorded events and reports for one class: launches,
  * summed device ms, summed algorithmic FLOPs (2MNK) and bytes
- * (N*K*34/32 + M*K*sx + M*N*sy + 4N).  reset != 0 clears the record. */
+ * (N*K*34/32 + M*K*sx + M*N*sy + 4N).  reset != 0 clears that class's
+ * records. */
 int nq_profile_read(int kernel_class, int64_t *launches, double *total_ms, double *flops, double *bytes,
                     int reset);
+
+/* Kernels this library has launched in this process (all devices and
+ * streams); reset != 0 returns the count and zeroes it.  No counterpart in
+ * the reference: launch accounting for benchmarks and tests. */
+int nq_launch_counter(int64_t *count, int reset);
 
 /* Thread-local message of the last failure ("" if none); returns its length. */
 int nq_last_error(char *buf, int len);
@@ -241,6 +249,17 @@ int nq_status(void *stream, int *bits);
 /* Cycle budget of every bounded wait in the kernels (default ~2^31 cycles,
  * about one second).  Lowered only by tests. */
 int nq_set_wait_limit(int64_t cycles);
+
+/* Which kernel serves a GEMM call (M > 16).  No counterpart in the
+ * reference: a B200 dispatch knob.  AUTO (default) dequantizes the weight
+ * once into scratch and runs the bf16 tcgen05 GEMM from 128 tokens, and
+ * runs the fused in-kernel-dequantizing GEMM below that; FUSED and DEQUANT
+ * force one of them (tests use this to cover both on the same shapes).
+ * Process-wide; returns NQ_ERR_ARG for an unknown value. */
+#define NQ_GEMM_AUTO 0
+#define NQ_GEMM_FUSED 1
+#define NQ_GEMM_DEQUANT 2
+int nq_set_gemm_path(int path);
 
 /* Test hook for failure detection: launches a kernel that waits on an
  * mbarrier nothing arrives on, bounded by the wait limit; the kernel records

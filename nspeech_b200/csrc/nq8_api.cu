@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -58,6 +59,10 @@ struct DeviceCtx {
 DeviceCtx g_ctx[kMaxDevices];
 std::mutex g_init_mu;
 long long g_wait_limit = 1LL << 31;
+int g_gemm_path = NQ_GEMM_AUTO;
+// Token count from which a GEMM call dequantizes the weight once and runs
+// the bf16 tensor-core GEMM (measured crossover on B200).
+constexpr int64_t kDequantMinM = 128;
 thread_local std::string t_err;
 
 int fail(int code, const char *fmt, ...) {
@@ -307,41 +312,69 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
 }
 
 // ------------------------------------------------------------------ GEMM
+// How one GEMM call (M > 16) is carried out.
+struct GemmPlan {
+  bool deq;        // dequantize-once path (dequant_tiles + K3), else fused K1
+  bool split_x;    // activations staged to bf16 planes first (f32, or unaligned bf16)
+  int bt;          // tokens per pair unit
+  int grid_m, grid_n, splits, cps, pairs;
+  int launches() const { return 1 + (deq ? 1 : 0) + (splits > 1 ? 1 : 0) + (split_x ? 1 : 0); }
+};
+
+// The fused kernel (K1) re-dequantizes the weight for every 192-token tile
+// and is issue-bound; the dequantize-once path is tensor-bound and wins from
+// kDequantMinM tokens (measured on B200), unless a path is forced.
+GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, bool direct) {
+  GemmPlan g;
+  const bool splitx = x_dtype == NQ_F32;
+  g.deq = g_gemm_path == NQ_GEMM_DEQUANT || (g_gemm_path == NQ_GEMM_AUTO && m >= kDequantMinM);
+  g.split_x = !direct;
+  g.pairs = std::max(1, sm_count / 2);
+  g.bt = g.deq ? nq::gemm_bf16_block_t() : nq::gemm_block_t(splitx ? nq::kGemmBt128SplitX : nq::kGemmBt128);
+  g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
+  g.grid_n = (w->n_tiles + 1) / 2;
+  // Split K when the output tiles do not fill the SM pairs (>= 4 k chunks per split).
+  const int tiles = g.grid_m * g.grid_n;
+  const int kc = w->kc;
+  int splits = 1;
+  if (tiles < g.pairs) splits = std::max(1, std::min((g.pairs + tiles - 1) / tiles, std::max(1, kc / 4)));
+  g.cps = (kc + splits - 1) / splits;
+  g.splits = (kc + g.cps - 1) / g.cps;
+  return g;
+}
+
+bool direct_bf16(const void *x, int x_dtype, int64_t ldx) {
+  return x_dtype == NQ_BF16 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 8 == 0);
+}
+
 int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, int64_t m, int64_t ldx, int epilogue,
              int y_dtype, cudaStream_t stream) {
   const nq_weight *w = a.w;
   const int kc = w->kc;
   const int64_t k_pad = static_cast<int64_t>(kc) * nq::kPackK;
   const bool splitx = x_dtype == NQ_F32;
-  const bool direct = !splitx && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 8 == 0);
+  const bool direct = direct_bf16(x, x_dtype, ldx);
+  const GemmPlan plan = plan_gemm(ctx->sm_count, w, m, x_dtype, direct);
+  const bool deq = plan.deq;
+  const int pairs = plan.pairs, bt = plan.bt, grid_m = plan.grid_m, grid_n = plan.grid_n;
+  const int splits = plan.splits, cps = plan.cps;
+  const int ldp = w->n_tiles * nq::kPackRows;  // rows of partials / of the dequantized weight
 
-  const nq::GemmVariant var = splitx ? nq::kGemmBt128SplitX : nq::kGemmBt128;
-  const int bt = nq::gemm_block_t(var);
-  const int grid_m = static_cast<int>((m + bt - 1) / bt);
-  const int grid_n = w->n_tiles;
-  const int bn = bt;  // partial tile is [128][BT]
-  const int tiles = grid_m * grid_n;
-  int splits = 1;
-  if (tiles < ctx->sm_count) {
-    splits = std::min((ctx->sm_count + tiles - 1) / tiles, std::max(1, kc / 4));
-    splits = std::max(splits, 1);
-  }
-  int cps = (kc + splits - 1) / splits;
-  splits = (kc + cps - 1) / cps;
-
+  // Workspace: [activation planes][dequantized weight][split-K partials].
   size_t xbytes = 0;
   if (!direct) xbytes = align_up(static_cast<size_t>(m) * k_pad * 2, 1024) * (splitx ? 2 : 1);
-  size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * tiles * 128 * bn * sizeof(float) : 0;
+  const size_t wbytes = deq ? align_up(static_cast<size_t>(ldp) * k_pad * 2, 1024) : 0;
+  const size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * m * ldp * sizeof(float) : 0;
   Workspace *ws = nullptr;
-  int rc = get_workspace(ctx, stream, xbytes + part_bytes, &ws);
+  int rc = get_workspace(ctx, stream, xbytes + wbytes + part_bytes, &ws);
   if (rc) return rc;
-  if (splits > 1 && static_cast<size_t>(tiles) > kCounterSlots) return fail(NQ_ERR_SHAPE, "too many tiles for the counter pool");
+  float *partials = splits > 1 ? reinterpret_cast<float *>(ws->buf + xbytes + wbytes) : nullptr;
 
   const void *a_ptr = x;
   int64_t a_k = w->k, a_ld = ldx;
-  __nv_bfloat16 *hi = nullptr, *lo = nullptr;
+  __nv_bfloat16 *lo = nullptr;
   if (!direct) {
-    hi = reinterpret_cast<__nv_bfloat16 *>(ws->buf);
+    __nv_bfloat16 *hi = reinterpret_cast<__nv_bfloat16 *>(ws->buf);
     if (splitx) lo = reinterpret_cast<__nv_bfloat16 *>(ws->buf + xbytes / 2);
     cudaError_t e = nq::launch_split_x(x, x_dtype, ldx, m, w->k, k_pad, hi, lo, stream);
     if (e != cudaSuccess) return cuda_fail(e, "activation split launch");
@@ -350,45 +383,97 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     a_ld = k_pad;
   }
   CUtensorMap tm_a, tm_alo;
-  rc = make_tmap(ctx, &tm_a, a_ptr, a_k, m, a_ld, bt);
+  rc = make_tmap(ctx, &tm_a, a_ptr, a_k, m, a_ld, bt / 2);
   if (rc) return rc;
   if (splitx) {
-    rc = make_tmap(ctx, &tm_alo, lo, a_k, m, a_ld, bt);
+    rc = make_tmap(ctx, &tm_alo, lo, a_k, m, a_ld, bt / 2);
     if (rc) return rc;
   } else {
     tm_alo = tm_a;
   }
 
-  nq::GemmParams p;
-  std::memset(&p, 0, sizeof(p));
-  p.w = w->dev;
-  p.n_tiles = w->n_tiles;
-  p.kc_total = kc;
-  p.N = w->n;
-  p.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
-  p.n_out = out_width(w);
-  p.M = static_cast<int>(m);
-  p.bias = a.bias;
-  p.epi = epilogue;
-  p.y = a.y;
-  p.y_dtype = y_dtype;
-  p.ldy = a.ldy;
-  p.splits = splits;
-  p.cps = cps;
-  p.grid_n = grid_n;
-  p.grid_m = grid_m;
-  p.partials = splits > 1 ? reinterpret_cast<float *>(ws->buf + xbytes) : nullptr;
-  p.counters = ws->counters;
-  p.ctl.status = ctx->status;
-  p.ctl.wait_limit = g_wait_limit;
   const double flops = 2.0 * m * w->n * w->k;
   const double bytes = w->n * (w->k / 32) * 34.0 + m * w->k * (x_dtype == NQ_F32 ? 4.0 : 2.0) +
                        m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (a.bias ? 4.0 * w->n : 0.0);
-  ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
-  const int units = tiles * splits;
-  const int grid = std::min(units, ctx->sm_count);
-  cudaError_t e = nq::launch_gemm(var, tm_a, tm_alo, p, grid, stream);
-  if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  const int units = grid_m * grid_n * splits;
+  if (deq) {
+    __nv_bfloat16 *wb = reinterpret_cast<__nv_bfloat16 *>(ws->buf + xbytes);
+    {
+      ProfScope ps(NQ_KCLASS_DEQUANT, stream, 0.0, w->bytes + static_cast<double>(ldp) * k_pad * 2);
+      cudaError_t e = nq::launch_dequant_tiles(w->dev, w->n_tiles, kc, wb, stream);
+      if (e != cudaSuccess) return cuda_fail(e, "weight dequantize launch");
+    }
+    CUtensorMap tm_w;
+    rc = make_tmap(ctx, &tm_w, wb, k_pad, ldp, k_pad, nq::gemm_bf16_block_w() / 2);
+    if (rc) return rc;
+    nq::GemmBf16Params p;
+    std::memset(&p, 0, sizeof(p));
+    p.N = w->n;
+    p.n_rows = ldp;
+    p.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
+    p.n_out = out_width(w);
+    p.M = static_cast<int>(m);
+    p.kc_total = kc;
+    p.bias = a.bias;
+    p.epi = epilogue;
+    p.y = a.y;
+    p.y_dtype = y_dtype;
+    p.ldy = a.ldy;
+    p.splits = splits;
+    p.cps = cps;
+    p.grid_n = grid_n;
+    p.grid_m = grid_m;
+    p.partials = partials;
+    p.ctl.status = ctx->status;
+    p.ctl.wait_limit = g_wait_limit;
+    ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
+    cudaError_t e = nq::launch_gemm_bf16(splitx, tm_w, tm_a, tm_alo, p, std::min(units, pairs), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  } else {
+    nq::GemmParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.w = w->dev;
+    p.n_tiles = w->n_tiles;
+    p.kc_total = kc;
+    p.N = w->n;
+    p.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
+    p.n_out = out_width(w);
+    p.M = static_cast<int>(m);
+    p.bias = a.bias;
+    p.epi = epilogue;
+    p.y = a.y;
+    p.y_dtype = y_dtype;
+    p.ldy = a.ldy;
+    p.splits = splits;
+    p.cps = cps;
+    p.grid_n = grid_n;
+    p.grid_m = grid_m;
+    p.partials = partials;
+    p.ldp = ldp;
+    p.ctl.status = ctx->status;
+    p.ctl.wait_limit = g_wait_limit;
+    ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
+    cudaError_t e = nq::launch_gemm(splitx ? nq::kGemmBt128SplitX : nq::kGemmBt128, tm_a, tm_alo, p,
+                                    std::min(units, pairs), stream);
+    if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
+  }
+  if (splits > 1) {
+    nq::SplitkReduceParams r;
+    r.partials = partials;
+    r.splits = splits;
+    r.M = static_cast<int>(m);
+    r.ldp = ldp;
+    r.n_out = out_width(w);
+    r.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
+    r.bias = a.bias;
+    r.epi = epilogue;
+    r.y = a.y;
+    r.y_dtype = y_dtype;
+    r.ldy = a.ldy;
+    ProfScope ps(NQ_KCLASS_REDUCE, stream, 0.0, static_cast<double>(splits) * m * ldp * 4);
+    cudaError_t e = nq::launch_splitk_reduce(r, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
+  }
   return NQ_OK;
 }
 
@@ -419,6 +504,18 @@ int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, i
 
 namespace nq {
 int api_fail(int code, const std::string &msg) { return fail(code, "%s", msg.c_str()); }
+
+std::atomic<long long> g_launches{0};
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+int linear_launches(const nq_weight *w, int64_t m, int x_dtype, bool aligned) {
+  if (!w || m <= 0) return 0;
+  if (m <= 16) return 1;  // split-K GEMV (one launch for up to three weights)
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  const int sm = current_ctx(&ctx, &dev) == NQ_OK ? ctx->sm_count : kSmCountB200;
+  return plan_gemm(sm, w, m, x_dtype, x_dtype == NQ_BF16 && aligned).launches();
+}
 }  // namespace nq
 
 // ======================================================================= ABI
@@ -629,6 +726,12 @@ int nq_status(void *stream, int *bits) {
   return NQ_OK;
 }
 
+int nq_launch_counter(int64_t *count, int reset) {
+  if (!count) return fail(NQ_ERR_ARG, "null count");
+  *count = reset ? nq::g_launches.exchange(0) : nq::g_launches.load();
+  return NQ_OK;
+}
+
 int nq_profile_enable(int on) {
   std::lock_guard<std::mutex> lk(g_prof.mu);
   g_prof.on = on != 0;
@@ -656,13 +759,25 @@ int nq_profile_read(int kernel_class, int64_t *launches, double *total_ms, doubl
   if (flops) *flops = fl;
   if (bytes) *bytes = by;
   if (reset) {
+    std::vector<ProfRecord> keep;
     for (const auto &r : g_prof.records) {
+      if (r.kclass != kernel_class) {
+        keep.push_back(r);
+        continue;
+      }
       cudaEventSynchronize(r.stop);
       g_prof.pool.push_back(r.start);
       g_prof.pool.push_back(r.stop);
     }
-    g_prof.records.clear();
+    g_prof.records.swap(keep);
   }
+  return NQ_OK;
+}
+
+int nq_set_gemm_path(int path) {
+  if (path != NQ_GEMM_AUTO && path != NQ_GEMM_FUSED && path != NQ_GEMM_DEQUANT)
+    return fail(NQ_ERR_ARG, "unknown GEMM path %d", path);
+  g_gemm_path = path;
   return NQ_OK;
 }
 

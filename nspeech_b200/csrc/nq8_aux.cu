@@ -43,7 +43,79 @@ cudaError_t launch_split_x(const void *x, int x_dtype, int64_t ldx, int64_t M, i
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
   split_x_kernel<<<blocks, 256, 0, stream>>>(x, x_dtype, ldx, M, K, k_pad, hi, lo);
-  return cudaGetLastError();
+  return launched();
+}
+
+// One block per (k chunk, tile): 256 threads, thread t dequantizes Q8_0 block
+// (t & 1) of row t / 2 (32 elements) and writes 64 contiguous bytes.
+__global__ void __launch_bounds__(256) dequant_tiles_kernel(const uint8_t *__restrict__ w, int kc,
+                                                           __nv_bfloat16 *__restrict__ out) {
+  const int c = blockIdx.x, tile = blockIdx.y;
+  const uint8_t *t = w + (static_cast<size_t>(tile) * kc + c) * kTileBytes;
+  const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
+  const uint4 q0 = __ldg(reinterpret_cast<const uint4 *>(t + qs_offset(r, 2 * h)));
+  const uint4 q1 = __ldg(reinterpret_cast<const uint4 *>(t + qs_offset(r, 2 * h + 1)));
+  const float d = __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short *>(t + scale_offset(r, h)))));
+  uint32_t o[16];
+  const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) dequant4_bf16(qw[i], d, o[2 * i], o[2 * i + 1]);
+  const size_t ldk = static_cast<size_t>(kc) * kPackK;
+  uint4 *dst = reinterpret_cast<uint4 *>(out + (static_cast<size_t>(tile) * kPackRows + r) * ldk + c * kPackK + h * 32);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+}
+
+cudaError_t launch_dequant_tiles(const uint8_t *w, int n_tiles, int kc, __nv_bfloat16 *out, cudaStream_t stream) {
+  if (n_tiles <= 0 || kc <= 0) return cudaSuccess;
+  dequant_tiles_kernel<<<dim3(kc, n_tiles), 256, 0, stream>>>(w, kc, out);
+  return launched();
+}
+
+// Thread per (token, 4 consecutive output columns); the partial sums of the
+// splits are added in split order, so the result does not depend on timing.
+__global__ void splitk_reduce_kernel(SplitkReduceParams p) {
+  const int64_t quads = (p.n_out + 3) / 4;
+  const int64_t total = static_cast<int64_t>(p.M) * quads;
+  const size_t split_stride = static_cast<size_t>(p.M) * p.ldp;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
+       t += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t m = t / quads;
+    const int64_t j0 = (t - m * quads) * 4;
+    const float *base = p.partials + static_cast<size_t>(m) * p.ldp;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int64_t j = j0 + e;
+      if (j >= p.n_out) break;
+      if (!p.glu) {
+        float v = 0.f;
+        for (int s = 0; s < p.splits; ++s) v += __ldcs(base + s * split_stride + j);
+        if (p.bias) v += p.bias[j];
+        store_out(p.y, p.y_dtype, m * p.ldy + j, act_single(p.epi, v));
+      } else {
+        const int64_t row = (j / 64) * kPackRows + (j % 64);
+        float v = 0.f, g = 0.f;
+        for (int s = 0; s < p.splits; ++s) {
+          v += __ldcs(base + s * split_stride + row);
+          g += __ldcs(base + s * split_stride + row + 64);
+        }
+        if (p.bias) {
+          v += p.bias[j];
+          g += p.bias[p.n_out + j];
+        }
+        store_out(p.y, p.y_dtype, m * p.ldy + j, act_glu(p.epi, v, g));
+      }
+    }
+  }
+}
+
+cudaError_t launch_splitk_reduce(const SplitkReduceParams &p, cudaStream_t stream) {
+  const int64_t total = static_cast<int64_t>(p.M) * ((p.n_out + 3) / 4);
+  if (total == 0) return cudaSuccess;
+  int blocks = static_cast<int>((total + 255) / 256);
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p);
+  return launched();
 }
 
 // Failure-detection probe: waits on an mbarrier that nothing arrives on,
@@ -67,7 +139,7 @@ __global__ void wait_timeout_probe_kernel(DevCtl ctl) {
 
 cudaError_t launch_wait_timeout_probe(DevCtl ctl, cudaStream_t stream) {
   wait_timeout_probe_kernel<<<1, 32, 0, stream>>>(ctl);
-  return cudaGetLastError();
+  return launched();
 }
 
 }  // namespace nq

@@ -11,6 +11,15 @@
 
 namespace nq {
 
+// Host side: count one kernel launch of this library (process-wide counter
+// read by nq_launch_counter); `launched()` closes a <<<>>> launch with it.
+void note_launch();
+inline cudaError_t launched() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) note_launch();
+  return e;
+}
+
 // Device status bits (mirrors NQ_DEV_* in include/nq8.h).
 constexpr int kDevTimeoutProducer = 0x1;
 constexpr int kDevTimeoutConsumer = 0x2;

@@ -518,13 +518,26 @@ int nq_encoder_forward_host(nq_encoder *enc, const float *mel_host, const int32_
 }
 
 int nq_encoder_launch_count(const nq_encoder *enc, int batch, int t_mel) {
-  (void)batch;
-  (void)t_mel;
   if (!enc) return api_fail(NQ_ERR_ARG, "null encoder");
-  // subsampling: conv0, dw, pw(GEMM), dw, pw(GEMM), flatten, linear(GEMM), ln, relpos
-  // per layer: 9 GEMMs + attention + dwconv + 4 LN; final masked copy.
-  // GEMMs with f32 activations or unaligned bf16 add one split kernel (none here).
-  return 9 + enc->cfg.n_layers * (9 + 1 + 1 + 4) + 1;
+  if (!enc->ready) return api_fail(NQ_ERR_ARG, "encoder not finalized");
+  if (batch < 1 || t_mel < 1) return api_fail(NQ_ERR_SHAPE, "batch and t_mel must be positive");
+  // Same kernel sequence as forward(): glue kernels plus the launches each
+  // nq_linear call makes for its M (GEMV, or GEMM with its dequantize,
+  // activation-staging and split-K reduction kernels).
+  const Shapes s = shapes(enc, batch, t_mel);
+  const int M = s.M, Tp = s.T3;
+  auto lin = [&](const nq_weight *w, int64_t m, int64_t ldx) { return nq::linear_launches(w, m, NQ_BF16, ldx % 8 == 0); };
+  int n = 6;  // conv0, dwconv x2, flatten, scaled LN, relpos
+  n += lin(enc->pw3, static_cast<int64_t>(s.B) * s.T2 * s.F2, s.C);
+  n += lin(enc->pw6, static_cast<int64_t>(s.B) * s.T3 * s.F3, s.C);
+  n += lin(enc->lin, M, static_cast<int64_t>(s.F3) * s.C);
+  for (const Layer &L : enc->layers) {
+    n += 6;  // 4 LN, attention, depthwise conv
+    n += lin(L.ff1_w1, M, s.D) + lin(L.ff1_w2, M, s.D * enc->cfg.ff_mult) + lin(L.qkv, M, s.D) +
+         lin(L.rel, 2 * Tp - 1, s.D) + lin(L.o, M, s.D) + lin(L.pw1, M, s.D) + lin(L.pw2, M, s.D) +
+         lin(L.ff2_w1, M, s.D) + lin(L.ff2_w2, M, s.D * enc->cfg.ff_mult);
+  }
+  return n + 1;  // final masked copy
 }
 
 void nq_encoder_free(nq_encoder *enc) { delete enc; }

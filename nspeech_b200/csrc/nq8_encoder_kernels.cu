@@ -494,7 +494,7 @@ __global__ void copy_masked_kernel(const float *__restrict__ x, const int *__res
 cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, float *out, cudaStream_t s) {
   if (B * Tp == 0) return cudaSuccess;
   copy_masked_kernel<<<B * Tp, 256, 0, s>>>(x, len, Tp, D, out);
-  return cudaGetLastError();
+  return launched();
 }
 
 size_t attention_smem_bytes() {
@@ -507,7 +507,7 @@ cudaError_t conv0_relu(const float *mel, const int *len0, int B, int T, int F, i
   if (F > kMaxFeat || 2 * (F1 - 1) + 2 > F + 1) return cudaErrorInvalidValue;
   dim3 grid(T1, B);
   conv0_relu_kernel<<<grid, C <= 1024 ? C : 1024, 0, s>>>(mel, len0, T, F, T1, F1, C, w, bias, out);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int Tin, int Fin, int Tout, int Fout, int C,
@@ -516,12 +516,12 @@ cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int T
   const int threads = 256;
   dim3 grid((per + threads - 1) / threads, Tout, B);
   dwconv2d_s2_kernel<<<grid, threads, 0, s>>>(in, len_in, Tin, Fin, Tout, Fout, C, w, bias, out);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t flatten_cf(const __nv_bfloat16 *in, int rows, int F, int C, __nv_bfloat16 *out, cudaStream_t s) {
   flatten_cf_kernel<<<rows, 256, 0, s>>>(in, rows, F, C, out);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t ln_rows(int mode, float *x, const void *u, float alpha, int rows, int D, const float *g1, const float *b1,
@@ -533,7 +533,7 @@ cudaError_t ln_rows(int mode, float *x, const void *u, float alpha, int rows, in
     ln_row_kernel<8><<<blocks, threads, 0, s>>>(mode, x, u, alpha, rows, g1, b1, g2, b2, h, eps);
   else
     ln_row_kernel<4><<<blocks, threads, 0, s>>>(mode, x, u, alpha, rows, g1, b1, g2, b2, h, eps);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int Tp, int D, int K, const float *w,
@@ -542,12 +542,12 @@ cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int
   if (K > 31) return cudaErrorInvalidValue;
   dim3 grid((D + 127) / 128, (Tp + 15) / 16, B);
   dwconv1d_bn_silu_kernel<<<grid, 128, 0, s>>>(in, len, Tp, D, K, w, bias, bn_scale, bn_shift, out);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t relpos(int T, int D, __nv_bfloat16 *pos, cudaStream_t s) {
   relpos_kernel<<<2 * T - 1, 256, 0, s>>>(T, D, pos);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, const float *bias_u,
@@ -567,7 +567,7 @@ cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel
   dim3 grid((Tp + kQT - 1) / kQT, H, B);
   relpos_attention_kernel<<<grid, 128, smem, s>>>(qkv, krel, bias_u, bias_v, len, Tp, D,
                                                   1.0f / sqrtf(static_cast<float>(kHd)), out);
-  return cudaGetLastError();
+  return launched();
 }
 
 }  // namespace enc

@@ -1,0 +1,375 @@
+// nq8_gemm_bf16.cu -- K3: persistent 2-SM tcgen05 bf16 x bf16 GEMM over a
+// dequantized copy of a Q8_0 weight (sm_100a), for large token counts.
+//
+// Same contract as K1 (nq8_gemm.cu) and the reference's tiled matmul family
+// (kernels/moonshine_kernels.py:20-299 via src/triton_kernels.rs:170-309,
+// 1205-1289); the weight operand is bf16(f32(d) * q) computed once per call by
+// dequant_tiles (nq8_aux.cu) -- the values the reference's FbgemmBf16Op
+// multiplies (src/fast_matmul.rs:127-167, weights pre-dequantized to bf16).
+// Dequantizing once instead of once per token tile is what makes the
+// contraction tensor-bound rather than issue-bound when M is large.
+//
+// A cluster of two CTAs computes D[256 weight rows x 256 tokens] per work unit
+// with tcgen05.mma.cta_group::2 (M=256, N=256, K=16, both operands in shared
+// memory, 128-byte swizzle): CTA r holds weight rows 128r.. and token rows
+// 128r.. of the unit.  TMEM holds two 256-column accumulators per CTA, so the
+// epilogue of unit j overlaps the main loop of unit j+1.  Per CTA:
+//   warp 0      producer: TMA 2-D loads of its weight rows [128 x 64 k] and
+//               token rows [128 x 64 k] (hi and lo planes for f32 inputs)
+//               into stage s; the bytes complete on the leader's full[s].
+//   warp 1      allocates the pair's 512 TMEM columns; the leader's lane 0
+//               issues the MMAs and commits to empty[s] / accum_full[b] of
+//               both CTAs (multicast commit; no multicast loads anywhere).
+//   warps 2-17  epilogue: warp w reads TMEM lane quarter w % 4 and a 64-token
+//               column group; bias + activation (GLU through shared memory
+//               between the value and gate warps of a column group); split-K
+//               partials are raw f32 sums for splitk_reduce.
+// Every mbarrier wait is bounded; on give-up the kernel records a status bit,
+// drains, frees TMEM and returns.
+#include "nq8_common.cuh"
+#include "nq8_kernels.h"
+#include "nq8_sm100_pair.cuh"
+
+namespace nq {
+namespace {
+
+constexpr int kPT = 256;         // tokens per pair unit (MMA N)
+constexpr int kPTHalf = 128;     // token rows per CTA
+constexpr int kPW = 256;         // weight rows per pair unit (MMA M)
+constexpr int kEpiW = 16;        // epilogue warps: 4 column groups x 4 lane quarters
+constexpr int kThreads = 32 * (2 + kEpiW);  // 576
+constexpr int kEpi0 = 2;
+constexpr int kColsPerWarp = kPT / 4;  // 64
+constexpr int kAgreeBar = 9;     // named barrier of all epilogue warps (1..8: GLU pairs)
+
+template <bool SPLITX>
+struct Cfg {
+  static constexpr int kStages = SPLITX ? 4 : 6;
+  static constexpr int kABytes = 128 * kPackK * 2;      // 16 KB of weight rows
+  static constexpr int kBBytes = kPTHalf * kPackK * 2;  // 16 KB per activation plane
+  static constexpr int kStageBytes = kABytes + kBBytes * (SPLITX ? 2 : 1);
+  static constexpr int kGluOffset = kStages * kStageBytes;
+  static constexpr int kGluBytes = 8 * kEc * 32 * 4;    // 8 value/gate warp pairs
+  static constexpr int kBarOffset = kGluOffset + kGluBytes;
+  static constexpr int kNumBars = 2 * kStages + 4;
+  static constexpr int kSmemBytes = 1024 /*align slack*/ + kBarOffset + kNumBars * 8 + 64;
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(kPW, kPT);
+  static constexpr int kTmemCols = 512;  // D0 [0,256), D1 [256,512)
+  static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle alignment");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+};
+
+struct Unit {
+  int ft, tt, split, kc0, nk;
+};
+__device__ __forceinline__ Unit decode_unit(const GemmBf16Params &p, int u) {
+  Unit r;
+  const int per_split = p.grid_n * p.grid_m;
+  r.split = u / per_split;
+  const int rem = u - r.split * per_split;
+  r.tt = rem / p.grid_n;
+  r.ft = rem - r.tt * p.grid_n;
+  r.kc0 = r.split * p.cps;
+  r.nk = max(min(r.kc0 + p.cps, p.kc_total) - r.kc0, 0);
+  return r;
+}
+
+template <bool SPLITX>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
+                           const __grid_constant__ CUtensorMap tm_alo, const __grid_constant__ GemmBf16Params p) {
+  using C = Cfg<SPLITX>;
+  constexpr int kStages = C::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0: leader (issues the pair MMA), 1: peer
+  const int cl = blockIdx.x >> 1;
+  const int ncl = gridDim.x >> 1;
+  const int n_units = p.grid_n * p.grid_m * p.splits;
+
+  auto stage_w = [&](int s) { return smem + s * C::kStageBytes; };
+  auto stage_b = [&](int s) { return smem + s * C::kStageBytes + C::kABytes; };
+  auto stage_blo = [&](int s) { return smem + s * C::kStageBytes + C::kABytes + C::kBBytes; };
+  float *glu_s = reinterpret_cast<float *>(smem + C::kGluOffset);  // [8 pairs][kEc][32]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::kBarOffset);
+  auto full = [&](int s) { return smem_u32(&bars[s]); };            // leader: both CTAs' bytes landed
+  auto empty = [&](int s) { return smem_u32(&bars[kStages + s]); }; // pair MMA read the stage
+  auto accum_full = [&](int b) { return smem_u32(&bars[2 * kStages + b]); };
+  auto accum_empty = [&](int b) { return smem_u32(&bars[2 * kStages + 2 + b]); };
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(&bars[C::kNumBars]);
+  // [0] abort (any role)  [1] epilogue gave up
+  volatile int *flags = reinterpret_cast<volatile int *>(tmem_slot + 2);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full(s), 1);   // leader producer's expect_tx (+ both CTAs' bytes)
+      mbar_init(empty(s), 1);  // multicast commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(accum_full(b), 1);  // multicast commit
+      mbar_init(accum_empty(b), 2 * kEpiW);
+    }
+    flags[0] = 0;
+    flags[1] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc2(smem_u32(tmem_slot), C::kTmemCols);
+    tmem_relinquish2();
+  }
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // both CTAs' barriers exist before anyone signals across the pair
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      prefetch_tmap(&tm_w);
+      prefetch_tmap(&tm_a);
+      if (SPLITX) prefetch_tmap(&tm_alo);
+      int g = 0;
+      bool ok = true;
+      for (int u = cl; u < n_units && ok; u += ncl) {
+        const Unit un = decode_unit(p, u);
+        const int wrow0 = un.ft * kPW + static_cast<int>(rank) * 128;
+        const int trow0 = un.tt * kPT + static_cast<int>(rank) * kPTHalf;
+        for (int i = 0; i < un.nk; ++i, ++g) {
+          const int s = g % kStages;
+          if (g >= kStages && !mbar_wait(empty(s), ((g / kStages) - 1) & 1, p.ctl.wait_limit, flags)) {
+            if (!flags[0]) report(p.ctl, flags, kDevTimeoutProducer);
+            ok = false;
+            break;
+          }
+          if (flags[0]) {
+            ok = false;
+            break;
+          }
+          if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * C::kStageBytes);
+          const uint32_t bar = map_rank(full(s), 0);
+          const int kx = (un.kc0 + i) * kPackK;
+          // Weight rows past the matrix (odd tile count) and token rows past M
+          // are zero-filled by the TMA unit.
+          tma_load_2d_pair(smem_u32(stage_w(s)), &tm_w, bar, kx, wrow0);
+          tma_load_2d_pair(smem_u32(stage_b(s)), &tm_a, bar, kx, trow0);
+          if (SPLITX) tma_load_2d_pair(smem_u32(stage_blo(s)), &tm_alo, bar, kx, trow0);
+        }
+      }
+      // Drain: every copy into this CTA's shared memory has landed (the
+      // leader's full barrier, or the commit of the MMA that read it).
+      volatile int no_abort = 0;
+      for (int s = 0; s < kStages && s < g; ++s) {
+        const int last = s + kStages * ((g - 1 - s) / kStages);
+        const bool done = rank == 0 ? mbar_wait(full(s), (last / kStages) & 1, p.ctl.wait_limit, &no_abort)
+                                    : mbar_wait(empty(s), (last / kStages) & 1, p.ctl.wait_limit, &no_abort);
+        if (!done) atomicOr(p.ctl.status, kDevTimeoutDrain);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ------------------------------------------------------- MMA (leader)
+      int g = 0, j = 0;
+      bool ok = true;
+      for (int u = cl; u < n_units && ok; u += ncl, ++j) {
+        const Unit un = decode_unit(p, u);
+        const int b = j & 1;
+        if (j >= 2 && !mbar_wait(accum_empty(b), ((j >> 1) - 1) & 1, p.ctl.wait_limit, flags)) {
+          if (!flags[0]) report(p.ctl, flags, kDevTimeoutMma);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + b * kPT;
+        for (int i = 0; i < un.nk; ++i, ++g) {
+          const int s = g % kStages;
+          if (!mbar_wait(full(s), (g / kStages) & 1, p.ctl.wait_limit, flags)) {
+            if (!flags[0]) report(p.ctl, flags, kDevTimeoutMma);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(stage_w(s));
+          const uint32_t b_addr = smem_u32(stage_b(s));
+          const uint32_t blo_addr = smem_u32(stage_blo(s));
+#pragma unroll
+          for (int kk = 0; kk < kPackK / 16; ++kk) {
+            const uint64_t ad = sw128_kmajor_desc(a_addr + kk * 32);
+            umma2_bf16_ss(d_tmem, ad, sw128_kmajor_desc(b_addr + kk * 32), C::kIdesc, (i > 0 || kk > 0) ? 1u : 0u);
+            if (SPLITX) umma2_bf16_ss(d_tmem, ad, sw128_kmajor_desc(blo_addr + kk * 32), C::kIdesc, 1u);
+          }
+          umma2_commit_both(empty(s));
+        }
+        if (!ok) break;
+        umma2_commit_both(accum_full(b));
+      }
+      if (!ok && g > 0) {
+        // Aborted: the MMAs already issued must finish before TMEM is freed.
+        volatile int no_abort = 0;
+        const int last = g - 1;
+        if (!mbar_wait(empty(last % kStages), (last / kStages) & 1, p.ctl.wait_limit, &no_abort))
+          atomicOr(p.ctl.status, kDevTimeoutDrain);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int e = warp - kEpi0;  // 0..15
+    const int q = warp & 3;      // TMEM lane quarter this warp may access
+    const int cg = e >> 2;       // 64-token column group
+    const int frow = 32 * q + lane;  // weight row within this CTA's 128 == TMEM lane
+    const uint32_t tlane = static_cast<uint32_t>(32 * q) << 16;
+    // GLU: value rows are lanes [0, 64) (quarters 0, 1), gate rows [64, 128)
+    // (quarters 2, 3); warps (q, cg) and (q + 2, cg) form pair `pr`.
+    const int pr = (q & 1) * 4 + cg;
+    float *gbuf = glu_s + pr * (kEc * 32);
+    int j = 0;
+    for (int u = cl; u < n_units; u += ncl, ++j) {
+      const Unit un = decode_unit(p, u);
+      const int b = j & 1;
+      bool ok = mbar_wait(accum_full(b), (j >> 1) & 1, p.ctl.wait_limit, flags);
+      ok = __all_sync(0xffffffffu, ok);
+      // The GLU pairs share named barriers, so all epilogue warps agree on
+      // giving up before any of them leaves the loop.
+      if (!ok && lane == 0) {
+        flags[1] = 1;
+        if (!flags[0]) report(p.ctl, flags, kDevTimeoutEpilogue);
+      }
+      named_bar_sync(kAgreeBar, 32 * kEpiW);
+      const bool give_up = flags[1] != 0;
+      named_bar_sync(kAgreeBar, 32 * kEpiW);
+      if (give_up) break;
+      tc_fence_after();
+      const uint32_t trow = tmem_base + tlane + b * kPT + cg * kColsPerWarp;
+      const int m0 = un.tt * kPT + cg * kColsPerWarp;  // first token of this warp's columns
+      const int cols = max(0, min(kColsPerWarp, ((p.M - m0 + kEc - 1) / kEc) * kEc));
+      const int tile = 2 * un.ft + static_cast<int>(rank);
+      const int64_t n = static_cast<int64_t>(tile) * kPackRows + frow;  // packed row
+      auto fetch = [&](int col, float (&v)[kEc]) {
+        uint32_t r[kEc];
+        __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
+        tmem_ld16(trow + col, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int x = 0; x < kEc; ++x) v[x] = __uint_as_float(r[x]);
+      };
+      if (p.splits > 1) {
+        const bool nvalid = n < p.n_rows;
+        float *part = p.partials + (static_cast<size_t>(un.split) * p.M + m0) * p.n_rows + n;
+        for (int col = 0; col < cols; col += kEc) {
+          float v[kEc];
+          fetch(col, v);
+          const int valid = p.M - (m0 + col);
+          if (!nvalid) continue;
+#pragma unroll
+          for (int x = 0; x < kEc; ++x)
+            if (x < valid) part[static_cast<size_t>(col + x) * p.n_rows] = v[x];
+        }
+      } else if (!p.glu) {
+        const bool nvalid = n < p.N;
+        const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
+        for (int col = 0; col < cols; col += kEc) {
+          float v[kEc];
+          fetch(col, v);
+          if (!nvalid) continue;
+          const int valid = p.M - (m0 + col);
+          store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
+        }
+      } else {
+        const bool is_gate = q >= 2;
+        const int vrow = frow & 63;
+        const int64_t jcol = static_cast<int64_t>(tile) * 64 + vrow;
+        const bool jvalid = jcol < p.n_out;
+        const float bv = (p.bias && jvalid) ? p.bias[is_gate ? p.n_out + jcol : jcol] : 0.f;
+        for (int col = 0; col < cols; col += kEc) {
+          float v[kEc];
+          fetch(col, v);
+          if (is_gate) {
+#pragma unroll
+            for (int x = 0; x < kEc; ++x) gbuf[x * 32 + lane] = v[x] + bv;
+          }
+          named_bar_sync(1 + pr, 64);
+          if (!is_gate && jvalid) {
+            float gv[kEc];
+#pragma unroll
+            for (int x = 0; x < kEc; ++x) gv[x] = gbuf[x * 32 + lane];
+            const int valid = p.M - (m0 + col);
+            store_glu_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + jcol, p.ldy, valid, v,
+                          bv, gv);
+          }
+          named_bar_sync(1 + pr, 64);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0) mbar_arrive(accum_empty(b));
+        else mbar_arrive_remote(map_rank(accum_empty(b), 0));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncwarp();
+  cluster_sync_all();  // nobody leaves while the pair may still signal it
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc2(tmem_base, C::kTmemCols);
+  }
+}
+
+template <bool SPLITX>
+cudaError_t launch_t(const CUtensorMap &w, const CUtensorMap &a_hi, const CUtensorMap &a_lo, const GemmBf16Params &p,
+                     int pairs, cudaStream_t stream) {
+  using C = Cfg<SPLITX>;
+  auto kern = gemm_bf16_sm100_kernel<SPLITX>;
+  static bool attr_set[64] = {false};  // once per device (the attribute is per-context state)
+  static int max_pairs[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (dev >= 64 || !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    cfg.gridDim = dim3(2 * 74);
+    e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (n <= 0) return cudaErrorInvalidConfiguration;
+    if (dev < 64) {
+      attr_set[dev] = true;
+      max_pairs[dev] = n;
+    }
+  }
+  const int cap = dev < 64 ? max_pairs[dev] : 1;
+  cfg.gridDim = dim3(2 * (pairs < cap ? pairs : cap));
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, w, a_hi, a_lo, p);
+  if (e == cudaSuccess) note_launch();
+  return e;
+}
+
+}  // namespace
+
+int gemm_bf16_block_t() { return kPT; }
+int gemm_bf16_block_w() { return kPW; }
+
+cudaError_t launch_gemm_bf16(bool splitx, const CUtensorMap &w, const CUtensorMap &a_hi, const CUtensorMap &a_lo,
+                             const GemmBf16Params &p, int pairs, cudaStream_t stream) {
+  return splitx ? launch_t<true>(w, a_hi, a_lo, p, pairs, stream) : launch_t<false>(w, a_hi, a_lo, p, pairs, stream);
+}
+
+}  // namespace nq

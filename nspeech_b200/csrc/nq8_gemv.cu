@@ -268,7 +268,7 @@ static cudaError_t launch_gemv_t(const GemvParams &p, int nprob, int grid_x, cud
   if (p.cps > kGemvMaxCps) return cudaErrorInvalidValue;
   dim3 grid(grid_x, p.splits, nprob);
   kern<<<grid, kGemvThreads, smem, stream>>>(p);
-  return cudaGetLastError();
+  return launched();
 }
 
 cudaError_t launch_gemv(const GemvParams &p, int nprob, int grid_x, bool splitx, cudaStream_t stream) {

@@ -9,6 +9,8 @@
 
 #include "nq8_layout.h"
 
+struct nq_weight;  // include/nq8.h
+
 namespace nq {
 
 constexpr int kPackGlu = 1;
@@ -17,6 +19,10 @@ constexpr int kErrFormat = -7;
 
 // Record `msg` as the calling thread's last error (nq_last_error) and return code.
 int api_fail(int code, const std::string &msg);
+
+// Kernel launches one nq_linear call of M rows makes on the current device
+// (`aligned`: bf16 activations 16-byte aligned with ldx % 8 == 0).
+int linear_launches(const ::nq_weight *w, int64_t m, int x_dtype, bool aligned);
 
 int pack_n_tiles(int64_t n, int flags);
 int pack_k_chunks(int64_t k);

@@ -43,6 +43,8 @@ struct GemvParams {
 size_t gemv_smem_bytes(int mrows, bool splitx, int cps);
 cudaError_t launch_gemv(const GemvParams &p, int nprob, int grid_x, bool splitx, cudaStream_t stream);
 
+// K1: fused Q8_0 GEMM (dequantizes in the kernel; best below a few thousand
+// tokens, where the weights dominate the traffic).
 struct GemmParams {
   const uint8_t *w;
   int n_tiles;
@@ -58,21 +60,70 @@ struct GemmParams {
   int64_t ldy;
   int splits;
   int cps;
-  int grid_n;       // 128-row weight tiles (= n_tiles)
+  int grid_n;       // weight pair tiles: ceil(n_tiles / 2), 256 rows each
   int grid_m;       // token tiles of BT rows
-  float *partials;  // [splits][grid_m][grid_n][128][BT] f32 (split-K only)
-  int *counters;    // [grid_m * grid_n]
+  float *partials;  // split-K only: [splits][M][ldp] f32, token-major, summed by splitk_reduce
+  int ldp;          // n_tiles * 128
   DevCtl ctl;
 };
 
-// Which compiled token-tile configuration to launch.
+// Which compiled configuration to launch (bf16 activations, or f32 ones as
+// hi/lo bf16 planes).
 enum GemmVariant : int { kGemmBt256 = 0, kGemmBt128 = 1, kGemmBt64 = 2, kGemmBt128SplitX = 3 };
+// Tokens per work unit of an SM pair (each CTA stages half of them).
 int gemm_block_t(GemmVariant v);
 size_t gemm_smem_bytes(GemmVariant v);
-// Persistent launch: `grid` CTAs (<= one per SM) walk grid_n * grid_m * splits
-// work units.
+// Persistent cluster launch: up to `pairs` two-CTA clusters (capped at the
+// number that fit on the device at once) walk grid_n * grid_m * splits units.
 cudaError_t launch_gemm(GemmVariant v, const CUtensorMap &a_hi, const CUtensorMap &a_lo,
-                        const GemmParams &p, int grid, cudaStream_t stream);
+                        const GemmParams &p, int pairs, cudaStream_t stream);
+
+// K3: bf16 x bf16 GEMM over a dequantized copy of the weights (packed row
+// order: row t*128 + r is row r of packed tile t), for large token counts.
+struct GemmBf16Params {
+  int64_t N;        // logical weight rows
+  int n_rows;       // rows of the dequantized matrix (n_tiles * 128)
+  int glu;
+  int64_t n_out;
+  int M;
+  int kc_total;
+  const float *bias;
+  int epi;
+  void *y;
+  int y_dtype;
+  int64_t ldy;
+  int splits;
+  int cps;
+  int grid_n;       // 256-row weight pair tiles
+  int grid_m;       // 256-token tiles
+  float *partials;  // split-K only: [splits][M][n_rows] f32
+  DevCtl ctl;
+};
+int gemm_bf16_block_t();     // tokens per pair unit
+int gemm_bf16_block_w();     // weight rows per pair unit
+cudaError_t launch_gemm_bf16(bool splitx, const CUtensorMap &w, const CUtensorMap &a_hi, const CUtensorMap &a_lo,
+                             const GemmBf16Params &p, int pairs, cudaStream_t stream);
+
+// Packed Q8_0 tiles -> bf16 [n_tiles * 128][kc * 64] (row-major, packed row
+// order), each element bf16(f32(d) * q).
+cudaError_t launch_dequant_tiles(const uint8_t *w, int n_tiles, int kc, __nv_bfloat16 *out, cudaStream_t stream);
+
+// Deterministic split-K reduction: y[m, j] = act(sum_s P[s][m][row(j)] + bias)
+// with the splits summed in order (GLU: value row and gate row of column j).
+struct SplitkReduceParams {
+  const float *partials;
+  int splits;
+  int M;
+  int ldp;
+  int64_t n_out;
+  int glu;
+  const float *bias;
+  int epi;
+  void *y;
+  int y_dtype;
+  int64_t ldy;
+};
+cudaError_t launch_splitk_reduce(const SplitkReduceParams &p, cudaStream_t stream);
 
 // f32 -> bf16 planes: hi = bf16(x), lo = bf16(x - hi) (lo may be null); rows
 // of k_pad elements, zero beyond K.  Also used for bf16 -> bf16 copies when a

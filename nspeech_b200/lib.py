@@ -101,6 +101,8 @@ SIGNATURES = {
                              ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _I]),
     "nq_last_error": (_I, [ctypes.c_char_p, _I]),
     "nq_status": (_I, [_P, ctypes.POINTER(_I)]),
+    "nq_launch_counter": (_I, [ctypes.POINTER(_I64), _I]),
+    "nq_set_gemm_path": (_I, [_I]),
     "nq_set_wait_limit": (_I, [_I64]),
     "nq_debug_wait_timeout": (_I, [_P]),
 }
@@ -153,6 +155,18 @@ def status(stream_ptr: int = 0) -> int:
 
 NQ_KCLASS_GEMM = 0
 NQ_KCLASS_GEMV = 1
+NQ_KCLASS_DEQUANT = 2
+NQ_KCLASS_REDUCE = 3
+NQ_GEMM_AUTO = 0
+NQ_GEMM_FUSED = 1
+NQ_GEMM_DEQUANT = 2
+
+
+def launch_counter(reset: bool = False) -> int:
+    """Kernels launched by libnq8 in this process (optionally zeroing the count)."""
+    n = ctypes.c_int64()
+    check(load().nq_launch_counter(ctypes.byref(n), 1 if reset else 0))
+    return n.value
 
 
 def profile_enable(on: bool) -> None:

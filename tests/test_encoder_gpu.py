@@ -157,3 +157,24 @@ def test_encoder_rejects_bad_config(nq):
     with pytest.raises(lib.NqError) as e:
         enc.finalize()  # nothing staged
     assert "missing tensor" in str(e.value)
+
+
+@pytest.mark.parametrize("path", ["auto", "fused"])
+def test_launch_count_matches_counter(nq, oracle, path):
+    """nq_encoder_launch_count equals the kernels one forward actually launches."""
+    from nspeech_b200 import synthetic as S
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=2, sub_channels=64)
+    enc = _gpu_encoder(spec, _model(oracle, spec, seed=7))
+    L = nq.load()
+    nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_AUTO if path == "auto" else nq.NQ_GEMM_FUSED))
+    try:
+        for batch, t_mel in [(1, 120), (3, 400), (8, 1000)]:
+            mel = torch.from_numpy(oracle.normal(batch + t_mel, (batch, t_mel, 128))).cuda()
+            enc.forward(mel)  # arena sized outside the counted call
+            torch.cuda.synchronize()
+            n0 = nq.launch_counter()
+            enc.forward(mel)
+            torch.cuda.synchronize()
+            assert nq.launch_counter() - n0 == enc.launch_count(batch, t_mel), (path, batch, t_mel)
+    finally:
+        nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_AUTO))
