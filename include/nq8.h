@@ -152,6 +152,25 @@ int nq_gemv_glu_splitk(const nq_weight *w, const void *x, int x_dtype, const flo
 int nq_gemv_qkv_splitk(const nq_weight *wq, const nq_weight *wk, const nq_weight *wv,
                        const void *x, int x_dtype, void *q, void *k, void *v, int out_dtype,
                        void *stream);
+/* No counterpart in the reference.  The split-K GEMV of nq_linear (M <= 16
+ * rows, same arguments and result) without any allocation: its split-K
+ * partial sums and arrival counters live in a static device array of this
+ * library (4 MiB of partials plus 4096 counters per device) instead of the
+ * per-stream workspace nq_linear grows with cudaMalloc.  For callers that
+ * cannot allocate at call time: a streaming decoder step on a latency budget
+ * (cudaMalloc / cudaFree can synchronize the device and stall every stream),
+ * or a process running at a fixed device-memory cap where a workspace growth
+ * could fail mid-stream.  Requires nq_init on the device.  The first call on
+ * a device looks up the array's address (cudaGetSymbolAddress, which may load
+ * the module), so make that first call before any stream capture.  Every
+ * call on a device shares the one array and leaves its contents behind (the
+ * counters are cleared by each call): calls that overlap on the GPU -- on
+ * two streams, or from two threads -- race and give wrong results; serialize
+ * them.  A weight whose split-K partials exceed the array (large K with
+ * large N) is rejected with NQ_ERR_SHAPE before any launch; M > 16 too. */
+int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx,
+                    const float *bias, int epilogue, void *y, int y_dtype, int64_t ldy,
+                    void *stream);
 
 /* ---- FastConformer encoder (the caller of the Q8_0 path for configs 2/5) ---
  * Mirrors FastConformerConfig (src/parakeet/fast_conformer.rs:31-45) and

@@ -500,6 +500,33 @@ int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, i
   return NQ_OK;
 }
 
+// ------------------------------------------------- static-scratch GEMV
+// Scratch of nq_gemv_noalloc: split-K partial tiles followed by the per-tile
+// arrival counters, in this module's own device memory (a file-scope device
+// array), so a call needs no allocation.  One array per device, shared by
+// every call on that device.
+constexpr size_t kNoAllocPartialBytes = size_t(4) << 20;  // 4 MiB of partial tiles
+constexpr int kNoAllocCounters = 4096;                     // weight tiles (N <= 524288)
+constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + kNoAllocCounters * sizeof(int);
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+unsigned char *g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_noalloc_scratch for device `dev` (current), looked up
+// once per device.
+int noalloc_scratch(int dev, unsigned char **out) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static GEMV scratch)");
+    g_noalloc_ptr[dev] = static_cast<unsigned char *>(ptr);
+  }
+  *out = g_noalloc_ptr[dev];
+  return NQ_OK;
+}
+
 }  // namespace
 
 namespace nq {
@@ -656,6 +683,74 @@ int nq_linear(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t
               void *y, int y_dtype, int64_t ldy, void *stream) {
   LinearArgs a{w, bias, y, ldy};
   return linear_impl(&a, 1, x, x_dtype, m, ldx, epilogue, y_dtype, stream);
+}
+
+int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx, const float *bias,
+                    int epilogue, void *y, int y_dtype, int64_t ldy, void *stream) {
+  int rc = validate(w, x, x_dtype, m, ldx, epilogue, y, y_dtype, ldy);
+  if (rc) return rc;
+  if (m > 16) return fail(NQ_ERR_SHAPE, "nq_gemv_noalloc serves M <= 16 rows (got %lld)", (long long)m);
+  if (m == 0) return NQ_OK;
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  if (w->device != dev) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, dev);
+  cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
+  // Same split-K choice as nq_linear's GEMV, so both give the same sums.
+  const int kc = w->kc;
+  int splits = std::max(1, std::min(kc, (2 * ctx->sm_count + w->n_tiles - 1) / w->n_tiles));
+  int cps = std::min((kc + splits - 1) / splits, 8);
+  splits = (kc + cps - 1) / cps;
+  const size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * w->n_tiles * 16 * nq::kPackRows * sizeof(float) : 0;
+  if (part_bytes > kNoAllocPartialBytes)
+    return fail(NQ_ERR_SHAPE,
+                "nq_gemv_noalloc: this weight (N=%lld, K=%lld) needs %zu bytes of split-K scratch; the static "
+                "scratch holds %zu",
+                (long long)w->n, (long long)w->k, part_bytes, kNoAllocPartialBytes);
+  if (w->n_tiles > kNoAllocCounters)
+    return fail(NQ_ERR_SHAPE, "nq_gemv_noalloc: %d weight tiles exceed the %d counters of the static scratch",
+                w->n_tiles, kNoAllocCounters);
+  unsigned char *scratch = nullptr;
+  rc = noalloc_scratch(dev, &scratch);
+  if (rc) return rc;
+  int *counters = reinterpret_cast<int *>(scratch + kNoAllocPartialBytes);
+  if (splits > 1) {
+    // The array keeps the last call's contents: the arrival counters must
+    // start at zero (a call that gave up on a wait can leave them armed).
+    cudaError_t e = cudaMemsetAsync(counters, 0, w->n_tiles * sizeof(int), stream_);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static GEMV counters)");
+  }
+  nq::GemvParams p;
+  std::memset(&p, 0, sizeof(p));
+  nq::GemvProblem &pr = p.prob[0];
+  pr.w = w->dev;
+  pr.n_tiles = w->n_tiles;
+  pr.kc_total = kc;
+  pr.N = w->n;
+  pr.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
+  pr.n_out = out_width(w);
+  pr.bias = bias;
+  pr.y = y;
+  pr.ldy = ldy;
+  if (splits > 1) {
+    pr.partials = reinterpret_cast<float *>(scratch);
+    pr.counters = counters;
+  }
+  p.x = x;
+  p.x_dtype = x_dtype;
+  p.ldx = ldx;
+  p.M = static_cast<int>(m);
+  p.K = w->k;
+  p.epi = epilogue;
+  p.y_dtype = y_dtype;
+  p.splits = splits;
+  p.cps = cps;
+  p.ctl.status = ctx->status;
+  p.ctl.wait_limit = g_wait_limit;
+  cudaError_t e = nq::launch_gemv(p, 1, w->n_tiles, x_dtype == NQ_F32, stream_);
+  if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+  return NQ_OK;
 }
 
 int nq_matmul(const nq_weight *w, const void *a, int a_dtype, void *c, int c_dtype, int64_t m, void *stream) {

@@ -101,6 +101,7 @@ SIGNATURES = {
                              ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double), _I]),
     "nq_last_error": (_I, [ctypes.c_char_p, _I]),
     "nq_status": (_I, [_P, ctypes.POINTER(_I)]),
+    "nq_gemv_noalloc": (_I, [_P, _P, _I, _I64, _I64, _P, _I, _P, _I, _I64, _P]),
     "nq_launch_counter": (_I, [ctypes.POINTER(_I64), _I]),
     "nq_set_gemm_path": (_I, [_I]),
     "nq_set_wait_limit": (_I, [_I64]),
