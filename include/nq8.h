@@ -117,6 +117,14 @@ int nq_weight_to_q8_0(const nq_weight *w, void *blocks_out);
 
 int nq_weight_shape(const nq_weight *w, int64_t *n, int64_t *k, int *flags);
 void nq_weight_free(nq_weight *w);
+/* keep != 0: dequantize the weight once into an owned bf16 copy (2 bytes per
+ * element, next to the Q8_0 tiles) that every later GEMM with M >= 128 reads
+ * directly -- the reference's pre-dequantized MatMul::PackedBf16 /
+ * FbgemmBf16Op weights (src/fast_matmul.rs:127-167, :176-226); the values
+ * and results are the same as without it.  keep == 0 frees the copy (after a
+ * device synchronize).  GEMV and M < 128 calls keep reading the Q8_0 tiles.
+ * Synchronous; call on the weight's device. */
+int nq_weight_keep_bf16(nq_weight *w, int keep);
 
 /* y[m, :] = act(x[m, :K] . W^T + bias), m in [0, M).
  *   x: device, x_dtype NQ_F32 | NQ_BF16, row stride ldx elements (>= K).

@@ -29,6 +29,10 @@ struct nq_weight {
   int n_tiles = 0, kc = 0;
   uint8_t *dev = nullptr;
   size_t bytes = 0;
+  // Optional dequantized copy, bf16 [n_tiles * 128][kc * 64] in packed row
+  // order (nq_weight_keep_bf16): the dequantize-once GEMM reads it instead of
+  // dequantizing per call.
+  __nv_bfloat16 *bf16 = nullptr;
 };
 
 namespace {
@@ -315,10 +319,11 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
 // How one GEMM call (M > 16) is carried out.
 struct GemmPlan {
   bool deq;        // dequantize-once path (dequant_tiles + K3), else fused K1
+  bool cached;     // deq with the weight's kept bf16 copy: no dequantize launch
   bool split_x;    // activations staged to bf16 planes first (f32, or unaligned bf16)
   int bt;          // tokens per pair unit
   int grid_m, grid_n, splits, cps, pairs;
-  int launches() const { return 1 + (deq ? 1 : 0) + (splits > 1 ? 1 : 0) + (split_x ? 1 : 0); }
+  int launches() const { return 1 + (deq && !cached ? 1 : 0) + (splits > 1 ? 1 : 0) + (split_x ? 1 : 0); }
 };
 
 // The fused kernel (K1) re-dequantizes the weight for every 192-token tile
@@ -328,6 +333,7 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
   GemmPlan g;
   const bool splitx = x_dtype == NQ_F32;
   g.deq = g_gemm_path == NQ_GEMM_DEQUANT || (g_gemm_path == NQ_GEMM_AUTO && m >= kDequantMinM);
+  g.cached = g.deq && w->bf16 != nullptr;
   g.split_x = !direct;
   g.pairs = std::max(1, sm_count / 2);
   g.bt = g.deq ? nq::gemm_bf16_block_t() : nq::gemm_block_t(splitx ? nq::kGemmBt128SplitX : nq::kGemmBt128);
@@ -363,7 +369,7 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
   // Workspace: [activation planes][dequantized weight][split-K partials].
   size_t xbytes = 0;
   if (!direct) xbytes = align_up(static_cast<size_t>(m) * k_pad * 2, 1024) * (splitx ? 2 : 1);
-  const size_t wbytes = deq ? align_up(static_cast<size_t>(ldp) * k_pad * 2, 1024) : 0;
+  const size_t wbytes = deq && !plan.cached ? align_up(static_cast<size_t>(ldp) * k_pad * 2, 1024) : 0;
   const size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * m * ldp * sizeof(float) : 0;
   Workspace *ws = nullptr;
   int rc = get_workspace(ctx, stream, xbytes + wbytes + part_bytes, &ws);
@@ -397,8 +403,8 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
                        m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (a.bias ? 4.0 * w->n : 0.0);
   const int units = grid_m * grid_n * splits;
   if (deq) {
-    __nv_bfloat16 *wb = reinterpret_cast<__nv_bfloat16 *>(ws->buf + xbytes);
-    {
+    __nv_bfloat16 *wb = plan.cached ? w->bf16 : reinterpret_cast<__nv_bfloat16 *>(ws->buf + xbytes);
+    if (!plan.cached) {
       ProfScope ps(NQ_KCLASS_DEQUANT, stream, 0.0, w->bytes + static_cast<double>(ldp) * k_pad * 2);
       cudaError_t e = nq::launch_dequant_tiles(w->dev, w->n_tiles, kc, wb, stream);
       if (e != cudaSuccess) return cuda_fail(e, "weight dequantize launch");
@@ -669,11 +675,45 @@ int nq_weight_shape(const nq_weight *w, int64_t *n, int64_t *k, int *flags) {
   return NQ_OK;
 }
 
+int nq_weight_keep_bf16(nq_weight *w, int keep) {
+  if (!w) return fail(NQ_ERR_ARG, "null weight");
+  int cur = 0;
+  cudaError_t e = cudaGetDevice(&cur);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (cur != w->device) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, cur);
+  if (!keep) {
+    if (w->bf16) {
+      e = cudaDeviceSynchronize();  // no launch in flight may still read it
+      if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize(drop bf16 copy)");
+      cudaFree(w->bf16);
+      w->bf16 = nullptr;
+    }
+    return NQ_OK;
+  }
+  if (w->bf16) return NQ_OK;
+  const size_t bytes = static_cast<size_t>(w->n_tiles) * nq::kPackRows * w->kc * nq::kPackK * 2;
+  __nv_bfloat16 *buf = nullptr;
+  e = cudaMalloc(&buf, bytes);
+  if (e != cudaSuccess) return fail(NQ_ERR_CUDA, "cudaMalloc(bf16 weight copy, %zu bytes): %s", bytes, cudaGetErrorString(e));
+  cudaStream_t st = nullptr;
+  e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = nq::launch_dequant_tiles(w->dev, w->n_tiles, w->kc, buf, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (st) cudaStreamDestroy(st);
+  if (e != cudaSuccess) {
+    cudaFree(buf);
+    return cuda_fail(e, "dequantize bf16 weight copy");
+  }
+  w->bf16 = buf;
+  return NQ_OK;
+}
+
 void nq_weight_free(nq_weight *w) {
   if (!w) return;
   int cur = 0;
   cudaGetDevice(&cur);
   if (cur != w->device) cudaSetDevice(w->device);
+  if (w->bf16) cudaFree(w->bf16);
   cudaFree(w->dev);
   if (cur != w->device) cudaSetDevice(cur);
   delete w;

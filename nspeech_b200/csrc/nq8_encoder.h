@@ -14,6 +14,12 @@ constexpr int kLnResAddOut = 2;  // x = LN1(x + alpha * u); h = LN2(x) if LN2 gi
 
 cudaError_t conv0_relu(const float *mel, const int *len0, int B, int T, int F, int T1, int F1, int C, const float *w,
                        const float *bias, __nv_bfloat16 *out, cudaStream_t s);
+// conv0_relu followed by the first dwconv2d_s2, without the intermediate in
+// HBM (identical results); supported when C % 64 == 0 and the staged rows fit.
+bool conv0_dw_s2_supported(int F, int F1, int C);
+cudaError_t conv0_dw_s2(const float *mel, const int *len0, const int *len1, int B, int T, int F, int T1, int F1, int T2,
+                        int F2, int C, const float *w0, const float *b0, const float *w2, const float *b2,
+                        __nv_bfloat16 *out, cudaStream_t s);
 cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int Tin, int Fin, int Tout, int Fout, int C,
                         const float *w, const float *bias, __nv_bfloat16 *out, cudaStream_t s);
 cudaError_t flatten_cf(const __nv_bfloat16 *in, int rows, int F, int C, __nv_bfloat16 *out, cudaStream_t s);

@@ -278,6 +278,15 @@ int finalize(nq_encoder *e) {
       NQ_TRY(vec(e, p + norms[j] + ".bias", d, true, 0.f, bs[j]));
     }
   }
+  // Every encoder GEMM runs the dequantize-once path for M >= 128 tokens:
+  // keep each weight's bf16 copy (MatMul::PackedBf16 semantics) instead of
+  // re-dequantizing it on every call.  Costs 2 bytes per weight element.
+  NQ_TRY(nq_weight_keep_bf16(e->pw3, 1));
+  NQ_TRY(nq_weight_keep_bf16(e->pw6, 1));
+  NQ_TRY(nq_weight_keep_bf16(e->lin, 1));
+  for (Layer &L : e->layers)
+    for (nq_weight *w : {L.ff1_w1, L.ff1_w2, L.qkv, L.rel, L.o, L.pw1, L.pw2, L.ff2_w1, L.ff2_w2})
+      NQ_TRY(nq_weight_keep_bf16(w, 1));
   e->staged.clear();
   e->ready = true;
   return NQ_OK;
@@ -318,7 +327,7 @@ int ensure_arena(nq_encoder *e, const Shapes &s) {
   NQ_TRY(e->att.ensure(M * D * 2));
   NQ_TRY(e->g.ensure(M * D * 2));
   NQ_TRY(e->c.ensure(M * D * 2));
-  NQ_TRY(e->s1.ensure(static_cast<size_t>(s.B) * s.T1 * s.F1 * s.C * 2));
+  if (!nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C)) NQ_TRY(e->s1.ensure(static_cast<size_t>(s.B) * s.T1 * s.F1 * s.C * 2));
   NQ_TRY(e->s2a.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
   NQ_TRY(e->s2b.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
   NQ_TRY(e->s3a.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
@@ -368,9 +377,14 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
   float *x = e->x.as<float>();
 
   // --- subsampling (fast_conformer.rs:172-188)
-  NQ_K(nq::enc::conv0_relu(mel, L0, s.B, s.Tm, s.F, s.T1, s.F1, s.C, e->c0_w, e->c0_b, e->s1.as<__nv_bfloat16>(), st));
-  NQ_K(nq::enc::dwconv2d_s2(e->s1.as<__nv_bfloat16>(), L1, s.B, s.T1, s.F1, s.T2, s.F2, s.C, e->dw2_w, e->dw2_b,
-                            e->s2a.as<__nv_bfloat16>(), st));
+  if (nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C)) {
+    NQ_K(nq::enc::conv0_dw_s2(mel, L0, L1, s.B, s.Tm, s.F, s.T1, s.F1, s.T2, s.F2, s.C, e->c0_w, e->c0_b, e->dw2_w,
+                              e->dw2_b, e->s2a.as<__nv_bfloat16>(), st));
+  } else {
+    NQ_K(nq::enc::conv0_relu(mel, L0, s.B, s.Tm, s.F, s.T1, s.F1, s.C, e->c0_w, e->c0_b, e->s1.as<__nv_bfloat16>(), st));
+    NQ_K(nq::enc::dwconv2d_s2(e->s1.as<__nv_bfloat16>(), L1, s.B, s.T1, s.F1, s.T2, s.F2, s.C, e->dw2_w, e->dw2_b,
+                              e->s2a.as<__nv_bfloat16>(), st));
+  }
   NQ_TRY(nq_linear(e->pw3, e->s2a.p, NQ_BF16, static_cast<int64_t>(s.B) * s.T2 * s.F2, s.C, e->pw3_b, NQ_EPI_RELU,
                    e->s2b.p, NQ_BF16, s.C, stv));
   NQ_K(nq::enc::dwconv2d_s2(e->s2b.as<__nv_bfloat16>(), L2, s.B, s.T2, s.F2, s.T3, s.F3, s.C, e->dw5_w, e->dw5_b,
@@ -527,7 +541,8 @@ int nq_encoder_launch_count(const nq_encoder *enc, int batch, int t_mel) {
   const Shapes s = shapes(enc, batch, t_mel);
   const int M = s.M, Tp = s.T3;
   auto lin = [&](const nq_weight *w, int64_t m, int64_t ldx) { return nq::linear_launches(w, m, NQ_BF16, ldx % 8 == 0); };
-  int n = 6;  // conv0, dwconv x2, flatten, scaled LN, relpos
+  // conv0 + dwconv (fused when supported), dwconv, flatten, scaled LN, relpos
+  int n = nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C) ? 5 : 6;
   n += lin(enc->pw3, static_cast<int64_t>(s.B) * s.T2 * s.F2, s.C);
   n += lin(enc->pw6, static_cast<int64_t>(s.B) * s.T3 * s.F3, s.C);
   n += lin(enc->lin, M, static_cast<int64_t>(s.F3) * s.C);

@@ -55,6 +55,107 @@ __global__ void conv0_relu_kernel(const float *__restrict__ mel, const int *__re
   }
 }
 
+// conv0 + the first depthwise conv of the subsampling stack in one pass:
+//   out[b, t2, f2, c] = b2[c] + sum_{dt,df} w2[c][dt,df] * s1[2 t2 - 1 + dt][2 f2 - 1 + df][c]
+//   s1[t1][f1][c]     = bf16(relu(b0[c] + sum_{dt,df} w0[c][dt,df] * mel[2 t1 - 1 + dt][2 f1 - 1 + df]))
+// (the same arithmetic, order and bf16 rounding as conv0_relu followed by
+// dwconv2d_s2; fast_conformer.rs:172-180).  The s1 rows a tile of kCdTT
+// output rows needs (2 kCdTT + 1) are computed into shared memory and never
+// reach HBM.  Block = (64 channels, kCdTT output rows, one segment).
+constexpr int kCdTT = 4;   // output rows (t2) per block
+constexpr int kCdCG = 64;  // channels per block
+constexpr int kCdRows1 = 2 * kCdTT + 1;
+constexpr int kCdMelRows = 4 * kCdTT + 3;
+
+size_t conv0_dw_smem_bytes(int F, int F1) {
+  return static_cast<size_t>(kCdMelRows) * (F + 2) * sizeof(float) +
+         static_cast<size_t>(kCdRows1) * F1 * kCdCG * sizeof(__nv_bfloat16);
+}
+
+__global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
+    const float *__restrict__ mel, const int *__restrict__ len0, const int *__restrict__ len1, int T, int F, int T1,
+    int F1, int T2, int F2, int C, const float *__restrict__ w0, const float *__restrict__ b0,
+    const float *__restrict__ w2, const float *__restrict__ b2, __nv_bfloat16 *__restrict__ out) {
+  extern __shared__ __align__(16) unsigned char cd_smem[];
+  const int FP = F + 2;  // padded mel row: column j holds frequency j - 1
+  float *melS = reinterpret_cast<float *>(cd_smem);
+  __nv_bfloat16 *s1S = reinterpret_cast<__nv_bfloat16 *>(cd_smem + static_cast<size_t>(kCdMelRows) * FP * sizeof(float));
+  const int b = blockIdx.z;
+  const int t2s = blockIdx.y * kCdTT;
+  const int cg0 = blockIdx.x * kCdCG;
+  const int L0 = len0[b], L1 = min(len1[b], T1);
+  // 1. mel rows 4 t2s - 3 .. 4 t2s + 4 kCdTT - 1 (zero outside [0, min(T, L0)) and the frequency range)
+  for (int idx = threadIdx.x; idx < kCdMelRows * FP; idx += blockDim.x) {
+    const int r = idx / FP;
+    const int j = idx - r * FP;
+    const int t = 4 * t2s - 3 + r;
+    const int f = j - 1;
+    float v = 0.f;
+    if (t >= 0 && t < T && t < L0 && f >= 0 && f < F) v = mel[(static_cast<int64_t>(b) * T + t) * F + f];
+    melS[idx] = v;
+  }
+  __syncthreads();
+  const int c = threadIdx.x % kCdCG;  // a warp covers 32 consecutive channels
+  const int grp = threadIdx.x / kCdCG;
+  const int ngrp = blockDim.x / kCdCG;
+  const int cc = cg0 + c;
+  // 2. s1 rows t1 = 2 t2s - 1 + r1; four f1 per task (27 mel loads for 4 outputs)
+  {
+    float wr[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) wr[i] = w0[cc * 9 + i];
+    const float bc = b0[cc];
+    const int quads = (F1 + 3) / 4;
+    for (int task = grp; task < kCdRows1 * quads; task += ngrp) {
+      const int r1 = task / quads;
+      const int f1q = (task - r1 * quads) * 4;
+      float acc[4] = {bc, bc, bc, bc};
+#pragma unroll
+      for (int dt = 0; dt < 3; ++dt) {
+        const float *row = melS + (2 * r1 + dt) * FP + 2 * f1q;
+        float m[9];
+#pragma unroll
+        for (int x = 0; x < 9; ++x) m[x] = (2 * f1q + x < FP) ? row[x] : 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int df = 0; df < 3; ++df) acc[q] += wr[dt * 3 + df] * m[2 * q + df];
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        if (f1q + q < F1) s1S[(r1 * F1 + f1q + q) * kCdCG + c] = __float2bfloat16_rn(fmaxf(acc[q], 0.f));
+    }
+  }
+  __syncthreads();
+  // 3. depthwise 3x3 stride 2 over the staged rows
+  {
+    float wr[9];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) wr[i] = w2[cc * 9 + i];
+    const float bc = b2[cc];
+    for (int task = grp; task < kCdTT * F2; task += ngrp) {
+      const int r2 = task / F2;
+      const int f2 = task - r2 * F2;
+      const int t2 = t2s + r2;
+      if (t2 >= T2) break;
+      float acc = bc;
+#pragma unroll
+      for (int dt = 0; dt < 3; ++dt) {
+        const int t1 = 2 * t2 - 1 + dt;
+        if (t1 < 0 || t1 >= L1) continue;
+#pragma unroll
+        for (int df = 0; df < 3; ++df) {
+          const int f1 = 2 * f2 - 1 + df;
+          if (f1 < 0 || f1 >= F1) continue;
+          acc += wr[dt * 3 + df] * bf(s1S[((2 * r2 + dt) * F1 + f1) * kCdCG + c]);
+        }
+      }
+      out[((static_cast<int64_t>(b) * T2 + t2) * F2 + f2) * C + cc] = __float2bfloat16_rn(acc);
+    }
+  }
+}
+
+
 // Depthwise conv2d(C, 3x3, stride 2, pad 1, groups C) + bias on NHWC bf16
 // (fast_conformer.rs:109-122, 135-146).  Input frames t >= len_in[b] are zero.
 __global__ void dwconv2d_s2_kernel(const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len_in, int Tin,
@@ -196,29 +297,52 @@ __global__ void ln_row_kernel(int mode, float *__restrict__ x, const void *__res
 // --------------------------------------------------- conv module middle part
 // Depthwise conv1d over time (kernel K, pad K/2, groups D) + bias, eval-mode
 // BatchNorm folded to scale/shift, SiLU (fast_conformer.rs:486-488).
-// in/out [B, Tp, D] bf16; input frames t >= len[b] are zero.
-__global__ void dwconv1d_bn_silu_kernel(const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len, int Tp,
-                                        int D, int K, const float *__restrict__ w, const float *__restrict__ bias,
-                                        const float *__restrict__ bn_scale, const float *__restrict__ bn_shift,
-                                        __nv_bfloat16 *__restrict__ out) {
+// in/out [B, Tp, D] bf16; input frames t >= len[b] count as zero.
+// Thread = two adjacent channels (bf16x2: a warp moves 128 contiguous bytes
+// per frame) sliding over a chunk of frames with the K input taps held in
+// registers, so every input element is read once per chunk.
+template <int K>
+__global__ void __launch_bounds__(128) dwconv1d_bn_silu_kernel(
+    const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len, int Tp, int D, int t_chunk,
+    const float *__restrict__ w, const float *__restrict__ bias, const float *__restrict__ bn_scale,
+    const float *__restrict__ bn_shift, __nv_bfloat16 *__restrict__ out) {
   const int b = blockIdx.z;
-  const int L = len[b];
-  const int t0 = blockIdx.y * 16;
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int L = min(len[b], Tp);
+  const int c = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
   if (c >= D) return;
-  float wr[31];
-  const int kk = min(K, 31);
-  for (int i = 0; i < kk; ++i) wr[i] = w[c * K + i];
-  const int pad = K / 2;
-  for (int t = t0; t < min(Tp, t0 + 16); ++t) {
-    float acc = bias[c];
-    for (int i = 0; i < kk; ++i) {
-      const int ts = t - pad + i;
-      if (ts < 0 || ts >= L) continue;
-      acc += wr[i] * bf(in[(static_cast<int64_t>(b) * Tp + ts) * D + c]);
+  const int t0 = blockIdx.y * t_chunk;
+  const int t1 = min(Tp, t0 + t_chunk);
+  constexpr int pad = K / 2;
+  float w0[K], w1[K];
+#pragma unroll
+  for (int i = 0; i < K; ++i) {
+    w0[i] = w[c * K + i];
+    w1[i] = w[(c + 1) * K + i];
+  }
+  const float b0 = bias[c], b1 = bias[c + 1];
+  const float s0 = bn_scale[c], s1 = bn_scale[c + 1], h0 = bn_shift[c], h1 = bn_shift[c + 1];
+  const __nv_bfloat162 *src = reinterpret_cast<const __nv_bfloat162 *>(in + static_cast<int64_t>(b) * Tp * D + c);
+  __nv_bfloat162 *dst = reinterpret_cast<__nv_bfloat162 *>(out + static_cast<int64_t>(b) * Tp * D + c);
+  const int dstride = D / 2;
+  auto load = [&](int t) -> float2 {
+    if (t < 0 || t >= L) return make_float2(0.f, 0.f);
+    return __bfloat1622float2(src[static_cast<int64_t>(t) * dstride]);
+  };
+  float2 x[K];  // x[i] = input frame t - pad + i
+#pragma unroll
+  for (int i = 0; i < K - 1; ++i) x[i] = load(t0 - pad + i);
+  for (int t = t0; t < t1; ++t) {
+    x[K - 1] = load(t + pad);
+    float a0 = b0, a1 = b1;
+#pragma unroll
+    for (int i = 0; i < K; ++i) {
+      a0 += w0[i] * x[i].x;
+      a1 += w1[i] * x[i].y;
     }
-    const float y = acc * bn_scale[c] + bn_shift[c];
-    out[(static_cast<int64_t>(b) * Tp + t) * D + c] = __float2bfloat16_rn(y * sigmoidf_(y));
+    const float y0 = a0 * s0 + h0, y1 = a1 * s1 + h1;
+    dst[static_cast<int64_t>(t) * dstride] = __floats2bfloat162_rn(y0 * sigmoidf_(y0), y1 * sigmoidf_(y1));
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) x[i] = x[i + 1];
   }
 }
 
@@ -510,6 +634,28 @@ cudaError_t conv0_relu(const float *mel, const int *len0, int B, int T, int F, i
   return launched();
 }
 
+bool conv0_dw_s2_supported(int F, int F1, int C) {
+  return C % kCdCG == 0 && F <= kMaxFeat && conv0_dw_smem_bytes(F, F1) <= 160 * 1024;
+}
+
+cudaError_t conv0_dw_s2(const float *mel, const int *len0, const int *len1, int B, int T, int F, int T1, int F1, int T2,
+                        int F2, int C, const float *w0, const float *b0, const float *w2, const float *b2,
+                        __nv_bfloat16 *out, cudaStream_t s) {
+  if (!conv0_dw_s2_supported(F, F1, C) || 2 * (F1 - 1) + 2 > F + 1) return cudaErrorInvalidValue;
+  const size_t smem = conv0_dw_smem_bytes(F, F1);
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(conv0_dw_s2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 160 * 1024);
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  dim3 grid(C / kCdCG, (T2 + kCdTT - 1) / kCdTT, B);
+  conv0_dw_s2_kernel<<<grid, 256, smem, s>>>(mel, len0, len1, T, F, T1, F1, T2, F2, C, w0, b0, w2, b2, out);
+  return launched();
+}
+
 cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int Tin, int Fin, int Tout, int Fout, int C,
                         const float *w, const float *bias, __nv_bfloat16 *out, cudaStream_t s) {
   const int per = Fout * C;
@@ -539,9 +685,22 @@ cudaError_t ln_rows(int mode, float *x, const void *u, float alpha, int rows, in
 cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int Tp, int D, int K, const float *w,
                              const float *bias, const float *bn_scale, const float *bn_shift, __nv_bfloat16 *out,
                              cudaStream_t s) {
-  if (K > 31) return cudaErrorInvalidValue;
-  dim3 grid((D + 127) / 128, (Tp + 15) / 16, B);
-  dwconv1d_bn_silu_kernel<<<grid, 128, 0, s>>>(in, len, Tp, D, K, w, bias, bn_scale, bn_shift, out);
+  if (K < 1 || K > 31 || (D & 1)) return cudaErrorInvalidValue;
+  constexpr int kThreads = 128;
+  const int t_chunk = 32;
+  dim3 grid((D / 2 + kThreads - 1) / kThreads, (Tp + t_chunk - 1) / t_chunk, B);
+  switch (K) {
+#define NQ_DW1D_CASE(k) \
+  case k: dwconv1d_bn_silu_kernel<k><<<grid, kThreads, 0, s>>>(in, len, Tp, D, t_chunk, w, bias, bn_scale, bn_shift, out); break;
+    NQ_DW1D_CASE(1) NQ_DW1D_CASE(2) NQ_DW1D_CASE(3) NQ_DW1D_CASE(4) NQ_DW1D_CASE(5) NQ_DW1D_CASE(6)
+    NQ_DW1D_CASE(7) NQ_DW1D_CASE(8) NQ_DW1D_CASE(9) NQ_DW1D_CASE(10) NQ_DW1D_CASE(11) NQ_DW1D_CASE(12)
+    NQ_DW1D_CASE(13) NQ_DW1D_CASE(14) NQ_DW1D_CASE(15) NQ_DW1D_CASE(16) NQ_DW1D_CASE(17) NQ_DW1D_CASE(18)
+    NQ_DW1D_CASE(19) NQ_DW1D_CASE(20) NQ_DW1D_CASE(21) NQ_DW1D_CASE(22) NQ_DW1D_CASE(23) NQ_DW1D_CASE(24)
+    NQ_DW1D_CASE(25) NQ_DW1D_CASE(26) NQ_DW1D_CASE(27) NQ_DW1D_CASE(28) NQ_DW1D_CASE(29) NQ_DW1D_CASE(30)
+    NQ_DW1D_CASE(31)
+#undef NQ_DW1D_CASE
+    default: return cudaErrorInvalidValue;
+  }
   return launched();
 }
 

@@ -93,6 +93,11 @@ class QWeight:
         _l.check(_l.load().nq_weight_shape(h, ctypes.byref(n), ctypes.byref(k), ctypes.byref(f)))
         return cls(h.value, n.value, k.value, f.value, device)
 
+    def keep_bf16(self, keep: bool = True) -> "QWeight":
+        """Keep (or drop) a dequantized bf16 copy for large-M GEMMs (MatMul::PackedBf16)."""
+        _l.check(_l.load().nq_weight_keep_bf16(self._h, 1 if keep else 0))
+        return self
+
     @classmethod
     def fuse(cls, ws: Sequence["QWeight"], flags: int = 0) -> "QWeight":
         arr = (_P * len(ws))(*[w._h for w in ws])

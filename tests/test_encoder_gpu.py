@@ -69,10 +69,13 @@ def _compare(oracle, got, ref, tag, tol):
     return err
 
 
-@pytest.mark.parametrize("d_model,heads,layers,t_mel,tol", [(512, 4, 2, 400, 0.05), (1024, 8, 2, 800, 0.05)])
-def test_encoder_matches_oracle(nq, oracle, d_model, heads, layers, t_mel, tol):
+# sub_channels 64 / 256 run the fused conv0 + depthwise subsampling kernel;
+# 96 (not a multiple of 64) runs conv0 and the depthwise conv separately.
+@pytest.mark.parametrize("d_model,heads,layers,t_mel,tol,sub", [(512, 4, 2, 400, 0.05, 64), (1024, 8, 2, 800, 0.05, 256),
+                                                                (512, 4, 1, 333, 0.05, 96)])
+def test_encoder_matches_oracle(nq, oracle, d_model, heads, layers, t_mel, tol, sub):
     from nspeech_b200 import synthetic as S
-    spec = S.EncoderSpec(d_model=d_model, n_heads=heads, n_layers=layers, sub_channels=64 if d_model == 512 else 256)
+    spec = S.EncoderSpec(d_model=d_model, n_heads=heads, n_layers=layers, sub_channels=sub)
     q = _model(oracle, spec)
     enc = _gpu_encoder(spec, q)
     mel = oracle.normal(1, (t_mel, 128))

@@ -129,3 +129,25 @@ def test_auto_path_selection(nq, oracle):
         nq.profile_enable(False)
     with pytest.raises(nq.NqError):
         nq.check(nq.load().nq_set_gemm_path(7))
+
+
+def test_kept_bf16_copy_is_identical_and_skips_dequant(nq, oracle):
+    """nq_weight_keep_bf16: same bits as the per-call dequantize, no dequantize launch."""
+    from nspeech_b200.fast_matmul import QWeight
+    for (m, k, n, glu) in [(1500, 1024, 4096, False), (300, 640, 1920, True), (129, 96, 130, False)]:
+        q = oracle.quantize_q8_0(oracle.normal(350 + n, (n, k), 0.0, 0.02))
+        w = QWeight.from_q8_0(q, n, k, flags=nq.NQ_PACK_GLU if glu else 0)
+        epi = nq.NQ_EPI_GLU_SIGMOID if glu else nq.NQ_EPI_NONE
+        x = torch.from_numpy(oracle.normal(351, (m, k))).cuda().to(torch.bfloat16)
+        a = w.linear(x, epilogue=epi, out_dtype=torch.float32).clone()
+        w.keep_bf16(True)
+        nq.profile_enable(True)
+        nq.profile_read(nq.NQ_KCLASS_DEQUANT, True)
+        b = w.linear(x, epilogue=epi, out_dtype=torch.float32).clone()
+        assert nq.profile_read(nq.NQ_KCLASS_DEQUANT, True)["launches"] == 0
+        nq.profile_enable(False)
+        assert torch.equal(a, b), (m, k, n)
+        w.keep_bf16(False)
+        c = w.linear(x, epilogue=epi, out_dtype=torch.float32)
+        assert torch.equal(a, c)
+    assert nq.status() == 0
