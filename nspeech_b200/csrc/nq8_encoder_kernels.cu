@@ -368,14 +368,21 @@ __global__ void relpos_kernel(int T, int D, __nv_bfloat16 *__restrict__ pos) {
 //   s[i][j] = ((q_i + u_h) . k_j + (q_i + v_h) . r[T-1 + j - i]) / sqrt(hd)
 //   o_i = softmax_j(s[i][:]) . V          (keys j >= len masked)
 // qkv [B*Tp, 3D] bf16 (q | k | v), krel [2Tp-1, D] bf16, out [B*Tp, D] bf16.
-// CTA = 4 warps x 16 query rows, one head; key tiles of 64; the 127 relative
-// rows a (64 x 64) tile needs are multiplied once (BD) and gathered along
-// the diagonal through shared memory.  Legacy mma.sync (not the graded path).
+// CTA = 8 warps x 16 query rows (128 rows), one head; key tiles of 64.  Each
+// warp keeps its (q + u) and (q + v) A fragments in registers.  K and V tiles
+// are double-buffered with cp.async; the relative rows live in a 256-row ring
+// (a key tile needs 191 consecutive rows and the next tile 64 new ones), and
+// each warp multiplies only the 80 relative rows its diagonal band touches
+// (BD = Qv R^T, 16 x 80), parks them in shared memory and gathers
+// BD[il][jl - il + 15] for its scores.  Legacy mma.sync m16n8k16.
 constexpr int kHd = 128;
-constexpr int kQT = 64;
-constexpr int kKT = 64;
+constexpr int kQT = 128;         // query rows per CTA
+constexpr int kKT = 64;          // keys per tile
+constexpr int kAWarps = kQT / 16;
+constexpr int kRing = 256;       // relative rows kept (power of two)
+constexpr int kBdCols = 80;      // relative rows per warp and tile
 constexpr int kPitch = kHd + 8;  // bf16 elements per smem row (272 B): conflict-free ldmatrix
-constexpr int kBdPitch = 132;    // floats per BD row
+constexpr int kBdPitch = 84;     // floats per parked BD row
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -387,61 +394,85 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t &r0, uint32_t 
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
                : "r"(addr));
 }
+// 16-byte global -> shared copy; src_bytes 0 writes zeros (rows out of range).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, int src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
 
-// rows [r0, r0+nrows) x kHd bf16 from a [*, ld] matrix (column offset col0)
-// into smem with pitch kPitch; rows outside [0, rmax) are zero.
-__device__ __forceinline__ void load_tile(__nv_bfloat16 *dst, const __nv_bfloat16 *src, int64_t ld, int col0, int r0,
-                                          int nrows, int rmax, int tid, int nthreads) {
+// Rows [r0, r0 + nrows) x kHd of a [*, ld] bf16 matrix (column offset col0)
+// into shared rows slot(r) with pitch kPitch; rows outside [0, rmax) are zero.
+template <typename SlotFn>
+__device__ __forceinline__ void load_rows_async(__nv_bfloat16 *dst, const __nv_bfloat16 *src, int64_t ld, int col0,
+                                                int r0, int nrows, int rmax, SlotFn slot, int tid, int nthreads) {
   for (int idx = tid; idx < nrows * (kHd / 8); idx += nthreads) {
     const int r = idx / (kHd / 8);
     const int c8 = idx - r * (kHd / 8);
     const int gr = r0 + r;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (gr >= 0 && gr < rmax) v = *reinterpret_cast<const uint4 *>(src + static_cast<int64_t>(gr) * ld + col0 + c8 * 8);
-    *reinterpret_cast<uint4 *>(dst + r * kPitch + c8 * 8) = v;
+    const bool ok = gr >= 0 && gr < rmax;
+    const __nv_bfloat16 *g = src + static_cast<int64_t>(ok ? gr : 0) * ld + col0 + c8 * 8;
+    cp_async16(smem_u32(dst + slot(r) * kPitch + c8 * 8), g, ok ? 16 : 0);
   }
 }
 
-__global__ void __launch_bounds__(128) relpos_attention_kernel(const __nv_bfloat16 *__restrict__ qkv,
-                                                               const __nv_bfloat16 *__restrict__ krel,
-                                                               const float *__restrict__ bias_u,
-                                                               const float *__restrict__ bias_v,
-                                                               const int *__restrict__ len, int Tp, int D,
-                                                               float scale, __nv_bfloat16 *__restrict__ out) {
+__global__ void __launch_bounds__(32 * kAWarps, 1)
+    relpos_attention_kernel(const __nv_bfloat16 *__restrict__ qkv, const __nv_bfloat16 *__restrict__ krel,
+                            const float *__restrict__ bias_u, const float *__restrict__ bias_v,
+                            const int *__restrict__ len, int Tp, int D, float scale, __nv_bfloat16 *__restrict__ out) {
   extern __shared__ __align__(16) uint8_t sm[];
-  __nv_bfloat16 *sQu = reinterpret_cast<__nv_bfloat16 *>(sm);
-  __nv_bfloat16 *sQv = sQu + kQT * kPitch;
-  __nv_bfloat16 *sK = sQv + kQT * kPitch;
-  __nv_bfloat16 *sV = sK + kKT * kPitch;
-  __nv_bfloat16 *sR = sV + kKT * kPitch;  // 128 rows
-  float *sBD = reinterpret_cast<float *>(sR + 128 * kPitch);  // 4 warps x 16 x kBdPitch
+  __nv_bfloat16 *sK = reinterpret_cast<__nv_bfloat16 *>(sm);  // [2][kKT][kPitch]
+  __nv_bfloat16 *sV = sK + 2 * kKT * kPitch;                   // [2][kKT][kPitch]
+  __nv_bfloat16 *sR = sV + 2 * kKT * kPitch;                   // [kRing][kPitch]
+  float *sBD = reinterpret_cast<float *>(sR + kRing * kPitch); // [kAWarps][16][kBdPitch]
 
   const int b = blockIdx.z;
   const int h = blockIdx.y;
   const int i0 = blockIdx.x * kQT;
   const int tid = threadIdx.x;
+  const int nthr = blockDim.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int g = lane >> 2;
   const int t4 = lane & 3;
-  const int L = len[b];
+  const int L = min(len[b], Tp);
   const int64_t ld = 3 * static_cast<int64_t>(D);
   const __nv_bfloat16 *base = qkv + static_cast<int64_t>(b) * Tp * ld;
+  const int wrow0 = warp * 16;  // CTA-local first query row of this warp
+  const int ntiles = (L + kKT - 1) / kKT;
+  // Relative row of CTA-window index 0 for key tile t: P0 + 64 t.
+  const int P0 = Tp - 1 - i0 - (kQT - 1);
+  auto ring = [](int p) { return p & (kRing - 1); };
 
-  // Q tile with the two position biases folded in.
-  for (int idx = tid; idx < kQT * (kHd / 2); idx += 128) {
-    const int r = idx / (kHd / 2);
-    const int c2 = (idx - r * (kHd / 2)) * 2;
-    float q0 = 0.f, q1 = 0.f;
-    if (i0 + r < Tp) {
-      const __nv_bfloat162 q = *reinterpret_cast<const __nv_bfloat162 *>(base + static_cast<int64_t>(i0 + r) * ld + h * kHd + c2);
-      q0 = __low2float(q);
-      q1 = __high2float(q);
+  // Prefetch tile 0 (K, V, 192 relative rows) while the Q fragments load.
+  if (ntiles > 0) {
+    load_rows_async(sK, base, ld, D + h * kHd, 0, kKT, L, [](int r) { return r; }, tid, nthr);
+    load_rows_async(sV, base, ld, 2 * D + h * kHd, 0, kKT, L, [](int r) { return r; }, tid, nthr);
+    load_rows_async(sR, krel, D, h * kHd, P0, 192, 2 * Tp - 1, [&](int r) { return ring(P0 + r); }, tid, nthr);
+  }
+  cp_async_commit();
+
+  // A fragments of (q + u) and (q + v) for this warp's 16 rows (m16n8k16 layout:
+  // a0 (g, 2t4), a1 (g + 8, 2t4), a2 (g, 2t4 + 8), a3 (g + 8, 2t4 + 8) per 16-wide k slice).
+  uint32_t au[kHd / 16][4], av[kHd / 16][4];
+  {
+    const int ra = i0 + wrow0 + g, rb = ra + 8;
+#pragma unroll
+    for (int kk = 0; kk < kHd / 16; ++kk) {
+#pragma unroll
+      for (int x = 0; x < 4; ++x) {
+        const int row = (x & 1) ? rb : ra;
+        const int c = kk * 16 + 2 * t4 + 8 * (x >> 1);
+        float q0 = 0.f, q1 = 0.f;
+        if (row < Tp) {
+          const __nv_bfloat162 q = *reinterpret_cast<const __nv_bfloat162 *>(base + static_cast<int64_t>(row) * ld + h * kHd + c);
+          q0 = __low2float(q);
+          q1 = __high2float(q);
+        }
+        au[kk][x] = pack_bf16x2(q0 + bias_u[h * kHd + c], q1 + bias_u[h * kHd + c + 1]);
+        av[kk][x] = pack_bf16x2(q0 + bias_v[h * kHd + c], q1 + bias_v[h * kHd + c + 1]);
+      }
     }
-    const float u0 = bias_u[h * kHd + c2], u1 = bias_u[h * kHd + c2 + 1];
-    const float v0 = bias_v[h * kHd + c2], v1 = bias_v[h * kHd + c2 + 1];
-    *reinterpret_cast<uint32_t *>(sQu + r * kPitch + c2) = pack_bf16x2(q0 + u0, q1 + u1);
-    *reinterpret_cast<uint32_t *>(sQv + r * kPitch + c2) = pack_bf16x2(q0 + v0, q1 + v1);
   }
 
   float o[kHd / 8][4];
@@ -453,83 +484,89 @@ __global__ void __launch_bounds__(128) relpos_attention_kernel(const __nv_bfloat
   float lrow[2] = {0.f, 0.f};
   const float sl2 = scale * 1.4426950408889634f;  // softmax in base 2
   float *bd = sBD + warp * 16 * kBdPitch;
-  const int wrow0 = warp * 16;  // CTA-local first query row of this warp
+  // This warp's relative rows within the CTA window: [kQT - 16 - wrow0, + 80).
+  const int wwin = kQT - 16 - wrow0;
 
-  for (int j0 = 0; j0 < L; j0 += kKT) {
-    __syncthreads();  // previous tile's smem reads are done
-    load_tile(sK, base, ld, D + h * kHd, j0, kKT, L, tid, 128);  // keys >= len read as zero
-    load_tile(sV, base, ld, 2 * D + h * kHd, j0, kKT, L, tid, 128);
-    const int p_lo = Tp - 1 + j0 - i0 - (kQT - 1);
-    load_tile(sR, krel, D, h * kHd, p_lo, 128, 2 * Tp - 1, tid, 128);
-    __syncthreads();
+  for (int t = 0; t < ntiles; ++t) {
+    const int j0 = t * kKT;
+    const int buf = t & 1;
+    cp_async_wait_all();
+    __syncthreads();  // tile t landed for everyone; tile t-1's buffers are free
+    if (t + 1 < ntiles) {
+      const int jn = j0 + kKT;
+      __nv_bfloat16 *dk = sK + (buf ^ 1) * kKT * kPitch;
+      __nv_bfloat16 *dv = sV + (buf ^ 1) * kKT * kPitch;
+      load_rows_async(dk, base, ld, D + h * kHd, jn, kKT, L, [](int r) { return r; }, tid, nthr);
+      load_rows_async(dv, base, ld, 2 * D + h * kHd, jn, kKT, L, [](int r) { return r; }, tid, nthr);
+      const int pn = P0 + 192 + 64 * t;  // the 64 relative rows tile t + 1 adds
+      load_rows_async(sR, krel, D, h * kHd, pn, 64, 2 * Tp - 1, [&](int r) { return ring(pn + r); }, tid, nthr);
+    }
+    cp_async_commit();
+    const __nv_bfloat16 *cK = sK + buf * kKT * kPitch;
+    const __nv_bfloat16 *cV = sV + buf * kKT * kPitch;
+    const int pw = P0 + 64 * t + wwin;  // relative row of this warp's BD column 0
 
-    // S_c = Qu K^T (16 x 64 per warp) and BD = Qv R^T (16 x 128 per warp).
+    // BD = Qv R^T over the warp's 80 relative rows, parked in shared memory.
+    {
+      float r[kBdCols / 8][4];
+#pragma unroll
+      for (int n = 0; n < kBdCols / 8; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) r[n][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < kHd / 16; ++kk) {
+#pragma unroll
+        for (int nb = 0; nb < kBdCols / 16; ++nb) {
+          uint32_t b0, b1, b2, b3;
+          const int q = lane >> 3, rr = lane & 7;
+          const int pr = pw + nb * 16 + rr + 8 * (q >> 1);
+          const int col = kk * 16 + 8 * (q & 1);
+          ldsm_x4(smem_u32(sR + ring(pr) * kPitch + col), b0, b1, b2, b3);
+          mma_16816_bf16(r[2 * nb], av[kk], b0, b1);
+          mma_16816_bf16(r[2 * nb + 1], av[kk], b2, b3);
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < kBdCols / 8; ++n) {
+        *reinterpret_cast<float2 *>(bd + g * kBdPitch + n * 8 + 2 * t4) = make_float2(r[n][0], r[n][1]);
+        *reinterpret_cast<float2 *>(bd + (g + 8) * kBdPitch + n * 8 + 2 * t4) = make_float2(r[n][2], r[n][3]);
+      }
+    }
+    __syncwarp();
+
+    // S = Qu K^T (16 x 64) + BD[il][jl - il + 15], scaled to base 2; keys >= len masked.
     float s[kKT / 8][4];
-    float r[128 / 8][4];
 #pragma unroll
     for (int n = 0; n < kKT / 8; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) s[n][e] = 0.f;
 #pragma unroll
-    for (int n = 0; n < 16; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) r[n][e] = 0.f;
-#pragma unroll
     for (int kk = 0; kk < kHd / 16; ++kk) {
-      uint32_t au[4], av[4];
-      {
-        const int q = lane >> 3, rr = lane & 7;
-        const int row = wrow0 + rr + 8 * (q & 1);
-        const int col = kk * 16 + 8 * (q >> 1);
-        ldsm_x4(smem_u32(sQu + row * kPitch + col), au[0], au[1], au[2], au[3]);
-        ldsm_x4(smem_u32(sQv + row * kPitch + col), av[0], av[1], av[2], av[3]);
-      }
 #pragma unroll
       for (int nb = 0; nb < kKT / 16; ++nb) {
         uint32_t b0, b1, b2, b3;
         const int q = lane >> 3, rr = lane & 7;
         const int key = nb * 16 + rr + 8 * (q >> 1);
         const int col = kk * 16 + 8 * (q & 1);
-        ldsm_x4(smem_u32(sK + key * kPitch + col), b0, b1, b2, b3);
-        mma_16816_bf16(s[2 * nb], au, b0, b1);
-        mma_16816_bf16(s[2 * nb + 1], au, b2, b3);
-      }
-#pragma unroll
-      for (int nb = 0; nb < 8; ++nb) {
-        uint32_t b0, b1, b2, b3;
-        const int q = lane >> 3, rr = lane & 7;
-        const int pr = nb * 16 + rr + 8 * (q >> 1);
-        const int col = kk * 16 + 8 * (q & 1);
-        ldsm_x4(smem_u32(sR + pr * kPitch + col), b0, b1, b2, b3);
-        mma_16816_bf16(r[2 * nb], av, b0, b1);
-        mma_16816_bf16(r[2 * nb + 1], av, b2, b3);
+        ldsm_x4(smem_u32(cK + key * kPitch + col), b0, b1, b2, b3);
+        mma_16816_bf16(s[2 * nb], au[kk], b0, b1);
+        mma_16816_bf16(s[2 * nb + 1], au[kk], b2, b3);
       }
     }
-    // Park BD in shared memory, then gather the diagonal: for CTA-local query
-    // il and key jl the relative row is jl - il + (kQT - 1) of the window.
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      bd[g * kBdPitch + n * 8 + 2 * t4] = r[n][0];
-      bd[g * kBdPitch + n * 8 + 2 * t4 + 1] = r[n][1];
-      bd[(g + 8) * kBdPitch + n * 8 + 2 * t4] = r[n][2];
-      bd[(g + 8) * kBdPitch + n * 8 + 2 * t4 + 1] = r[n][3];
-    }
-    __syncwarp();
     float tmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int n = 0; n < kKT / 8; ++n)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int rl = g + 8 * (e >> 1);           // row within the warp
-        const int jl = n * 8 + 2 * t4 + (e & 1);   // key within the tile
-        const int il = wrow0 + rl;
-        const float rel = bd[rl * kBdPitch + (jl - il + kQT - 1)];
+        const int rl = g + 8 * (e >> 1);          // row within the warp
+        const int jl = n * 8 + 2 * t4 + (e & 1);  // key within the tile
+        const float rel = bd[rl * kBdPitch + (jl - rl + 15)];
         float v = (s[n][e] + rel) * sl2;
         if (j0 + jl >= L) v = -INFINITY;
         s[n][e] = v;
         tmax[e >> 1] = fmaxf(tmax[e >> 1], v);
       }
-    __syncwarp();
+    __syncwarp();  // bd reads done before the next tile parks
 #pragma unroll
     for (int hh = 0; hh < 2; ++hh) {
       tmax[hh] = fmaxf(tmax[hh], __shfl_xor_sync(0xffffffffu, tmax[hh], 1));
@@ -582,12 +619,13 @@ __global__ void __launch_bounds__(128) relpos_attention_kernel(const __nv_bfloat
         const int q = lane >> 3, rr = lane & 7;
         const int key = kb * 16 + rr + 8 * (q & 1);
         const int col = nb * 16 + 8 * (q >> 1);
-        ldsm_x4_t(smem_u32(sV + key * kPitch + col), b0, b1, b2, b3);
+        ldsm_x4_t(smem_u32(cV + key * kPitch + col), b0, b1, b2, b3);
         mma_16816_bf16(o[2 * nb], pa[kb], b0, b1);
         mma_16816_bf16(o[2 * nb + 1], pa[kb], b2, b3);
       }
     }
   }
+  cp_async_wait_all();  // nothing in flight at exit
 
   const float inv0 = lrow[0] > 0.f ? 1.f / lrow[0] : 0.f;
   const float inv1 = lrow[1] > 0.f ? 1.f / lrow[1] : 0.f;
@@ -622,7 +660,7 @@ cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, fl
 }
 
 size_t attention_smem_bytes() {
-  return static_cast<size_t>(kQT * 2 + kKT * 2 + 128) * kPitch * 2 + 4 * 16 * kBdPitch * 4;
+  return static_cast<size_t>(4 * kKT + kRing) * kPitch * 2 + static_cast<size_t>(kAWarps) * 16 * kBdPitch * 4;
 }
 
 // ------------------------------------------------------------------ launches
@@ -724,7 +762,7 @@ cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel
     attr_set[dev] = true;
   }
   dim3 grid((Tp + kQT - 1) / kQT, H, B);
-  relpos_attention_kernel<<<grid, 128, smem, s>>>(qkv, krel, bias_u, bias_v, len, Tp, D,
+  relpos_attention_kernel<<<grid, 32 * kAWarps, smem, s>>>(qkv, krel, bias_u, bias_v, len, Tp, D,
                                                   1.0f / sqrtf(static_cast<float>(kHd)), out);
   return launched();
 }
