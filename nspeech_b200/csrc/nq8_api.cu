@@ -67,6 +67,12 @@ int g_gemm_path = NQ_GEMM_AUTO;
 // Token count from which a GEMM call dequantizes the weight once and runs
 // the bf16 tensor-core GEMM (measured crossover on B200).
 constexpr int64_t kDequantMinM = 128;
+// Cost model of the bf16 GEMM's split-K choice, measured on B200: time of one
+// 64-wide k step of a 256 x 256 pair unit within a full wave, and the split-K
+// reduction's partial-sum traffic rate and fixed launch cost.
+constexpr double kNsPerUnitStep = 390.0;
+constexpr double kReduceBytesPerNs = 5000.0;
+constexpr double kReduceLaunchNs = 3000.0;
 thread_local std::string t_err;
 
 int fail(int code, const char *fmt, ...) {
@@ -336,16 +342,43 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
   g.cached = g.deq && w->bf16 != nullptr;
   g.split_x = !direct;
   g.pairs = std::max(1, sm_count / 2);
-  g.bt = g.deq ? nq::gemm_bf16_block_t() : nq::gemm_block_t(splitx ? nq::kGemmBt128SplitX : nq::kGemmBt128);
-  g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
   g.grid_n = (w->n_tiles + 1) / 2;
-  // Split K when the output tiles do not fill the SM pairs (>= 4 k chunks per split).
-  const int tiles = g.grid_m * g.grid_n;
   const int kc = w->kc;
-  int splits = 1;
-  if (tiles < g.pairs) splits = std::max(1, std::min((g.pairs + tiles - 1) / tiles, std::max(1, kc / 4)));
-  g.cps = (kc + splits - 1) / splits;
-  g.splits = (kc + g.cps - 1) / g.cps;
+  if (!g.deq) {
+    // Fused kernel: split K when the output tiles do not fill the SM pairs
+    // (>= 4 k chunks per split).
+    g.bt = nq::gemm_block_t(splitx ? nq::kGemmBt128SplitX : nq::kGemmBt128);
+    g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
+    const int tiles = g.grid_m * g.grid_n;
+    int splits = 1;
+    if (tiles < g.pairs) splits = std::max(1, std::min((g.pairs + tiles - 1) / tiles, std::max(1, kc / 4)));
+    g.cps = (kc + splits - 1) / splits;
+    g.splits = (kc + g.cps - 1) / g.cps;
+    return g;
+  }
+  // bf16 GEMM: pick the split factor with the least estimated time: full
+  // waves of 256 x 256 units times their k steps, plus, when split, one write
+  // and one read of the f32 partials and the reduction launch.
+  const int ldp = w->n_tiles * nq::kPackRows;
+  g.bt = nq::gemm_bf16_block_t();
+  g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
+  const int tiles = g.grid_m * g.grid_n;
+  double best = 1e300;
+  const int max_splits = std::max(1, std::min(8, kc / 4));
+  for (int sp = 1; sp <= max_splits; ++sp) {
+    const int cps = (kc + sp - 1) / sp;
+    const int splits = (kc + cps - 1) / cps;
+    if (splits != sp) continue;
+    const int64_t units = static_cast<int64_t>(tiles) * splits;
+    const int64_t rounds = (units + g.pairs - 1) / g.pairs;
+    double t = static_cast<double>(rounds) * cps * kNsPerUnitStep;
+    if (splits > 1) t += 2.0 * splits * static_cast<double>(m) * ldp * 4.0 / kReduceBytesPerNs + kReduceLaunchNs;
+    if (t < best) {
+      best = t;
+      g.splits = splits;
+      g.cps = cps;
+    }
+  }
   return g;
 }
 

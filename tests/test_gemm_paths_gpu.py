@@ -98,7 +98,7 @@ def test_paths_ragged(nq, oracle, path, m, n, k):
 def test_paths_split_k_deterministic(nq, oracle, path):
     """Shapes with few output tiles split K; the reduction sums splits in order."""
     from nspeech_b200.fast_matmul import QWeight
-    for (m, k, n) in [(40, 4096, 1024), (375, 4096, 1024), (1200, 2048, 256)]:
+    for (m, k, n) in [(40, 4096, 1024), (375, 4096, 1024), (300, 4096, 256)]:
         q = oracle.quantize_q8_0(oracle.normal(330 + m, (n, k), 0.0, 0.02))
         w = QWeight.from_q8_0(q, n, k)
         x = torch.from_numpy(oracle.normal(331, (m, k))).cuda()
