@@ -63,12 +63,16 @@ __global__ void conv0_relu_kernel(const float *__restrict__ mel, const int *__re
 // output rows needs (2 kCdTT + 1) are computed into shared memory and never
 // reach HBM.  Block = (64 channels, kCdTT output rows, one segment).
 constexpr int kCdTT = 4;   // output rows (t2) per block
-constexpr int kCdCG = 64;  // channels per block
+constexpr int kCdCG = 64;  // channels per block (a thread owns a channel pair)
 constexpr int kCdRows1 = 2 * kCdTT + 1;
-constexpr int kCdMelRows = 4 * kCdTT + 3;
+constexpr int kCdMelData = 4 * kCdTT + 3;   // mel rows the block's s1 rows read
+constexpr int kCdMelRows = kCdMelData + 2;  // + two zero rows read by the unused tenth s1 row
+
+// 16-byte rows with room for the 9-wide window of the last f1 quad.
+__host__ __device__ constexpr int cd_mel_pitch(int F) { return ((F + 8 + 3) / 4) * 4; }
 
 size_t conv0_dw_smem_bytes(int F, int F1) {
-  return static_cast<size_t>(kCdMelRows) * (F + 2) * sizeof(float) +
+  return static_cast<size_t>(kCdMelRows) * cd_mel_pitch(F) * sizeof(float) +
          static_cast<size_t>(kCdRows1) * F1 * kCdCG * sizeof(__nv_bfloat16);
 }
 
@@ -77,68 +81,103 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
     int F1, int T2, int F2, int C, const float *__restrict__ w0, const float *__restrict__ b0,
     const float *__restrict__ w2, const float *__restrict__ b2, __nv_bfloat16 *__restrict__ out) {
   extern __shared__ __align__(16) unsigned char cd_smem[];
-  const int FP = F + 2;  // padded mel row: column j holds frequency j - 1
+  const int FP = cd_mel_pitch(F);  // padded mel row: column j holds frequency j - 1
   float *melS = reinterpret_cast<float *>(cd_smem);
   __nv_bfloat16 *s1S = reinterpret_cast<__nv_bfloat16 *>(cd_smem + static_cast<size_t>(kCdMelRows) * FP * sizeof(float));
   const int b = blockIdx.z;
   const int t2s = blockIdx.y * kCdTT;
   const int cg0 = blockIdx.x * kCdCG;
   const int L0 = len0[b], L1 = min(len1[b], T1);
-  // 1. mel rows 4 t2s - 3 .. 4 t2s + 4 kCdTT - 1 (zero outside [0, min(T, L0)) and the frequency range)
+  // 1. mel rows 4 t2s - 3 .. (zero outside [0, min(T, L0)), the frequency range
+  //    and the last, padding row)
   for (int idx = threadIdx.x; idx < kCdMelRows * FP; idx += blockDim.x) {
     const int r = idx / FP;
     const int j = idx - r * FP;
     const int t = 4 * t2s - 3 + r;
     const int f = j - 1;
     float v = 0.f;
-    if (t >= 0 && t < T && t < L0 && f >= 0 && f < F) v = mel[(static_cast<int64_t>(b) * T + t) * F + f];
+    if (r < kCdMelData && t >= 0 && t < T && t < L0 && f >= 0 && f < F)
+      v = mel[(static_cast<int64_t>(b) * T + t) * F + f];
     melS[idx] = v;
   }
   __syncthreads();
-  const int c = threadIdx.x % kCdCG;  // a warp covers 32 consecutive channels
-  const int grp = threadIdx.x / kCdCG;
-  const int ngrp = blockDim.x / kCdCG;
-  const int cc = cg0 + c;
-  // 2. s1 rows t1 = 2 t2s - 1 + r1; four f1 per task (27 mel loads for 4 outputs)
+  const int cp = threadIdx.x & 31;  // channel pair: channels cg0 + 2 cp, + 1
+  const int grp = threadIdx.x >> 5;
+  const int ngrp = blockDim.x >> 5;
+  const int cc = cg0 + 2 * cp;
+  // 2. s1 rows t1 = 2 t2s - 1 + r1: a task is two rows x four f1 x two
+  //    channels; each mel value is read once (16-byte loads) for both rows.
   {
-    float wr[9];
+    float wa[9], wb[9];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) wr[i] = w0[cc * 9 + i];
-    const float bc = b0[cc];
+    for (int i = 0; i < 9; ++i) {
+      wa[i] = w0[cc * 9 + i];
+      wb[i] = w0[(cc + 1) * 9 + i];
+    }
+    const float ba = b0[cc], bb = b0[cc + 1];
     const int quads = (F1 + 3) / 4;
-    for (int task = grp; task < kCdRows1 * quads; task += ngrp) {
-      const int r1 = task / quads;
-      const int f1q = (task - r1 * quads) * 4;
-      float acc[4] = {bc, bc, bc, bc};
+    const int pairs = (kCdRows1 + 1) / 2;
+    for (int task = grp; task < pairs * quads; task += ngrp) {
+      const int rp = task / quads;
+      const int f1q = (task - rp * quads) * 4;
+      float acc[2][4][2];
 #pragma unroll
-      for (int dt = 0; dt < 3; ++dt) {
-        const float *row = melS + (2 * r1 + dt) * FP + 2 * f1q;
-        float m[9];
+      for (int r = 0; r < 2; ++r)
 #pragma unroll
-        for (int x = 0; x < 9; ++x) m[x] = (2 * f1q + x < FP) ? row[x] : 0.f;
+        for (int q = 0; q < 4; ++q) {
+          acc[r][q][0] = ba;
+          acc[r][q][1] = bb;
+        }
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+      for (int mr = 0; mr < 5; ++mr) {
+        const float *row = melS + (4 * rp + mr) * FP + 2 * f1q;
+        float m[12];
+        const float4 m0 = *reinterpret_cast<const float4 *>(row);
+        const float4 m1 = *reinterpret_cast<const float4 *>(row + 4);
+        m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
+        m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
+        m[8] = row[8];
 #pragma unroll
-          for (int df = 0; df < 3; ++df) acc[q] += wr[dt * 3 + df] * m[2 * q + df];
+        for (int r = 0; r < 2; ++r) {
+          const int dt = mr - 2 * r;
+          if (dt < 0 || dt > 2) continue;
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int df = 0; df < 3; ++df) {
+              acc[r][q][0] += wa[dt * 3 + df] * m[2 * q + df];
+              acc[r][q][1] += wb[dt * 3 + df] * m[2 * q + df];
+            }
+        }
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        if (f1q + q < F1) s1S[(r1 * F1 + f1q + q) * kCdCG + c] = __float2bfloat16_rn(fmaxf(acc[q], 0.f));
+      for (int r = 0; r < 2; ++r) {
+        const int r1 = 2 * rp + r;
+        if (r1 >= kCdRows1) continue;
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          if (f1q + q < F1)
+            *reinterpret_cast<__nv_bfloat162 *>(s1S + (r1 * F1 + f1q + q) * kCdCG + 2 * cp) =
+                __floats2bfloat162_rn(fmaxf(acc[r][q][0], 0.f), fmaxf(acc[r][q][1], 0.f));
+      }
     }
   }
   __syncthreads();
-  // 3. depthwise 3x3 stride 2 over the staged rows
+  // 3. depthwise 3x3 stride 2 over the staged rows, two channels per thread
   {
-    float wr[9];
+    float wa[9], wb[9];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) wr[i] = w2[cc * 9 + i];
-    const float bc = b2[cc];
+    for (int i = 0; i < 9; ++i) {
+      wa[i] = w2[cc * 9 + i];
+      wb[i] = w2[(cc + 1) * 9 + i];
+    }
+    const float ba = b2[cc], bb = b2[cc + 1];
     for (int task = grp; task < kCdTT * F2; task += ngrp) {
       const int r2 = task / F2;
       const int f2 = task - r2 * F2;
       const int t2 = t2s + r2;
       if (t2 >= T2) break;
-      float acc = bc;
+      float a0 = ba, a1 = bb;
 #pragma unroll
       for (int dt = 0; dt < 3; ++dt) {
         const int t1 = 2 * t2 - 1 + dt;
@@ -147,17 +186,18 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
         for (int df = 0; df < 3; ++df) {
           const int f1 = 2 * f2 - 1 + df;
           if (f1 < 0 || f1 >= F1) continue;
-          acc += wr[dt * 3 + df] * bf(s1S[((2 * r2 + dt) * F1 + f1) * kCdCG + c]);
+          const float2 v =
+              __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(s1S + ((2 * r2 + dt) * F1 + f1) * kCdCG + 2 * cp));
+          a0 += wa[dt * 3 + df] * v.x;
+          a1 += wb[dt * 3 + df] * v.y;
         }
       }
-      out[((static_cast<int64_t>(b) * T2 + t2) * F2 + f2) * C + cc] = __float2bfloat16_rn(acc);
+      *reinterpret_cast<__nv_bfloat162 *>(out + ((static_cast<int64_t>(b) * T2 + t2) * F2 + f2) * C + cc) =
+          __floats2bfloat162_rn(a0, a1);
     }
   }
 }
 
-
-// Depthwise conv2d(C, 3x3, stride 2, pad 1, groups C) + bias on NHWC bf16
-// (fast_conformer.rs:109-122, 135-146).  Input frames t >= len_in[b] are zero.
 __global__ void dwconv2d_s2_kernel(const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len_in, int Tin,
                                    int Fin, int Tout, int Fout, int C, const float *__restrict__ w,
                                    const float *__restrict__ bias, __nv_bfloat16 *__restrict__ out) {
@@ -328,21 +368,30 @@ __global__ void __launch_bounds__(128) dwconv1d_bn_silu_kernel(
     if (t < 0 || t >= L) return make_float2(0.f, 0.f);
     return __bfloat1622float2(src[static_cast<int64_t>(t) * dstride]);
   };
-  float2 x[K];  // x[i] = input frame t - pad + i
+  // Four output frames per step; their four new input frames are loaded
+  // together (x[i] = input frame t - pad + i).
+  constexpr int kU = 4;
+  float2 x[K - 1 + kU];
 #pragma unroll
   for (int i = 0; i < K - 1; ++i) x[i] = load(t0 - pad + i);
-  for (int t = t0; t < t1; ++t) {
-    x[K - 1] = load(t + pad);
-    float a0 = b0, a1 = b1;
+  for (int t = t0; t < t1; t += kU) {
 #pragma unroll
-    for (int i = 0; i < K; ++i) {
-      a0 += w0[i] * x[i].x;
-      a1 += w1[i] * x[i].y;
+    for (int u = 0; u < kU; ++u) x[K - 1 + u] = load(t + pad + u);
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      if (t + u < t1) {
+        float a0 = b0, a1 = b1;
+#pragma unroll
+        for (int i = 0; i < K; ++i) {
+          a0 += w0[i] * x[u + i].x;
+          a1 += w1[i] * x[u + i].y;
+        }
+        const float y0 = a0 * s0 + h0, y1 = a1 * s1 + h1;
+        dst[static_cast<int64_t>(t + u) * dstride] = __floats2bfloat162_rn(y0 * sigmoidf_(y0), y1 * sigmoidf_(y1));
+      }
     }
-    const float y0 = a0 * s0 + h0, y1 = a1 * s1 + h1;
-    dst[static_cast<int64_t>(t) * dstride] = __floats2bfloat162_rn(y0 * sigmoidf_(y0), y1 * sigmoidf_(y1));
 #pragma unroll
-    for (int i = 0; i < K - 1; ++i) x[i] = x[i + 1];
+    for (int i = 0; i < K - 1; ++i) x[i] = x[i + kU];
   }
 }
 
