@@ -5,34 +5,35 @@
 // in src/triton_kernels.rs:170-309,1205-1289; CPU FbgemmBf16Op in
 // src/fast_matmul.rs:138-167).
 //
-// Y[tok, n] = act(X[tok, :] . bf16(dequant(W[n, :])) + bias[n]).  A cluster of
-// two CTAs (an SM pair) computes transposed tiles D[256 weight rows x 192
-// tokens] with tcgen05.mma.cta_group::2: each CTA owns 128 weight rows (its
-// TMEM lanes) and stages half of the token tile (96 rows) in its shared
-// memory, so per SM the activation operand costs half of what a 1-SM tile
-// does.  The weights are operand A *in tensor memory*: dequantized in
-// registers and written with tcgen05.st, they never touch shared memory.  The
+// Y[tok, n] = act(X[tok, :] . bf16(dequant(W[n, :])) + bias[n]).  Serves
+// calls below ~128 tokens, where the weight bytes dominate (larger calls
+// dequantize once and run K3, nq8_gemm_bf16.cu).  A cluster of two CTAs (an
+// SM pair) computes transposed tiles D[256 weight rows x 192 tokens] with
+// tcgen05.mma.cta_group::2: each CTA owns 128 weight rows (its TMEM lanes)
+// and stages half of the token tile (96 rows).  The weights are operand A *in
+// tensor memory*: dequantized in registers and written with tcgen05.st.  The
 // pair walks a static list of work units (weight-row pair tile, token tile,
-// k split); TMEM holds two accumulators, so the epilogue of unit j overlaps the
-// main loop of unit j+1.  Per CTA:
-//   warp 0      producer: TMA 2-D load of its half token tile [96 x 64 k]
-//               (bf16, 128-byte swizzle); completion is counted on the
-//               leader CTA's full_b barrier (the leader expects both halves).
+// k split); TMEM holds two accumulators, so the epilogue of unit j overlaps
+// the main loop of unit j+1.  Per CTA:
+//   warp 0      producer: per 64-wide k step, a bulk copy of its packed
+//               weight tile (8.7 KB) into shared stage s (completes on its
+//               own full_w[s]) and a TMA 2-D load of its 96 token rows (bf16,
+//               128-byte swizzle; completes on the leader's full_b[s]).
 //   warp 1      allocates 512 TMEM columns for the pair (D0, D1: 192 columns
 //               each; 4 A stages of 32); in the leader, lane 0 issues
 //               tcgen05.mma (M=256, N=192, K=16, kind::f16, A from TMEM) and
-//               commits to empty[s] / accum_full[b] of both CTAs (multicast
-//               commit; no multicast loads anywhere).
+//               commits to empty_a / empty_b / accum_full of both CTAs
+//               (multicast commit; no multicast loads anywhere).
 //   warps 2-5   epilogue: tcgen05.ld (one weight row per lane, 16 tokens at a
 //               time), bias + activation (GLU through shared memory), stores
 //               contiguous along the output row across the warp, then arrive
-//               on the leader's accum_empty; split-K partials with an arrival
-//               counter (the last split sums in order).
+//               on the leader's accum_empty; split-K writes raw partials for
+//               splitk_reduce.
 //   warps 6-21  dequant: the four warps of a TMEM lane quarter take turns by
-//               64-wide k step (warp `sub` fills A stage `sub`): coalesced
-//               16-byte loads prefetched a turn ahead, bf16(f32(d)*q) with
-//               packed f32x2 arithmetic, tcgen05.st 32x32b.x32, arrive on the
-//               leader's full_a.
+//               k step (warp `sub` fills A stage `sub`): read the weight
+//               chunk from shared memory, bf16(f32(d)*q) with packed f32x2
+//               arithmetic, tcgen05.st 32x32b.x32, arrive on the leader's
+//               full_a.
 // f32 activations arrive as two bf16 planes (hi, lo): two MMAs per k step.
 // Every mbarrier wait is bounded; on give-up the kernel records a status bit,
 // drains, frees TMEM and returns.
