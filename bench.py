@@ -193,6 +193,23 @@ def run_reference(args, rank: int, world: int) -> None:
 
 
 # ----------------------------------------------------------------------- ours
+def reduce_over_ranks(t_s: float, t_e2e: float, audio_s: float, dist, device: str):
+    """Whole-job figures: the slowest rank's device and e2e times, the audio of all ranks.
+
+    Every rank calls it once after its timed regions (two all-reduces, same
+    order on every rank); with dist None (one process) it returns its inputs.
+    """
+    if not dist:
+        return t_s, t_e2e, audio_s
+    import torch
+    vals = torch.tensor([t_s, t_e2e, audio_s], dtype=torch.float64, device=device)
+    mx = vals.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    tot = vals.clone()
+    dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    return float(mx[0]), float(mx[1]), float(tot[2])
+
+
 def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     import torch
     from nspeech_b200 import lib, synthetic as S
@@ -277,17 +294,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     cfg2_ms = a0.elapsed_time(a1) / 10
 
     # ---- max over ranks
-    vals = torch.tensor([t_s, t_e2e, audio_s, gemm["ms"], gemm["flops"], float(gemm["launches"])], dtype=torch.float64,
-                        device="cuda")
-    if dist:
-        mx = vals.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = vals.clone()
-        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        t_max, te2e_max = float(mx[0]), float(mx[1])
-        audio_total = float(tot[2])
-    else:
-        t_max, te2e_max, audio_total = t_s, t_e2e, audio_s
+    t_max, te2e_max, audio_total = reduce_over_ranks(t_s, t_e2e, audio_s, dist, "cuda")
 
     if rank == 0:
         pk = peaks()
