@@ -8,6 +8,8 @@ namespace nq {
 // Four consecutive k per thread (8-byte stores).
 __global__ void split_x_kernel(const void *__restrict__ x, int x_dtype, int64_t ldx, int64_t M, int64_t K,
                                int64_t k_pad, __nv_bfloat16 *__restrict__ hi, __nv_bfloat16 *__restrict__ lo) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int64_t quads = k_pad / 4;
   const int64_t total = M * quads;
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; t < total;
@@ -42,14 +44,15 @@ cudaError_t launch_split_x(const void *x, int x_dtype, int64_t ldx, int64_t M, i
   if (total == 0) return cudaSuccess;
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 16) blocks = 148 * 16;
-  split_x_kernel<<<blocks, 256, 0, stream>>>(x, x_dtype, ldx, M, K, k_pad, hi, lo);
-  return launched();
+  return launch_pdl(split_x_kernel, dim3(blocks), dim3(256), 0, stream, 1, x, x_dtype, ldx, M, K, k_pad, hi, lo);
 }
 
 // One block per (k chunk, tile): 256 threads, thread t dequantizes Q8_0 block
 // (t & 1) of row t / 2 (32 elements) and writes 64 contiguous bytes.
 __global__ void __launch_bounds__(256) dequant_tiles_kernel(const uint8_t *__restrict__ w, int kc,
                                                            __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int c = blockIdx.x, tile = blockIdx.y;
   const uint8_t *t = w + (static_cast<size_t>(tile) * kc + c) * kTileBytes;
   const int r = threadIdx.x >> 1, h = threadIdx.x & 1;
@@ -68,13 +71,14 @@ __global__ void __launch_bounds__(256) dequant_tiles_kernel(const uint8_t *__res
 
 cudaError_t launch_dequant_tiles(const uint8_t *w, int n_tiles, int kc, __nv_bfloat16 *out, cudaStream_t stream) {
   if (n_tiles <= 0 || kc <= 0) return cudaSuccess;
-  dequant_tiles_kernel<<<dim3(kc, n_tiles), 256, 0, stream>>>(w, kc, out);
-  return launched();
+  return launch_pdl(dequant_tiles_kernel, dim3(kc, n_tiles), dim3(256), 0, stream, 1, w, kc, out);
 }
 
 // Thread per (token, 4 consecutive output columns); the partial sums of the
 // splits are added in split order, so the result does not depend on timing.
 __global__ void splitk_reduce_kernel(SplitkReduceParams p) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int64_t quads = (p.n_out + 3) / 4;
   const int64_t total = static_cast<int64_t>(p.M) * quads;
   const size_t split_stride = static_cast<size_t>(p.M) * p.ldp;
@@ -114,8 +118,7 @@ cudaError_t launch_splitk_reduce(const SplitkReduceParams &p, cudaStream_t strea
   if (total == 0) return cudaSuccess;
   int blocks = static_cast<int>((total + 255) / 256);
   if (blocks > 148 * 8) blocks = 148 * 8;
-  splitk_reduce_kernel<<<blocks, 256, 0, stream>>>(p);
-  return launched();
+  return launch_pdl(splitk_reduce_kernel, dim3(blocks), dim3(256), 0, stream, 1, p);
 }
 
 // Failure-detection probe: waits on an mbarrier that nothing arrives on,

@@ -20,6 +20,44 @@ inline cudaError_t launched() {
   return e;
 }
 
+// Programmatic dependent launch.  Kernels of this library start with
+// pdl_wait() before their first global-memory access (and pdl_trigger()
+// after it), so they may be launched with programmatic stream serialization:
+// a launch then overlaps its launch latency and prologue with the tail of
+// the previous kernel on the stream, and waits for that kernel's completion
+// (and memory) before touching data.  A predecessor that never triggers
+// completes first, as without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch `kern` with programmatic stream serialization (plus an optional
+// cluster shape); counts the launch.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       unsigned cluster_x, Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int n = 1;
+  if (cluster_x > 1) {
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = cluster_x;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    n = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, static_cast<Args &&>(args)...);
+  if (e == cudaSuccess) note_launch();
+  return e;
+}
+
 // Device status bits (mirrors NQ_DEV_* in include/nq8.h).
 constexpr int kDevTimeoutProducer = 0x1;
 constexpr int kDevTimeoutConsumer = 0x2;

@@ -24,6 +24,8 @@ constexpr int kMaxFeat = 512;
 __global__ void conv0_relu_kernel(const float *__restrict__ mel, const int *__restrict__ len0, int T, int F,
                                   int T1, int F1, int C, const float *__restrict__ w, const float *__restrict__ bias,
                                   __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   __shared__ float rows[3][kMaxFeat + 2];  // column j holds frequency j - 1
   const int b = blockIdx.y;
   const int t1 = blockIdx.x;
@@ -80,6 +82,8 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
     const float *__restrict__ mel, const int *__restrict__ len0, const int *__restrict__ len1, int T, int F, int T1,
     int F1, int T2, int F2, int C, const float *__restrict__ w0, const float *__restrict__ b0,
     const float *__restrict__ w2, const float *__restrict__ b2, __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   extern __shared__ __align__(16) unsigned char cd_smem[];
   const int FP = cd_mel_pitch(F);  // padded mel row: column j holds frequency j - 1
   float *melS = reinterpret_cast<float *>(cd_smem);
@@ -201,6 +205,8 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
 __global__ void dwconv2d_s2_kernel(const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len_in, int Tin,
                                    int Fin, int Tout, int Fout, int C, const float *__restrict__ w,
                                    const float *__restrict__ bias, __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int b = blockIdx.z;
   const int to = blockIdx.y;
   const int L = len_in[b];
@@ -227,6 +233,8 @@ __global__ void dwconv2d_s2_kernel(const __nv_bfloat16 *__restrict__ in, const i
 // NCHW, feature index c*F + f; fast_conformer.rs:184-186).
 __global__ void flatten_cf_kernel(const __nv_bfloat16 *__restrict__ in, int rows, int F, int C,
                                   __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int r = blockIdx.x;
   for (int idx = threadIdx.x; idx < F * C; idx += blockDim.x) {
     const int c = idx / F;
@@ -246,6 +254,8 @@ __global__ void ln_row_kernel(int mode, float *__restrict__ x, const void *__res
                               const float *__restrict__ g1, const float *__restrict__ b1,
                               const float *__restrict__ g2, const float *__restrict__ b2,
                               __nv_bfloat16 *__restrict__ h, float eps) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   constexpr int D = 32 * 4 * kVec;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -346,6 +356,8 @@ __global__ void __launch_bounds__(128) dwconv1d_bn_silu_kernel(
     const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len, int Tp, int D, int t_chunk,
     const float *__restrict__ w, const float *__restrict__ bias, const float *__restrict__ bn_scale,
     const float *__restrict__ bn_shift, __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int b = blockIdx.z;
   const int L = min(len[b], Tp);
   const int c = 2 * (blockIdx.x * blockDim.x + threadIdx.x);
@@ -399,6 +411,8 @@ __global__ void __launch_bounds__(128) dwconv1d_bn_silu_kernel(
 // row idx <-> relative position p = idx - (T-1); even columns
 // sign(p) * sin(|p| / 10000^(2i/d)) with sign -1 for p > 0, odd columns cos.
 __global__ void relpos_kernel(int T, int D, __nv_bfloat16 *__restrict__ pos) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int idx = blockIdx.x;
   const int p = idx - (T - 1);
   const float ap = fabsf(static_cast<float>(p));
@@ -469,6 +483,8 @@ __global__ void __launch_bounds__(32 * kAWarps, 1)
     relpos_attention_kernel(const __nv_bfloat16 *__restrict__ qkv, const __nv_bfloat16 *__restrict__ krel,
                             const float *__restrict__ bias_u, const float *__restrict__ bias_v,
                             const int *__restrict__ len, int Tp, int D, float scale, __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t sm[];
   __nv_bfloat16 *sK = reinterpret_cast<__nv_bfloat16 *>(sm);  // [2][kKT][kPitch]
   __nv_bfloat16 *sV = sK + 2 * kKT * kPitch;                   // [2][kKT][kPitch]
@@ -693,6 +709,8 @@ __global__ void __launch_bounds__(32 * kAWarps, 1)
 
 __global__ void copy_masked_kernel(const float *__restrict__ x, const int *__restrict__ len, int Tp, int D,
                                    float *__restrict__ out) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   const int row = blockIdx.x;  // b * Tp + t
   const int b = row / Tp;
   const int t = row - b * Tp;
@@ -704,8 +722,7 @@ __global__ void copy_masked_kernel(const float *__restrict__ x, const int *__res
 
 cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, float *out, cudaStream_t s) {
   if (B * Tp == 0) return cudaSuccess;
-  copy_masked_kernel<<<B * Tp, 256, 0, s>>>(x, len, Tp, D, out);
-  return launched();
+  return launch_pdl(copy_masked_kernel, dim3(B * Tp), dim3(256), 0, s, 1, x, len, Tp, D, out);
 }
 
 size_t attention_smem_bytes() {
@@ -717,8 +734,8 @@ cudaError_t conv0_relu(const float *mel, const int *len0, int B, int T, int F, i
                        const float *bias, __nv_bfloat16 *out, cudaStream_t s) {
   if (F > kMaxFeat || 2 * (F1 - 1) + 2 > F + 1) return cudaErrorInvalidValue;
   dim3 grid(T1, B);
-  conv0_relu_kernel<<<grid, C <= 1024 ? C : 1024, 0, s>>>(mel, len0, T, F, T1, F1, C, w, bias, out);
-  return launched();
+  return launch_pdl(conv0_relu_kernel, grid, dim3(C <= 1024 ? C : 1024), 0, s, 1, mel, len0, T, F, T1, F1, C, w, bias,
+                    out);
 }
 
 bool conv0_dw_s2_supported(int F, int F1, int C) {
@@ -739,8 +756,8 @@ cudaError_t conv0_dw_s2(const float *mel, const int *len0, const int *len1, int 
     attr_set[dev] = true;
   }
   dim3 grid(C / kCdCG, (T2 + kCdTT - 1) / kCdTT, B);
-  conv0_dw_s2_kernel<<<grid, 256, smem, s>>>(mel, len0, len1, T, F, T1, F1, T2, F2, C, w0, b0, w2, b2, out);
-  return launched();
+  return launch_pdl(conv0_dw_s2_kernel, grid, dim3(256), smem, s, 1, mel, len0, len1, T, F, T1, F1, T2, F2, C, w0, b0,
+                    w2, b2, out);
 }
 
 cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int Tin, int Fin, int Tout, int Fout, int C,
@@ -748,13 +765,11 @@ cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int T
   const int per = Fout * C;
   const int threads = 256;
   dim3 grid((per + threads - 1) / threads, Tout, B);
-  dwconv2d_s2_kernel<<<grid, threads, 0, s>>>(in, len_in, Tin, Fin, Tout, Fout, C, w, bias, out);
-  return launched();
+  return launch_pdl(dwconv2d_s2_kernel, grid, dim3(threads), 0, s, 1, in, len_in, Tin, Fin, Tout, Fout, C, w, bias, out);
 }
 
 cudaError_t flatten_cf(const __nv_bfloat16 *in, int rows, int F, int C, __nv_bfloat16 *out, cudaStream_t s) {
-  flatten_cf_kernel<<<rows, 256, 0, s>>>(in, rows, F, C, out);
-  return launched();
+  return launch_pdl(flatten_cf_kernel, dim3(rows), dim3(256), 0, s, 1, in, rows, F, C, out);
 }
 
 cudaError_t ln_rows(int mode, float *x, const void *u, float alpha, int rows, int D, const float *g1, const float *b1,
@@ -763,10 +778,10 @@ cudaError_t ln_rows(int mode, float *x, const void *u, float alpha, int rows, in
   const int threads = 256;
   const int blocks = (rows * 32 + threads - 1) / threads;
   if (D == 1024)
-    ln_row_kernel<8><<<blocks, threads, 0, s>>>(mode, x, u, alpha, rows, g1, b1, g2, b2, h, eps);
-  else
-    ln_row_kernel<4><<<blocks, threads, 0, s>>>(mode, x, u, alpha, rows, g1, b1, g2, b2, h, eps);
-  return launched();
+    return launch_pdl(ln_row_kernel<8>, dim3(blocks), dim3(threads), 0, s, 1, mode, x, u, alpha, rows, g1, b1, g2, b2, h,
+                      eps);
+  return launch_pdl(ln_row_kernel<4>, dim3(blocks), dim3(threads), 0, s, 1, mode, x, u, alpha, rows, g1, b1, g2, b2, h,
+                    eps);
 }
 
 cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int Tp, int D, int K, const float *w,
@@ -778,7 +793,9 @@ cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int
   dim3 grid((D / 2 + kThreads - 1) / kThreads, (Tp + t_chunk - 1) / t_chunk, B);
   switch (K) {
 #define NQ_DW1D_CASE(k) \
-  case k: dwconv1d_bn_silu_kernel<k><<<grid, kThreads, 0, s>>>(in, len, Tp, D, t_chunk, w, bias, bn_scale, bn_shift, out); break;
+  case k:                                                                                                      \
+    return launch_pdl(dwconv1d_bn_silu_kernel<k>, grid, dim3(kThreads), 0, s, 1, in, len, Tp, D, t_chunk, w, bias, \
+                      bn_scale, bn_shift, out);
     NQ_DW1D_CASE(1) NQ_DW1D_CASE(2) NQ_DW1D_CASE(3) NQ_DW1D_CASE(4) NQ_DW1D_CASE(5) NQ_DW1D_CASE(6)
     NQ_DW1D_CASE(7) NQ_DW1D_CASE(8) NQ_DW1D_CASE(9) NQ_DW1D_CASE(10) NQ_DW1D_CASE(11) NQ_DW1D_CASE(12)
     NQ_DW1D_CASE(13) NQ_DW1D_CASE(14) NQ_DW1D_CASE(15) NQ_DW1D_CASE(16) NQ_DW1D_CASE(17) NQ_DW1D_CASE(18)
@@ -788,12 +805,10 @@ cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int
 #undef NQ_DW1D_CASE
     default: return cudaErrorInvalidValue;
   }
-  return launched();
 }
 
 cudaError_t relpos(int T, int D, __nv_bfloat16 *pos, cudaStream_t s) {
-  relpos_kernel<<<2 * T - 1, 256, 0, s>>>(T, D, pos);
-  return launched();
+  return launch_pdl(relpos_kernel, dim3(2 * T - 1), dim3(256), 0, s, 1, T, D, pos);
 }
 
 cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, const float *bias_u,
@@ -811,9 +826,8 @@ cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel
     attr_set[dev] = true;
   }
   dim3 grid((Tp + kQT - 1) / kQT, H, B);
-  relpos_attention_kernel<<<grid, 32 * kAWarps, smem, s>>>(qkv, krel, bias_u, bias_v, len, Tp, D,
-                                                  1.0f / sqrtf(static_cast<float>(kHd)), out);
-  return launched();
+  return launch_pdl(relpos_attention_kernel, grid, dim3(32 * kAWarps), smem, s, 1, qkv, krel, bias_u, bias_v, len, Tp,
+                    D, 1.0f / sqrtf(static_cast<float>(kHd)), out);
 }
 
 }  // namespace enc

@@ -126,6 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before anyone signals across the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();  // barriers and TMEM are set up; now wait for the predecessor's data
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -356,10 +358,8 @@ cudaError_t launch_t(const CUtensorMap &w, const CUtensorMap &a_hi, const CUtens
     }
   }
   const int cap = dev < 64 ? max_pairs[dev] : 1;
-  cfg.gridDim = dim3(2 * (pairs < cap ? pairs : cap));
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, w, a_hi, a_lo, p);
-  if (e == cudaSuccess) note_launch();
-  return e;
+  return launch_pdl(kern, dim3(2 * (pairs < cap ? pairs : cap)), dim3(kThreads), C::kSmemBytes, stream, 2, w, a_hi,
+                    a_lo, p);
 }
 
 }  // namespace

@@ -43,6 +43,8 @@ size_t gemv_smem_bytes(int mrows, bool splitx, int cps) {
 
 template <int MT, bool SPLITX>
 __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_constant__ GemvParams p) {
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
   constexpr int MROWS = 8 * MT;
   extern __shared__ __align__(128) uint8_t smem[];
   const GemvProblem &pr = p.prob[blockIdx.z];
@@ -267,8 +269,7 @@ static cudaError_t launch_gemv_t(const GemvParams &p, int nprob, int grid_x, cud
   }
   if (p.cps > kGemvMaxCps) return cudaErrorInvalidValue;
   dim3 grid(grid_x, p.splits, nprob);
-  kern<<<grid, kGemvThreads, smem, stream>>>(p);
-  return launched();
+  return launch_pdl(kern, grid, dim3(kGemvThreads), smem, stream, 1, p);
 }
 
 cudaError_t launch_gemv(const GemvParams &p, int nprob, int grid_x, bool splitx, cudaStream_t stream) {
