@@ -29,7 +29,8 @@ cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int
                              const float *bias, const float *bn_scale, const float *bn_shift, __nv_bfloat16 *out,
                              cudaStream_t s);
 cudaError_t relpos(int T, int D, __nv_bfloat16 *pos, cudaStream_t s);
-cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, const float *bias_u,
+// krel: relative keys [2 Tp - 1] rows of stride ldr elements (this layer's D columns).
+cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_t ldr, const float *bias_u,
                              const float *bias_v, const int *len, int B, int Tp, int H, int D, __nv_bfloat16 *out,
                              cudaStream_t s);
 // out[b, t, :] = x[b, t, :] for t < len[b], else 0 (f32 rows of D).

@@ -72,6 +72,10 @@ struct nq_encoder {
   // subsampling
   float *c0_w, *c0_b, *dw2_w, *dw2_b, *dw5_w, *dw5_b, *pw3_b, *pw6_b, *lin_b;
   nq_weight *pw3 = nullptr, *pw6 = nullptr, *lin = nullptr;
+  // The layers' relative-key projections stacked along N ([n_layers * d, d]):
+  // they depend only on the positions, so one GEMM per forward serves all
+  // layers (krel holds [2T-1][n_layers * d]).
+  nq_weight *rel_all = nullptr;
   // activation arena
   DevBuf x, h, t, u, u32, qkv, pos, krel, att, g, c, s1, s2a, s2b, s3a, s3b, flat, mel_in, out_buf;
   // Per-forward segment lengths (4 x batch ints) travel through a ring of
@@ -281,11 +285,18 @@ int finalize(nq_encoder *e) {
   // Every encoder GEMM runs the dequantize-once path for M >= 128 tokens:
   // keep each weight's bf16 copy (MatMul::PackedBf16 semantics) instead of
   // re-dequantizing it on every call.  Costs 2 bytes per weight element.
+  {
+    std::vector<const nq_weight *> rels;
+    for (const Layer &L : e->layers) rels.push_back(L.rel);
+    NQ_TRY(nq_weights_fuse(rels.data(), static_cast<int>(rels.size()), 0, &e->rel_all));
+    e->weights.push_back(e->rel_all);
+  }
   NQ_TRY(nq_weight_keep_bf16(e->pw3, 1));
   NQ_TRY(nq_weight_keep_bf16(e->pw6, 1));
   NQ_TRY(nq_weight_keep_bf16(e->lin, 1));
+  NQ_TRY(nq_weight_keep_bf16(e->rel_all, 1));
   for (Layer &L : e->layers)
-    for (nq_weight *w : {L.ff1_w1, L.ff1_w2, L.qkv, L.rel, L.o, L.pw1, L.pw2, L.ff2_w1, L.ff2_w2})
+    for (nq_weight *w : {L.ff1_w1, L.ff1_w2, L.qkv, L.o, L.pw1, L.pw2, L.ff2_w1, L.ff2_w2})
       NQ_TRY(nq_weight_keep_bf16(w, 1));
   e->staged.clear();
   e->ready = true;
@@ -323,7 +334,7 @@ int ensure_arena(nq_encoder *e, const Shapes &s) {
   NQ_TRY(e->u32.ensure(M * D * 4));
   NQ_TRY(e->qkv.ensure(M * 3 * D * 2));
   NQ_TRY(e->pos.ensure(P * D * 2));
-  NQ_TRY(e->krel.ensure(P * D * 2));
+  NQ_TRY(e->krel.ensure(P * D * e->cfg.n_layers * 2));
   NQ_TRY(e->att.ensure(M * D * 2));
   NQ_TRY(e->g.ensure(M * D * 2));
   NQ_TRY(e->c.ensure(M * D * 2));
@@ -399,6 +410,9 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
   NQ_K(nq::enc::ln_rows(nq::enc::kLnScale, x, e->u32.p, alpha, M, D, L_0.ln_ff1_g, L_0.ln_ff1_b, nullptr, nullptr, h,
                         eps, st));
   NQ_K(nq::enc::relpos(Tp, D, e->pos.as<__nv_bfloat16>(), st));
+  // relative keys of every layer: krel[p][li * D + :] = pos[p] . W_rel(li)^T
+  NQ_TRY(nq_linear(e->rel_all, e->pos.p, NQ_BF16, 2 * Tp - 1, D, nullptr, NQ_EPI_NONE, e->krel.p, NQ_BF16,
+                   static_cast<int64_t>(c.n_layers) * D, stv));
 
   for (int li = 0; li < c.n_layers; ++li) {
     const Layer &L = e->layers[li];
@@ -408,8 +422,8 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 0.5f, M, D, L.ln_mha_g, L.ln_mha_b, nullptr, nullptr, h, eps, st));
     // MHSA with relative positions -> norm_conv
     NQ_TRY(nq_linear(L.qkv, h, NQ_BF16, M, D, L.qkv_b, NQ_EPI_NONE, e->qkv.p, NQ_BF16, 3 * D, stv));
-    NQ_TRY(nq_linear(L.rel, e->pos.p, NQ_BF16, 2 * Tp - 1, D, nullptr, NQ_EPI_NONE, e->krel.p, NQ_BF16, D, stv));
-    NQ_K(nq::enc::relpos_attention(e->qkv.as<__nv_bfloat16>(), e->krel.as<__nv_bfloat16>(), L.bias_u, L.bias_v, L3,
+    NQ_K(nq::enc::relpos_attention(e->qkv.as<__nv_bfloat16>(), e->krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
+                                   static_cast<int64_t>(c.n_layers) * D, L.bias_u, L.bias_v, L3,
                                    s.B, Tp, H, D, e->att.as<__nv_bfloat16>(), st));
     NQ_TRY(nq_linear(L.o, e->att.p, NQ_BF16, M, D, L.o_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_conv_g, L.ln_conv_b, nullptr, nullptr, h, eps, st));
@@ -546,10 +560,11 @@ int nq_encoder_launch_count(const nq_encoder *enc, int batch, int t_mel) {
   n += lin(enc->pw3, static_cast<int64_t>(s.B) * s.T2 * s.F2, s.C);
   n += lin(enc->pw6, static_cast<int64_t>(s.B) * s.T3 * s.F3, s.C);
   n += lin(enc->lin, M, static_cast<int64_t>(s.F3) * s.C);
+  n += lin(enc->rel_all, 2 * Tp - 1, s.D);  // every layer's relative keys
   for (const Layer &L : enc->layers) {
     n += 6;  // 4 LN, attention, depthwise conv
     n += lin(L.ff1_w1, M, s.D) + lin(L.ff1_w2, M, s.D * enc->cfg.ff_mult) + lin(L.qkv, M, s.D) +
-         lin(L.rel, 2 * Tp - 1, s.D) + lin(L.o, M, s.D) + lin(L.pw1, M, s.D) + lin(L.pw2, M, s.D) +
+         lin(L.o, M, s.D) + lin(L.pw1, M, s.D) + lin(L.pw2, M, s.D) +
          lin(L.ff2_w1, M, s.D) + lin(L.ff2_w2, M, s.D * enc->cfg.ff_mult);
   }
   return n + 1;  // final masked copy

@@ -430,7 +430,9 @@ __global__ void relpos_kernel(int T, int D, __nv_bfloat16 *__restrict__ pos) {
 // 407-425):
 //   s[i][j] = ((q_i + u_h) . k_j + (q_i + v_h) . r[T-1 + j - i]) / sqrt(hd)
 //   o_i = softmax_j(s[i][:]) . V          (keys j >= len masked)
-// qkv [B*Tp, 3D] bf16 (q | k | v), krel [2Tp-1, D] bf16, out [B*Tp, D] bf16.
+// qkv [B*Tp, 3D] bf16 (q | k | v), krel [2Tp-1, D] bf16 with row stride ldr
+// (the layers' relative projections are computed together, side by side),
+// out [B*Tp, D] bf16.
 // CTA = 8 warps x 16 query rows (128 rows), one head; key tiles of 64.  Each
 // warp keeps its (q + u) and (q + v) A fragments in registers.  K and V tiles
 // are double-buffered with cp.async; the relative rows live in a 256-row ring
@@ -480,7 +482,7 @@ __device__ __forceinline__ void load_rows_async(__nv_bfloat16 *dst, const __nv_b
 }
 
 __global__ void __launch_bounds__(32 * kAWarps, 1)
-    relpos_attention_kernel(const __nv_bfloat16 *__restrict__ qkv, const __nv_bfloat16 *__restrict__ krel,
+    relpos_attention_kernel(const __nv_bfloat16 *__restrict__ qkv, const __nv_bfloat16 *__restrict__ krel, int64_t ldr,
                             const float *__restrict__ bias_u, const float *__restrict__ bias_v,
                             const int *__restrict__ len, int Tp, int D, float scale, __nv_bfloat16 *__restrict__ out) {
   pdl_wait();  // predecessor kernel complete, its writes visible
@@ -513,7 +515,7 @@ __global__ void __launch_bounds__(32 * kAWarps, 1)
   if (ntiles > 0) {
     load_rows_async(sK, base, ld, D + h * kHd, 0, kKT, L, [](int r) { return r; }, tid, nthr);
     load_rows_async(sV, base, ld, 2 * D + h * kHd, 0, kKT, L, [](int r) { return r; }, tid, nthr);
-    load_rows_async(sR, krel, D, h * kHd, P0, 192, 2 * Tp - 1, [&](int r) { return ring(P0 + r); }, tid, nthr);
+    load_rows_async(sR, krel, ldr, h * kHd, P0, 192, 2 * Tp - 1, [&](int r) { return ring(P0 + r); }, tid, nthr);
   }
   cp_async_commit();
 
@@ -564,7 +566,7 @@ __global__ void __launch_bounds__(32 * kAWarps, 1)
       load_rows_async(dk, base, ld, D + h * kHd, jn, kKT, L, [](int r) { return r; }, tid, nthr);
       load_rows_async(dv, base, ld, 2 * D + h * kHd, jn, kKT, L, [](int r) { return r; }, tid, nthr);
       const int pn = P0 + 192 + 64 * t;  // the 64 relative rows tile t + 1 adds
-      load_rows_async(sR, krel, D, h * kHd, pn, 64, 2 * Tp - 1, [&](int r) { return ring(pn + r); }, tid, nthr);
+      load_rows_async(sR, krel, ldr, h * kHd, pn, 64, 2 * Tp - 1, [&](int r) { return ring(pn + r); }, tid, nthr);
     }
     cp_async_commit();
     const __nv_bfloat16 *cK = sK + buf * kKT * kPitch;
@@ -811,7 +813,7 @@ cudaError_t relpos(int T, int D, __nv_bfloat16 *pos, cudaStream_t s) {
   return launch_pdl(relpos_kernel, dim3(2 * T - 1), dim3(256), 0, s, 1, T, D, pos);
 }
 
-cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, const float *bias_u,
+cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_t ldr, const float *bias_u,
                              const float *bias_v, const int *len, int B, int Tp, int H, int D, __nv_bfloat16 *out,
                              cudaStream_t s) {
   if (D / H != kHd) return cudaErrorInvalidValue;
@@ -826,7 +828,7 @@ cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel
     attr_set[dev] = true;
   }
   dim3 grid((Tp + kQT - 1) / kQT, H, B);
-  return launch_pdl(relpos_attention_kernel, grid, dim3(32 * kAWarps), smem, s, 1, qkv, krel, bias_u, bias_v, len, Tp,
+  return launch_pdl(relpos_attention_kernel, grid, dim3(32 * kAWarps), smem, s, 1, qkv, krel, ldr, bias_u, bias_v, len, Tp,
                     D, 1.0f / sqrtf(static_cast<float>(kHd)), out);
 }
 
