@@ -60,22 +60,37 @@ __global__ void conv0_relu_kernel(const float *__restrict__ mel, const int *__re
 // conv0 + the first depthwise conv of the subsampling stack in one pass:
 //   out[b, t2, f2, c] = b2[c] + sum_{dt,df} w2[c][dt,df] * s1[2 t2 - 1 + dt][2 f2 - 1 + df][c]
 //   s1[t1][f1][c]     = bf16(relu(b0[c] + sum_{dt,df} w0[c][dt,df] * mel[2 t1 - 1 + dt][2 f1 - 1 + df]))
-// (the same arithmetic, order and bf16 rounding as conv0_relu followed by
-// dwconv2d_s2; fast_conformer.rs:172-180).  The s1 rows a tile of kCdTT
+// (fast_conformer.rs:172-180; s1 terms with t1 outside [0, len1) or f1 < 0
+// are zero, as in conv0_relu + dwconv2d_s2).  The s1 rows a tile of kCdTT
 // output rows needs (2 kCdTT + 1) are computed into shared memory and never
-// reach HBM.  Block = (64 channels, kCdTT output rows, one segment).
+// reach HBM.  conv0 runs on the tensor cores: a GEMM [positions x 16 taps
+// (9 used)] x [16 x 64 channels] with mma.sync m16n8k16, the mel patches and
+// weights split into bf16 hi + lo parts (x w = xh wh + xh wl + xl wh: f32-level
+// accuracy).  The depthwise conv is plain f32, two channels per thread.
+// Block = (64 channels, kCdTT output rows, one segment), 8 warps.
 constexpr int kCdTT = 4;   // output rows (t2) per block
-constexpr int kCdCG = 64;  // channels per block (a thread owns a channel pair)
+constexpr int kCdCG = 64;  // channels per block
 constexpr int kCdRows1 = 2 * kCdTT + 1;
-constexpr int kCdMelData = 4 * kCdTT + 3;   // mel rows the block's s1 rows read
-constexpr int kCdMelRows = kCdMelData + 2;  // + two zero rows read by the unused tenth s1 row
+constexpr int kCdMelRows = 4 * kCdTT + 3;
 
-// 16-byte rows with room for the 9-wide window of the last f1 quad.
-__host__ __device__ constexpr int cd_mel_pitch(int F) { return ((F + 8 + 3) / 4) * 4; }
+// Padded mel row (16-byte multiple): column j holds frequency j - 1, with
+// room for the last 16-position tile's patches.
+__host__ __device__ constexpr int cd_mel_pitch(int F1) { return ((2 * (((F1 + 15) / 16) * 16) + 6 + 3) / 4) * 4; }
+// s1 rows in shared memory: column 0 is the zero f1 = -1 guard.
+__host__ __device__ constexpr int cd_s1_cols(int F1) { return F1 + 1; }
 
 size_t conv0_dw_smem_bytes(int F, int F1) {
-  return static_cast<size_t>(kCdMelRows) * cd_mel_pitch(F) * sizeof(float) +
-         static_cast<size_t>(kCdRows1) * F1 * kCdCG * sizeof(__nv_bfloat16);
+  (void)F;
+  return static_cast<size_t>(kCdMelRows) * cd_mel_pitch(F1) * sizeof(float) +
+         static_cast<size_t>(kCdRows1) * cd_s1_cols(F1) * kCdCG * sizeof(__nv_bfloat16);
+}
+
+__device__ __forceinline__ uint32_t bf16x2_hi_lo(float a, float b, uint32_t &lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  const float2 hf = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+  lo = *reinterpret_cast<const uint32_t *>(&l);
+  return *reinterpret_cast<const uint32_t *>(&h);
 }
 
 __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
@@ -85,90 +100,98 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
   pdl_wait();  // predecessor kernel complete, its writes visible
   pdl_trigger();
   extern __shared__ __align__(16) unsigned char cd_smem[];
-  const int FP = cd_mel_pitch(F);  // padded mel row: column j holds frequency j - 1
+  const int FP = cd_mel_pitch(F1);
+  const int S1C = cd_s1_cols(F1);
   float *melS = reinterpret_cast<float *>(cd_smem);
   __nv_bfloat16 *s1S = reinterpret_cast<__nv_bfloat16 *>(cd_smem + static_cast<size_t>(kCdMelRows) * FP * sizeof(float));
   const int b = blockIdx.z;
   const int t2s = blockIdx.y * kCdTT;
   const int cg0 = blockIdx.x * kCdCG;
   const int L0 = len0[b], L1 = min(len1[b], T1);
-  // 1. mel rows 4 t2s - 3 .. (zero outside [0, min(T, L0)), the frequency range
-  //    and the last, padding row)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t4 = lane & 3;
+  // 1. mel rows 4 t2s - 3 .. (zero outside [0, min(T, L0)) and the frequency range)
   for (int idx = threadIdx.x; idx < kCdMelRows * FP; idx += blockDim.x) {
     const int r = idx / FP;
     const int j = idx - r * FP;
     const int t = 4 * t2s - 3 + r;
     const int f = j - 1;
     float v = 0.f;
-    if (r < kCdMelData && t >= 0 && t < T && t < L0 && f >= 0 && f < F)
-      v = mel[(static_cast<int64_t>(b) * T + t) * F + f];
+    if (t >= 0 && t < T && t < L0 && f >= 0 && f < F) v = mel[(static_cast<int64_t>(b) * T + t) * F + f];
     melS[idx] = v;
   }
+  // zero guard column of every s1 row
+  for (int idx = threadIdx.x; idx < kCdRows1 * kCdCG; idx += blockDim.x)
+    s1S[(idx / kCdCG) * S1C * kCdCG + (idx % kCdCG)] = __float2bfloat16_rn(0.f);
   __syncthreads();
-  const int cp = threadIdx.x & 31;  // channel pair: channels cg0 + 2 cp, + 1
-  const int grp = threadIdx.x >> 5;
-  const int ngrp = blockDim.x >> 5;
-  const int cc = cg0 + 2 * cp;
-  // 2. s1 rows t1 = 2 t2s - 1 + r1: a task is two rows x four f1 x two
-  //    channels; each mel value is read once (16-byte loads) for both rows.
+  // 2. conv0 on tensor cores.  B fragments (weights, col-major [tap][channel]):
+  //    b0 = taps (2 t4, 2 t4 + 1), b1 = taps (2 t4 + 8, 2 t4 + 9) of channel n = nt * 8 + g.
   {
-    float wa[9], wb[9];
+    uint32_t bh[8][2], bl[8][2];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) {
-      wa[i] = w0[cc * 9 + i];
-      wb[i] = w0[(cc + 1) * 9 + i];
+    for (int nt = 0; nt < 8; ++nt) {
+      const float *wc = w0 + (cg0 + nt * 8 + g) * 9;
+      const int k0 = 2 * t4, k2 = 2 * t4 + 8;
+      bh[nt][0] = bf16x2_hi_lo(wc[k0], wc[k0 + 1], bl[nt][0]);
+      bh[nt][1] = bf16x2_hi_lo(k2 < 9 ? wc[k2] : 0.f, 0.f, bl[nt][1]);  // tap 9 and beyond are padding
     }
-    const float ba = b0[cc], bb = b0[cc + 1];
-    const int quads = (F1 + 3) / 4;
-    const int pairs = (kCdRows1 + 1) / 2;
-    for (int task = grp; task < pairs * quads; task += ngrp) {
-      const int rp = task / quads;
-      const int f1q = (task - rp * quads) * 4;
-      float acc[2][4][2];
+    // this lane's tap offsets in the mel tile (taps 2t4, 2t4+1, 2t4+8, 2t4+9; -1 = padding)
+    int off[4];
 #pragma unroll
-      for (int r = 0; r < 2; ++r)
+    for (int x = 0; x < 4; ++x) {
+      const int k = 2 * t4 + (x & 1) + 8 * (x >> 1);
+      off[x] = k < 9 ? (k / 3) * FP + (k % 3) : -1;
+    }
+    float bias_c[8][2];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[r][q][0] = ba;
-          acc[r][q][1] = bb;
-        }
+    for (int nt = 0; nt < 8; ++nt) {
+      bias_c[nt][0] = b0[cg0 + nt * 8 + 2 * t4];
+      bias_c[nt][1] = b0[cg0 + nt * 8 + 2 * t4 + 1];
+    }
+    const int mtr = (F1 + 15) / 16;  // 16-position tiles per s1 row
+    for (int mt = warp; mt < kCdRows1 * mtr; mt += 8) {
+      const int r1 = mt / mtr;
+      const int f10 = (mt - r1 * mtr) * 16;
+      const int t1 = 2 * t2s - 1 + r1;
+      const bool row_live = t1 >= 0 && t1 < L1;  // other rows are zero for the depthwise conv
+      // A fragments: rows g and g + 8 = positions f10 + g, f10 + g + 8 of row r1
+      const float *base = melS + (2 * r1) * FP + 2 * (f10 + g);
+      float xa[4], xb[4];
 #pragma unroll
-      for (int mr = 0; mr < 5; ++mr) {
-        const float *row = melS + (4 * rp + mr) * FP + 2 * f1q;
-        float m[12];
-        const float4 m0 = *reinterpret_cast<const float4 *>(row);
-        const float4 m1 = *reinterpret_cast<const float4 *>(row + 4);
-        m[0] = m0.x; m[1] = m0.y; m[2] = m0.z; m[3] = m0.w;
-        m[4] = m1.x; m[5] = m1.y; m[6] = m1.z; m[7] = m1.w;
-        m[8] = row[8];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          const int dt = mr - 2 * r;
-          if (dt < 0 || dt > 2) continue;
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-#pragma unroll
-            for (int df = 0; df < 3; ++df) {
-              acc[r][q][0] += wa[dt * 3 + df] * m[2 * q + df];
-              acc[r][q][1] += wb[dt * 3 + df] * m[2 * q + df];
-            }
-        }
+      for (int x = 0; x < 4; ++x) {
+        xa[x] = off[x] >= 0 ? base[off[x]] : 0.f;
+        xb[x] = off[x] >= 0 ? base[off[x] + 16] : 0.f;
       }
+      uint32_t ah[4], al[4];
+      ah[0] = bf16x2_hi_lo(xa[0], xa[1], al[0]);
+      ah[1] = bf16x2_hi_lo(xb[0], xb[1], al[1]);
+      ah[2] = bf16x2_hi_lo(xa[2], xa[3], al[2]);
+      ah[3] = bf16x2_hi_lo(xb[2], xb[3], al[3]);
 #pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        const int r1 = 2 * rp + r;
-        if (r1 >= kCdRows1) continue;
+      for (int nt = 0; nt < 8; ++nt) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        mma_16816_bf16(acc, ah, bh[nt][0], bh[nt][1]);
+        mma_16816_bf16(acc, ah, bl[nt][0], bl[nt][1]);
+        mma_16816_bf16(acc, al, bh[nt][0], bh[nt][1]);
+        const int ch = nt * 8 + 2 * t4;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          if (f1q + q < F1)
-            *reinterpret_cast<__nv_bfloat162 *>(s1S + (r1 * F1 + f1q + q) * kCdCG + 2 * cp) =
-                __floats2bfloat162_rn(fmaxf(acc[r][q][0], 0.f), fmaxf(acc[r][q][1], 0.f));
+        for (int h = 0; h < 2; ++h) {
+          const int f1 = f10 + g + 8 * h;
+          if (f1 >= F1) continue;
+          const float v0 = row_live ? fmaxf(acc[2 * h] + bias_c[nt][0], 0.f) : 0.f;
+          const float v1 = row_live ? fmaxf(acc[2 * h + 1] + bias_c[nt][1], 0.f) : 0.f;
+          *reinterpret_cast<__nv_bfloat162 *>(s1S + (r1 * S1C + f1 + 1) * kCdCG + ch) = __floats2bfloat162_rn(v0, v1);
+        }
       }
     }
   }
   __syncthreads();
-  // 3. depthwise 3x3 stride 2 over the staged rows, two channels per thread
+  // 3. depthwise 3x3 stride 2 over the staged rows (zero rows / guard column
+  //    stand in for the taps outside the segment), two channels per thread
   {
+    const int cp = threadIdx.x & 31;
+    const int grp = threadIdx.x >> 5;
+    const int cc = cg0 + 2 * cp;
     float wa[9], wb[9];
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
@@ -176,7 +199,7 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
       wb[i] = w2[(cc + 1) * 9 + i];
     }
     const float ba = b2[cc], bb = b2[cc + 1];
-    for (int task = grp; task < kCdTT * F2; task += ngrp) {
+    for (int task = grp; task < kCdTT * F2; task += 8) {
       const int r2 = task / F2;
       const int f2 = task - r2 * F2;
       const int t2 = t2s + r2;
@@ -184,14 +207,11 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
       float a0 = ba, a1 = bb;
 #pragma unroll
       for (int dt = 0; dt < 3; ++dt) {
-        const int t1 = 2 * t2 - 1 + dt;
-        if (t1 < 0 || t1 >= L1) continue;
+        const __nv_bfloat16 *row = s1S + ((2 * r2 + dt) * S1C + 2 * f2) * kCdCG + 2 * cp;  // column f1 = 2 f2 - 1
 #pragma unroll
         for (int df = 0; df < 3; ++df) {
-          const int f1 = 2 * f2 - 1 + df;
-          if (f1 < 0 || f1 >= F1) continue;
-          const float2 v =
-              __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(s1S + ((2 * r2 + dt) * F1 + f1) * kCdCG + 2 * cp));
+          if (2 * f2 - 1 + df >= F1) continue;
+          const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(row + df * kCdCG));
           a0 += wa[dt * 3 + df] * v.x;
           a1 += wb[dt * 3 + df] * v.y;
         }
