@@ -239,6 +239,19 @@ int nq_encoder_forward(nq_encoder *enc, const float *mel, const int32_t *lengths
 int nq_encoder_forward_host(nq_encoder *enc, const float *mel_host, const int32_t *lengths, int batch,
                             int t_mel, float *out_host, int32_t *out_lengths, void *stream);
 
+/* Queued form of nq_encoder_forward_host for a stream of batches (configs[4]:
+ * many VAD segments); no counterpart in the reference, whose run_encoder is
+ * synchronous.  Enqueues the copy of mel_host to the device, the forward on
+ * `stream` and the copy of the output to out_host, then returns: the copies
+ * run on the encoder's own copy streams and overlap the forwards of the
+ * neighbouring calls (two device staging slots, event-ordered).  mel_host and
+ * out_host must be pinned host memory and stay untouched until
+ * nq_encoder_wait returns; out_lengths is filled before this returns. */
+int nq_encoder_forward_host_async(nq_encoder *enc, const float *mel_host, const int32_t *lengths, int batch,
+                                  int t_mel, float *out_host, int32_t *out_lengths, void *stream);
+/* Block until every queued nq_encoder_forward_host_async output is in host memory. */
+int nq_encoder_wait(nq_encoder *enc);
+
 /* Number of kernels nq_encoder_forward launches for (batch, t_mel). */
 int nq_encoder_launch_count(const nq_encoder *enc, int batch, int t_mel);
 

@@ -87,7 +87,25 @@ struct nq_encoder {
   int lens_cap = 0;
   int lens_next = 0;
 
+  // nq_encoder_forward_host_async: two device staging slots (mel in, output
+  // out) used in turn, copies on their own streams ordered by events.
+  struct HostSlot {
+    DevBuf in, out;
+    cudaEvent_t h2d_done = nullptr, comp_done = nullptr, d2h_done = nullptr;
+    bool used = false;
+  };
+  HostSlot host_slots[2];
+  cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;
+  int host_next = 0;
+
   ~nq_encoder() {
+    if (h2d_stream) cudaStreamSynchronize(h2d_stream);
+    if (d2h_stream) cudaStreamSynchronize(d2h_stream);
+    for (auto &hs : host_slots)
+      for (cudaEvent_t ev : {hs.h2d_done, hs.comp_done, hs.d2h_done})
+        if (ev) cudaEventDestroy(ev);
+    if (h2d_stream) cudaStreamDestroy(h2d_stream);
+    if (d2h_stream) cudaStreamDestroy(d2h_stream);
     for (auto *w : weights) nq_weight_free(w);
     for (auto *p : dev_allocs) cudaFree(p);
     for (int i = 0; i < kLenSlots; ++i) {
@@ -542,6 +560,52 @@ int nq_encoder_forward_host(nq_encoder *enc, const float *mel_host, const int32_
   NQ_TRY(forward(enc, enc->mel_in.as<float>(), lengths, batch, t_mel, enc->out_buf.as<float>(), out_lengths, st));
   NQ_CUDA(cudaMemcpyAsync(out_host, enc->out_buf.p, out_bytes, cudaMemcpyDeviceToHost, st));
   NQ_CUDA(cudaStreamSynchronize(st));
+  return NQ_OK;
+}
+
+int nq_encoder_forward_host_async(nq_encoder *enc, const float *mel_host, const int32_t *lengths, int batch, int t_mel,
+                                  float *out_host, int32_t *out_lengths, void *stream) {
+  if (!enc || !mel_host || !out_host) return api_fail(NQ_ERR_ARG, "null argument");
+  if (!enc->ready) return api_fail(NQ_ERR_ARG, "encoder not finalized");
+  if (batch < 1 || t_mel < 1) return api_fail(NQ_ERR_SHAPE, "batch and t_mel must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (!enc->h2d_stream) {
+    NQ_CUDA(cudaStreamCreateWithFlags(&enc->h2d_stream, cudaStreamNonBlocking));
+    NQ_CUDA(cudaStreamCreateWithFlags(&enc->d2h_stream, cudaStreamNonBlocking));
+    for (auto &hs : enc->host_slots)
+      for (cudaEvent_t *ev : {&hs.h2d_done, &hs.comp_done, &hs.d2h_done})
+        NQ_CUDA(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+  }
+  nq_encoder::HostSlot &hs = enc->host_slots[enc->host_next];
+  enc->host_next ^= 1;
+  const size_t in_bytes = static_cast<size_t>(batch) * t_mel * enc->cfg.feat_in * sizeof(float);
+  const size_t out_bytes = static_cast<size_t>(batch) * nq_encoder_out_frames(t_mel) * enc->cfg.d_model * sizeof(float);
+  if (hs.in.bytes < in_bytes || hs.out.bytes < out_bytes) {
+    // growing a slot frees its buffers: let its previous use finish first
+    if (hs.used) NQ_CUDA(cudaEventSynchronize(hs.d2h_done));
+    NQ_TRY(hs.in.ensure(in_bytes));
+    NQ_TRY(hs.out.ensure(out_bytes));
+  }
+  // The slot's previous forward must have consumed its input, and its
+  // previous output must have left for the host, before they are overwritten.
+  if (hs.used) NQ_CUDA(cudaStreamWaitEvent(enc->h2d_stream, hs.comp_done, 0));
+  NQ_CUDA(cudaMemcpyAsync(hs.in.p, mel_host, in_bytes, cudaMemcpyHostToDevice, enc->h2d_stream));
+  NQ_CUDA(cudaEventRecord(hs.h2d_done, enc->h2d_stream));
+  NQ_CUDA(cudaStreamWaitEvent(st, hs.h2d_done, 0));
+  if (hs.used) NQ_CUDA(cudaStreamWaitEvent(st, hs.d2h_done, 0));
+  NQ_TRY(forward(enc, hs.in.as<float>(), lengths, batch, t_mel, hs.out.as<float>(), out_lengths, st));
+  NQ_CUDA(cudaEventRecord(hs.comp_done, st));
+  NQ_CUDA(cudaStreamWaitEvent(enc->d2h_stream, hs.comp_done, 0));
+  NQ_CUDA(cudaMemcpyAsync(out_host, hs.out.p, out_bytes, cudaMemcpyDeviceToHost, enc->d2h_stream));
+  NQ_CUDA(cudaEventRecord(hs.d2h_done, enc->d2h_stream));
+  hs.used = true;
+  return NQ_OK;
+}
+
+int nq_encoder_wait(nq_encoder *enc) {
+  if (!enc) return api_fail(NQ_ERR_ARG, "null encoder");
+  if (enc->h2d_stream) NQ_CUDA(cudaStreamSynchronize(enc->h2d_stream));
+  if (enc->d2h_stream) NQ_CUDA(cudaStreamSynchronize(enc->d2h_stream));
   return NQ_OK;
 }
 

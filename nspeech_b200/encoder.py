@@ -95,6 +95,20 @@ class ParakeetEncoder:
                                                    _P(stream)))
         return out, list(olens)
 
+    def forward_host_async(self, mel: np.ndarray, lengths: Optional[Sequence[int]], out: np.ndarray,
+                           stream: int = 0) -> list:
+        """Queue a forward with pinned host buffers (mel in, out back); see wait()."""
+        B, T, _ = mel.shape
+        lens = (ctypes.c_int32 * B)(*(lengths if lengths is not None else [T] * B))
+        olens = (ctypes.c_int32 * B)()
+        _l.check(_l.load().nq_encoder_forward_host_async(self._h, mel.ctypes.data, lens, B, T, out.ctypes.data,
+                                                         olens, _P(stream)))
+        return list(olens)
+
+    def wait(self) -> None:
+        """Block until every queued forward_host_async output is in host memory."""
+        _l.check(_l.load().nq_encoder_wait(self._h))
+
     def launch_count(self, batch: int, t_mel: int) -> int:
         return int(_l.load().nq_encoder_launch_count(self._h, batch, t_mel))
 

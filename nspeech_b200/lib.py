@@ -94,6 +94,9 @@ SIGNATURES = {
     "nq_encoder_forward": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int32), _I, _I, _P, ctypes.POINTER(ctypes.c_int32), _P]),
     "nq_encoder_forward_host": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int32), _I, _I, _P,
                                      ctypes.POINTER(ctypes.c_int32), _P]),
+    "nq_encoder_forward_host_async": (_I, [_P, _P, ctypes.POINTER(ctypes.c_int32), _I, _I, _P,
+                                           ctypes.POINTER(ctypes.c_int32), _P]),
+    "nq_encoder_wait": (_I, [_P]),
     "nq_encoder_launch_count": (_I, [_P, _I, _I]),
     "nq_encoder_free": (None, [_P]),
     "nq_profile_enable": (_I, [_I]),

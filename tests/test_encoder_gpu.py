@@ -181,3 +181,23 @@ def test_launch_count_matches_counter(nq, oracle, path):
             assert nq.launch_counter() - n0 == enc.launch_count(batch, t_mel), (path, batch, t_mel)
     finally:
         nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_AUTO))
+
+
+def test_forward_host_async_queue_matches_sync(nq, oracle):
+    """Queued host-buffer forwards (copies overlapping neighbouring forwards) give the synchronous results."""
+    from nspeech_b200 import synthetic as S
+    from nspeech_b200.encoder import out_frames
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=1, sub_channels=64)
+    enc = _gpu_encoder(spec, _model(oracle, spec, seed=9))
+    jobs = []
+    for i, (b, t) in enumerate([(2, 300), (3, 512), (1, 180), (4, 700), (2, 300)]):
+        mel = torch.from_numpy(oracle.normal(20 + i, (b, t, 128))).pin_memory()
+        lens = [t - 7 * j for j in range(b)]
+        out = torch.empty((b, out_frames(t), 512), dtype=torch.float32).pin_memory()
+        jobs.append((mel, lens, out))
+    got_lens = [enc.forward_host_async(m.numpy(), l, o.numpy()) for m, l, o in jobs]
+    enc.wait()
+    for (mel, lens, out), gl in zip(jobs, got_lens):
+        ref, rl = enc.forward_host(mel.numpy(), lens)
+        assert gl == rl
+        np.testing.assert_array_equal(out.numpy(), ref)
