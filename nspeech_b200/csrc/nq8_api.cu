@@ -252,17 +252,25 @@ struct ProfScope {
 };
 
 // ------------------------------------------------------------------ GEMV
+// Split-K factor of the GEMV: about one wave of CTAs, at most 16 splits (the
+// last CTA of a tile sums them) unless K needs more (at most 8 k chunks per
+// split: the activation slice staged in shared memory).
+void gemv_splits(int sm_count, int tiles, int kc, int *splits_out, int *cps_out) {
+  int splits = std::max(1, std::min({kc, 16, (sm_count + tiles - 1) / tiles}));
+  int cps = std::min((kc + splits - 1) / splits, 8);
+  splits = (kc + cps - 1) / cps;
+  *splits_out = splits;
+  *cps_out = cps;
+}
+
 int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
              int epilogue, int y_dtype, cudaStream_t stream) {
   const nq_weight *w0 = args[0].w;
   int max_tiles = 0;
   for (int i = 0; i < nprob; ++i) max_tiles = std::max(max_tiles, args[i].w->n_tiles);
   const int kc = w0->kc;
-  const int target = 2 * ctx->sm_count;
-  int splits = std::max(1, std::min(kc, (target + max_tiles * nprob - 1) / (max_tiles * nprob)));
-  int cps = (kc + splits - 1) / splits;
-  cps = std::min(cps, 8);  // bounds the activation slice staged in shared memory
-  splits = (kc + cps - 1) / cps;
+  int splits, cps;
+  gemv_splits(ctx->sm_count, max_tiles * nprob, kc, &splits, &cps);
   const int mrows = m <= 8 ? 8 : 16;
 
   size_t part_bytes = 0;
@@ -772,9 +780,8 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
   // Same split-K choice as nq_linear's GEMV, so both give the same sums.
   const int kc = w->kc;
-  int splits = std::max(1, std::min(kc, (2 * ctx->sm_count + w->n_tiles - 1) / w->n_tiles));
-  int cps = std::min((kc + splits - 1) / splits, 8);
-  splits = (kc + cps - 1) / cps;
+  int splits, cps;
+  gemv_splits(ctx->sm_count, w->n_tiles, kc, &splits, &cps);
   const size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * w->n_tiles * 16 * nq::kPackRows * sizeof(float) : 0;
   if (part_bytes > kNoAllocPartialBytes)
     return fail(NQ_ERR_SHAPE,

@@ -248,6 +248,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             ok = false;
             break;
           }
+          // The converters read weight stages with ordinary shared loads: order
+          // those reads before the async-proxy copies that refill the stage.
+          fence_proxy_async_smem();
           if (tile < p.n_tiles) {
             mbar_arrive_expect_tx(full_w(s), kTileBytes);
             bulk_load(smem_u32(stage_w(s)), wsrc + static_cast<size_t>(i) * kTileBytes, kTileBytes, full_w(s),

@@ -101,6 +101,9 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_cons
             break;
           }
         }
+        // The consumers read the stage with ordinary shared loads; order those
+        // reads before the async-proxy bulk write that refills it.
+        fence_proxy_async_smem();
         mbar_arrive_expect_tx(full_bar(s), kTileBytes);
         bulk_load(smem_u32(ring + s * kTileBytes), wbase + static_cast<size_t>(i) * kTileBytes,
                   kTileBytes, full_bar(s), pol);
@@ -201,9 +204,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_cons
 
   const int nth = blockDim.x;
   if (p.splits > 1) {
-    float *part = pr.partials + (static_cast<size_t>(split) * pr.n_tiles + tile) * (MROWS * kPackRows);
-    for (int idx = threadIdx.x; idx < MROWS * kPackRows; idx += nth)
-      part[idx] = acc_s[(idx >> 7) * kAccPitch + (idx & 127)];
+    // Partials hold the M live rows only: [split][tile][M][128] f32.
+    const int elems = p.M * kPackRows;
+    const size_t sstride = static_cast<size_t>(pr.n_tiles) * elems;
+    float *part = pr.partials + split * sstride + static_cast<size_t>(tile) * elems;
+    for (int idx = threadIdx.x; idx < elems; idx += nth) part[idx] = acc_s[(idx >> 7) * kAccPitch + (idx & 127)];
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -213,10 +218,19 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_cons
     __syncthreads();
     if (!flags[1]) return;  // uniform: not the last split of this tile
     __threadfence();
-    for (int idx = threadIdx.x; idx < MROWS * kPackRows; idx += nth) {
+    // Sum the splits in index order; eight loads are issued before their adds.
+    for (int idx = threadIdx.x; idx < elems; idx += nth) {
+      const float *src = pr.partials + static_cast<size_t>(tile) * elems + idx;
       float sum = 0.f;
-      for (int sp = 0; sp < p.splits; ++sp)
-        sum += __ldcg(pr.partials + (static_cast<size_t>(sp) * pr.n_tiles + tile) * (MROWS * kPackRows) + idx);
+      int sp = 0;
+      for (; sp + 8 <= p.splits; sp += 8) {
+        float v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (sp + u) * sstride);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) sum += v[u];
+      }
+      for (; sp < p.splits; ++sp) sum += __ldcg(src + sp * sstride);
       acc_s[(idx >> 7) * kAccPitch + (idx & 127)] = sum;
     }
     __syncthreads();

@@ -116,8 +116,11 @@ def test_epilogues(nq, oracle, m, epi):
     assert _check(oracle, got, _ref(oracle, x, q, n, bias, epi), f"epi={epi} m={m}") <= EXPECT_TOL
 
 
+# (1, 4096, 4096), (2, 32768, 512), (16, 8192, 1024): GEMV CTAs that stream more
+# k chunks than their shared-memory ring holds, so every stage is refilled.
 @pytest.mark.parametrize("m,n,k", [(1, 17, 32), (3, 130, 96), (17, 200, 160), (33, 129, 64), (129, 96, 32),
-                                   (16, 640, 640), (300, 1920, 768), (2, 32768, 640)])
+                                   (16, 640, 640), (300, 1920, 768), (2, 32768, 640), (1, 4096, 4096),
+                                   (2, 32768, 512), (16, 8192, 1024), (1, 640, 2560), (9, 1024, 4096)])
 def test_ragged_shapes(nq, oracle, m, n, k):
     from nspeech_b200.fast_matmul import QWeight
     q = oracle.quantize_q8_0(oracle.normal(m + n + k, (n, k), 0.0, 0.02))
