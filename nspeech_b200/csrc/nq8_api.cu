@@ -252,26 +252,34 @@ struct ProfScope {
 };
 
 // ------------------------------------------------------------------ GEMV
-// Split-K factor of the GEMV: about one wave of CTAs, at most 16 splits (the
-// last CTA of a tile sums them) unless K needs more (at most 8 k chunks per
-// split: the activation slice staged in shared memory).
-void gemv_splits(int sm_count, int tiles, int kc, int *splits_out, int *cps_out) {
-  int splits = std::max(1, std::min({kc, 16, (sm_count + tiles - 1) / tiles}));
-  int cps = std::min((kc + splits - 1) / splits, 8);
+// GEMV work plan: about two CTAs per SM, each owning one k split and a
+// strided set of weight tiles (persistent), at least four k chunks per split
+// when K allows, and at most as many chunks per split as the staged
+// activation slice holds.
+struct GemvPlan {
+  int splits, cps, tgroups;
+};
+GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int64_t m, bool splitx) {
+  GemvPlan g;
+  const int target = 2 * sm_count;
+  const int cps_max = nq::gemv_max_cps(static_cast<int>(m), splitx);
+  int splits = std::max(1, std::min((target + total_tiles - 1) / total_tiles, std::max(1, kc / 4)));
+  int cps = std::min((kc + splits - 1) / splits, cps_max);
   splits = (kc + cps - 1) / cps;
-  *splits_out = splits;
-  *cps_out = cps;
+  g.splits = splits;
+  g.cps = cps;
+  g.tgroups = std::max(1, std::min(total_tiles, target / splits));
+  return g;
 }
 
 int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
              int epilogue, int y_dtype, cudaStream_t stream) {
   const nq_weight *w0 = args[0].w;
-  int max_tiles = 0;
-  for (int i = 0; i < nprob; ++i) max_tiles = std::max(max_tiles, args[i].w->n_tiles);
+  int total_tiles = 0;
+  for (int i = 0; i < nprob; ++i) total_tiles += args[i].w->n_tiles;
   const int kc = w0->kc;
-  int splits, cps;
-  gemv_splits(ctx->sm_count, max_tiles * nprob, kc, &splits, &cps);
-  const int mrows = m <= 8 ? 8 : 16;
+  const GemvPlan plan = gemv_plan(ctx->sm_count, total_tiles, kc, m, x_dtype == NQ_F32);
+  const int splits = plan.splits, cps = plan.cps;
 
   size_t part_bytes = 0;
   if (splits > 1)
@@ -313,9 +321,10 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
   p.y_dtype = y_dtype;
   p.splits = splits;
   p.cps = cps;
+  p.nprob = nprob;
+  p.tgroups = plan.tgroups;
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
-  (void)mrows;
   double flops = 0, bytes = 0;
   for (int i = 0; i < nprob; ++i) {
     const nq_weight *w = args[i].w;
@@ -324,7 +333,7 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
              m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (args[i].bias ? 4.0 * w->n : 0.0);
   }
   ProfScope ps(NQ_KCLASS_GEMV, stream, flops, bytes);
-  cudaError_t e = nq::launch_gemv(p, nprob, max_tiles, x_dtype == NQ_F32, stream);
+  cudaError_t e = nq::launch_gemv(p, x_dtype == NQ_F32, stream);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return NQ_OK;
 }
@@ -780,8 +789,8 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
   // Same split-K choice as nq_linear's GEMV, so both give the same sums.
   const int kc = w->kc;
-  int splits, cps;
-  gemv_splits(ctx->sm_count, w->n_tiles, kc, &splits, &cps);
+  const GemvPlan plan = gemv_plan(ctx->sm_count, w->n_tiles, kc, m, x_dtype == NQ_F32);
+  const int splits = plan.splits, cps = plan.cps;
   const size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * w->n_tiles * 16 * nq::kPackRows * sizeof(float) : 0;
   if (part_bytes > kNoAllocPartialBytes)
     return fail(NQ_ERR_SHAPE,
@@ -826,9 +835,11 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   p.y_dtype = y_dtype;
   p.splits = splits;
   p.cps = cps;
+  p.nprob = 1;
+  p.tgroups = plan.tgroups;
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
-  cudaError_t e = nq::launch_gemv(p, 1, w->n_tiles, x_dtype == NQ_F32, stream_);
+  cudaError_t e = nq::launch_gemv(p, x_dtype == NQ_F32, stream_);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return NQ_OK;
 }

@@ -289,6 +289,39 @@ __device__ __forceinline__ void dequant4_bf16(uint32_t q4, float d, uint32_t &p0
   p23 = pack_bf16x2(f[2] * d, f[3] * d);
 }
 
+// Packed f32x2 helpers and an eight-element Q8_0 dequantization with the
+// same exact result as dequant4_bf16, in fewer instructions.
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_of(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return pack_bf16x2(a, b);
+}
+// Eight int8 (two words) of one Q8_0 block -> four bf16x2 of bf16(f32(d) * q),
+// exact like dequant4_bf16, with packed f32x2 subtract / multiply.
+__device__ __forceinline__ void dequant8_bf16(uint32_t w0, uint32_t w1, uint64_t dd, uint32_t *out) {
+  const uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u;
+  const uint64_t bias = f2(8388736.0f, 8388736.0f);
+  uint64_t v[4];
+  v[0] = f2(__uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7440)), __uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7441)));
+  v[1] = f2(__uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7442)), __uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7443)));
+  v[2] = f2(__uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7440)), __uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7441)));
+  v[3] = f2(__uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7442)), __uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7443)));
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint64_t q;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(q) : "l"(v[i]), "l"(bias));
+    uint64_t s;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(s) : "l"(q), "l"(dd));
+    out[i] = bf16x2_of(s);
+  }
+}
+
+
 // Legacy warp-level MMA (used by the skinny GEMV where the tensor pipe is not
 // the bound): D(16x8) += A(16x16) . B(16x8), bf16 in, f32 accumulate.
 __device__ __forceinline__ void mma_16816_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,

@@ -75,36 +75,6 @@ struct GemmCfg {
 };
 
 // ---------------------------------------------------------------- dequant
-__device__ __forceinline__ uint64_t f2(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ uint32_t bf16x2_of(uint64_t v) {
-  float a, b;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
-  return pack_bf16x2(a, b);
-}
-// Eight int8 (two words) of one Q8_0 block -> four bf16x2 of bf16(f32(d) * q),
-// exact like dequant4_bf16, with packed f32x2 subtract / multiply.
-__device__ __forceinline__ void dequant8_bf16(uint32_t w0, uint32_t w1, uint64_t dd, uint32_t *out) {
-  const uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u;
-  const uint64_t bias = f2(8388736.0f, 8388736.0f);
-  uint64_t v[4];
-  v[0] = f2(__uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7440)), __uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7441)));
-  v[1] = f2(__uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7442)), __uint_as_float(__byte_perm(u0, 0x4B000000u, 0x7443)));
-  v[2] = f2(__uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7440)), __uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7441)));
-  v[3] = f2(__uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7442)), __uint_as_float(__byte_perm(u1, 0x4B000000u, 0x7443)));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint64_t q;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(q) : "l"(v[i]), "l"(bias));
-    uint64_t s;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(s) : "l"(q), "l"(dd));
-    out[i] = bf16x2_of(s);
-  }
-}
-
 struct WChunk64 {
   uint4 q[4];           // the 64 int8 of one row in a 64-wide k step
   unsigned short d[2];  // the row's two Q8_0 block scales (f16)

@@ -22,7 +22,7 @@ struct GemvProblem {
   const float *bias;
   void *y;
   int64_t ldy;
-  float *partials;  // [splits][n_tiles][16][128] f32 (split-K only)
+  float *partials;  // [splits][n_tiles][M][128] f32 (split-K only)
   int *counters;    // [n_tiles], zero between calls
 };
 
@@ -36,12 +36,17 @@ struct GemvParams {
   int epi;
   int y_dtype;
   int splits;
-  int cps;  // k chunks per split
+  int cps;       // k chunks per split
+  int nprob;     // problems (weights) sharing x
+  int tgroups;   // CTAs per split; CTA c takes split c % splits and every tgroups-th tile
   DevCtl ctl;
 };
 
+// Most k chunks per split whose activation slice fits the staging buffer.
+int gemv_max_cps(int m, bool splitx);
 size_t gemv_smem_bytes(int mrows, bool splitx, int cps);
-cudaError_t launch_gemv(const GemvParams &p, int nprob, int grid_x, bool splitx, cudaStream_t stream);
+// Persistent launch of splits * tgroups CTAs.
+cudaError_t launch_gemv(const GemvParams &p, bool splitx, cudaStream_t stream);
 
 // K1: fused Q8_0 GEMM (dequantizes in the kernel; best below a few thousand
 // tokens, where the weights dominate the traffic).
