@@ -15,7 +15,7 @@
  *   - Activations x, outputs y and bias live in caller-owned device memory
  *     (the `enc_*` convention of src/triton_kernels.rs:862-1397).
  *   - The library owns a per-(device, stream) workspace (activation split
- *     planes, split-K partial sums, arrival counters).  It grows on demand,
+ *     planes, partial sums, work counters).  It grows on demand,
  *     so the first call of a given size on a stream may cudaMalloc; make that
  *     call once before capturing the stream into a CUDA graph.
  *   - Calls on different streams may run concurrently; calls on one stream
@@ -131,7 +131,8 @@ int nq_weight_keep_bf16(nq_weight *w, int keep);
  *   bias: device f32 [N] or NULL.  epilogue: NQ_EPI_*.
  *   y: device, y_dtype NQ_F32 | NQ_BF16, row stride ldy (>= N_out; N_out = N/2
  *      for GLU epilogues).  M = 0 is a no-op.
- * M <= 16 runs the split-K GEMV kernel, larger M the tcgen05 GEMM.
+ * M <= 16 runs the GEMV kernel (dynamically scheduled units of k, fixed-order
+ * sum of their partials), larger M the tcgen05 GEMM.
  * Replaces MatMul::forward / FbgemmBf16Op::cpu_fwd (src/fast_matmul.rs:
  * 138-167, 210-226) and QLinear::forward (src/parakeet/quantized_layers.rs:
  * 31-38). */
@@ -160,10 +161,11 @@ int nq_gemv_glu_splitk(const nq_weight *w, const void *x, int x_dtype, const flo
 int nq_gemv_qkv_splitk(const nq_weight *wq, const nq_weight *wk, const nq_weight *wv,
                        const void *x, int x_dtype, void *q, void *k, void *v, int out_dtype,
                        void *stream);
-/* No counterpart in the reference.  The split-K GEMV of nq_linear (M <= 16
- * rows, same arguments and result) without any allocation: its split-K
- * partial sums and arrival counters live in a static device array of this
- * library (4 MiB of partials plus 4096 counters per device) instead of the
+/* No counterpart in the reference.  The GEMV of nq_linear (M <= 16 rows,
+ * same arguments and result) without any allocation: its partial sums,
+ * staged activations and work counter live in a static device array of this
+ * library (4 MiB of partials, 2 MiB of bf16 activation planes and the
+ * counter, per device) instead of the
  * per-stream workspace nq_linear grows with cudaMalloc.  For callers that
  * cannot allocate at call time: a streaming decoder step on a latency budget
  * (cudaMalloc / cudaFree can synchronize the device and stall every stream),
@@ -172,10 +174,11 @@ int nq_gemv_qkv_splitk(const nq_weight *wq, const nq_weight *wk, const nq_weight
  * a device looks up the array's address (cudaGetSymbolAddress, which may load
  * the module), so make that first call before any stream capture.  Every
  * call on a device shares the one array and leaves its contents behind (the
- * counters are cleared by each call): calls that overlap on the GPU -- on
+ * counter is re-armed by each call): calls that overlap on the GPU -- on
  * two streams, or from two threads -- race and give wrong results; serialize
- * them.  A weight whose split-K partials exceed the array (large K with
- * large N) is rejected with NQ_ERR_SHAPE before any launch; M > 16 too. */
+ * them.  A call whose partial sums or staged activations (f32 or
+ * unaligned x, or K not a multiple of 64) exceed the array is rejected with
+ * NQ_ERR_SHAPE before any launch; M > 16 too. */
 int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx,
                     const float *bias, int epilogue, void *y, int y_dtype, int64_t ldy,
                     void *stream);
@@ -263,7 +266,7 @@ void nq_encoder_free(nq_encoder *enc);
  * TRITON_ENCODER_PROFILE / forward_profile, src/moonshine/gpu_encoder.rs:
  * 367-369,508).  Kernel classes: */
 #define NQ_KCLASS_GEMM 0    /* tcgen05 GEMM (M > 16) */
-#define NQ_KCLASS_GEMV 1    /* split-K GEMV (M <= 16) */
+#define NQ_KCLASS_GEMV 1    /* GEMV (M <= 16), its partial-sum pass included */
 #define NQ_KCLASS_DEQUANT 2 /* Q8_0 -> bf16 weight pass of the large-M GEMM */
 #define NQ_KCLASS_REDUCE 3  /* split-K reduction after a split GEMM */
 int nq_profile_enable(int on);

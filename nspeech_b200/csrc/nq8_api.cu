@@ -256,20 +256,16 @@ struct ProfScope {
 // strided set of weight tiles (persistent), at least four k chunks per split
 // when K allows, and at most as many chunks per split as the staged
 // activation slice holds.
-struct GemvPlan {
-  int splits, cps, tgroups;
-};
-GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int64_t m, bool splitx) {
-  GemvPlan g;
-  const int target = 2 * sm_count;
-  const int cps_max = nq::gemv_max_cps(static_cast<int>(m), splitx);
-  int splits = std::max(1, std::min((target + total_tiles - 1) / total_tiles, std::max(1, kc / 4)));
-  int cps = std::min((kc + splits - 1) / splits, cps_max);
-  splits = (kc + cps - 1) / cps;
-  g.splits = splits;
-  g.cps = cps;
-  g.tgroups = std::max(1, std::min(total_tiles, target / splits));
-  return g;
+// The GEMV reads bf16 activation rows in place when they are 16-byte aligned
+// rows of whole 64-wide chunks; otherwise split_x first writes zero-padded
+// bf16 planes (hi, and lo for f32) to the workspace.
+bool gemv_x_direct(const void *x, int x_dtype, int64_t ldx, int64_t k) {
+  return x_dtype == NQ_BF16 && (reinterpret_cast<uintptr_t>(x) % 16 == 0) && (ldx % 8 == 0) &&
+         (k % nq::kPackK == 0);
+}
+
+size_t gemv_partial_bytes(const nq::GemvPlan &plan, int n_tiles, int64_t m) {
+  return align_up(static_cast<size_t>(plan.upt) * m * n_tiles * nq::kPackRows * sizeof(float), 256);
 }
 
 int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
@@ -278,51 +274,59 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
   int total_tiles = 0;
   for (int i = 0; i < nprob; ++i) total_tiles += args[i].w->n_tiles;
   const int kc = w0->kc;
-  const GemvPlan plan = gemv_plan(ctx->sm_count, total_tiles, kc, m, x_dtype == NQ_F32);
-  const int splits = plan.splits, cps = plan.cps;
+  const nq::GemvPlan plan = nq::gemv_plan(ctx->sm_count, total_tiles, kc, static_cast<int>(m));
+  const bool splitx = x_dtype == NQ_F32;
+  const bool direct = gemv_x_direct(x, x_dtype, ldx, w0->k);
+  const int64_t k_pad = static_cast<int64_t>(kc) * nq::kPackK;
 
+  // Workspace: [activation planes][partials of problem 0, 1, 2].
+  const size_t plane = align_up(static_cast<size_t>(m) * k_pad * 2, 256);
+  const size_t x_bytes = direct ? 0 : plane * (splitx ? 2 : 1);
   size_t part_bytes = 0;
-  if (splits > 1)
-    for (int i = 0; i < nprob; ++i)
-      part_bytes += align_up(static_cast<size_t>(splits) * args[i].w->n_tiles * 16 * nq::kPackRows * sizeof(float), 256);
+  for (int i = 0; i < nprob; ++i) part_bytes += gemv_partial_bytes(plan, args[i].w->n_tiles, m);
   Workspace *ws = nullptr;
-  int rc = get_workspace(ctx, stream, part_bytes, &ws);
+  int rc = get_workspace(ctx, stream, x_bytes + part_bytes, &ws);
   if (rc) return rc;
 
   nq::GemvParams p;
   std::memset(&p, 0, sizeof(p));
-  size_t part_off = 0, ctr_off = 0;
+  size_t part_off = x_bytes;
   for (int i = 0; i < nprob; ++i) {
     const nq_weight *w = args[i].w;
     nq::GemvProblem &pr = p.prob[i];
     pr.w = w->dev;
     pr.n_tiles = w->n_tiles;
-    pr.kc_total = w->kc;
     pr.N = w->n;
     pr.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
     pr.n_out = out_width(w);
     pr.bias = args[i].bias;
     pr.y = args[i].y;
     pr.ldy = args[i].ldy;
-    if (splits > 1) {
-      pr.partials = reinterpret_cast<float *>(ws->buf + part_off);
-      part_off += align_up(static_cast<size_t>(splits) * w->n_tiles * 16 * nq::kPackRows * sizeof(float), 256);
-      if (ctr_off + w->n_tiles > kCounterSlots) return fail(NQ_ERR_SHAPE, "too many tiles for the counter pool");
-      pr.counters = ws->counters + ctr_off;
-      ctr_off += w->n_tiles;
-    }
+    pr.partials = reinterpret_cast<float *>(ws->buf + part_off);
+    part_off += gemv_partial_bytes(plan, w->n_tiles, m);
   }
-  p.x = x;
-  p.x_dtype = x_dtype;
-  p.ldx = ldx;
+  p.sched = ws->counters;  // work counter
+  if (direct) {
+    p.xh = static_cast<const __nv_bfloat16 *>(x);
+    p.ldx = ldx;
+  } else {
+    __nv_bfloat16 *hi = reinterpret_cast<__nv_bfloat16 *>(ws->buf);
+    __nv_bfloat16 *lo = splitx ? reinterpret_cast<__nv_bfloat16 *>(ws->buf + plane) : nullptr;
+    cudaError_t e = nq::launch_split_x(x, x_dtype, ldx, m, w0->k, k_pad, hi, lo, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "split_x launch");
+    p.xh = hi;
+    p.xl = lo;
+    p.ldx = k_pad;
+  }
   p.M = static_cast<int>(m);
-  p.K = w0->k;
   p.epi = epilogue;
   p.y_dtype = y_dtype;
-  p.splits = splits;
-  p.cps = cps;
   p.nprob = nprob;
-  p.tgroups = plan.tgroups;
+  p.kc = kc;
+  p.unit = plan.unit;
+  p.upt = plan.upt;
+  p.units = plan.units;
+  p.ctas = plan.ctas;
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
   double flops = 0, bytes = 0;
@@ -333,7 +337,7 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
              m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (args[i].bias ? 4.0 * w->n : 0.0);
   }
   ProfScope ps(NQ_KCLASS_GEMV, stream, flops, bytes);
-  cudaError_t e = nq::launch_gemv(p, x_dtype == NQ_F32, stream);
+  cudaError_t e = nq::launch_gemv(p, plan.ctas, stream);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return NQ_OK;
 }
@@ -557,13 +561,14 @@ int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, i
 }
 
 // ------------------------------------------------- static-scratch GEMV
-// Scratch of nq_gemv_noalloc: split-K partial tiles followed by the per-tile
-// arrival counters, in this module's own device memory (a file-scope device
-// array), so a call needs no allocation.  One array per device, shared by
-// every call on that device.
-constexpr size_t kNoAllocPartialBytes = size_t(4) << 20;  // 4 MiB of partial tiles
-constexpr int kNoAllocCounters = 4096;                     // weight tiles (N <= 524288)
-constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + kNoAllocCounters * sizeof(int);
+// Scratch of nq_gemv_noalloc: the GEMV's unit partials, then the activation
+// planes split_x writes when x is not read in place, then the work counter,
+// in this module's own device memory (a file-scope device array), so a call
+// needs no allocation.  One array per device, shared by every call on that
+// device.
+constexpr size_t kNoAllocPartialBytes = size_t(4) << 20;  // 4 MiB of unit partials
+constexpr size_t kNoAllocXBytes = size_t(2) << 20;        // 2 MiB of bf16 activation planes
+constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + kNoAllocXBytes + 256;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 std::mutex g_noalloc_mu;
@@ -593,7 +598,8 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int linear_launches(const nq_weight *w, int64_t m, int x_dtype, bool aligned) {
   if (!w || m <= 0) return 0;
-  if (m <= 16) return 1;  // split-K GEMV (one launch for up to three weights)
+  if (m <= 16)  // GEMV + gemv_reduce (for up to three weights), after split_x unless x is read in place
+    return x_dtype == NQ_BF16 && aligned && w->k % nq::kPackK == 0 ? 2 : 3;
   DeviceCtx *ctx = nullptr;
   int dev = 0;
   const int sm = current_ctx(&ctx, &dev) == NQ_OK ? ctx->sm_count : kSmCountB200;
@@ -787,59 +793,69 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   if (rc) return rc;
   if (w->device != dev) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, dev);
   cudaStream_t stream_ = static_cast<cudaStream_t>(stream);
-  // Same split-K choice as nq_linear's GEMV, so both give the same sums.
+  // Same work split as nq_linear's GEMV, so both give the same sums.
   const int kc = w->kc;
-  const GemvPlan plan = gemv_plan(ctx->sm_count, w->n_tiles, kc, m, x_dtype == NQ_F32);
-  const int splits = plan.splits, cps = plan.cps;
-  const size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * w->n_tiles * 16 * nq::kPackRows * sizeof(float) : 0;
+  const nq::GemvPlan plan = nq::gemv_plan(ctx->sm_count, w->n_tiles, kc, static_cast<int>(m));
+  const bool splitx = x_dtype == NQ_F32;
+  const bool direct = gemv_x_direct(x, x_dtype, ldx, w->k);
+  const int64_t k_pad = static_cast<int64_t>(kc) * nq::kPackK;
+  const size_t plane = align_up(static_cast<size_t>(m) * k_pad * 2, 256);
+  const size_t x_bytes = direct ? 0 : plane * (splitx ? 2 : 1);
+  const size_t part_bytes = gemv_partial_bytes(plan, w->n_tiles, m);
   if (part_bytes > kNoAllocPartialBytes)
     return fail(NQ_ERR_SHAPE,
                 "nq_gemv_noalloc: this weight (N=%lld, K=%lld) needs %zu bytes of split-K scratch; the static "
                 "scratch holds %zu",
                 (long long)w->n, (long long)w->k, part_bytes, kNoAllocPartialBytes);
-  if (w->n_tiles > kNoAllocCounters)
-    return fail(NQ_ERR_SHAPE, "nq_gemv_noalloc: %d weight tiles exceed the %d counters of the static scratch",
-                w->n_tiles, kNoAllocCounters);
+  if (x_bytes > kNoAllocXBytes)
+    return fail(NQ_ERR_SHAPE,
+                "nq_gemv_noalloc: staging these activations (M=%lld, K=%lld) needs %zu bytes; the static scratch "
+                "holds %zu",
+                (long long)m, (long long)w->k, x_bytes, kNoAllocXBytes);
   unsigned char *scratch = nullptr;
   rc = noalloc_scratch(dev, &scratch);
   if (rc) return rc;
-  int *counters = reinterpret_cast<int *>(scratch + kNoAllocPartialBytes);
-  if (splits > 1) {
-    // The array keeps the last call's contents: the arrival counters must
-    // start at zero (a call that gave up on a wait can leave them armed).
-    cudaError_t e = cudaMemsetAsync(counters, 0, w->n_tiles * sizeof(int), stream_);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static GEMV counters)");
-  }
+  unsigned char *xplanes = scratch + kNoAllocPartialBytes;
+  // The work counter starts at zero (static storage) and every call's
+  // gemv_reduce re-arms it.
+  int *sched = reinterpret_cast<int *>(scratch + kNoAllocPartialBytes + kNoAllocXBytes);
   nq::GemvParams p;
   std::memset(&p, 0, sizeof(p));
   nq::GemvProblem &pr = p.prob[0];
   pr.w = w->dev;
   pr.n_tiles = w->n_tiles;
-  pr.kc_total = kc;
   pr.N = w->n;
   pr.glu = (w->flags & NQ_PACK_GLU) ? 1 : 0;
   pr.n_out = out_width(w);
   pr.bias = bias;
   pr.y = y;
   pr.ldy = ldy;
-  if (splits > 1) {
-    pr.partials = reinterpret_cast<float *>(scratch);
-    pr.counters = counters;
+  pr.partials = reinterpret_cast<float *>(scratch);
+  p.sched = sched;
+  if (direct) {
+    p.xh = static_cast<const __nv_bfloat16 *>(x);
+    p.ldx = ldx;
+  } else {
+    __nv_bfloat16 *hi = reinterpret_cast<__nv_bfloat16 *>(xplanes);
+    __nv_bfloat16 *lo = splitx ? reinterpret_cast<__nv_bfloat16 *>(xplanes + plane) : nullptr;
+    cudaError_t e = nq::launch_split_x(x, x_dtype, ldx, m, w->k, k_pad, hi, lo, stream_);
+    if (e != cudaSuccess) return cuda_fail(e, "split_x launch");
+    p.xh = hi;
+    p.xl = lo;
+    p.ldx = k_pad;
   }
-  p.x = x;
-  p.x_dtype = x_dtype;
-  p.ldx = ldx;
   p.M = static_cast<int>(m);
-  p.K = w->k;
   p.epi = epilogue;
   p.y_dtype = y_dtype;
-  p.splits = splits;
-  p.cps = cps;
   p.nprob = 1;
-  p.tgroups = plan.tgroups;
+  p.kc = kc;
+  p.unit = plan.unit;
+  p.upt = plan.upt;
+  p.units = plan.units;
+  p.ctas = plan.ctas;
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
-  cudaError_t e = nq::launch_gemv(p, x_dtype == NQ_F32, stream_);
+  cudaError_t e = nq::launch_gemv(p, plan.ctas, stream_);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return NQ_OK;
 }

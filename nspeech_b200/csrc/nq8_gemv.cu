@@ -1,91 +1,112 @@
-// nq8_gemv.cu -- K2: persistent split-K Q8_0 GEMV / skinny GEMM (M <= 16).
+// nq8_gemv.cu -- K2: dynamically scheduled Q8_0 GEMV / skinny GEMM (M <= 16).
 //
 // Replaces the split-K GEMV family of the reference (Triton source
 // kernels/moonshine_kernels.py:1039-1276, dispatched by enc_gemv_splitk*,
 // src/triton_kernels.rs:1036-1202) and the M=1 decoder projections of
 // src/moonshine/decoder.rs.  HBM-bound: every weight byte is read once.
 //
-// Work: the weight tiles of up to three problems sharing x (fused Q/K/V) form
-// one list; K is cut into `splits` ranges of cps 64-wide chunks.  CTA c owns
-// split c % splits and walks tiles c / splits, + tgroups, ... (persistent:
-// one continuous copy stream per CTA, so launch and prologue costs are paid
-// once per CTA rather than per tile).  CTA = 1 producer warp + 8 consumer
-// warps:
-//   producer: cp.async.bulk of whole 8704-byte packed tiles into a ring of
-//             kStages shared-memory slots, chunk after chunk across the CTA's
-//             tiles; a proxy fence orders the consumers' shared reads of a
-//             slot before the copy that refills it.
-//   consumers: the CTA's activation slice [M][cps*64] is staged once (bf16,
-//             hi + lo planes for f32 x, k order permuted to match the lanes'
-//             weight bytes).  Warp w owns rows [16w, 16w+16) of each tile:
-//             each lane loads 16 int8 of two rows, dequantizes them to
-//             bf16(d*q) and issues mma.m16n8k16 with the weight as the 16-row
-//             operand and the activations as the 8-column operand.
-//   per tile: the accumulators go through shared memory; with split-K they
-//             become f32 partials [split][tile][M][128] and the last CTA of a
-//             tile (arrival counter) sums the splits in index order
-//             (deterministic); then bias / activation / GLU and the store.
-// Every wait is bounded; a consumer that gives up keeps taking part in the
-// per-tile barriers (skipping work) until the CTA leaves together.
+// Work: the weight tiles of up to three problems sharing x (fused Q/K/V) are
+// cut into units of `unit` 64-wide k chunks (upt units per tile, tile-major).
+// The cut is fixed by the shape, not by timing: unit j of a tile always owns
+// the same k range and writes its f32 partial to slot j, and gemv_reduce
+// (the next launch) sums each tile's slots in a fixed order, so results are
+// reproducible bit for bit.  Which CTA computes a unit is dynamic: CTA c
+// starts with unit c and then takes the next unit from a work counter, so
+// CTAs that stream faster take more units (per-CTA HBM rates differ by tens
+// of percent on B200).  CTA = 1 producer warp + 4 consumer warps:
+//   producer: cp.async.bulk of whole 8704-byte packed chunks into a ring of
+//             shared-memory stages, tagged with (unit, chunk); a proxy fence
+//             orders the consumers' shared reads of a stage before the copy
+//             that refills it.  The weights are constant, so the first unit
+//             is fetched before the programmatic dependency wait and overlaps
+//             the previous kernel's tail.
+//   consumers: warp w owns rows [32w, 32w+32) of each tile as two 16-row
+//             groups: each lane reads 16 int8 of four rows, dequantizes them
+//             to bf16(d*q) and issues mma.m16n8k16 with the weight as the
+//             16-row operand and the activations (bf16 rows, read from
+//             global / L1 one chunk ahead) as the 8-column operand.  At the
+//             end of a unit each lane stores its accumulators to the unit's
+//             partial slot and goes on with the next unit.
+// gemv_reduce: one CTA per (tile, row of x) sums the tile's slots, applies
+// bias / activation / GLU, stores the output and re-arms the work counter.
+// Every wait is bounded; a role that gives up raises the CTA's abort flag and
+// the others leave their loops at their next wait.
+#include <algorithm>
+
 #include "nq8_common.cuh"
 #include "nq8_kernels.h"
 
 namespace nq {
 
-constexpr int kGemvStages = 6;
-constexpr int kGemvConsumerWarps = 8;
+constexpr int kGemvConsumerWarps = 4;
 constexpr int kGemvConsumers = 32 * kGemvConsumerWarps;
-constexpr int kGemvThreads = 32 + kGemvConsumers;
-constexpr int kAccPitch = 132;           // floats per row of the staged accumulator tile
-constexpr int kGemvXStageBytes = 16384;  // activation slice budget (per plane set)
-constexpr int kGemvBarEpi = 1;           // named barrier of the consumer warps
+constexpr int kGemvThreads = 32 + kGemvConsumers;  // producer warp, consumers
+constexpr int kGemvCtasPerSm = 4;
+constexpr int kGemvStages = 6;
+constexpr int kGemvUnitsPerCta = 6;  // scheduling granularity target
+constexpr size_t kGemvMetaOff = static_cast<size_t>(kGemvStages) * kTileBytes;     // int2 (unit, chunk) per stage
+constexpr size_t kGemvBarOff = kGemvMetaOff + kGemvStages * 2 * sizeof(int);      // full, empty
+constexpr size_t kGemvFlagOff = kGemvBarOff + 2 * kGemvStages * sizeof(uint64_t);  // abort flag
+constexpr size_t kGemvSmemBytes = kGemvFlagOff + 16;
 
-static __host__ __device__ inline int gemv_x_pitch(int cps) { return cps * kPackK * 2 + 8; }  // bytes
-
-int gemv_max_cps(int m, bool splitx) {
-  const int mrows = m <= 8 ? 8 : 16;
-  return kGemvXStageBytes / (mrows * kPackK * 2 * (splitx ? 2 : 1));
+GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int m) {
+  GemvPlan g;
+  const int64_t slots = static_cast<int64_t>(kGemvCtasPerSm) * sm_count;
+  const int64_t work = static_cast<int64_t>(total_tiles) * kc;
+  // About kGemvUnitsPerCta units per CTA; at least two chunks, and at least
+  // M/2 so that the f32 partials stay a small fraction of the weight bytes.
+  int64_t u = work / (kGemvUnitsPerCta * slots);
+  u = std::max<int64_t>(u, std::max(2, (m + 1) / 2));
+  g.unit = static_cast<int>(std::min<int64_t>(u, kc));
+  g.upt = (kc + g.unit - 1) / g.unit;
+  g.units = total_tiles * g.upt;
+  g.ctas = static_cast<int>(std::min<int64_t>(slots, g.units));
+  return g;
 }
 
-size_t gemv_smem_bytes(int mrows, bool splitx, int cps) {
-  size_t off = static_cast<size_t>(kGemvStages) * kTileBytes;                  // ring
-  off += static_cast<size_t>(mrows) * gemv_x_pitch(cps) * (splitx ? 2 : 1);    // x planes
-  off = (off + 15) & ~static_cast<size_t>(15);
-  off += static_cast<size_t>(16) * kAccPitch * sizeof(float);                  // accumulator tile
-  off += 2 * kGemvStages * sizeof(uint64_t) + 16;                              // barriers + flags
-  return off;
+// Activation fragments of one 64-wide chunk for this lane: 16 bf16 of one row
+// (two 16-byte loads), zero for rows beyond M.
+template <int MT>
+__device__ __forceinline__ void load_x_chunk(uint4 (&v)[MT][2], const __nv_bfloat16 *const (&xr)[MT],
+                                             const bool (&live)[MT], int ch) {
+#pragma unroll
+  for (int mt = 0; mt < MT; ++mt) {
+    if (live[mt]) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(xr[mt] + static_cast<size_t>(ch) * kPackK);
+      v[mt][0] = __ldg(src);
+      v[mt][1] = __ldg(src + 1);
+    } else {
+      v[mt][0] = make_uint4(0u, 0u, 0u, 0u);
+      v[mt][1] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
 }
+
+__device__ __forceinline__ uint2 xpair(const uint4 (&v)[2], int j) {
+  const uint4 &h = v[j >> 1];
+  return (j & 1) ? make_uint2(h.z, h.w) : make_uint2(h.x, h.y);
+}
+
 
 template <int MT, bool SPLITX>
-__global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_constant__ GemvParams p) {
-  pdl_wait();  // predecessor kernel complete, its writes visible
+__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(const __grid_constant__ GemvParams p) {
+  constexpr int S = kGemvStages;
+  // No dependency wait here: the producer's first unit only reads the
+  // (constant) weights; every other access waits first.
   pdl_trigger();
-  constexpr int MROWS = 8 * MT;
   extern __shared__ __align__(128) uint8_t smem[];
-  const int split = blockIdx.x % p.splits;
-  const int tg0 = blockIdx.x / p.splits;
+  const int kc = p.kc;
   const int t1 = p.prob[0].n_tiles, t2 = t1 + p.prob[1].n_tiles;
-  const int total_tiles = t2 + (p.nprob > 2 ? p.prob[2].n_tiles : 0);
-  const int kc0 = split * p.cps;
-  const int nchunks = max(min(kc0 + p.cps, p.prob[0].kc_total) - kc0, 0);
-  if (tg0 >= total_tiles || nchunks == 0) return;  // whole CTA, before any barrier is touched
-  const int xpitch = gemv_x_pitch(p.cps);
 
   uint8_t *ring = smem;
-  uint8_t *xs = smem + kGemvStages * kTileBytes;
-  const int xplane = MROWS * xpitch;
-  size_t off = static_cast<size_t>(kGemvStages) * kTileBytes + static_cast<size_t>(xplane) * (SPLITX ? 2 : 1);
-  off = (off + 15) & ~static_cast<size_t>(15);
-  float *acc_s = reinterpret_cast<float *>(smem + off);
-  off += static_cast<size_t>(16) * kAccPitch * sizeof(float);
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + off);
-  // [0] abort (any role)  [1] last split of the current tile  [2] abort as sampled for this tile
-  volatile int *flags = reinterpret_cast<volatile int *>(bars + 2 * kGemvStages);
+  volatile int *meta = reinterpret_cast<volatile int *>(smem + kGemvMetaOff);  // (unit, chunk) per stage
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kGemvBarOff);
+  volatile int *flags = reinterpret_cast<volatile int *>(smem + kGemvFlagOff);  // [0] abort (any role)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
-  auto empty_bar = [&](int s) { return smem_u32(&bars[kGemvStages + s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[S + s]); };
   auto tile_prob = [&](int T, int &local) {
     const int pi = (T >= t1) + (T >= t2);
     local = T - (pi == 0 ? 0 : (pi == 1 ? t1 : t2));
@@ -93,13 +114,11 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_cons
   };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemvStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), kGemvConsumerWarps);
     }
     flags[0] = 0;
-    flags[1] = 0;
-    flags[2] = 0;
     fence_mbar_init();
   }
   __syncthreads();
@@ -108,101 +127,150 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_cons
     if (lane == 0) {
       // ---------------------------------------------------------- producer
       const uint64_t pol = policy_evict_first();
-      int g = 0;
-      bool ok = true;
-      for (int T = tg0; T < total_tiles && ok; T += p.tgroups) {
+      int s = 0, issued = 0;
+      uint32_t ph = 0;  // (issued / S) & 1
+      bool ok = true, waited = false;
+      auto next_stage = [&](bool &good) {
+        if (issued >= S && !mbar_wait(empty_bar(s), ph ^ 1u, p.ctl.wait_limit, flags)) {
+          if (!flags[0]) report(p.ctl, flags, kDevTimeoutProducer);
+          good = false;
+        }
+        if (flags[0]) good = false;
+      };
+      auto advance = [&]() {
+        ++issued;
+        if (++s == S) {
+          s = 0;
+          ph ^= 1u;
+        }
+      };
+      int u = blockIdx.x;
+      while (ok && u < p.units) {
+        const int T = u / p.upt;
+        const int c0 = (u - T * p.upt) * p.unit;
+        const int c1 = min(c0 + p.unit, kc);
         int tl = 0;
         const GemvProblem &pr = p.prob[tile_prob(T, tl)];
-        const uint8_t *wbase = pr.w + (static_cast<size_t>(tl) * pr.kc_total + kc0) * kTileBytes;
-        for (int i = 0; i < nchunks; ++i, ++g) {
-          const int s = g % kGemvStages;
-          if (g >= kGemvStages && !mbar_wait(empty_bar(s), ((g / kGemvStages) - 1) & 1, p.ctl.wait_limit, flags)) {
-            if (!flags[0]) report(p.ctl, flags, kDevTimeoutProducer);
-            ok = false;
-            break;
-          }
-          if (flags[0]) {
-            ok = false;
-            break;
-          }
-          // The consumers read the slot with ordinary shared loads; order those
-          // reads before the async-proxy bulk write that refills it.
+        const uint8_t *src = pr.w + (static_cast<size_t>(tl) * kc + c0) * kTileBytes;
+        for (int ch = c0; ch < c1; ++ch, src += kTileBytes) {
+          next_stage(ok);
+          if (!ok) break;
+          meta[2 * s] = u;
+          meta[2 * s + 1] = ch;
+          // The consumers read the stage with ordinary shared loads; order
+          // those reads before the async-proxy bulk write that refills it.
           fence_proxy_async_smem();
           mbar_arrive_expect_tx(full_bar(s), kTileBytes);
-          bulk_load(smem_u32(ring + s * kTileBytes), wbase + static_cast<size_t>(i) * kTileBytes, kTileBytes,
-                    full_bar(s), pol);
+          bulk_load(smem_u32(ring + s * kTileBytes), src, kTileBytes, full_bar(s), pol);
+          advance();
+        }
+        if (!ok) break;
+        if (!waited) {
+          pdl_wait();  // the previous launch's gemv_reduce re-armed the work counter
+          waited = true;
+        }
+        u = p.ctas + atomicAdd(p.sched, 1);
+      }
+      if (ok) {
+        // end marker: a stage whose phase completes with no copy
+        next_stage(ok);
+        if (ok) {
+          meta[2 * s] = -1;
+          mbar_arrive(full_bar(s));
+          advance();
         }
       }
       // Drain: every issued copy has landed before the CTA leaves.
       volatile int no_abort = 0;
-      for (int s = 0; s < kGemvStages && s < g; ++s) {
-        const int last = s + kGemvStages * ((g - 1 - s) / kGemvStages);
-        if (!mbar_wait(full_bar(s), (last / kGemvStages) & 1, p.ctl.wait_limit, &no_abort))
+      for (int st = 0; st < S && st < issued; ++st) {
+        const int last = st + S * ((issued - 1 - st) / S);
+        if (!mbar_wait(full_bar(st), (last / S) & 1, p.ctl.wait_limit, &no_abort))
           atomicOr(p.ctl.status, kDevTimeoutDrain);
       }
     }
   } else {
     // ------------------------------------------------------------ consumers
-    const int ct = threadIdx.x - 32;
+    pdl_wait();  // predecessor kernel complete, its writes visible
     const int cw = warp - 1;
     const int g4 = lane >> 2;
     const int c = lane & 3;
     const int M = p.M;
-    // Stage the activation slice [MROWS][cps*64] once (bf16 hi [, lo] planes).
-    {
-      const int klen = p.cps * kPackK;
-      const int64_t kbase = static_cast<int64_t>(kc0) * kPackK;
-      for (int idx = ct; idx < MROWS * klen; idx += kGemvConsumers) {
-        const int m = idx / klen;
-        const int kk = idx - m * klen;
-        const int64_t k = kbase + kk;
-        float v = 0.f;
-        if (m < M && k < p.K) {
-          if (p.x_dtype == 0)
-            v = static_cast<const float *>(p.x)[m * p.ldx + k];
-          else
-            v = __bfloat162float(static_cast<const __nv_bfloat16 *>(p.x)[m * p.ldx + k]);
-        }
-        const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-        *reinterpret_cast<__nv_bfloat16 *>(xs + m * xpitch + kk * 2) = hi;
-        if (SPLITX) {
-          const __nv_bfloat16 lo = __float2bfloat16_rn(v - __bfloat162float(hi));
-          *reinterpret_cast<__nv_bfloat16 *>(xs + xplane + m * xpitch + kk * 2) = lo;
-        }
-      }
-      named_bar_sync(kGemvBarEpi, kGemvConsumers);
+    // rows of the two 16-row groups: (r0, r0 + 8), (r1, r1 + 8)
+    const int r0 = 32 * cw + g4, r1 = r0 + 16;
+    const int off0 = qs_offset(r0, c), off1 = qs_offset(r0 + 8, c);
+    const int off2 = qs_offset(r1, c), off3 = qs_offset(r1 + 8, c);
+    const int sof0 = scale_offset(r0, c >> 1), sof1 = scale_offset(r0 + 8, c >> 1);
+    const int sof2 = scale_offset(r1, c >> 1), sof3 = scale_offset(r1 + 8, c >> 1);
+    const __nv_bfloat16 *xh[MT];
+    const __nv_bfloat16 *xl[MT];
+    bool live[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const int m = mt * 8 + g4;
+      live[mt] = m < M;
+      xh[mt] = p.xh + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + c * 16;
+      xl[mt] = SPLITX ? p.xl + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + c * 16 : nullptr;
     }
-    const int row_a = 16 * cw + g4;
-    const int row_b = row_a + 8;
-    bool alive = true;  // this warp's waits have all succeeded
-    int g = 0;
-    for (int T = tg0; T < total_tiles; T += p.tgroups) {
-      float acc[MT][4];
+    float acc[2][MT][4];
+    uint4 xc[MT][2], xcl[MT][2];
+    int s = 0, cur = -1, c_end = 0;
+    uint32_t ph = 0;
+    while (true) {
+      const int st = s;
+      const uint32_t par = ph;
+      if (++s == S) {
+        s = 0;
+        ph ^= 1u;
+      }
+      bool ok = mbar_wait(full_bar(st), par, p.ctl.wait_limit, flags);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0 && !flags[0]) report(p.ctl, flags, kDevTimeoutConsumer);
+        break;
+      }
+      const int unit = meta[2 * st];
+      const int ch = meta[2 * st + 1];
+      if (unit < 0) break;  // end marker: no more units
+      const uint8_t *sp = ring + st * kTileBytes;
+      uint4 q[4];
+      q[0] = *reinterpret_cast<const uint4 *>(sp + off0);
+      q[1] = *reinterpret_cast<const uint4 *>(sp + off1);
+      q[2] = *reinterpret_cast<const uint4 *>(sp + off2);
+      q[3] = *reinterpret_cast<const uint4 *>(sp + off3);
+      float d[4];
+      d[0] = __half2float(*reinterpret_cast<const __half *>(sp + sof0));
+      d[1] = __half2float(*reinterpret_cast<const __half *>(sp + sof1));
+      d[2] = __half2float(*reinterpret_cast<const __half *>(sp + sof2));
+      d[3] = __half2float(*reinterpret_cast<const __half *>(sp + sof3));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(st));
+      if (unit != cur) {
+        // first chunk of a unit: clear the accumulators, fetch its activations
+        cur = unit;
+        const int T = cur / p.upt;
+        c_end = min((cur - T * p.upt + 1) * p.unit, kc);
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt)
+        for (int gi = 0; gi < 2; ++gi)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[mt][e] = 0.f;
-      for (int i = 0; i < nchunks; ++i, ++g) {
-        if (!alive) continue;  // keep g in step; no more waits after a give-up
-        const int s = g % kGemvStages;
-        bool ok = mbar_wait(full_bar(s), (g / kGemvStages) & 1, p.ctl.wait_limit, flags);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) {
-          if (lane == 0 && !flags[0]) report(p.ctl, flags, kDevTimeoutConsumer);
-          alive = false;
-          continue;
-        }
-        const uint8_t *st = ring + s * kTileBytes;
-        const uint4 qa = *reinterpret_cast<const uint4 *>(st + qs_offset(row_a, c));
-        const uint4 qb = *reinterpret_cast<const uint4 *>(st + qs_offset(row_b, c));
-        const float da = __half2float(*reinterpret_cast<const __half *>(st + scale_offset(row_a, c >> 1)));
-        const float db = __half2float(*reinterpret_cast<const __half *>(st + scale_offset(row_b, c >> 1)));
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty_bar(s));
-
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[gi][mt][e] = 0.f;
+        load_x_chunk<MT>(xc, xh, live, ch);
+        if (SPLITX) load_x_chunk<MT>(xcl, xl, live, ch);
+      }
+      const bool more = ch + 1 < c_end;
+      // next chunk's activations, one chunk ahead of their use
+      uint4 xn[MT][2], xnl[MT][2];
+      if (more) {
+        load_x_chunk<MT>(xn, xh, live, ch + 1);
+        if (SPLITX) load_x_chunk<MT>(xnl, xl, live, ch + 1);
+      }
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
         // bf16(f32(d) * q), eight elements per call with packed f32x2 arithmetic
         uint32_t oa[8], ob[8];
-        const uint64_t dda = f2(da, da), ddb = f2(db, db);
+        const uint64_t dda = f2(d[2 * gi], d[2 * gi]), ddb = f2(d[2 * gi + 1], d[2 * gi + 1]);
+        const uint4 &qa = q[2 * gi], &qb = q[2 * gi + 1];
         dequant8_bf16(qa.x, qa.y, dda, oa);
         dequant8_bf16(qa.z, qa.w, dda, oa + 4);
         dequant8_bf16(qb.x, qb.y, ddb, ob);
@@ -211,127 +279,155 @@ __global__ void __launch_bounds__(kGemvThreads) gemv_q8_kernel(const __grid_cons
         for (int j = 0; j < 4; ++j) {
           // A fragment of word j: rows (a, b) x k pairs (4j, 4j+1), (4j+2, 4j+3)
           const uint32_t a[4] = {oa[2 * j], ob[2 * j], oa[2 * j + 1], ob[2 * j + 1]};
-          const int kk = i * kPackK + c * 16 + 4 * j;
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
-            const uint2 xv = *reinterpret_cast<const uint2 *>(xs + (mt * 8 + g4) * xpitch + kk * 2);
-            mma_16816_bf16(acc[mt], a, xv.x, xv.y);
+            const uint2 xv = xpair(xc[mt], j);
+            mma_16816_bf16(acc[gi][mt], a, xv.x, xv.y);
             if (SPLITX) {
-              const uint2 xl = *reinterpret_cast<const uint2 *>(xs + xplane + (mt * 8 + g4) * xpitch + kk * 2);
-              mma_16816_bf16(acc[mt], a, xl.x, xl.y);
+              const uint2 xw = xpair(xcl[mt], j);
+              mma_16816_bf16(acc[gi][mt], a, xw.x, xw.y);
             }
           }
         }
       }
-      // ---------------------------------------------------- tile epilogue
+      if (more) {
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        const int m0 = mt * 8 + 2 * c;
-        acc_s[m0 * kAccPitch + row_a] = acc[mt][0];
-        acc_s[(m0 + 1) * kAccPitch + row_a] = acc[mt][1];
-        acc_s[m0 * kAccPitch + row_a + 8] = acc[mt][2];
-        acc_s[(m0 + 1) * kAccPitch + row_a + 8] = acc[mt][3];
-      }
-      // One consumer samples the abort flag (any role may raise it at any time)
-      // so that all consumers take the same path through the barriers below.
-      if (ct == 0) flags[2] = flags[0];
-      named_bar_sync(kGemvBarEpi, kGemvConsumers);
-      const bool abort = flags[2] != 0;
-      int tl = 0;
-      const GemvProblem &pr = p.prob[tile_prob(T, tl)];
-      bool store = !abort;
-      if (!abort && p.splits > 1) {
-        // Partials hold the M live rows only: [split][tile][M][128] f32.
-        const int elems = M * kPackRows;
-        const size_t sstride = static_cast<size_t>(pr.n_tiles) * elems;
-        float *part = pr.partials + split * sstride + static_cast<size_t>(tl) * elems;
-        for (int idx = ct; idx < elems; idx += kGemvConsumers) part[idx] = acc_s[(idx >> 7) * kAccPitch + (idx & 127)];
-        __threadfence();
-        named_bar_sync(kGemvBarEpi, kGemvConsumers);
-        if (ct == 0) {
-          const int prev = atomicAdd(&pr.counters[tl], 1);
-          flags[1] = (prev == p.splits - 1) ? 1 : 0;
+        for (int mt = 0; mt < MT; ++mt) {
+          xc[mt][0] = xn[mt][0];
+          xc[mt][1] = xn[mt][1];
+          if (SPLITX) {
+            xcl[mt][0] = xnl[mt][0];
+            xcl[mt][1] = xnl[mt][1];
+          }
         }
-        named_bar_sync(kGemvBarEpi, kGemvConsumers);
-        store = flags[1] != 0;
-        if (store) {
-          __threadfence();
-          // Sum the splits in index order; eight loads are issued before their adds.
-          for (int idx = ct; idx < elems; idx += kGemvConsumers) {
-            const float *src = pr.partials + static_cast<size_t>(tl) * elems + idx;
-            float sum = 0.f;
-            int sp = 0;
-            for (; sp + 8 <= p.splits; sp += 8) {
-              float v[8];
+      } else {
+        // end of the unit: its partial slot [j][M][ldp] of the problem
+        const int T = cur / p.upt;
+        const int j = cur - T * p.upt;
+        int tl = 0;
+        const GemvProblem &pr = p.prob[tile_prob(T, tl)];
+        const size_t ldp = static_cast<size_t>(pr.n_tiles) * kPackRows;
+        float *base = pr.partials + static_cast<size_t>(j) * M * ldp + static_cast<size_t>(tl) * kPackRows;
 #pragma unroll
-              for (int u = 0; u < 8; ++u) v[u] = __ldcg(src + (sp + u) * sstride);
+        for (int gi = 0; gi < 2; ++gi) {
+          const int ra = gi ? r1 : r0;
 #pragma unroll
-              for (int u = 0; u < 8; ++u) sum += v[u];
+          for (int mt = 0; mt < MT; ++mt) {
+            const int m0 = mt * 8 + 2 * c;
+            if (m0 < M) {
+              base[m0 * ldp + ra] = acc[gi][mt][0];
+              base[m0 * ldp + ra + 8] = acc[gi][mt][2];
             }
-            for (; sp < p.splits; ++sp) sum += __ldcg(src + sp * sstride);
-            acc_s[(idx >> 7) * kAccPitch + (idx & 127)] = sum;
-          }
-          if (ct == 0) pr.counters[tl] = 0;  // re-armed for the next call on this stream
-        }
-        named_bar_sync(kGemvBarEpi, kGemvConsumers);
-      }
-      if (store) {
-        if (pr.glu) {
-          for (int idx = ct; idx < M * 64; idx += kGemvConsumers) {
-            const int m = idx >> 6;
-            const int r = idx & 63;
-            const int64_t j = static_cast<int64_t>(tl) * 64 + r;
-            if (j < pr.n_out) {
-              float v = acc_s[m * kAccPitch + r];
-              float gt = acc_s[m * kAccPitch + 64 + r];
-              if (pr.bias) {
-                v += pr.bias[j];
-                gt += pr.bias[pr.n_out + j];
-              }
-              store_out(pr.y, p.y_dtype, m * pr.ldy + j, act_glu(p.epi, v, gt));
-            }
-          }
-        } else {
-          for (int idx = ct; idx < M * kPackRows; idx += kGemvConsumers) {
-            const int m = idx >> 7;
-            const int r = idx & 127;
-            const int64_t j = static_cast<int64_t>(tl) * kPackRows + r;
-            if (j < pr.N) {
-              float v = acc_s[m * kAccPitch + r];
-              if (pr.bias) v += pr.bias[j];
-              store_out(pr.y, p.y_dtype, m * pr.ldy + j, act_single(p.epi, v));
+            if (m0 + 1 < M) {
+              base[(m0 + 1) * ldp + ra] = acc[gi][mt][1];
+              base[(m0 + 1) * ldp + ra + 8] = acc[gi][mt][3];
             }
           }
         }
+        cur = -1;
       }
-      named_bar_sync(kGemvBarEpi, kGemvConsumers);  // acc_s and flags[1] free for the next tile
-      if (abort) break;
     }
   }
   __syncthreads();
 }
 
+// Sum of a tile's unit partials for one row of x: warp w adds slots w, w+4,
+// w+8, ... in order (each lane four outputs), then the four warp sums are
+// added in warp order -- a fixed order, so the result does not depend on
+// which CTA computed which unit.  Then bias / activation / GLU and the store;
+// the first CTA re-arms the GEMV's work counter for the next launch.
+constexpr int kReduceWarps = 4;
+
+__global__ void __launch_bounds__(32 * kReduceWarps) gemv_reduce_kernel(const __grid_constant__ GemvParams p) {
+  pdl_wait();  // the GEMV's partials are complete and visible
+  pdl_trigger();
+  __shared__ float4 wsum[kReduceWarps][32];
+  __shared__ float tot[kPackRows];
+  const int T = blockIdx.x, m = blockIdx.y;
+  const int t1 = p.prob[0].n_tiles, t2 = t1 + p.prob[1].n_tiles;
+  const int pi = (T >= t1) + (T >= t2);
+  const int tl = T - (pi == 0 ? 0 : (pi == 1 ? t1 : t2));
+  const GemvProblem &pr = p.prob[pi];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const size_t ldp = static_cast<size_t>(pr.n_tiles) * kPackRows;
+  const size_t slot_stride = static_cast<size_t>(p.M) * ldp;
+  const float *src = pr.partials + static_cast<size_t>(m) * ldp + static_cast<size_t>(tl) * kPackRows + lane * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j0 = warp; j0 < p.upt; j0 += 8 * kReduceWarps) {
+    float4 v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int j = j0 + e * kReduceWarps;
+      v[e] = j < p.upt ? __ldcg(reinterpret_cast<const float4 *>(src + j * slot_stride)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      acc.x += v[e].x;
+      acc.y += v[e].y;
+      acc.z += v[e].z;
+      acc.w += v[e].w;
+    }
+  }
+  wsum[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    float4 t = wsum[0][lane];
+#pragma unroll
+    for (int w = 1; w < kReduceWarps; ++w) {
+      t.x += wsum[w][lane].x;
+      t.y += wsum[w][lane].y;
+      t.z += wsum[w][lane].z;
+      t.w += wsum[w][lane].w;
+    }
+    reinterpret_cast<float4 *>(tot)[lane] = t;
+  }
+  __syncthreads();
+  const int r = threadIdx.x;
+  if (pr.glu) {
+    const int64_t j = static_cast<int64_t>(tl) * 64 + r;
+    if (r < 64 && j < pr.n_out) {
+      float v = tot[r], gt = tot[64 + r];
+      if (pr.bias) {
+        v += pr.bias[j];
+        gt += pr.bias[pr.n_out + j];
+      }
+      store_out(pr.y, p.y_dtype, m * pr.ldy + j, act_glu(p.epi, v, gt));
+    }
+  } else {
+    const int64_t j = static_cast<int64_t>(tl) * kPackRows + r;
+    if (j < pr.N) {
+      float v = tot[r];
+      if (pr.bias) v += pr.bias[j];
+      store_out(pr.y, p.y_dtype, m * pr.ldy + j, act_single(p.epi, v));
+    }
+  }
+  if (T == 0 && m == 0 && threadIdx.x == 0) p.sched[0] = 0;
+}
+
 template <int MT, bool SPLITX>
-static cudaError_t launch_gemv_t(const GemvParams &p, cudaStream_t stream) {
-  const int cps_max = gemv_max_cps(8 * MT, SPLITX);
-  if (p.cps > cps_max) return cudaErrorInvalidValue;
-  const size_t smem = gemv_smem_bytes(8 * MT, SPLITX, p.cps);
+static cudaError_t launch_gemv_t(const GemvParams &p, int ctas, cudaStream_t stream) {
   auto kern = gemv_q8_kernel<MT, SPLITX>;
-  static bool attr_set[64] = {false};  // once per device, sized for the largest slice
+  static bool attr_set[64] = {false};  // once per device
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(gemv_smem_bytes(8 * MT, SPLITX, cps_max)));
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGemvSmemBytes));
     if (e != cudaSuccess) return e;
     if (dev < 64) attr_set[dev] = true;
   }
-  return launch_pdl(kern, dim3(p.splits * p.tgroups), dim3(kGemvThreads), smem, stream, 1, p);
+  return launch_pdl(kern, dim3(ctas), dim3(kGemvThreads), kGemvSmemBytes, stream, 1, p);
 }
 
-cudaError_t launch_gemv(const GemvParams &p, bool splitx, cudaStream_t stream) {
-  if (p.M <= 8) return splitx ? launch_gemv_t<1, true>(p, stream) : launch_gemv_t<1, false>(p, stream);
-  return splitx ? launch_gemv_t<2, true>(p, stream) : launch_gemv_t<2, false>(p, stream);
+cudaError_t launch_gemv(const GemvParams &p, int ctas, cudaStream_t stream) {
+  const bool splitx = p.xl != nullptr;
+  cudaError_t e;
+  if (p.M <= 8)
+    e = splitx ? launch_gemv_t<1, true>(p, ctas, stream) : launch_gemv_t<1, false>(p, ctas, stream);
+  else
+    e = splitx ? launch_gemv_t<2, true>(p, ctas, stream) : launch_gemv_t<2, false>(p, ctas, stream);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(gemv_reduce_kernel, dim3(p.units / p.upt, p.M), dim3(32 * kReduceWarps), 0, stream, 1, p);
 }
 
 }  // namespace nq

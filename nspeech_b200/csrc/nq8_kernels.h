@@ -15,38 +15,40 @@ namespace nq {
 struct GemvProblem {
   const uint8_t *w;  // packed tiles
   int n_tiles;       // ceil(N_pad / 128)
-  int kc_total;      // k chunks of 64
   int64_t N;         // logical output rows of W
   int glu;           // weight packed NQ_PACK_GLU
   int64_t n_out;     // output columns (N, or N/2 for GLU)
   const float *bias;
   void *y;
   int64_t ldy;
-  float *partials;  // [splits][n_tiles][M][128] f32 (split-K only)
-  int *counters;    // [n_tiles], zero between calls
+  float *partials;  // [upt][M][n_tiles * 128] f32: slot j holds unit j of every tile
 };
 
 struct GemvParams {
   GemvProblem prob[3];
-  const void *x;
-  int x_dtype;  // 0 f32, 1 bf16
-  int64_t ldx;
+  const __nv_bfloat16 *xh;  // activations: bf16 rows of ldx elements, zero beyond K up to kc * 64
+  const __nv_bfloat16 *xl;  // bf16(x - hi) rows for f32 activations, else null
+  int64_t ldx;              // multiple of 8 elements; xh / xl 16-byte aligned
   int M;
-  int64_t K;
   int epi;
   int y_dtype;
-  int splits;
-  int cps;       // k chunks per split
-  int nprob;     // problems (weights) sharing x
-  int tgroups;   // CTAs per split; CTA c takes split c % splits and every tgroups-th tile
+  int nprob;   // problems (weights) sharing x
+  int kc;      // 64-wide k chunks per tile (same for every problem)
+  int unit;    // k chunks per work unit
+  int upt;     // units per tile: ceil(kc / unit)
+  int units;   // units of all problems, tile-major
+  int ctas;    // CTAs launched; CTA c starts with unit c
+  int *sched;  // [0] work counter: zero between calls (gemv_reduce re-arms it)
   DevCtl ctl;
 };
 
-// Most k chunks per split whose activation slice fits the staging buffer.
-int gemv_max_cps(int m, bool splitx);
-size_t gemv_smem_bytes(int mrows, bool splitx, int cps);
-// Persistent launch of splits * tgroups CTAs.
-cudaError_t launch_gemv(const GemvParams &p, bool splitx, cudaStream_t stream);
+// Work split of one GEMV launch (fixed by the shape and the SM count).
+struct GemvPlan {
+  int unit, upt, units, ctas;
+};
+GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int m);
+// The GEMV (ctas CTAs) and its gemv_reduce: two launches.
+cudaError_t launch_gemv(const GemvParams &p, int ctas, cudaStream_t stream);
 
 // K1: fused Q8_0 GEMM (dequantizes in the kernel; best below a few thousand
 // tokens, where the weights dominate the traffic).

@@ -73,13 +73,13 @@ def test_noalloc_matches_linear_twice(nq, m, k, n, epi, glu, xdt):
 
 
 def test_noalloc_rejects_oversized_and_wide(nq):
-    """Split-K scratch beyond the static array, and M > 16, fail with a clear error."""
+    """Scratch beyond the static array, and M > 16, fail with a clear error."""
     L = nq.load()
     rng = np.random.default_rng(5)
-    w = _weight(nq, rng, 1024, 65536)  # 128 splits x 8 tiles x 8 KiB = 8 MiB of partials
-    x = torch.zeros((1, 65536), device="cuda")
-    y = torch.zeros((1, 1024), device="cuda")
-    rc = _call(L, L.nq_gemv_noalloc, w, x, 1, None, 0, y, 0)
+    w = _weight(nq, rng, 256, 65536)  # f32 x of 16 rows: hi + lo planes of 4 MiB > 2 MiB
+    x = torch.zeros((16, 65536), device="cuda")
+    y = torch.zeros((16, 256), device="cuda")
+    rc = _call(L, L.nq_gemv_noalloc, w, x, 16, None, 0, y, 0)
     assert rc == nq.NQ_ERR_SHAPE
     assert "static" in nq.last_error()
     w2 = _weight(nq, rng, 256, 256)
