@@ -322,6 +322,32 @@ __device__ __forceinline__ void dequant8_bf16(uint32_t w0, uint32_t w1, uint64_t
 }
 
 
+// Four int8 (one word) of one Q8_0 block -> two bf16x2 of bf16(f32(d) * q)
+// with the mixed-precision FMA (f16 operands, f32 result): a byte u' = q + 128
+// placed in the mantissa of f16 1024 gives the exact f16 value 1024 + u', and
+// fma((1024 + u'), d, -1152 d) = q d exactly (-1152 d is exact in f32 for an
+// f16 d; the sum needs at most 18 significant bits), so the single rounding
+// is the final cvt to bf16.  d16: the f16 bits of d; c: -1152 * f32(d).
+__device__ __forceinline__ void dequant4_bf16_mix(uint32_t w, uint16_t d16, float c, uint32_t &p01,
+                                                  uint32_t &p23) {
+  const uint32_t u = w ^ 0x80808080u;
+  const uint32_t h01 = __byte_perm(u, 0x64646464u, 0x4140);  // f16x2 (1024 + u'0, 1024 + u'1)
+  const uint32_t h23 = __byte_perm(u, 0x64646464u, 0x4342);  // f16x2 (1024 + u'2, 1024 + u'3)
+  float r0, r1, r2, r3;
+  asm("{\n\t.reg .f16 a0, a1, a2, a3, dd;\n\t"
+      "mov.b32 {a0, a1}, %4;\n\t"
+      "mov.b32 {a2, a3}, %5;\n\t"
+      "mov.b16 dd, %6;\n\t"
+      "fma.rn.f32.f16 %0, a0, dd, %7;\n\t"
+      "fma.rn.f32.f16 %1, a1, dd, %7;\n\t"
+      "fma.rn.f32.f16 %2, a2, dd, %7;\n\t"
+      "fma.rn.f32.f16 %3, a3, dd, %7;\n\t}"
+      : "=f"(r0), "=f"(r1), "=f"(r2), "=f"(r3)
+      : "r"(h01), "r"(h23), "h"(d16), "f"(c));
+  p01 = pack_bf16x2(r0, r1);
+  p23 = pack_bf16x2(r2, r3);
+}
+
 // Legacy warp-level MMA (used by the skinny GEMV where the tensor pipe is not
 // the bound): D(16x8) += A(16x16) . B(16x8), bf16 in, f32 accumulate.
 __device__ __forceinline__ void mma_16816_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,

@@ -21,10 +21,12 @@
 //             is fetched before the programmatic dependency wait and overlaps
 //             the previous kernel's tail.
 //   consumers: warp w owns rows [32w, 32w+32) of each tile as two 16-row
-//             groups: each lane reads 16 int8 of four rows, dequantizes them
-//             to bf16(d*q) and issues mma.m16n8k16 with the weight as the
-//             16-row operand and the activations (bf16 rows, read from
-//             global / L1 one chunk ahead) as the 8-column operand.  At the
+//             groups: ldmatrix hands each lane 16 int8 of four rows (four
+//             bytes from each 16-byte k quarter; whole 128-byte rows per
+//             matrix, so no bank conflicts), which it dequantizes to
+//             bf16(d*q) and feeds to mma.m16n8k16 as the 16-row operand, with
+//             the activations (bf16, the same k order, read from global / L1
+//             one chunk ahead) as the 8-column operand.  At the
 //             end of a unit each lane stores its accumulators to the unit's
 //             partial slot and goes on with the next unit.
 // gemv_reduce: one CTA per (tile, row of x) sums the tile's slots, applies
@@ -64,27 +66,36 @@ GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int m) {
   return g;
 }
 
-// Activation fragments of one 64-wide chunk for this lane: 16 bf16 of one row
-// (two 16-byte loads), zero for rows beyond M.
+// Activation fragments of one 64-wide chunk for this lane (g, c): for each
+// k quarter q the four bf16 at k = 16q + 4c .. +3 of its row (the k order of
+// the weight words ldsm_x4 hands the lane), zero for rows beyond M.
 template <int MT>
-__device__ __forceinline__ void load_x_chunk(uint4 (&v)[MT][2], const __nv_bfloat16 *const (&xr)[MT],
+__device__ __forceinline__ void load_x_chunk(uint2 (&v)[MT][4], const __nv_bfloat16 *const (&xr)[MT],
                                              const bool (&live)[MT], int ch) {
 #pragma unroll
   for (int mt = 0; mt < MT; ++mt) {
-    if (live[mt]) {
-      const uint4 *src = reinterpret_cast<const uint4 *>(xr[mt] + static_cast<size_t>(ch) * kPackK);
-      v[mt][0] = __ldg(src);
-      v[mt][1] = __ldg(src + 1);
-    } else {
-      v[mt][0] = make_uint4(0u, 0u, 0u, 0u);
-      v[mt][1] = make_uint4(0u, 0u, 0u, 0u);
-    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      v[mt][q] = live[mt] ? __ldg(reinterpret_cast<const uint2 *>(xr[mt] + static_cast<size_t>(ch) * kPackK + 16 * q))
+                          : make_uint2(0u, 0u);
   }
 }
 
-__device__ __forceinline__ uint2 xpair(const uint4 (&v)[2], int j) {
-  const uint4 &h = v[j >> 1];
-  return (j & 1) ? make_uint2(h.z, h.w) : make_uint2(h.x, h.y);
+// Four 8x8 b16 matrices from shared memory (lane i addresses row i % 8 of
+// matrix i / 8); lane (g, c) receives 32 bits [g][2c, 2c+1] of each.
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// c = -1152 * d exactly in f32, from the f16 bits of d (mixed-precision FMA).
+__device__ __forceinline__ float neg1152(uint16_t d16) {
+  float c;
+  asm("{\n\t.reg .f16 dd, m;\n\tmov.b16 dd, %1;\n\tmov.b16 m, 0xE480;\n\tfma.rn.f32.f16 %0, dd, m, 0f00000000;\n\t}"
+      : "=f"(c)
+      : "h"(d16));
+  return c;
 }
 
 
@@ -195,12 +206,16 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
     const int g4 = lane >> 2;
     const int c = lane & 3;
     const int M = p.M;
-    // rows of the two 16-row groups: (r0, r0 + 8), (r1, r1 + 8)
-    const int r0 = 32 * cw + g4, r1 = r0 + 16;
-    const int off0 = qs_offset(r0, c), off1 = qs_offset(r0 + 8, c);
-    const int off2 = qs_offset(r1, c), off3 = qs_offset(r1 + 8, c);
-    const int sof0 = scale_offset(r0, c >> 1), sof1 = scale_offset(r0 + 8, c >> 1);
-    const int sof2 = scale_offset(r1, c >> 1), sof3 = scale_offset(r1 + 8, c >> 1);
+    // Rows 32cw + 8b + g4 (b = 0..3): groups (b0, b1) and (b2, b3) are the
+    // (row, row + 8) halves of the two 16-row MMA operands.  ldsm_x4 block b:
+    // lane i addresses row 32cw + 8b + i % 8, k quarter i / 8.
+    uint32_t lofs[4], sofs[4][2];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      lofs[b] = qs_offset(32 * cw + 8 * b + (lane & 7), lane >> 3);
+      sofs[b][0] = scale_offset(32 * cw + 8 * b + g4, 0);
+      sofs[b][1] = scale_offset(32 * cw + 8 * b + g4, 1);
+    }
     const __nv_bfloat16 *xh[MT];
     const __nv_bfloat16 *xl[MT];
     bool live[MT];
@@ -208,12 +223,12 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
     for (int mt = 0; mt < MT; ++mt) {
       const int m = mt * 8 + g4;
       live[mt] = m < M;
-      xh[mt] = p.xh + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + c * 16;
-      xl[mt] = SPLITX ? p.xl + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + c * 16 : nullptr;
+      xh[mt] = p.xh + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + 4 * c;
+      xl[mt] = SPLITX ? p.xl + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + 4 * c : nullptr;
     }
     float acc[2][MT][4];
-    uint4 xc[MT][2], xcl[MT][2];
-    int s = 0, cur = -1, c_end = 0;
+    uint2 xc[MT][4], xcl[MT][4];
+    int s = 0, cur = -1, ch = 0, c_end = 0;
     uint32_t ph = 0;
     while (true) {
       const int st = s;
@@ -228,25 +243,11 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
         if (lane == 0 && !flags[0]) report(p.ctl, flags, kDevTimeoutConsumer);
         break;
       }
-      const int unit = meta[2 * st];
-      const int ch = meta[2 * st + 1];
-      if (unit < 0) break;  // end marker: no more units
-      const uint8_t *sp = ring + st * kTileBytes;
-      uint4 q[4];
-      q[0] = *reinterpret_cast<const uint4 *>(sp + off0);
-      q[1] = *reinterpret_cast<const uint4 *>(sp + off1);
-      q[2] = *reinterpret_cast<const uint4 *>(sp + off2);
-      q[3] = *reinterpret_cast<const uint4 *>(sp + off3);
-      float d[4];
-      d[0] = __half2float(*reinterpret_cast<const __half *>(sp + sof0));
-      d[1] = __half2float(*reinterpret_cast<const __half *>(sp + sof1));
-      d[2] = __half2float(*reinterpret_cast<const __half *>(sp + sof2));
-      d[3] = __half2float(*reinterpret_cast<const __half *>(sp + sof3));
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty_bar(st));
-      if (unit != cur) {
-        // first chunk of a unit: clear the accumulators, fetch its activations
-        cur = unit;
+      if (cur < 0) {
+        // first chunk of a unit (the stage's tag), or the end marker
+        cur = meta[2 * st];
+        if (cur < 0) break;
+        ch = meta[2 * st + 1];
         const int T = cur / p.upt;
         c_end = min((cur - T * p.upt + 1) * p.unit, kc);
 #pragma unroll
@@ -257,49 +258,55 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
             for (int e = 0; e < 4; ++e) acc[gi][mt][e] = 0.f;
         load_x_chunk<MT>(xc, xh, live, ch);
         if (SPLITX) load_x_chunk<MT>(xcl, xl, live, ch);
+      } else {
+        ++ch;  // units are streamed chunk after chunk
       }
+      const uint8_t *sp = ring + st * kTileBytes;
+      const uint32_t sa = smem_u32(sp);
+      uint32_t R[4][4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) ldsm_x4(sa + lofs[b], R[b]);
+      uint16_t dv[4][2];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        dv[b][0] = *reinterpret_cast<const uint16_t *>(sp + sofs[b][0]);
+        dv[b][1] = *reinterpret_cast<const uint16_t *>(sp + sofs[b][1]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(st));
       const bool more = ch + 1 < c_end;
       // next chunk's activations, one chunk ahead of their use
-      uint4 xn[MT][2], xnl[MT][2];
+      uint2 xn[MT][4], xnl[MT][4];
       if (more) {
         load_x_chunk<MT>(xn, xh, live, ch + 1);
         if (SPLITX) load_x_chunk<MT>(xnl, xl, live, ch + 1);
       }
 #pragma unroll
       for (int gi = 0; gi < 2; ++gi) {
-        // bf16(f32(d) * q), eight elements per call with packed f32x2 arithmetic
-        uint32_t oa[8], ob[8];
-        const uint64_t dda = f2(d[2 * gi], d[2 * gi]), ddb = f2(d[2 * gi + 1], d[2 * gi + 1]);
-        const uint4 &qa = q[2 * gi], &qb = q[2 * gi + 1];
-        dequant8_bf16(qa.x, qa.y, dda, oa);
-        dequant8_bf16(qa.z, qa.w, dda, oa + 4);
-        dequant8_bf16(qb.x, qb.y, ddb, ob);
-        dequant8_bf16(qb.z, qb.w, ddb, ob + 4);
+        const int ba = 2 * gi, bb = 2 * gi + 1;
+        const float ca[2] = {neg1152(dv[ba][0]), neg1152(dv[ba][1])};
+        const float cb[2] = {neg1152(dv[bb][0]), neg1152(dv[bb][1])};
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          // A fragment of word j: rows (a, b) x k pairs (4j, 4j+1), (4j+2, 4j+3)
-          const uint32_t a[4] = {oa[2 * j], ob[2 * j], oa[2 * j + 1], ob[2 * j + 1]};
+        for (int q = 0; q < 4; ++q) {
+          // bf16(f32(d) * q) of the lane's word in k quarter q (Q8_0 block q / 2)
+          uint32_t a[4];
+          dequant4_bf16_mix(R[ba][q], dv[ba][q >> 1], ca[q >> 1], a[0], a[2]);
+          dequant4_bf16_mix(R[bb][q], dv[bb][q >> 1], cb[q >> 1], a[1], a[3]);
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
-            const uint2 xv = xpair(xc[mt], j);
-            mma_16816_bf16(acc[gi][mt], a, xv.x, xv.y);
-            if (SPLITX) {
-              const uint2 xw = xpair(xcl[mt], j);
-              mma_16816_bf16(acc[gi][mt], a, xw.x, xw.y);
-            }
+            mma_16816_bf16(acc[gi][mt], a, xc[mt][q].x, xc[mt][q].y);
+            if (SPLITX) mma_16816_bf16(acc[gi][mt], a, xcl[mt][q].x, xcl[mt][q].y);
           }
         }
       }
       if (more) {
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt) {
-          xc[mt][0] = xn[mt][0];
-          xc[mt][1] = xn[mt][1];
-          if (SPLITX) {
-            xcl[mt][0] = xnl[mt][0];
-            xcl[mt][1] = xnl[mt][1];
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            xc[mt][q] = xn[mt][q];
+            if (SPLITX) xcl[mt][q] = xnl[mt][q];
           }
-        }
       } else {
         // end of the unit: its partial slot [j][M][ldp] of the problem
         const int T = cur / p.upt;
@@ -310,7 +317,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
         float *base = pr.partials + static_cast<size_t>(j) * M * ldp + static_cast<size_t>(tl) * kPackRows;
 #pragma unroll
         for (int gi = 0; gi < 2; ++gi) {
-          const int ra = gi ? r1 : r0;
+          const int ra = 32 * cw + 16 * gi + g4;
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt) {
             const int m0 = mt * 8 + 2 * c;
