@@ -45,7 +45,7 @@ constexpr int kGemvConsumers = 32 * kGemvConsumerWarps;
 constexpr int kGemvThreads = 32 + kGemvConsumers;  // producer warp, consumers
 constexpr int kGemvCtasPerSm = 4;
 constexpr int kGemvStages = 6;
-constexpr int kGemvUnitsPerCta = 6;  // scheduling granularity target
+constexpr int kGemvSlotsPerTile = 32;  // scheduling granularity target
 constexpr size_t kGemvMetaOff = static_cast<size_t>(kGemvStages) * kTileBytes;     // int2 (unit, chunk) per stage
 constexpr size_t kGemvBarOff = kGemvMetaOff + kGemvStages * 2 * sizeof(int);      // full, empty
 constexpr size_t kGemvFlagOff = kGemvBarOff + 2 * kGemvStages * sizeof(uint64_t);  // abort flag
@@ -54,11 +54,12 @@ constexpr size_t kGemvSmemBytes = kGemvFlagOff + 16;
 GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int m) {
   GemvPlan g;
   const int64_t slots = static_cast<int64_t>(kGemvCtasPerSm) * sm_count;
-  const int64_t work = static_cast<int64_t>(total_tiles) * kc;
-  // About kGemvUnitsPerCta units per CTA; at least two chunks, and at least
-  // M/2 so that the f32 partials stay a small fraction of the weight bytes.
-  int64_t u = work / (kGemvUnitsPerCta * slots);
-  u = std::max<int64_t>(u, std::max(2, (m + 1) / 2));
+  // About kGemvSlotsPerTile units per tile (measured on B200 from 640 x 640
+  // to 16384 x 16384: fewer, longer units leave a longer tail, more slots
+  // cost partial traffic and a longer sum), at least two chunks, and at
+  // least M/2 so that the f32 partials stay a small share of the bytes.
+  int64_t u = std::max<int64_t>(2, (kc + kGemvSlotsPerTile - 1) / kGemvSlotsPerTile);
+  u = std::max<int64_t>(u, (m + 1) / 2);
   g.unit = static_cast<int>(std::min<int64_t>(u, kc));
   g.upt = (kc + g.unit - 1) / g.unit;
   g.units = total_tiles * g.upt;
@@ -156,6 +157,7 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
         }
       };
       int u = blockIdx.x;
+      bool have_stage = false;  // a free stage is already waited for
       while (ok && u < p.units) {
         const int T = u / p.upt;
         const int c0 = (u - T * p.upt) * p.unit;
@@ -164,7 +166,8 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
         const GemvProblem &pr = p.prob[tile_prob(T, tl)];
         const uint8_t *src = pr.w + (static_cast<size_t>(tl) * kc + c0) * kTileBytes;
         for (int ch = c0; ch < c1; ++ch, src += kTileBytes) {
-          next_stage(ok);
+          if (!have_stage) next_stage(ok);
+          have_stage = false;
           if (!ok) break;
           meta[2 * s] = u;
           meta[2 * s + 1] = ch;
@@ -180,11 +183,17 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
           pdl_wait();  // the previous launch's gemv_reduce re-armed the work counter
           waited = true;
         }
+        // Take the next unit only once a stage is free: a CTA holds at most
+        // its ring of chunks beyond the unit being computed, which bounds the
+        // imbalance when the work runs out.
+        next_stage(ok);
+        if (!ok) break;
+        have_stage = true;
         u = p.ctas + atomicAdd(p.sched, 1);
       }
       if (ok) {
         // end marker: a stage whose phase completes with no copy
-        next_stage(ok);
+        if (!have_stage) next_stage(ok);
         if (ok) {
           meta[2 * s] = -1;
           mbar_arrive(full_bar(s));
@@ -338,12 +347,12 @@ __global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(c
   __syncthreads();
 }
 
-// Sum of a tile's unit partials for one row of x: warp w adds slots w, w+4,
-// w+8, ... in order (each lane four outputs), then the four warp sums are
+// Sum of a tile's unit partials for one row of x: warp w adds slots w, w+8,
+// w+16, ... in order (each lane four outputs), then the eight warp sums are
 // added in warp order -- a fixed order, so the result does not depend on
 // which CTA computed which unit.  Then bias / activation / GLU and the store;
 // the first CTA re-arms the GEMV's work counter for the next launch.
-constexpr int kReduceWarps = 4;
+constexpr int kReduceWarps = 8;
 
 __global__ void __launch_bounds__(32 * kReduceWarps) gemv_reduce_kernel(const __grid_constant__ GemvParams p) {
   pdl_wait();  // the GEMV's partials are complete and visible
@@ -402,7 +411,7 @@ __global__ void __launch_bounds__(32 * kReduceWarps) gemv_reduce_kernel(const __
     }
   } else {
     const int64_t j = static_cast<int64_t>(tl) * kPackRows + r;
-    if (j < pr.N) {
+    if (r < kPackRows && j < pr.N) {
       float v = tot[r];
       if (pr.bias) v += pr.bias[j];
       store_out(pr.y, p.y_dtype, m * pr.ldy + j, act_single(p.epi, v));
