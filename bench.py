@@ -10,11 +10,18 @@ are independent (segment sharding, no collective on the data path; one
 all-reduce of the timings after the timed region): weak scaling.
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python bench.py --gemv [--gemv-shapes MxKxN,...] [--gemv-plain CALLS]
 
 Prints one JSON line (rank 0).  `value`: RTFx = audio seconds of all ranks /
 max-over-ranks device time of K steps, inputs resident in HBM.  `e2e`: the
 same through the public host-buffer entry point (H2D of the mel features and
 D2H of the encoder output inside the timed region).
+
+`--gemv` instead times the Q8_0 GEMV (M <= 16, the decode-step projections)
+alone: per shape, a CUDA graph of back-to-back nq_linear calls over enough
+weight copies to stream past L2, reported as device time per call and HBM
+GB/s (weight + x + y bytes) against the measured peak; one JSON line.
+`--gemv-plain CALLS` only makes CALLS plain calls per shape (for ncu).
 """
 from __future__ import annotations
 
@@ -52,6 +59,10 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-s", type=float, default=10.0, help="audio seconds of the CPU-baseline sample")
+    ap.add_argument("--gemv", action="store_true", help="time the Q8_0 GEMV alone instead of the encoder")
+    ap.add_argument("--gemv-shapes", default="1x640x640,1x640x2560,1x2560x640,1x4096x4096,1x8192x8192,"
+                    "1x640x32768,8x4096x4096,16x4096x4096,1x16384x16384")
+    ap.add_argument("--gemv-plain", type=int, default=0, help="only make this many plain calls per shape")
     return ap.parse_args()
 
 
@@ -368,6 +379,64 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_gemv_sweep(args) -> None:
+    """Graph-timed Q8_0 GEMV per shape (synthetic Q8_0 weights, bf16 x and y)."""
+    import torch
+    from nspeech_b200 import lib
+    from nspeech_b200.fast_matmul import QWeight
+    torch.cuda.set_device(0)
+    lib.init(0)
+    pk = peaks()
+    rng = np.random.default_rng(0)
+    rows = []
+    for shp in args.gemv_shapes.split(","):
+        m, k, n = (int(v) for v in shp.split("x"))
+        q = rng.integers(0, 256, size=(n, k // 32, 34), dtype=np.uint8)
+        q[:, :, :2] = (rng.random((n, k // 32)) * 1e-3 + 1e-4).astype(np.float16).view(np.uint8).reshape(n, k // 32, 2)
+        blocks = np.ascontiguousarray(q.reshape(n, -1))
+        wbytes = n * k * 34 / 32
+        copies = 1 if args.gemv_plain else int(min(64, max(2, np.ceil(400e6 / wbytes))))
+        ws = [QWeight.from_q8_0(blocks, n, k) for _ in range(copies)]
+        x = torch.randn(m, k, device="cuda").bfloat16()
+        y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        if args.gemv_plain:
+            for _ in range(args.gemv_plain):
+                ws[0].linear(x, out=y)
+            torch.cuda.synchronize()
+            continue
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            for w in ws:
+                w.linear(x, out=y)  # workspace sized before capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for w in ws:
+                w.linear(x, out=y)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize()
+        reps = max(3, 200 // copies)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (reps * copies)
+        byts = wbytes + m * k * 2 + m * n * 2
+        rows.append({"m": m, "k": k, "n": n, "us": round(us, 2), "gbs": round(byts / us / 1e3, 1),
+                     "frac_hbm": round(byts / us / 1e3 / pk["hbm_gbs"], 3)})
+        del g, ws
+        torch.cuda.empty_cache()
+    if lib.status() != 0:
+        raise RuntimeError("device status bits set after the GEMV sweep")
+    if not args.gemv_plain:
+        print(json.dumps({"metric": "Q8_0 GEMV HBM GB/s (graph of back-to-back calls, weights past L2)",
+                          "peak_hbm_gbs": pk["hbm_gbs"], "peak_source": pk.get("source", "measured"),
+                          "shapes": rows}), flush=True)
+
+
 def main():
     args = parse_args()
     rank = int(os.environ.get("RANK", 0))
@@ -375,6 +444,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", 0))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.gemv:
+        run_gemv_sweep(args)
         return
     if world > 1:
         # stdout carries exactly one JSON line: keep NCCL's version banner off it
