@@ -233,7 +233,12 @@ int nq_encoder_out_frames(int t_mel);
  * [batch, T, d_model] with T = nq_encoder_out_frames(t_mel), frames beyond a
  * segment's own length zeroed; out_lengths (host, may be NULL) receives the
  * per-segment encoder lengths.  Replaces TransducerModel::run_encoder
- * (src/parakeet/transducer.rs:387-404) for a batch of VAD segments. */
+ * (src/parakeet/transducer.rs:387-404) for a batch of VAD segments.
+ * Each stream gets its own activation arena (allocated on its first
+ * forward, grown for larger batches): forwards on one stream run in stream
+ * order, forwards on different streams share only the weights and may run
+ * concurrently (two streams fill the GPU while one forward's kernels leave
+ * SMs idle). */
 int nq_encoder_forward(nq_encoder *enc, const float *mel, const int32_t *lengths, int batch, int t_mel,
                        float *out, int32_t *out_lengths, void *stream);
 

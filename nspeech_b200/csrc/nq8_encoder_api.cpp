@@ -9,6 +9,7 @@
 #include <cstring>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -61,6 +62,29 @@ struct Layer {
 
 }  // namespace
 
+// The buffers of one forward (sized for the largest batch seen), and the ring
+// of pinned host slots through which each forward's segment lengths (4 x
+// batch ints) travel, each slot reused only after its previous copy
+// completed.
+struct Arena {
+  DevBuf x, h, t, u, u32, qkv, pos, krel, att, g, c, s1, s2a, s2b, s3a, s3b, flat, mel_in, out_buf;
+  static constexpr int kLenSlots = 4;
+  DevBuf lens[kLenSlots];
+  int *lens_host[kLenSlots] = {nullptr, nullptr, nullptr, nullptr};
+  cudaEvent_t lens_done[kLenSlots] = {nullptr, nullptr, nullptr, nullptr};
+  int lens_cap = 0;
+  int lens_next = 0;
+  ~Arena() {
+    for (int i = 0; i < kLenSlots; ++i) {
+      if (lens_done[i]) {
+        cudaEventSynchronize(lens_done[i]);
+        cudaEventDestroy(lens_done[i]);
+      }
+      if (lens_host[i]) cudaFreeHost(lens_host[i]);
+    }
+  }
+};
+
 struct nq_encoder {
   nq_encoder_config cfg{};
   int device = 0;
@@ -76,16 +100,11 @@ struct nq_encoder {
   // they depend only on the positions, so one GEMM per forward serves all
   // layers (krel holds [2T-1][n_layers * d]).
   nq_weight *rel_all = nullptr;
-  // activation arena
-  DevBuf x, h, t, u, u32, qkv, pos, krel, att, g, c, s1, s2a, s2b, s3a, s3b, flat, mel_in, out_buf;
-  // Per-forward segment lengths (4 x batch ints) travel through a ring of
-  // pinned host slots, each reused only after its previous copy completed.
-  static constexpr int kLenSlots = 4;
-  DevBuf lens[kLenSlots];
-  int *lens_host[kLenSlots] = {nullptr, nullptr, nullptr, nullptr};
-  cudaEvent_t lens_done[kLenSlots] = {nullptr, nullptr, nullptr, nullptr};
-  int lens_cap = 0;
-  int lens_next = 0;
+  // Activation arenas, one per stream (created on a stream's first forward):
+  // forwards on one stream reuse its arena in stream order; forwards on
+  // different streams have their own and may run concurrently.
+  std::mutex arena_mu;
+  std::map<cudaStream_t, std::unique_ptr<Arena>> arenas;
 
   // nq_encoder_forward_host_async: two device staging slots (mel in, output
   // out) used in turn, copies on their own streams ordered by events.
@@ -106,12 +125,9 @@ struct nq_encoder {
         if (ev) cudaEventDestroy(ev);
     if (h2d_stream) cudaStreamDestroy(h2d_stream);
     if (d2h_stream) cudaStreamDestroy(d2h_stream);
+    arenas.clear();
     for (auto *w : weights) nq_weight_free(w);
     for (auto *p : dev_allocs) cudaFree(p);
-    for (int i = 0; i < kLenSlots; ++i) {
-      if (lens_host[i]) cudaFreeHost(lens_host[i]);
-      if (lens_done[i]) cudaEventDestroy(lens_done[i]);
-    }
   }
 };
 
@@ -342,35 +358,42 @@ Shapes shapes(const nq_encoder *e, int batch, int t_mel) {
   return s;
 }
 
-int ensure_arena(nq_encoder *e, const Shapes &s) {
+Arena *arena_for(nq_encoder *e, cudaStream_t st) {
+  std::lock_guard<std::mutex> lk(e->arena_mu);
+  std::unique_ptr<Arena> &a = e->arenas[st];
+  if (!a) a.reset(new Arena());
+  return a.get();
+}
+
+int ensure_arena(nq_encoder *e, Arena &A, const Shapes &s) {
   const size_t M = s.M, D = s.D, ff = static_cast<size_t>(D) * e->cfg.ff_mult;
   const size_t P = 2 * static_cast<size_t>(s.T3) - 1;
-  NQ_TRY(e->x.ensure(M * D * 4));
-  NQ_TRY(e->h.ensure(M * D * 2));
-  NQ_TRY(e->t.ensure(M * ff * 2));
-  NQ_TRY(e->u.ensure(M * D * 2));
-  NQ_TRY(e->u32.ensure(M * D * 4));
-  NQ_TRY(e->qkv.ensure(M * 3 * D * 2));
-  NQ_TRY(e->pos.ensure(P * D * 2));
-  NQ_TRY(e->krel.ensure(P * D * e->cfg.n_layers * 2));
-  NQ_TRY(e->att.ensure(M * D * 2));
-  NQ_TRY(e->g.ensure(M * D * 2));
-  NQ_TRY(e->c.ensure(M * D * 2));
-  if (!nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C)) NQ_TRY(e->s1.ensure(static_cast<size_t>(s.B) * s.T1 * s.F1 * s.C * 2));
-  NQ_TRY(e->s2a.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
-  NQ_TRY(e->s2b.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
-  NQ_TRY(e->s3a.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
-  NQ_TRY(e->s3b.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
-  NQ_TRY(e->flat.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
-  if (e->lens_cap < s.B) {
-    for (int i = 0; i < nq_encoder::kLenSlots; ++i) {
-      if (e->lens_done[i]) NQ_CUDA(cudaEventSynchronize(e->lens_done[i]));
-      if (e->lens_host[i]) cudaFreeHost(e->lens_host[i]);
-      NQ_CUDA(cudaMallocHost(&e->lens_host[i], static_cast<size_t>(4) * s.B * sizeof(int)));
-      NQ_TRY(e->lens[i].ensure(static_cast<size_t>(4) * s.B * sizeof(int)));
-      if (!e->lens_done[i]) NQ_CUDA(cudaEventCreateWithFlags(&e->lens_done[i], cudaEventDisableTiming));
+  NQ_TRY(A.x.ensure(M * D * 4));
+  NQ_TRY(A.h.ensure(M * D * 2));
+  NQ_TRY(A.t.ensure(M * ff * 2));
+  NQ_TRY(A.u.ensure(M * D * 2));
+  NQ_TRY(A.u32.ensure(M * D * 4));
+  NQ_TRY(A.qkv.ensure(M * 3 * D * 2));
+  NQ_TRY(A.pos.ensure(P * D * 2));
+  NQ_TRY(A.krel.ensure(P * D * e->cfg.n_layers * 2));
+  NQ_TRY(A.att.ensure(M * D * 2));
+  NQ_TRY(A.g.ensure(M * D * 2));
+  NQ_TRY(A.c.ensure(M * D * 2));
+  if (!nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C)) NQ_TRY(A.s1.ensure(static_cast<size_t>(s.B) * s.T1 * s.F1 * s.C * 2));
+  NQ_TRY(A.s2a.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
+  NQ_TRY(A.s2b.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
+  NQ_TRY(A.s3a.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
+  NQ_TRY(A.s3b.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
+  NQ_TRY(A.flat.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
+  if (A.lens_cap < s.B) {
+    for (int i = 0; i < Arena::kLenSlots; ++i) {
+      if (A.lens_done[i]) NQ_CUDA(cudaEventSynchronize(A.lens_done[i]));
+      if (A.lens_host[i]) cudaFreeHost(A.lens_host[i]);
+      NQ_CUDA(cudaMallocHost(&A.lens_host[i], static_cast<size_t>(4) * s.B * sizeof(int)));
+      NQ_TRY(A.lens[i].ensure(static_cast<size_t>(4) * s.B * sizeof(int)));
+      if (!A.lens_done[i]) NQ_CUDA(cudaEventCreateWithFlags(&A.lens_done[i], cudaEventDisableTiming));
     }
-    e->lens_cap = s.B;
+    A.lens_cap = s.B;
   }
   return NQ_OK;
 }
@@ -380,11 +403,12 @@ int ensure_arena(nq_encoder *e, const Shapes &s) {
 int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, int t_mel, float *out,
             int32_t *out_lengths, cudaStream_t st) {
   const Shapes s = shapes(e, batch, t_mel);
-  NQ_TRY(ensure_arena(e, s));
-  const int slot = e->lens_next;
-  e->lens_next = (slot + 1) % nq_encoder::kLenSlots;
-  NQ_CUDA(cudaEventSynchronize(e->lens_done[slot]));  // its previous upload has been consumed
-  int *lh = e->lens_host[slot];
+  Arena &A = *arena_for(e, st);
+  NQ_TRY(ensure_arena(e, A, s));
+  const int slot = A.lens_next;
+  A.lens_next = (slot + 1) % Arena::kLenSlots;
+  NQ_CUDA(cudaEventSynchronize(A.lens_done[slot]));  // its previous upload has been consumed
+  int *lh = A.lens_host[slot];
   for (int b = 0; b < batch; ++b) {
     const int L0 = lengths ? lengths[b] : t_mel;
     if (L0 < 1 || L0 > t_mel) return api_fail(NQ_ERR_SHAPE, "segment length out of range [1, t_mel]");
@@ -394,42 +418,42 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
     lh[3 * batch + b] = sub_len(lh[2 * batch + b]);
     if (out_lengths) out_lengths[b] = lh[3 * batch + b];
   }
-  int *ld = e->lens[slot].as<int>();
+  int *ld = A.lens[slot].as<int>();
   NQ_CUDA(cudaMemcpyAsync(ld, lh, static_cast<size_t>(4) * batch * sizeof(int), cudaMemcpyHostToDevice, st));
-  NQ_CUDA(cudaEventRecord(e->lens_done[slot], st));
+  NQ_CUDA(cudaEventRecord(A.lens_done[slot], st));
   const int *L0 = ld, *L1 = ld + batch, *L2 = ld + 2 * batch, *L3 = ld + 3 * batch;
   const auto &c = e->cfg;
   const int D = s.D, H = c.n_heads, FF = D * c.ff_mult, M = s.M, Tp = s.T3;
   void *stv = st;
   const float eps = 1e-5f;
-  __nv_bfloat16 *h = e->h.as<__nv_bfloat16>(), *t = e->t.as<__nv_bfloat16>(), *u = e->u.as<__nv_bfloat16>();
-  float *x = e->x.as<float>();
+  __nv_bfloat16 *h = A.h.as<__nv_bfloat16>(), *t = A.t.as<__nv_bfloat16>(), *u = A.u.as<__nv_bfloat16>();
+  float *x = A.x.as<float>();
 
   // --- subsampling (fast_conformer.rs:172-188)
   if (nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C)) {
     NQ_K(nq::enc::conv0_dw_s2(mel, L0, L1, s.B, s.Tm, s.F, s.T1, s.F1, s.T2, s.F2, s.C, e->c0_w, e->c0_b, e->dw2_w,
-                              e->dw2_b, e->s2a.as<__nv_bfloat16>(), st));
+                              e->dw2_b, A.s2a.as<__nv_bfloat16>(), st));
   } else {
-    NQ_K(nq::enc::conv0_relu(mel, L0, s.B, s.Tm, s.F, s.T1, s.F1, s.C, e->c0_w, e->c0_b, e->s1.as<__nv_bfloat16>(), st));
-    NQ_K(nq::enc::dwconv2d_s2(e->s1.as<__nv_bfloat16>(), L1, s.B, s.T1, s.F1, s.T2, s.F2, s.C, e->dw2_w, e->dw2_b,
-                              e->s2a.as<__nv_bfloat16>(), st));
+    NQ_K(nq::enc::conv0_relu(mel, L0, s.B, s.Tm, s.F, s.T1, s.F1, s.C, e->c0_w, e->c0_b, A.s1.as<__nv_bfloat16>(), st));
+    NQ_K(nq::enc::dwconv2d_s2(A.s1.as<__nv_bfloat16>(), L1, s.B, s.T1, s.F1, s.T2, s.F2, s.C, e->dw2_w, e->dw2_b,
+                              A.s2a.as<__nv_bfloat16>(), st));
   }
-  NQ_TRY(nq_linear(e->pw3, e->s2a.p, NQ_BF16, static_cast<int64_t>(s.B) * s.T2 * s.F2, s.C, e->pw3_b, NQ_EPI_RELU,
-                   e->s2b.p, NQ_BF16, s.C, stv));
-  NQ_K(nq::enc::dwconv2d_s2(e->s2b.as<__nv_bfloat16>(), L2, s.B, s.T2, s.F2, s.T3, s.F3, s.C, e->dw5_w, e->dw5_b,
-                            e->s3a.as<__nv_bfloat16>(), st));
-  NQ_TRY(nq_linear(e->pw6, e->s3a.p, NQ_BF16, static_cast<int64_t>(s.B) * s.T3 * s.F3, s.C, e->pw6_b, NQ_EPI_RELU,
-                   e->s3b.p, NQ_BF16, s.C, stv));
-  NQ_K(nq::enc::flatten_cf(e->s3b.as<__nv_bfloat16>(), M, s.F3, s.C, e->flat.as<__nv_bfloat16>(), st));
-  NQ_TRY(nq_linear(e->lin, e->flat.p, NQ_BF16, M, static_cast<int64_t>(s.F3) * s.C, e->lin_b, NQ_EPI_NONE, e->u32.p,
+  NQ_TRY(nq_linear(e->pw3, A.s2a.p, NQ_BF16, static_cast<int64_t>(s.B) * s.T2 * s.F2, s.C, e->pw3_b, NQ_EPI_RELU,
+                   A.s2b.p, NQ_BF16, s.C, stv));
+  NQ_K(nq::enc::dwconv2d_s2(A.s2b.as<__nv_bfloat16>(), L2, s.B, s.T2, s.F2, s.T3, s.F3, s.C, e->dw5_w, e->dw5_b,
+                            A.s3a.as<__nv_bfloat16>(), st));
+  NQ_TRY(nq_linear(e->pw6, A.s3a.p, NQ_BF16, static_cast<int64_t>(s.B) * s.T3 * s.F3, s.C, e->pw6_b, NQ_EPI_RELU,
+                   A.s3b.p, NQ_BF16, s.C, stv));
+  NQ_K(nq::enc::flatten_cf(A.s3b.as<__nv_bfloat16>(), M, s.F3, s.C, A.flat.as<__nv_bfloat16>(), st));
+  NQ_TRY(nq_linear(e->lin, A.flat.p, NQ_BF16, M, static_cast<int64_t>(s.F3) * s.C, e->lin_b, NQ_EPI_NONE, A.u32.p,
                    NQ_F32, D, stv));
   const float alpha = c.scale_input ? std::sqrt(static_cast<float>(D)) : 1.0f;
   const Layer &L_0 = e->layers[0];
-  NQ_K(nq::enc::ln_rows(nq::enc::kLnScale, x, e->u32.p, alpha, M, D, L_0.ln_ff1_g, L_0.ln_ff1_b, nullptr, nullptr, h,
+  NQ_K(nq::enc::ln_rows(nq::enc::kLnScale, x, A.u32.p, alpha, M, D, L_0.ln_ff1_g, L_0.ln_ff1_b, nullptr, nullptr, h,
                         eps, st));
-  NQ_K(nq::enc::relpos(Tp, D, e->pos.as<__nv_bfloat16>(), st));
+  NQ_K(nq::enc::relpos(Tp, D, A.pos.as<__nv_bfloat16>(), st));
   // relative keys of every layer: krel[p][li * D + :] = pos[p] . W_rel(li)^T
-  NQ_TRY(nq_linear(e->rel_all, e->pos.p, NQ_BF16, 2 * Tp - 1, D, nullptr, NQ_EPI_NONE, e->krel.p, NQ_BF16,
+  NQ_TRY(nq_linear(e->rel_all, A.pos.p, NQ_BF16, 2 * Tp - 1, D, nullptr, NQ_EPI_NONE, A.krel.p, NQ_BF16,
                    static_cast<int64_t>(c.n_layers) * D, stv));
 
   for (int li = 0; li < c.n_layers; ++li) {
@@ -439,17 +463,17 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
     NQ_TRY(nq_linear(L.ff1_w2, t, NQ_BF16, M, FF, L.ff1_b2, NQ_EPI_NONE, u, NQ_BF16, D, stv));
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 0.5f, M, D, L.ln_mha_g, L.ln_mha_b, nullptr, nullptr, h, eps, st));
     // MHSA with relative positions -> norm_conv
-    NQ_TRY(nq_linear(L.qkv, h, NQ_BF16, M, D, L.qkv_b, NQ_EPI_NONE, e->qkv.p, NQ_BF16, 3 * D, stv));
-    NQ_K(nq::enc::relpos_attention(e->qkv.as<__nv_bfloat16>(), e->krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
+    NQ_TRY(nq_linear(L.qkv, h, NQ_BF16, M, D, L.qkv_b, NQ_EPI_NONE, A.qkv.p, NQ_BF16, 3 * D, stv));
+    NQ_K(nq::enc::relpos_attention(A.qkv.as<__nv_bfloat16>(), A.krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
                                    static_cast<int64_t>(c.n_layers) * D, L.bias_u, L.bias_v, L3,
-                                   s.B, Tp, H, D, e->att.as<__nv_bfloat16>(), st));
-    NQ_TRY(nq_linear(L.o, e->att.p, NQ_BF16, M, D, L.o_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
+                                   s.B, Tp, H, D, A.att.as<__nv_bfloat16>(), st));
+    NQ_TRY(nq_linear(L.o, A.att.p, NQ_BF16, M, D, L.o_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_conv_g, L.ln_conv_b, nullptr, nullptr, h, eps, st));
     // Conv module -> norm_feed_forward2
-    NQ_TRY(nq_linear(L.pw1, h, NQ_BF16, M, D, L.pw1_b, NQ_EPI_GLU_SIGMOID, e->g.p, NQ_BF16, D, stv));
-    NQ_K(nq::enc::dwconv1d_bn_silu(e->g.as<__nv_bfloat16>(), L3, s.B, Tp, D, c.conv_kernel, L.dw_w, L.dw_b, L.bn_scale,
-                                   L.bn_shift, e->c.as<__nv_bfloat16>(), st));
-    NQ_TRY(nq_linear(L.pw2, e->c.p, NQ_BF16, M, D, L.pw2_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
+    NQ_TRY(nq_linear(L.pw1, h, NQ_BF16, M, D, L.pw1_b, NQ_EPI_GLU_SIGMOID, A.g.p, NQ_BF16, D, stv));
+    NQ_K(nq::enc::dwconv1d_bn_silu(A.g.as<__nv_bfloat16>(), L3, s.B, Tp, D, c.conv_kernel, L.dw_w, L.dw_b, L.bn_scale,
+                                   L.bn_shift, A.c.as<__nv_bfloat16>(), st));
+    NQ_TRY(nq_linear(L.pw2, A.c.p, NQ_BF16, M, D, L.pw2_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_ff2_g, L.ln_ff2_b, nullptr, nullptr, h, eps, st));
     // FF2 (x0.5) -> norm_out (-> next layer's norm_feed_forward1)
     NQ_TRY(nq_linear(L.ff2_w1, h, NQ_BF16, M, D, L.ff2_b1, NQ_EPI_SILU, t, NQ_BF16, FF, stv));
@@ -554,11 +578,12 @@ int nq_encoder_forward_host(nq_encoder *enc, const float *mel_host, const int32_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t in_bytes = static_cast<size_t>(batch) * t_mel * enc->cfg.feat_in * sizeof(float);
   const size_t out_bytes = static_cast<size_t>(batch) * nq_encoder_out_frames(t_mel) * enc->cfg.d_model * sizeof(float);
-  NQ_TRY(enc->mel_in.ensure(in_bytes));
-  NQ_TRY(enc->out_buf.ensure(out_bytes));
-  NQ_CUDA(cudaMemcpyAsync(enc->mel_in.p, mel_host, in_bytes, cudaMemcpyHostToDevice, st));
-  NQ_TRY(forward(enc, enc->mel_in.as<float>(), lengths, batch, t_mel, enc->out_buf.as<float>(), out_lengths, st));
-  NQ_CUDA(cudaMemcpyAsync(out_host, enc->out_buf.p, out_bytes, cudaMemcpyDeviceToHost, st));
+  Arena &A = *arena_for(enc, st);
+  NQ_TRY(A.mel_in.ensure(in_bytes));
+  NQ_TRY(A.out_buf.ensure(out_bytes));
+  NQ_CUDA(cudaMemcpyAsync(A.mel_in.p, mel_host, in_bytes, cudaMemcpyHostToDevice, st));
+  NQ_TRY(forward(enc, A.mel_in.as<float>(), lengths, batch, t_mel, A.out_buf.as<float>(), out_lengths, st));
+  NQ_CUDA(cudaMemcpyAsync(out_host, A.out_buf.p, out_bytes, cudaMemcpyDeviceToHost, st));
   NQ_CUDA(cudaStreamSynchronize(st));
   return NQ_OK;
 }

@@ -201,3 +201,45 @@ def test_forward_host_async_queue_matches_sync(nq, oracle):
         ref, rl = enc.forward_host(mel.numpy(), lens)
         assert gl == rl
         np.testing.assert_array_equal(out.numpy(), ref)
+
+
+def test_forwards_on_two_streams_match_one_stream(nq, oracle):
+    """Forwards alternating over two streams (own activation arena each, running
+    concurrently) give bit-identical outputs to the same forwards on one stream."""
+    from nspeech_b200 import synthetic as S
+    from nspeech_b200.encoder import out_frames
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=2, sub_channels=64)
+    enc = _gpu_encoder(spec, _model(oracle, spec, seed=11))
+    shapes = [(4, 700), (2, 300), (3, 512), (1, 180), (4, 640), (2, 300)]
+    mels = [torch.from_numpy(oracle.normal(40 + i, (b, t, 128))).cuda() for i, (b, t) in enumerate(shapes)]
+    lens = [[t - 5 * j for j in range(b)] for b, t in shapes]
+    ref = []
+    for m, l in zip(mels, lens):
+        o = torch.empty((m.shape[0], out_frames(m.shape[1]), 512), device="cuda")
+        enc.forward(m, l, out=o)
+        ref.append(o)
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    got = [torch.full_like(r, float("nan")) for r in ref]
+    for s in streams:
+        s.wait_stream(torch.cuda.current_stream())
+    for rep in range(2):  # the second pass reuses both arenas
+        for j, (m, l, o) in enumerate(zip(mels, lens, got)):
+            with torch.cuda.stream(streams[(j + rep) % 2]):
+                enc.forward(m, l, out=o)
+        for s in streams:
+            torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    for g, r in zip(got, ref):
+        assert torch.equal(g, r)
+    # queued host-buffer forwards alternating over the two streams
+    jobs = []
+    for m, l in zip(mels, lens):
+        out = torch.empty((m.shape[0], out_frames(m.shape[1]), 512), dtype=torch.float32).pin_memory()
+        jobs.append((m.cpu().pin_memory(), l, out))
+    for j, (hm, l, ho) in enumerate(jobs):
+        enc.forward_host_async(hm.numpy(), l, ho.numpy(), streams[j % 2].cuda_stream)
+    enc.wait()
+    for (hm, l, ho), r in zip(jobs, ref):
+        np.testing.assert_array_equal(ho.numpy(), r.cpu().numpy())
+    assert nq.status() == 0
