@@ -161,6 +161,20 @@ int nq_gemv_glu_splitk(const nq_weight *w, const void *x, int x_dtype, const flo
 int nq_gemv_qkv_splitk(const nq_weight *wq, const nq_weight *wk, const nq_weight *wv,
                        const void *x, int x_dtype, void *q, void *k, void *v, int out_dtype,
                        void *stream);
+/* DecoderBackend::gemv_resadd_ln (src/moonshine/gpu_decoder.rs:67-70) with the
+ * fused split-K reduce + residual add + LayerNorm of
+ * kernels/moonshine_kernels.py:1109-1146: for each row m < M (M <= 16),
+ *   y = x[m] . W^T + bias (bias may be NULL),
+ *   res_out[m] = res_in[m] + y                     (f32; res_out may be res_in),
+ *   norm_out[m] = LN(res_out[m]) * gamma + beta    (beta may be NULL).
+ * LN uses the mean and biased variance of the row in f32 (the CPU decoder's
+ * arithmetic; the Metal kernel's f16 round of y is not reproduced).  N <=
+ * 8192, W not GLU-packed; residual rows of ld_res floats, output rows of
+ * ld_out elements of out_dtype.  Two launches (the GEMV and its epilogue). */
+int nq_gemv_resadd_ln(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx,
+                      const float *bias, const float *res_in, float *res_out, int64_t ld_res,
+                      const float *ln_gamma, const float *ln_beta, float eps, void *norm_out,
+                      int out_dtype, int64_t ld_out, void *stream);
 /* No counterpart in the reference.  The GEMV of nq_linear (M <= 16 rows,
  * same arguments and result) without any allocation: its partial sums,
  * staged activations and work counter live in a static device array of this

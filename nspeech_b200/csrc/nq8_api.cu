@@ -268,8 +268,18 @@ size_t gemv_partial_bytes(const nq::GemvPlan &plan, int n_tiles, int64_t m) {
   return align_up(static_cast<size_t>(plan.upt) * m * n_tiles * nq::kPackRows * sizeof(float), 256);
 }
 
+// Decoder-step epilogue of a one-weight GEMV (nq_gemv_resadd_ln).
+struct GemvResLn {
+  const float *res_in;
+  float *res_out;
+  int64_t ld_res;
+  const float *g;
+  const float *b;
+  float eps;
+};
+
 int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
-             int epilogue, int y_dtype, cudaStream_t stream) {
+             int epilogue, int y_dtype, cudaStream_t stream, const GemvResLn *rl = nullptr) {
   const nq_weight *w0 = args[0].w;
   int total_tiles = 0;
   for (int i = 0; i < nprob; ++i) total_tiles += args[i].w->n_tiles;
@@ -327,6 +337,14 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
   p.upt = plan.upt;
   p.units = plan.units;
   p.ctas = plan.ctas;
+  if (rl) {
+    p.res_in = rl->res_in;
+    p.res_out = rl->res_out;
+    p.ld_res = rl->ld_res;
+    p.ln_g = rl->g;
+    p.ln_b = rl->b;
+    p.ln_eps = rl->eps;
+  }
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
   double flops = 0, bytes = 0;
@@ -359,7 +377,11 @@ struct GemmPlan {
 GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, bool direct) {
   GemmPlan g;
   const bool splitx = x_dtype == NQ_F32;
-  g.deq = g_gemm_path == NQ_GEMM_DEQUANT || (g_gemm_path == NQ_GEMM_AUTO && m >= kDequantMinM);
+  // A weight with a kept bf16 copy needs no dequantize pass: K3 on the copy
+  // is the faster path down to small M as well (M = 125, 1024 -> 4096:
+  // 10.0 vs 14.9 us for the fused kernel).
+  g.deq = g_gemm_path == NQ_GEMM_DEQUANT ||
+          (g_gemm_path == NQ_GEMM_AUTO && (m >= kDequantMinM || w->bf16 != nullptr));
   g.cached = g.deq && w->bf16 != nullptr;
   g.split_x = !direct;
   g.pairs = std::max(1, sm_count / 2);
@@ -858,6 +880,29 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   cudaError_t e = nq::launch_gemv(p, plan.ctas, stream_);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
   return NQ_OK;
+}
+
+int nq_gemv_resadd_ln(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx, const float *bias,
+                      const float *res_in, float *res_out, int64_t ld_res, const float *ln_gamma,
+                      const float *ln_beta, float eps, void *norm_out, int out_dtype, int64_t ld_out, void *stream) {
+  int rc = validate(w, x, x_dtype, m, ldx, NQ_EPI_NONE, norm_out, out_dtype, ld_out);
+  if (rc) return rc;
+  if (!res_in || !res_out || !ln_gamma) return fail(NQ_ERR_ARG, "nq_gemv_resadd_ln: null residual or gamma");
+  if (m > 16) return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln serves M <= 16 rows (got %lld)", (long long)m);
+  if (w->flags & NQ_PACK_GLU) return fail(NQ_ERR_ARG, "nq_gemv_resadd_ln: GLU-packed weight");
+  if (w->n > nq::kGemvLnMaxN)
+    return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln: N = %lld exceeds %d", (long long)w->n, nq::kGemvLnMaxN);
+  if (ld_res < w->n) return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln: ld_res < N");
+  if (!(eps >= 0.f)) return fail(NQ_ERR_ARG, "nq_gemv_resadd_ln: eps must be >= 0");
+  if (m == 0) return NQ_OK;
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  if (w->device != dev) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, dev);
+  LinearArgs a{w, bias, norm_out, ld_out};
+  GemvResLn rl{res_in, res_out, ld_res, ln_gamma, ln_beta, eps};
+  return run_gemv(ctx, &a, 1, x, x_dtype, m, ldx, NQ_EPI_NONE, out_dtype, static_cast<cudaStream_t>(stream), &rl);
 }
 
 int nq_matmul(const nq_weight *w, const void *a, int a_dtype, void *c, int c_dtype, int64_t m, void *stream) {

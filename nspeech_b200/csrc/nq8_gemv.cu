@@ -100,8 +100,14 @@ __device__ __forceinline__ float neg1152(uint16_t d16) {
 }
 
 
+// Resident CTAs per SM: 16 activation rows with hi + lo planes need more
+// registers than four CTAs leave (the plan still sizes the grid for four;
+// the dynamic unit schedule balances CTAs that start a wave later).
+constexpr int gemv_min_ctas(int mt, bool splitx) { return mt == 2 && splitx ? 3 : kGemvCtasPerSm; }
+
 template <int MT, bool SPLITX>
-__global__ void __launch_bounds__(kGemvThreads, kGemvCtasPerSm) gemv_q8_kernel(const __grid_constant__ GemvParams p) {
+__global__ void __launch_bounds__(kGemvThreads, gemv_min_ctas(MT, SPLITX))
+    gemv_q8_kernel(const __grid_constant__ GemvParams p) {
   constexpr int S = kGemvStages;
   // No dependency wait here: the producer's first unit only reads the
   // (constant) weights; every other access waits first.
@@ -420,6 +426,74 @@ __global__ void __launch_bounds__(32 * kReduceWarps) gemv_reduce_kernel(const __
   if (T == 0 && m == 0 && threadIdx.x == 0) p.sched[0] = 0;
 }
 
+// Decoder-step epilogue of the GEMV (the reference's split-K reduce +
+// residual add + LayerNorm, kernels/moonshine_kernels.py:1109-1146, behind
+// DecoderBackend::gemv_resadd_ln, src/moonshine/gpu_decoder.rs:67-70): one
+// CTA per row of x.  Each output n of the row: y = sum of its unit partials in
+// slot order + bias; res_out = res_in + y (f32, stored); then the row's mean
+// and variance (fixed-order block sums) and out = (res_out - mean) * rstd *
+// gamma + beta.  The first CTA re-arms the GEMV's work counter.
+constexpr int kLnThreads = 256;
+constexpr int kLnPerThread = kGemvLnMaxN / kLnThreads;
+
+__device__ __forceinline__ float block_sum_fixed(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();  // red is free (a previous sum has been read)
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kLnThreads / 32; ++w) t += red[w];
+  return t;
+}
+
+__global__ void __launch_bounds__(kLnThreads) gemv_reduce_resadd_ln_kernel(const __grid_constant__ GemvParams p) {
+  pdl_wait();  // the GEMV's partials are complete and visible
+  pdl_trigger();
+  __shared__ float red[kLnThreads / 32];
+  const int m = blockIdx.x;
+  const GemvProblem &pr = p.prob[0];
+  const int N = static_cast<int>(pr.N);
+  const size_t ldp = static_cast<size_t>(pr.n_tiles) * kPackRows;
+  const size_t slot_stride = static_cast<size_t>(p.M) * ldp;
+  const float *src = pr.partials + static_cast<size_t>(m) * ldp;
+  const float *rin = p.res_in + static_cast<int64_t>(m) * p.ld_res;
+  float *rout = p.res_out + static_cast<int64_t>(m) * p.ld_res;
+  float v[kLnPerThread];
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kLnPerThread; ++i) {
+    const int n = threadIdx.x + i * kLnThreads;
+    float a = 0.f;
+    if (n < N) {
+      for (int j = 0; j < p.upt; ++j) a += __ldcg(src + j * slot_stride + n);
+      if (pr.bias) a += pr.bias[n];
+      a += rin[n];
+      rout[n] = a;
+    }
+    v[i] = a;
+    sum += a;
+  }
+  const float mean = block_sum_fixed(sum, red) / static_cast<float>(N);
+  float sq = 0.f;
+#pragma unroll
+  for (int i = 0; i < kLnPerThread; ++i) {
+    const int n = threadIdx.x + i * kLnThreads;
+    const float dlt = n < N ? v[i] - mean : 0.f;
+    sq += dlt * dlt;
+  }
+  const float rstd = rsqrtf(block_sum_fixed(sq, red) / static_cast<float>(N) + p.ln_eps);
+#pragma unroll
+  for (int i = 0; i < kLnPerThread; ++i) {
+    const int n = threadIdx.x + i * kLnThreads;
+    if (n < N)
+      store_out(pr.y, p.y_dtype, m * pr.ldy + n, (v[i] - mean) * rstd * p.ln_g[n] + (p.ln_b ? p.ln_b[n] : 0.f));
+  }
+  if (m == 0 && threadIdx.x == 0) p.sched[0] = 0;
+}
+
 template <int MT, bool SPLITX>
 static cudaError_t launch_gemv_t(const GemvParams &p, int ctas, cudaStream_t stream) {
   auto kern = gemv_q8_kernel<MT, SPLITX>;
@@ -443,6 +517,7 @@ cudaError_t launch_gemv(const GemvParams &p, int ctas, cudaStream_t stream) {
   else
     e = splitx ? launch_gemv_t<2, true>(p, ctas, stream) : launch_gemv_t<2, false>(p, ctas, stream);
   if (e != cudaSuccess) return e;
+  if (p.res_out) return launch_pdl(gemv_reduce_resadd_ln_kernel, dim3(p.M), dim3(kLnThreads), 0, stream, 1, p);
   return launch_pdl(gemv_reduce_kernel, dim3(p.units / p.upt, p.M), dim3(32 * kReduceWarps), 0, stream, 1, p);
 }
 

@@ -39,8 +39,17 @@ struct GemvParams {
   int units;   // units of all problems, tile-major
   int ctas;    // CTAs launched; CTA c starts with unit c
   int *sched;  // [0] work counter: zero between calls (gemv_reduce re-arms it)
+  // Decoder-step epilogue (one problem; res_out non-null selects it): the
+  // row is y = W x + bias, res_out = res_in + y, prob[0].y = LN(res_out).
+  const float *res_in;
+  float *res_out;
+  int64_t ld_res;
+  const float *ln_g;  // LayerNorm gamma [N]
+  const float *ln_b;  // LayerNorm beta [N] or null
+  float ln_eps;
   DevCtl ctl;
 };
+constexpr int kGemvLnMaxN = 8192;  // row width the residual + LayerNorm epilogue holds
 
 // Work split of one GEMV launch (fixed by the shape and the SM count).
 struct GemvPlan {

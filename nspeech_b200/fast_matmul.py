@@ -19,7 +19,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from typing import Optional, Sequence
+from typing import Optional, Sequence, Tuple
 
 import numpy as np
 import torch
@@ -149,6 +149,41 @@ class QWeight:
                                  out.data_ptr(), _dtype_code(out), out.stride(0), _stream_ptr(stream))
         _l.check(rc)
         return out
+
+
+    def gemv_resadd_ln(self, x: torch.Tensor, residual_in: torch.Tensor, gamma: torch.Tensor,
+                       beta: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None,
+                       eps: float = 1e-5, residual_out: Optional[torch.Tensor] = None,
+                       out: Optional[torch.Tensor] = None, out_dtype: Optional[torch.dtype] = None,
+                       stream: Optional[torch.cuda.Stream] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Decoder step (M <= 16 rows): residual_out = residual_in + x . W^T + bias,
+        out = LayerNorm(residual_out) * gamma + beta (DecoderBackend::gemv_resadd_ln,
+        src/moonshine/gpu_decoder.rs:67-70).  Returns (residual_out, out);
+        residual_out may be residual_in itself."""
+        if x.dim() != 2 or x.stride(1) != 1 or x.shape[1] != self.k:
+            raise MatMulError(f"x must be 2-D [M, {self.k}] with unit column stride")
+        m = x.shape[0]
+        for name, t in (("residual_in", residual_in), ("gamma", gamma), ("beta", beta), ("bias", bias)):
+            if t is not None and t.dtype != torch.float32:
+                raise MatMulError(f"{name} must be f32")
+        if residual_in.dim() != 2 or residual_in.shape[0] != m or residual_in.shape[1] < self.n or residual_in.stride(1) != 1:
+            raise MatMulError(f"residual_in must be [M, >= {self.n}] f32 with unit column stride")
+        if residual_out is None:
+            residual_out = torch.empty_like(residual_in)
+        if residual_out.shape != residual_in.shape or residual_out.stride() != residual_in.stride():
+            raise MatMulError("residual_out must have residual_in's shape and strides")
+        for name, t in (("gamma", gamma), ("beta", beta), ("bias", bias)):
+            if t is not None and (not t.is_contiguous() or t.numel() != self.n):
+                raise MatMulError(f"{name} must be contiguous f32 [{self.n}]")
+        if out is None:
+            out = torch.empty((m, self.n), device=x.device, dtype=out_dtype or x.dtype)
+        rc = _l.load().nq_gemv_resadd_ln(self._h, x.data_ptr(), _dtype_code(x), m, x.stride(0),
+                                         bias.data_ptr() if bias is not None else None, residual_in.data_ptr(),
+                                         residual_out.data_ptr(), residual_in.stride(0), gamma.data_ptr(),
+                                         beta.data_ptr() if beta is not None else None, eps, out.data_ptr(),
+                                         _dtype_code(out), out.stride(0), _stream_ptr(stream))
+        _l.check(rc)
+        return residual_out, out
 
 
 class MatMul:

@@ -1,17 +1,27 @@
 """Time Q8_0 linear shapes on the GPU through the C ABI (nq_linear).
 
     python -m nspeech_b200.gemm_bench --shape 12000x1024x4096 --shape 1x640x640 [--x bf16] [--iters 20]
+    python -m nspeech_b200.gemm_bench --cfg1-sweep [--graph]
 
 Each shape is M x K x N (tokens x in-features x out-features).  Random Q8_0
 weights are rotated over enough copies to exceed the 126 MB L2, so weight
 reads come from HBM; times are CUDA events over `iters` back-to-back calls
-(host launch overhead included for small shapes).  Prints one JSON line per
-shape with TFLOP/s and algorithmic GB/s (N*K*34/32 + M*K*sx + M*N*sy bytes).
+(host launch overhead included for small shapes), or with --graph the
+device time per call of a CUDA graph of those calls.  Prints one JSON line
+per shape with TFLOP/s and algorithmic GB/s (N*K*34/32 + M*K*sx + M*N*sy
+bytes), and the fraction of the bound that applies (HBM for M <= 125, where
+the arithmetic intensity is below the ridge; tensor otherwise) against the
+measured peaks in MEASURED_PEAKS.json when present.
+
+--cfg1-sweep: the configs[0] block (K -> N: 1024->4096, 4096->1024,
+1024->3072, 1024->1024, 1024->2048, 1024->1024; f32 activations in and out)
+at M in {1, 2, 4, 8, 16, 125, 1024, 2048, 4096, 12000}.
 """
 from __future__ import annotations
 
 import argparse
 import json
+import os
 
 import numpy as np
 import torch
@@ -30,44 +40,87 @@ def _weights(n: int, k: int, copies: int, rng) -> list:
     return out
 
 
+CFG1_KN = [(1024, 4096), (4096, 1024), (1024, 3072), (1024, 1024), (1024, 2048), (1024, 1024)]
+CFG1_M = [1, 2, 4, 8, 16, 125, 1024, 2048, 4096, 12000]
+
+
+def _peaks() -> dict:
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
 def time_shape(m: int, k: int, n: int, x_dtype=torch.bfloat16, y_dtype=torch.bfloat16, iters: int = 20,
-               epilogue: int = lib.NQ_EPI_NONE, seed: int = 0) -> dict:
+               epilogue: int = lib.NQ_EPI_NONE, seed: int = 0, graph: bool = False) -> dict:
     rng = np.random.default_rng(seed)
     wbytes = n * k * 34 / 32
     copies = int(min(32, max(1, np.ceil(300e6 / wbytes))))
     ws = _weights(n, k, copies, rng)
     x = torch.randn(m, k, device="cuda").to(x_dtype)
     y = torch.empty(m, n, device="cuda", dtype=y_dtype)
-    for i in range(3):
-        ws[i % copies].linear(x, out=y, epilogue=epilogue)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(max(3, copies)):  # also sizes the stream's workspace before any capture
+            ws[i % copies].linear(x, out=y, epilogue=epilogue)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(iters):
-        ws[i % copies].linear(x, out=y, epilogue=epilogue)
-    e1.record()
-    torch.cuda.synchronize()
-    t = e0.elapsed_time(e1) / iters / 1e3
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(iters):
+                ws[i % copies].linear(x, out=y, epilogue=epilogue)
+        g.replay()
+        torch.cuda.synchronize()
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / (reps * iters) / 1e3
+        del g
+    else:
+        e0.record()
+        for i in range(iters):
+            ws[i % copies].linear(x, out=y, epilogue=epilogue)
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / iters / 1e3
     if lib.status() != 0:
         raise RuntimeError("device status reported a timeout")
     byts = wbytes + m * k * x.element_size() + m * n * y.element_size()
-    return {"m": m, "k": k, "n": n, "x": str(x_dtype).split(".")[-1], "us": round(t * 1e6, 2),
-            "tflops": round(2 * m * n * k / t / 1e12, 1), "gbs": round(byts / t / 1e9, 1)}
+    pk = _peaks()
+    tflops, gbs = 2 * m * n * k / t / 1e12, byts / t / 1e9
+    bound = "hbm" if m <= 125 else "tensor"
+    frac = gbs / pk["hbm_gbs"] if bound == "hbm" else tflops / pk["bf16_tflops"]
+    return {"m": m, "k": k, "n": n, "x": str(x_dtype).split(".")[-1], "y": str(y_dtype).split(".")[-1],
+            "us": round(t * 1e6, 2), "tflops": round(tflops, 1), "gbs": round(gbs, 1), "bound": bound,
+            "frac": round(frac, 3), "peak_source": pk["source"], "timing": "graph" if graph else "calls"}
 
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--shape", action="append", required=True, help="MxKxN")
+    ap.add_argument("--shape", action="append", default=[], help="MxKxN")
+    ap.add_argument("--cfg1-sweep", action="store_true", help="the configs[0] block over the M sweep (f32 in/out)")
     ap.add_argument("--x", choices=["bf16", "f32"], default="bf16")
+    ap.add_argument("--y", choices=["bf16", "f32"], default="bf16")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--graph", action="store_true", help="time a CUDA graph of the calls (device time)")
     ap.add_argument("--device", type=int, default=0)
     a = ap.parse_args()
     torch.cuda.set_device(a.device)
     lib.init(a.device)
-    xd = torch.bfloat16 if a.x == "bf16" else torch.float32
-    for s in a.shape:
-        m, k, n = (int(v) for v in s.lower().split("x"))
-        print(json.dumps(time_shape(m, k, n, x_dtype=xd, iters=a.iters)), flush=True)
+    dt = {"bf16": torch.bfloat16, "f32": torch.float32}
+    jobs = [(tuple(int(v) for v in s.lower().split("x")), dt[a.x], dt[a.y]) for s in a.shape]
+    if a.cfg1_sweep:
+        jobs += [((m, k, n), torch.float32, torch.float32) for m in CFG1_M for k, n in CFG1_KN]
+    if not jobs:
+        ap.error("give --shape or --cfg1-sweep")
+    for (m, k, n), xd, yd in jobs:
+        print(json.dumps(time_shape(m, k, n, x_dtype=xd, y_dtype=yd, iters=a.iters, graph=a.graph)), flush=True)
 
 
 if __name__ == "__main__":

@@ -168,6 +168,23 @@ def linear_exact(x, blocks, n, bias=None, epi=EPI_NONE) -> np.ndarray:
     return epilogue(matmul_exact(x, blocks, n), bias, epi)
 
 
+def resadd_layernorm(y, res_in, gamma, beta=None, eps: float = 1e-5):
+    """Decoder-step residual add + LayerNorm, in f64: r = res_in + y and
+    out = (r - mean) / sqrt(var + eps) * gamma (+ beta), biased variance over
+    the row.  Restates residual_add and LayerNorm::forward of
+    src/moonshine/decoder.rs:41-50,67-74 (weight-only LayerNorm, eps 1e-5),
+    the CPU form of the fused reduce + residual + LayerNorm of
+    kernels/moonshine_kernels.py:1109-1146.  Returns (r, out)."""
+    r = np.asarray(res_in, dtype=np.float64) + np.asarray(y, dtype=np.float64)
+    mean = r.mean(axis=1, keepdims=True)
+    c = r - mean
+    var = (c * c).mean(axis=1, keepdims=True)
+    out = c / np.sqrt(var + eps) * np.asarray(gamma, dtype=np.float64)[None, :]
+    if beta is not None:
+        out = out + np.asarray(beta, dtype=np.float64)[None, :]
+    return r, out
+
+
 def max_rel_err(y: np.ndarray, yref: np.ndarray, tau: float = 1e-3) -> float:
     """max |y - yref| / max(|yref|, tau * rms(yref row)) over all elements."""
     y = _f32(y)

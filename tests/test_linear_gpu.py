@@ -304,3 +304,69 @@ def test_wait_timeout_reports_and_recovers(nq, oracle):
     w = QWeight.from_q8_0(q, 256, 256)
     x = oracle.normal(98, (3, 256))
     _check(oracle, _run(w, x), _ref(oracle, x, q, 256), "after timeout")
+
+
+# nq_gemv_resadd_ln: decoder-step GEMV with the fused residual add + LayerNorm
+# (DecoderBackend::gemv_resadd_ln).  Moonshine decoder shapes (640 -> 640 O
+# projections, 2560 -> 640 fc2), an odd width, and several rows; in-place
+# residual, with and without bias / beta, bf16 and f32 outputs.
+@pytest.mark.parametrize("m,k,n,bias,beta,inplace,odt", [
+    (1, 640, 640, False, False, False, torch.bfloat16),
+    (1, 2560, 640, True, False, True, torch.bfloat16),
+    (4, 1024, 1000, True, True, False, torch.float32),
+    (16, 640, 640, True, True, True, torch.float32),
+    (1, 4096, 8192, False, True, False, torch.bfloat16),
+])
+def test_gemv_resadd_ln_matches_oracle(nq, oracle, m, k, n, bias, beta, inplace, odt):
+    from nspeech_b200.fast_matmul import QWeight
+    q = oracle.quantize_q8_0(oracle.normal(60 + n, (n, k), 0.0, 0.02))
+    w = QWeight.from_q8_0(q, n, k)
+    x = oracle.normal(61, (m, k))
+    res = oracle.normal(62, (m, n))
+    g = oracle.normal(63, (n,), 1.0, 0.1)
+    b = oracle.normal(64, (n,), 0.0, 0.1) if beta else None
+    bs = oracle.normal(65, (n,), 0.0, 0.01) if bias else None
+    y = oracle.matmul_fbgemm_bf16(x, q, n).astype(np.float64) + (bs if bias else 0.0)
+    r_ref, o_ref = oracle.resadd_layernorm(y, res, g, b, 1e-5)
+    dev = lambda a: torch.from_numpy(a).cuda() if a is not None else None
+    rin = dev(res)
+    rout, out = w.gemv_resadd_ln(dev(x), rin, dev(g), beta=dev(b), bias=dev(bs), eps=1e-5,
+                                 residual_out=rin if inplace else None, out_dtype=odt)
+    torch.cuda.synchronize()
+    if inplace:
+        assert rout.data_ptr() == rin.data_ptr()
+    r_got, o_got = rout.cpu().numpy(), out.float().cpu().numpy()
+    err_r = oracle.max_rel_err(r_got, r_ref, 1.0)
+    err_o = oracle.max_rel_err(o_got, o_ref, 1.0)
+    assert np.isfinite(o_got).all()
+    assert err_r <= EXPECT_TOL, err_r
+    assert err_o <= (EXPECT_TOL if odt == torch.float32 else 1e-2), err_o
+    # bit-reproducible: the same call again gives the same bits
+    rout2, out2 = w.gemv_resadd_ln(dev(x), dev(res), dev(g), beta=dev(b), bias=dev(bs), eps=1e-5, out_dtype=odt)
+    torch.cuda.synchronize()
+    if not inplace:
+        assert torch.equal(rout2, rout)
+        assert torch.equal(out2, out)
+    assert nq.status() == 0
+
+
+def test_gemv_resadd_ln_rejects_bad_arguments(nq):
+    from nspeech_b200 import lib
+    from nspeech_b200.fast_matmul import QWeight, MatMulError
+    q = np.zeros((8192 + 128, 64 // 32 * 34), dtype=np.uint8)
+    wide = QWeight.from_q8_0(q, 8192 + 128, 64)
+    x = torch.zeros((1, 64), device="cuda")
+    r = torch.zeros((1, 8192 + 128), device="cuda")
+    g = torch.ones(8192 + 128, device="cuda")
+    with pytest.raises(lib.NqError) as e:
+        wide.gemv_resadd_ln(x, r, g)
+    assert e.value.code == lib.NQ_ERR_SHAPE
+    w = QWeight.from_q8_0(np.zeros((64, 2 * 34), dtype=np.uint8), 64, 64)
+    x17 = torch.zeros((17, 64), device="cuda")
+    with pytest.raises(lib.NqError) as e:
+        w.gemv_resadd_ln(x17, torch.zeros((17, 64), device="cuda"), torch.ones(64, device="cuda"))
+    assert e.value.code == lib.NQ_ERR_SHAPE
+    with pytest.raises(MatMulError):
+        w.gemv_resadd_ln(torch.zeros((1, 64), device="cuda"), torch.zeros((1, 64), device="cuda", dtype=torch.float64),
+                         torch.ones(64, device="cuda"))
+    assert nq.status() == 0
