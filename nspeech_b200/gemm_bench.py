@@ -14,8 +14,9 @@ the arithmetic intensity is below the ridge; tensor otherwise) against the
 measured peaks in MEASURED_PEAKS.json when present.
 
 --cfg1-sweep: the configs[0] block (K -> N: 1024->4096, 4096->1024,
-1024->3072, 1024->1024, 1024->2048, 1024->1024; f32 activations in and out)
-at M in {1, 2, 4, 8, 16, 125, 1024, 2048, 4096, 12000}.
+1024->3072, 1024->1024, 1024->2048, 1024->1024) at M in {1, 2, 4, 8, 16,
+125, 1024, 2048, 4096, 12000}; f32 activations in and out, or
+bf16 with --sweep-dtype bf16 (the encoder's activations).
 """
 from __future__ import annotations
 
@@ -104,7 +105,9 @@ def time_shape(m: int, k: int, n: int, x_dtype=torch.bfloat16, y_dtype=torch.bfl
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--shape", action="append", default=[], help="MxKxN")
-    ap.add_argument("--cfg1-sweep", action="store_true", help="the configs[0] block over the M sweep (f32 in/out)")
+    ap.add_argument("--cfg1-sweep", action="store_true", help="the configs[0] block over the M sweep")
+    ap.add_argument("--sweep-dtype", choices=["f32", "bf16"], default="f32",
+                    help="activations in and out for --cfg1-sweep (f32: configs[0]; bf16: the encoder's)")
     ap.add_argument("--x", choices=["bf16", "f32"], default="bf16")
     ap.add_argument("--y", choices=["bf16", "f32"], default="bf16")
     ap.add_argument("--iters", type=int, default=20)
@@ -116,7 +119,8 @@ def main() -> None:
     dt = {"bf16": torch.bfloat16, "f32": torch.float32}
     jobs = [(tuple(int(v) for v in s.lower().split("x")), dt[a.x], dt[a.y]) for s in a.shape]
     if a.cfg1_sweep:
-        jobs += [((m, k, n), torch.float32, torch.float32) for m in CFG1_M for k, n in CFG1_KN]
+        sd = dt[a.sweep_dtype]
+        jobs += [((m, k, n), sd, sd) for m in CFG1_M for k, n in CFG1_KN]
     if not jobs:
         ap.error("give --shape or --cfg1-sweep")
     for (m, k, n), xd, yd in jobs:
