@@ -64,6 +64,7 @@ def parse_args():
     ap.add_argument("--gemv-shapes", default="1x640x640,1x640x2560,1x2560x640,1x4096x4096,1x8192x8192,"
                     "1x640x32768,8x4096x4096,16x4096x4096,1x16384x16384")
     ap.add_argument("--gemv-plain", type=int, default=0, help="only make this many plain calls per shape")
+    ap.add_argument("--no-decode-step", action="store_true", help="--gemv without the configs[2] decode step")
     return ap.parse_args()
 
 
@@ -448,12 +449,89 @@ def run_gemv_sweep(args) -> None:
                      "frac_hbm": round(byts / us / 1e3 / pk["hbm_gbs"], 3)})
         del g, ws
         torch.cuda.empty_cache()
+    decode = None if args.gemv_plain or args.no_decode_step else decode_step(rng, pk)
     if lib.status() != 0:
         raise RuntimeError("device status bits set after the GEMV sweep")
     if not args.gemv_plain:
         print(json.dumps({"metric": "Q8_0 GEMV HBM GB/s (graph of back-to-back calls, weights past L2)",
                           "peak_hbm_gbs": pk["hbm_gbs"], "peak_source": pk.get("source", "measured"),
-                          "shapes": rows}), flush=True)
+                          "shapes": rows, "decode_step": decode}), flush=True)
+
+
+def decode_step(rng, pk) -> dict:
+    """configs[2] decoder: the Q8_0 contractions of one greedy token (M = 1), as
+    a chain where each call's input is an earlier call's output: per layer the
+    fused Q/K/V (640 -> 3 x 640), the self-attention O projection with
+    residual + LayerNorm, the cross-attention Q projection, its O projection
+    with residual + LayerNorm, fc1 (640 -> 2 x 2560, GLU-SiLU) and fc2
+    (2560 -> 640) with residual + LayerNorm; 14 layers, then the lm_head
+    (640 -> 32768).  131.95 MB of Q8_0 weights per token (the cross K/V are
+    computed once per utterance).  The attention kernels between the
+    projections are not part of this path and are left out.  Timed as a CUDA
+    graph of 8 tokens over distinct weight copies (more than L2)."""
+    import torch
+    from nspeech_b200 import lib
+    from nspeech_b200.fast_matmul import QWeight
+
+    d, ff, layers, vocab = 640, 2560, 14, 32768
+
+    def qw(n, k, flags=0):
+        q = rng.integers(0, 256, size=(n, k // 32, 34), dtype=np.uint8)
+        q[:, :, :2] = (rng.random((n, k // 32)) * 1e-3 + 1e-4).astype(np.float16).view(np.uint8).reshape(n, k // 32, 2)
+        return QWeight.from_q8_0(np.ascontiguousarray(q.reshape(n, -1)), n, k, flags=flags)
+
+    copies = 2  # 2 x 132 MB > L2: consecutive tokens read their weights from HBM
+    nets = []
+    for _ in range(copies):
+        lay = [dict(qkv=qw(3 * d, d), o=qw(d, d), cq=qw(d, d), co=qw(d, d), fc1=qw(2 * ff, d, lib.NQ_PACK_GLU),
+                    fc2=qw(d, ff)) for _ in range(layers)]
+        nets.append((lay, qw(vocab, d)))
+    wbytes = sum(w.n * w.k * 34 / 32 for L in nets[0][0] for w in L.values()) + nets[0][1].n * nets[0][1].k * 34 / 32
+    x = torch.randn(1, d, device="cuda").bfloat16()
+    res = torch.randn(1, d, device="cuda")
+    g = torch.ones(d, device="cuda")
+    qkv = torch.empty(1, 3 * d, device="cuda", dtype=torch.bfloat16)
+    h = torch.empty(1, d, device="cuda", dtype=torch.bfloat16)
+    t = torch.empty(1, ff, device="cuda", dtype=torch.bfloat16)
+    logits = torch.empty(1, vocab, device="cuda", dtype=torch.bfloat16)
+
+    def token(net):
+        lay, head = net
+        for L in lay:
+            L["qkv"].linear(x, out=qkv)
+            L["o"].gemv_resadd_ln(qkv[:, :d], res, g, residual_out=res, out=h)  # attention output stands in
+            L["cq"].linear(h, out=qkv[:, :d])
+            L["co"].gemv_resadd_ln(qkv[:, :d], res, g, residual_out=res, out=h)
+            L["fc1"].linear(h, epilogue=lib.NQ_EPI_GLU_SILU, out=t)
+            L["fc2"].gemv_resadd_ln(t, res, g, residual_out=res, out=x)
+        head.linear(x, out=logits)
+
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for net in nets:
+            token(net)
+    torch.cuda.synchronize()
+    tokens = 8
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr, stream=s):
+        for i in range(tokens):
+            token(nets[i % copies])
+    for _ in range(2):
+        gr.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    reps = 5
+    e0.record()
+    for _ in range(reps):
+        gr.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * tokens)
+    floor_us = wbytes / pk["hbm_gbs"] / 1e3
+    calls = layers * 6 + 1
+    return {"config": "configs[2] Moonshine decoder, M = 1, 14 layers + lm_head", "weight_mb_per_token":
+            round(wbytes / 1e6, 2), "us_per_token": round(us, 1), "hbm_floor_us": round(floor_us, 1),
+            "frac_of_floor": round(floor_us / us, 3), "gemv_calls_per_token": calls, "launches_per_token": 2 * calls}
 
 
 def main():
