@@ -471,7 +471,17 @@ __global__ void __launch_bounds__(kLnThreads) gemv_reduce_resadd_ln_kernel(const
     const int n = threadIdx.x + i * kLnThreads;
     float a = 0.f;
     if (n < N) {
-      for (int j = 0; j < p.upt; ++j) a += __ldcg(src + j * slot_stride + n);
+      // slots in index order, eight loads in flight
+      const float *q = src + n;
+      int j = 0;
+      for (; j + 8 <= p.upt; j += 8) {
+        float t[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) t[e] = __ldcg(q + (j + e) * slot_stride);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) a += t[e];
+      }
+      for (; j < p.upt; ++j) a += __ldcg(q + j * slot_stride);
       if (pr.bias) a += pr.bias[n];
       a += rin[n];
       rout[n] = a;
