@@ -60,29 +60,37 @@ __global__ void conv0_relu_kernel(const float *__restrict__ mel, const int *__re
 // conv0 + the first depthwise conv of the subsampling stack in one pass:
 //   out[b, t2, f2, c] = b2[c] + sum_{dt,df} w2[c][dt,df] * s1[2 t2 - 1 + dt][2 f2 - 1 + df][c]
 //   s1[t1][f1][c]     = bf16(relu(b0[c] + sum_{dt,df} w0[c][dt,df] * mel[2 t1 - 1 + dt][2 f1 - 1 + df]))
-// (fast_conformer.rs:172-180; s1 terms with t1 outside [0, len1) or f1 < 0
-// are zero, as in conv0_relu + dwconv2d_s2).  The s1 rows a tile of kCdTT
-// output rows needs (2 kCdTT + 1) are computed into shared memory and never
-// reach HBM.  conv0 runs on the tensor cores: a GEMM [positions x 16 taps
+// (fast_conformer.rs:172-180; s1 terms with t1 outside [0, len1) or f1 outside
+// [0, F1) are zero, as in conv0_relu + dwconv2d_s2).  The s1 rows a tile of
+// kCdTT output rows needs (2 kCdTT + 1) are computed into shared memory and
+// never reach HBM.  conv0 runs on the tensor cores: a GEMM [positions x 16 taps
 // (9 used)] x [16 x 64 channels] with mma.sync m16n8k16, the mel patches and
 // weights split into bf16 hi + lo parts (x w = xh wh + xh wl + xl wh: f32-level
-// accuracy).  The depthwise conv is plain f32, two channels per thread.
+// accuracy).  The depthwise conv is f32 with packed f32x2 FMAs: each thread
+// owns two channels and a 4 x 4 patch of outputs, so the 9 x 9 s1 tile it
+// needs is read once and 32 independent accumulator chains keep the FMA pipe
+// busy.  An s1 position holds kCdPos bf16 (64 channels + 8 pad), which makes
+// both the fragment stores of the conv0 epilogue and the channel-contiguous
+// loads of the depthwise conv free of bank conflicts.
 // Block = (64 channels, kCdTT output rows, one segment), 8 warps.
 constexpr int kCdTT = 4;   // output rows (t2) per block
 constexpr int kCdCG = 64;  // channels per block
+constexpr int kCdPos = kCdCG + 8;  // bf16 per s1 position in shared memory
 constexpr int kCdRows1 = 2 * kCdTT + 1;
 constexpr int kCdMelRows = 4 * kCdTT + 3;
 
 // Padded mel row (16-byte multiple): column j holds frequency j - 1, with
 // room for the last 16-position tile's patches.
 __host__ __device__ constexpr int cd_mel_pitch(int F1) { return ((2 * (((F1 + 15) / 16) * 16) + 6 + 3) / 4) * 4; }
-// s1 rows in shared memory: column 0 is the zero f1 = -1 guard.
-__host__ __device__ constexpr int cd_s1_cols(int F1) { return F1 + 1; }
+// s1 positions per row in shared memory: index 0 is the zero f1 = -1 guard,
+// index f1 + 1 holds f1 for f1 < 16 ceil(F1 / 16) (zero from F1 on), which
+// covers every column the 4-wide output patches read (8 ceil(F2 / 4) <= 16 ceil(F1 / 16)).
+__host__ __device__ constexpr int cd_s1_cols(int F1) { return 1 + 16 * ((F1 + 15) / 16); }
 
 size_t conv0_dw_smem_bytes(int F, int F1) {
   (void)F;
   return static_cast<size_t>(kCdMelRows) * cd_mel_pitch(F1) * sizeof(float) +
-         static_cast<size_t>(kCdRows1) * cd_s1_cols(F1) * kCdCG * sizeof(__nv_bfloat16);
+         static_cast<size_t>(kCdRows1) * cd_s1_cols(F1) * kCdPos * sizeof(__nv_bfloat16);
 }
 
 __device__ __forceinline__ uint32_t bf16x2_hi_lo(float a, float b, uint32_t &lo) {
@@ -92,13 +100,33 @@ __device__ __forceinline__ uint32_t bf16x2_hi_lo(float a, float b, uint32_t &lo)
   lo = *reinterpret_cast<const uint32_t *>(&l);
   return *reinterpret_cast<const uint32_t *>(&h);
 }
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// bf16(relu(v.lo)) in the low half, bf16(relu(v.hi)) in the high half
+__device__ __forceinline__ uint32_t relu_bf16x2(uint64_t v) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+  uint32_t d;
+  asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+// bf16x2 (low half = element 0) -> f32x2 (low word = element 0), exact
+__device__ __forceinline__ uint64_t f32x2_of_bf16x2(uint32_t v) {
+  return f2(__uint_as_float(v << 16), __uint_as_float(v & 0xffff0000u));
+}
 
 __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
     const float *__restrict__ mel, const int *__restrict__ len0, const int *__restrict__ len1, int T, int F, int T1,
     int F1, int T2, int F2, int C, const float *__restrict__ w0, const float *__restrict__ b0,
     const float *__restrict__ w2, const float *__restrict__ b2, __nv_bfloat16 *__restrict__ out) {
-  pdl_wait();  // predecessor kernel complete, its writes visible
-  pdl_trigger();
   extern __shared__ __align__(16) unsigned char cd_smem[];
   const int FP = cd_mel_pitch(F1);
   const int S1C = cd_s1_cols(F1);
@@ -107,34 +135,60 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
   const int b = blockIdx.z;
   const int t2s = blockIdx.y * kCdTT;
   const int cg0 = blockIdx.x * kCdCG;
-  const int L0 = len0[b], L1 = min(len1[b], T1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
-  // 1. mel rows 4 t2s - 3 .. (zero outside [0, min(T, L0)) and the frequency range)
-  for (int idx = threadIdx.x; idx < kCdMelRows * FP; idx += blockDim.x) {
-    const int r = idx / FP;
-    const int j = idx - r * FP;
-    const int t = 4 * t2s - 3 + r;
-    const int f = j - 1;
-    float v = 0.f;
-    if (t >= 0 && t < T && t < L0 && f >= 0 && f < F) v = mel[(static_cast<int64_t>(b) * T + t) * F + f];
-    melS[idx] = v;
-  }
-  // zero guard column of every s1 row
-  for (int idx = threadIdx.x; idx < kCdRows1 * kCdCG; idx += blockDim.x)
-    s1S[(idx / kCdCG) * S1C * kCdCG + (idx % kCdCG)] = __float2bfloat16_rn(0.f);
-  __syncthreads();
-  // 2. conv0 on tensor cores.  B fragments (weights, col-major [tap][channel]):
-  //    b0 = taps (2 t4, 2 t4 + 1), b1 = taps (2 t4 + 8, 2 t4 + 9) of channel n = nt * 8 + g.
-  {
-    uint32_t bh[8][2], bl[8][2];
+  // Weights and biases are never written by a kernel: fetch them before the
+  // wait on the predecessor.  conv0 B fragments (col-major [tap][channel]):
+  // b0 = taps (2 t4, 2 t4 + 1), b1 = taps (2 t4 + 8, 2 t4 + 9) of channel nt * 8 + g.
+  uint32_t bh[8][2], bl[8][2];
+  uint64_t bias0[8];
 #pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      const float *wc = w0 + (cg0 + nt * 8 + g) * 9;
-      const int k0 = 2 * t4, k2 = 2 * t4 + 8;
-      bh[nt][0] = bf16x2_hi_lo(wc[k0], wc[k0 + 1], bl[nt][0]);
-      bh[nt][1] = bf16x2_hi_lo(k2 < 9 ? wc[k2] : 0.f, 0.f, bl[nt][1]);  // tap 9 and beyond are padding
+  for (int nt = 0; nt < 8; ++nt) {
+    const float *wc = w0 + (cg0 + nt * 8 + g) * 9;
+    const int k0 = 2 * t4, k2 = 2 * t4 + 8;
+    bh[nt][0] = bf16x2_hi_lo(wc[k0], wc[k0 + 1], bl[nt][0]);
+    bh[nt][1] = bf16x2_hi_lo(k2 < 9 ? wc[k2] : 0.f, 0.f, bl[nt][1]);  // tap 9 and beyond are padding
+    bias0[nt] = f2(b0[cg0 + nt * 8 + 2 * t4], b0[cg0 + nt * 8 + 2 * t4 + 1]);
+  }
+  // depthwise weights of this thread's channel pair (cc, cc + 1)
+  const int cc = cg0 + 2 * lane;
+  uint64_t wv[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) wv[i] = f2(w2[cc * 9 + i], w2[(cc + 1) * 9 + i]);
+  const uint64_t bias2 = f2(b2[cc], b2[cc + 1]);
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
+  const int L0 = len0[b], L1 = min(len1[b], T1);
+  // 1. mel rows 4 t2s - 3 .. (zero outside [0, min(T, L0)) and the frequency range),
+  //    one warp per row
+  {
+    const bool vec = (reinterpret_cast<uintptr_t>(mel) & 15) == 0 && (F & 3) == 0 && F + 1 <= FP;
+    for (int r = warp; r < kCdMelRows; r += 8) {
+      const int t = 4 * t2s - 3 + r;
+      float *dst = melS + r * FP;
+      const bool live = t >= 0 && t < T && t < L0;
+      const float *src = mel + (static_cast<int64_t>(b) * T + (live ? t : 0)) * F;
+      if (live && vec) {
+        for (int f = 4 * lane; f < F; f += 128) {
+          const float4 v = __ldg(reinterpret_cast<const float4 *>(src + f));
+          dst[f + 1] = v.x;
+          dst[f + 2] = v.y;
+          dst[f + 3] = v.z;
+          dst[f + 4] = v.w;
+        }
+        if (lane == 0) dst[0] = 0.f;
+        for (int j = F + 1 + lane; j < FP; j += 32) dst[j] = 0.f;
+      } else {
+        for (int j = lane; j < FP; j += 32) dst[j] = live && j >= 1 && j <= F ? src[j - 1] : 0.f;
+      }
     }
+  }
+  // zero guard position (f1 = -1) of every s1 row
+  for (int idx = threadIdx.x; idx < kCdRows1 * (kCdCG / 2); idx += blockDim.x)
+    reinterpret_cast<uint32_t *>(s1S + (idx / (kCdCG / 2)) * S1C * kCdPos)[idx % (kCdCG / 2)] = 0u;
+  __syncthreads();
+  // 2. conv0 on tensor cores, one 16-position x 64-channel tile per warp step
+  {
     // this lane's tap offsets in the mel tile (taps 2t4, 2t4+1, 2t4+8, 2t4+9; -1 = padding)
     int off[4];
 #pragma unroll
@@ -142,18 +196,21 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
       const int k = 2 * t4 + (x & 1) + 8 * (x >> 1);
       off[x] = k < 9 ? (k / 3) * FP + (k % 3) : -1;
     }
-    float bias_c[8][2];
-#pragma unroll
-    for (int nt = 0; nt < 8; ++nt) {
-      bias_c[nt][0] = b0[cg0 + nt * 8 + 2 * t4];
-      bias_c[nt][1] = b0[cg0 + nt * 8 + 2 * t4 + 1];
-    }
     const int mtr = (F1 + 15) / 16;  // 16-position tiles per s1 row
     for (int mt = warp; mt < kCdRows1 * mtr; mt += 8) {
       const int r1 = mt / mtr;
       const int f10 = (mt - r1 * mtr) * 16;
       const int t1 = 2 * t2s - 1 + r1;
-      const bool row_live = t1 >= 0 && t1 < L1;  // other rows are zero for the depthwise conv
+      // this lane's C-fragment positions f10 + g (+ 8), channels nt * 8 + 2 t4 (+ 1)
+      __nv_bfloat16 *dst = s1S + (r1 * S1C + f10 + g + 1) * kCdPos + 2 * t4;
+      if (!(t1 >= 0 && t1 < L1)) {  // row outside the segment: zero for the depthwise conv
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          *reinterpret_cast<uint32_t *>(dst + nt * 8) = 0u;
+          *reinterpret_cast<uint32_t *>(dst + 8 * kCdPos + nt * 8) = 0u;
+        }
+        continue;
+      }
       // A fragments: rows g and g + 8 = positions f10 + g, f10 + g + 8 of row r1
       const float *base = melS + (2 * r1) * FP + 2 * (f10 + g);
       float xa[4], xb[4];
@@ -167,62 +224,144 @@ __global__ void __launch_bounds__(256) conv0_dw_s2_kernel(
       ah[1] = bf16x2_hi_lo(xb[0], xb[1], al[1]);
       ah[2] = bf16x2_hi_lo(xa[2], xa[3], al[2]);
       ah[3] = bf16x2_hi_lo(xb[2], xb[3], al[3]);
+      const bool ok0 = f10 + g < F1, ok1 = f10 + g + 8 < F1;  // positions from F1 on stay zero
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
         mma_16816_bf16(acc, ah, bh[nt][0], bh[nt][1]);
         mma_16816_bf16(acc, ah, bl[nt][0], bl[nt][1]);
         mma_16816_bf16(acc, al, bh[nt][0], bh[nt][1]);
-        const int ch = nt * 8 + 2 * t4;
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int f1 = f10 + g + 8 * h;
-          if (f1 >= F1) continue;
-          const float v0 = row_live ? fmaxf(acc[2 * h] + bias_c[nt][0], 0.f) : 0.f;
-          const float v1 = row_live ? fmaxf(acc[2 * h + 1] + bias_c[nt][1], 0.f) : 0.f;
-          *reinterpret_cast<__nv_bfloat162 *>(s1S + (r1 * S1C + f1 + 1) * kCdCG + ch) = __floats2bfloat162_rn(v0, v1);
-        }
+        const uint32_t p0 = relu_bf16x2(add_f32x2(f2(acc[0], acc[1]), bias0[nt]));
+        const uint32_t p1 = relu_bf16x2(add_f32x2(f2(acc[2], acc[3]), bias0[nt]));
+        *reinterpret_cast<uint32_t *>(dst + nt * 8) = ok0 ? p0 : 0u;
+        *reinterpret_cast<uint32_t *>(dst + 8 * kCdPos + nt * 8) = ok1 ? p1 : 0u;
       }
     }
   }
   __syncthreads();
-  // 3. depthwise 3x3 stride 2 over the staged rows (zero rows / guard column
-  //    stand in for the taps outside the segment), two channels per thread
+  // 3. depthwise 3x3 stride 2 over the staged rows (zero rows / guard and pad
+  //    positions stand in for the taps outside the segment): warp w takes the
+  //    4-column output patches q = w, w + 8, ..., lane = channel pair
   {
-    const int cp = threadIdx.x & 31;
-    const int grp = threadIdx.x >> 5;
-    const int cc = cg0 + 2 * cp;
-    float wa[9], wb[9];
+    const int nq = (F2 + 3) / 4;
+    for (int q = warp; q < nq; q += 8) {
+      uint64_t acc[kCdTT][4];
 #pragma unroll
-    for (int i = 0; i < 9; ++i) {
-      wa[i] = w2[cc * 9 + i];
-      wb[i] = w2[(cc + 1) * 9 + i];
-    }
-    const float ba = b2[cc], bb = b2[cc + 1];
-    for (int task = grp; task < kCdTT * F2; task += 8) {
-      const int r2 = task / F2;
-      const int f2 = task - r2 * F2;
-      const int t2 = t2s + r2;
-      if (t2 >= T2) break;
-      float a0 = ba, a1 = bb;
+      for (int r2 = 0; r2 < kCdTT; ++r2)
 #pragma unroll
-      for (int dt = 0; dt < 3; ++dt) {
-        const __nv_bfloat16 *row = s1S + ((2 * r2 + dt) * S1C + 2 * f2) * kCdCG + 2 * cp;  // column f1 = 2 f2 - 1
+        for (int j = 0; j < 4; ++j) acc[r2][j] = bias2;
+      // s1 row rr feeds output rows r2 with rr = 2 r2 + dt; columns 8q - 1 .. 8q + 7
+      // (positions 8q .. 8q + 8) feed output columns 4q + j with column = 2 (4q + j) - 1 + df
 #pragma unroll
-        for (int df = 0; df < 3; ++df) {
-          if (2 * f2 - 1 + df >= F1) continue;
-          const float2 v = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(row + df * kCdCG));
-          a0 += wa[dt * 3 + df] * v.x;
-          a1 += wb[dt * 3 + df] * v.y;
+      for (int rr = 0; rr < kCdRows1; ++rr) {
+        const __nv_bfloat16 *row = s1S + (rr * S1C + 8 * q) * kCdPos + 2 * lane;
+        uint64_t v[9];
+#pragma unroll
+        for (int c = 0; c < 9; ++c) v[c] = f32x2_of_bf16x2(*reinterpret_cast<const uint32_t *>(row + c * kCdPos));
+#pragma unroll
+        for (int r2 = 0; r2 < kCdTT; ++r2) {
+          const int dt = rr - 2 * r2;
+          if (dt < 0 || dt > 2) continue;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int df = 0; df < 3; ++df) acc[r2][j] = fma_f32x2(wv[dt * 3 + df], v[2 * j + df], acc[r2][j]);
         }
       }
-      *reinterpret_cast<__nv_bfloat162 *>(out + ((static_cast<int64_t>(b) * T2 + t2) * F2 + f2) * C + cc) =
-          __floats2bfloat162_rn(a0, a1);
+#pragma unroll
+      for (int r2 = 0; r2 < kCdTT; ++r2) {
+        const int t2 = t2s + r2;
+        if (t2 >= T2) break;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int f2o = 4 * q + j;
+          if (f2o >= F2) break;
+          *reinterpret_cast<uint32_t *>(out + ((static_cast<int64_t>(b) * T2 + t2) * F2 + f2o) * C + cc) =
+              bf16x2_of(acc[r2][j]);
+        }
+      }
     }
   }
 }
 
-__global__ void dwconv2d_s2_kernel(const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len_in, int Tin,
+// Depthwise 3x3 stride-2 conv (pad 1) over [B, Tin, Fin, C] bf16, taps with
+// t outside [0, min(Tin, len)) or f outside [0, Fin) zero (fast_conformer.rs
+// dwconv2d_s2).  Warp task = (2 output rows x 4 output columns, 64 channels):
+// lane = channel pair, so every load is one 128-byte line of a position, the
+// 5 x 9 input patch the task needs is read once (instead of 9 taps per output)
+// and the eight outputs accumulate in independent packed f32x2 FMA chains, in
+// the same tap order (dt, then df) as a per-output loop.
+constexpr int kDwRows = 2, kDwCols = 4;
+
+__global__ void __launch_bounds__(256) dwconv2d_s2_kernel(const __nv_bfloat16 *__restrict__ in,
+                                                          const int *__restrict__ len_in, int Tin, int Fin, int Tout,
+                                                          int Fout, int C, const float *__restrict__ w,
+                                                          const float *__restrict__ bias,
+                                                          __nv_bfloat16 *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int c = blockIdx.y * 64 + 2 * lane;
+  uint64_t wv[9];
+#pragma unroll
+  for (int i = 0; i < 9; ++i) wv[i] = f2(w[c * 9 + i], w[(c + 1) * 9 + i]);
+  const uint64_t bv = f2(bias[c], bias[c + 1]);
+  pdl_wait();  // predecessor kernel complete, its writes visible
+  pdl_trigger();
+  const int b = blockIdx.z;
+  const int nfq = (Fout + kDwCols - 1) / kDwCols;
+  const int task = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int tr = task / nfq;
+  const int fq = task - tr * nfq;
+  const int to0 = kDwRows * tr, fo0 = kDwCols * fq;
+  if (to0 >= Tout) return;
+  const int L = min(len_in[b], Tin);
+  uint64_t acc[kDwRows][kDwCols];
+#pragma unroll
+  for (int r = 0; r < kDwRows; ++r)
+#pragma unroll
+    for (int j = 0; j < kDwCols; ++j) acc[r][j] = bv;
+  // input rows 2 to0 - 1 + rr (rr < 2 kDwRows + 1), columns 2 fo0 - 1 + cc (cc < 2 kDwCols + 1)
+#pragma unroll
+  for (int rr = 0; rr < 2 * kDwRows + 1; ++rr) {
+    const int t = 2 * to0 - 1 + rr;
+    if (t < 0 || t >= L) continue;  // zero row (warp-uniform)
+    const __nv_bfloat16 *row = in + (static_cast<int64_t>(b) * Tin + t) * Fin * C + c;
+    uint64_t v[2 * kDwCols + 1];
+#pragma unroll
+    for (int cc = 0; cc < 2 * kDwCols + 1; ++cc) {
+      const int f = 2 * fo0 - 1 + cc;
+      const uint32_t p = f >= 0 && f < Fin ? __ldg(reinterpret_cast<const unsigned int *>(row + static_cast<int64_t>(f) * C)) : 0u;
+      v[cc] = f2(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
+    }
+#pragma unroll
+    for (int r = 0; r < kDwRows; ++r) {
+      const int dt = rr - 2 * r;
+      if (dt < 0 || dt > 2) continue;
+#pragma unroll
+      for (int j = 0; j < kDwCols; ++j)
+#pragma unroll
+        for (int df = 0; df < 3; ++df) {
+          uint64_t d;
+          asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(wv[dt * 3 + df]), "l"(v[2 * j + df]), "l"(acc[r][j]));
+          acc[r][j] = d;
+        }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kDwRows; ++r) {
+    const int to = to0 + r;
+    if (to >= Tout) break;
+#pragma unroll
+    for (int j = 0; j < kDwCols; ++j) {
+      const int fo = fo0 + j;
+      if (fo >= Fout) break;
+      *reinterpret_cast<uint32_t *>(out + ((static_cast<int64_t>(b) * Tout + to) * Fout + fo) * C + c) =
+          bf16x2_of(acc[r][j]);
+    }
+  }
+}
+
+// Any C: one output per thread (the general fallback of the kernel above).
+__global__ void dwconv2d_s2_any_kernel(const __nv_bfloat16 *__restrict__ in, const int *__restrict__ len_in, int Tin,
                                    int Fin, int Tout, int Fout, int C, const float *__restrict__ w,
                                    const float *__restrict__ bias, __nv_bfloat16 *__restrict__ out) {
   pdl_wait();  // predecessor kernel complete, its writes visible
@@ -784,10 +923,17 @@ cudaError_t conv0_dw_s2(const float *mel, const int *len0, const int *len1, int 
 
 cudaError_t dwconv2d_s2(const __nv_bfloat16 *in, const int *len_in, int B, int Tin, int Fin, int Tout, int Fout, int C,
                         const float *w, const float *bias, __nv_bfloat16 *out, cudaStream_t s) {
-  const int per = Fout * C;
   const int threads = 256;
+  if (C % 64 == 0) {
+    const int tasks = ((Tout + kDwRows - 1) / kDwRows) * ((Fout + kDwCols - 1) / kDwCols);
+    dim3 grid((tasks + threads / 32 - 1) / (threads / 32), C / 64, B);
+    return launch_pdl(dwconv2d_s2_kernel, grid, dim3(threads), 0, s, 1, in, len_in, Tin, Fin, Tout, Fout, C, w, bias,
+                      out);
+  }
+  const int per = Fout * C;
   dim3 grid((per + threads - 1) / threads, Tout, B);
-  return launch_pdl(dwconv2d_s2_kernel, grid, dim3(threads), 0, s, 1, in, len_in, Tin, Fin, Tout, Fout, C, w, bias, out);
+  return launch_pdl(dwconv2d_s2_any_kernel, grid, dim3(threads), 0, s, 1, in, len_in, Tin, Fin, Tout, Fout, C, w, bias,
+                    out);
 }
 
 cudaError_t flatten_cf(const __nv_bfloat16 *in, int rows, int F, int C, __nv_bfloat16 *out, cudaStream_t s) {
