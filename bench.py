@@ -8,8 +8,11 @@ padded segments, through the full 24-layer encoder (configs[1] architecture,
 random-init Q8_0 weights).  One step = every bucket of this rank once.  Ranks
 are independent (segment sharding, no collective on the data path; one
 all-reduce of the timings after the timed region): weak scaling.
+`--shard lpt` instead splits ONE job of --segments segments over the ranks
+(length buckets assigned by greedy longest-processing-time on the estimated
+bucket cost, nspeech_b200/shard.py): strong scaling.
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--shard weak|lpt]
     python bench.py --gemv [--gemv-shapes MxKxN,...] [--gemv-plain CALLS]
 
 Prints one JSON line (rank 0).  `value`: RTFx = audio seconds of all ranks /
@@ -55,6 +58,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--segments", type=int, default=1024)
     ap.add_argument("--max-batch", type=int, default=32)
+    ap.add_argument("--shard", choices=["weak", "lpt"], default="weak",
+                    help="weak: each rank runs its own --segments; lpt: one job of --segments split over the ranks")
     ap.add_argument("--layers", type=int, default=24)
     ap.add_argument("--e2e-steps", type=int, default=1)
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the buckets of a step alternate over")
@@ -79,8 +84,27 @@ def peaks() -> dict:
 
 
 # ------------------------------------------------------------------ workload
-def make_buckets(rank: int, n_segments: int, max_batch: int, feat: int):
+def make_buckets(rank: int, n_segments: int, max_batch: int, feat: int, shard: str = "weak", world: int = 1):
+    """This rank's padded buckets [(mel [B, T, feat], lengths)] and their audio seconds.
+
+    shard "weak": the rank's own n_segments (seed 4 + rank), length-bucketed.
+    shard "lpt": one job of n_segments (seed 4) split over the ranks by
+    nspeech_b200.shard (length buckets, greedy LPT on the estimated bucket
+    cost); a segment's features depend only on its index, not on the world size.
+    """
     from nspeech_b200 import synthetic as S
+    if shard == "lpt":
+        from nspeech_b200 import shard as SH
+        secs = S.segment_lengths_s(n_segments, 2.0, 30.0, seed=4)
+        frames = [S.mel_frames(s) for s in secs]
+        buckets = []
+        for idx in SH.shard_segments(frames, max_batch, world, rank):
+            lens = [int(frames[j]) for j in idx]
+            mel = np.zeros((len(idx), max(lens), feat), np.float32)
+            for r, (j, L) in enumerate(zip(idx, lens)):
+                mel[r, :L] = np.random.default_rng(100000 + j).standard_normal((L, feat), dtype=np.float32)
+            buckets.append((mel, lens))
+        return buckets, float(sum(L for _, ls in buckets for L in ls)) * 0.01
     secs = S.segment_lengths_s(n_segments, 2.0, 30.0, seed=4 + rank)
     frames = np.array([S.mel_frames(s) for s in secs])
     order = np.argsort(frames, kind="stable")
@@ -234,7 +258,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     spec = S.EncoderSpec(n_layers=args.layers)
     enc, tensors = make_encoder(spec)
-    buckets, audio_s = make_buckets(rank, args.segments, args.max_batch, spec.feat_in)
+    buckets, audio_s = make_buckets(rank, args.segments, args.max_batch, spec.feat_in, args.shard, world)
+    if not buckets:
+        raise SystemExit(f"rank {rank}: no buckets (--shard lpt needs at least one bucket per rank)")
 
     mel_dev, out_dev = [], []
     for mel, lens in buckets:
@@ -361,18 +387,23 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "warmup": args.warmup,
             "ms_per_step": 1e3 * t_max / args.steps,
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "weak" if args.shard == "weak" else "strong",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) log-mel features, random-init Q8_0 weights",
             "config": {
-                "workload": "configs[4]: 1024 VAD segments/GPU, U[2,30] s, length-bucketed batches <= 32, "
+                "workload": (f"configs[4]: {args.segments} VAD segments/GPU" if args.shard == "weak" else
+                             f"configs[4]: one job of {args.segments} VAD segments split over {world} GPU(s) "
+                             "(length buckets, greedy LPT)") +
+                            f", U[2,30] s, length-bucketed batches <= {args.max_batch}, "
                             "full 24-layer encoder (configs[1] architecture)",
                 "model": "Parakeet TDT 0.6B FastConformer encoder (24 layers, d 1024, 8 heads, FFN 4096, conv 9)",
-                "segments_per_gpu": args.segments, "max_batch": args.max_batch, "audio_s_per_gpu": audio_s,
+                "segments_per_gpu": args.segments if args.shard == "weak" else sum(len(ls) for _, ls in buckets),
+                "shard": args.shard, "max_batch": args.max_batch, "audio_s_per_gpu": audio_s,
                 "buckets": len(buckets), "streams": len(streams),
                 "seq_len": max(out_frames(m.shape[1]) for m, _ in buckets),
-                "global_batch": args.segments * world, "parallelism": f"dp{world} (segment-sharded, no collective)",
+                "global_batch": args.segments * world if args.shard == "weak" else args.segments,
+                "parallelism": f"dp{world} (segment-sharded, no collective)",
                 "l2": "inputs larger than L2: 0.64 GB of Q8_0 weights stream per pass; activations up to 1.6 GB",
             },
             "e2e": {"value": args.e2e_steps * audio_total / te2e_max, "unit": UNIT, "h2d_bytes_per_step": h2d,
