@@ -86,6 +86,24 @@ def test_encoder_matches_oracle(nq, oracle, d_model, heads, layers, t_mel, tol, 
     _compare(oracle, out[0].cpu().numpy(), ref, f"encoder d{d_model} L{layers} T{t_mel}", tol)
 
 
+# 88 mel bins: every subsampling stage ends on a partial frequency tile
+# (F1 = 44 of the fused kernel's three 16-position conv0 tiles, F2 = 22 of its
+# six 4-column depthwise patches, F3 = 11 of the second depthwise conv's three
+# 4-column patches); 333 mel frames end on a partial 4-row output tile.
+@pytest.mark.parametrize("sub", [64, 256])
+def test_encoder_ragged_mel_bins_matches_oracle(nq, oracle, sub):
+    from nspeech_b200 import synthetic as S
+    spec = S.EncoderSpec(feat_in=88, d_model=512, n_heads=4, n_layers=1, sub_channels=sub)
+    q = _model(oracle, spec, seed=6)
+    enc = _gpu_encoder(spec, q)
+    mel = oracle.normal(3, (333, 88))
+    out, lens = enc.forward(torch.from_numpy(mel)[None].cuda())
+    torch.cuda.synchronize()
+    ref = oracle.encoder_forward(spec.as_dict(), _oracle_tensors(q), mel)
+    assert lens == [ref.shape[0]]
+    _compare(oracle, out[0].cpu().numpy(), ref, f"encoder F88 sub{sub} T333", 0.05)
+
+
 def test_batched_segments_equal_single(nq, oracle):
     """A padded batch of segments reproduces each segment's own forward."""
     from nspeech_b200 import synthetic as S
