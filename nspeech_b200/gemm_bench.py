@@ -16,7 +16,9 @@ measured peaks in MEASURED_PEAKS.json when present.
 --cfg1-sweep: the configs[0] block (K -> N: 1024->4096, 4096->1024,
 1024->3072, 1024->1024, 1024->2048, 1024->1024) at M in {1, 2, 4, 8, 16,
 125, 1024, 2048, 4096, 12000}; f32 activations in and out, or
-bf16 with --sweep-dtype bf16 (the encoder's activations).
+bf16 with --sweep-dtype bf16 (the encoder's activations); --sweep-m picks a
+subset of M.  --keep-bf16 gives every weight a kept bf16 copy, as the
+encoder does, so M >= 128 GEMMs skip the per-call dequantize pass.
 """
 from __future__ import annotations
 
@@ -31,13 +33,14 @@ from . import lib
 from .fast_matmul import QWeight
 
 
-def _weights(n: int, k: int, copies: int, rng) -> list:
+def _weights(n: int, k: int, copies: int, rng, keep_bf16: bool = False) -> list:
     out = []
     for _ in range(copies):
         q = rng.integers(-127, 128, size=(n, k // 32, 34), dtype=np.int64).astype(np.uint8)
         d = (rng.random((n, k // 32)) * 1e-3 + 1e-4).astype(np.float16)
         q[:, :, :2] = d.view(np.uint8).reshape(n, k // 32, 2)
-        out.append(QWeight.from_q8_0(q.reshape(n, -1), n, k))
+        w = QWeight.from_q8_0(q.reshape(n, -1), n, k)
+        out.append(w.keep_bf16() if keep_bf16 else w)
     return out
 
 
@@ -55,11 +58,12 @@ def _peaks() -> dict:
 
 
 def time_shape(m: int, k: int, n: int, x_dtype=torch.bfloat16, y_dtype=torch.bfloat16, iters: int = 20,
-               epilogue: int = lib.NQ_EPI_NONE, seed: int = 0, graph: bool = False) -> dict:
+               epilogue: int = lib.NQ_EPI_NONE, seed: int = 0, graph: bool = False, keep_bf16: bool = False) -> dict:
     rng = np.random.default_rng(seed)
     wbytes = n * k * 34 / 32
-    copies = int(min(32, max(1, np.ceil(300e6 / wbytes))))
-    ws = _weights(n, k, copies, rng)
+    # weights stream past L2 (the kept bf16 copy, when kept, is what the GEMM reads)
+    copies = int(min(32, max(1, np.ceil(300e6 / (n * k * 2 if keep_bf16 else wbytes)))))
+    ws = _weights(n, k, copies, rng, keep_bf16)
     x = torch.randn(m, k, device="cuda").to(x_dtype)
     y = torch.empty(m, n, device="cuda", dtype=y_dtype)
     stream = torch.cuda.Stream()
@@ -99,7 +103,8 @@ def time_shape(m: int, k: int, n: int, x_dtype=torch.bfloat16, y_dtype=torch.bfl
     frac = gbs / pk["hbm_gbs"] if bound == "hbm" else tflops / pk["bf16_tflops"]
     return {"m": m, "k": k, "n": n, "x": str(x_dtype).split(".")[-1], "y": str(y_dtype).split(".")[-1],
             "us": round(t * 1e6, 2), "tflops": round(tflops, 1), "gbs": round(gbs, 1), "bound": bound,
-            "frac": round(frac, 3), "peak_source": pk["source"], "timing": "graph" if graph else "calls"}
+            "frac": round(frac, 3), "peak_source": pk["source"], "timing": "graph" if graph else "calls",
+            "weights": "kept bf16 copy" if keep_bf16 else "q8_0"}
 
 
 def main() -> None:
@@ -113,6 +118,9 @@ def main() -> None:
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--graph", action="store_true", help="time a CUDA graph of the calls (device time)")
     ap.add_argument("--device", type=int, default=0)
+    ap.add_argument("--keep-bf16", action="store_true",
+                    help="give every weight a kept bf16 copy (nq_weight_keep_bf16), as the encoder does")
+    ap.add_argument("--sweep-m", default="", help="comma-separated subset of the sweep's M values")
     a = ap.parse_args()
     torch.cuda.set_device(a.device)
     lib.init(a.device)
@@ -120,11 +128,13 @@ def main() -> None:
     jobs = [(tuple(int(v) for v in s.lower().split("x")), dt[a.x], dt[a.y]) for s in a.shape]
     if a.cfg1_sweep:
         sd = dt[a.sweep_dtype]
-        jobs += [((m, k, n), sd, sd) for m in CFG1_M for k, n in CFG1_KN]
+        ms = [int(v) for v in a.sweep_m.split(",")] if a.sweep_m else CFG1_M
+        jobs += [((m, k, n), sd, sd) for m in ms for k, n in CFG1_KN]
     if not jobs:
         ap.error("give --shape or --cfg1-sweep")
     for (m, k, n), xd, yd in jobs:
-        print(json.dumps(time_shape(m, k, n, x_dtype=xd, y_dtype=yd, iters=a.iters, graph=a.graph)), flush=True)
+        print(json.dumps(time_shape(m, k, n, x_dtype=xd, y_dtype=yd, iters=a.iters, graph=a.graph,
+                                    keep_bf16=a.keep_bf16)), flush=True)
 
 
 if __name__ == "__main__":
