@@ -323,6 +323,13 @@ int nq_set_wait_limit(int64_t cycles);
 #define NQ_GEMM_DEQUANT 2
 int nq_set_gemm_path(int path);
 
+/* Tokens per 2-SM work unit of the dequantize-once (bf16 tcgen05) GEMM: 64,
+ * 128 or 256, or 0 for the default (256).  No counterpart in the reference:
+ * a B200 dispatch knob.  Narrower units give calls of a few thousand tokens
+ * more units to spread over the SM pairs instead of splitting K.
+ * Process-wide; returns NQ_ERR_ARG for other values. */
+int nq_set_gemm_unit_tokens(int tokens);
+
 /* Test hook for failure detection: launches a kernel that waits on an
  * mbarrier nothing arrives on, bounded by the wait limit; the kernel records
  * NQ_DEV_TIMEOUT_CONSUMER and returns, leaving the context usable. */

@@ -64,6 +64,7 @@ DeviceCtx g_ctx[kMaxDevices];
 std::mutex g_init_mu;
 long long g_wait_limit = 1LL << 31;
 int g_gemm_path = NQ_GEMM_AUTO;
+int g_gemm_unit_tokens = 0;  // 0: the kernel's default unit width
 // Token count from which a GEMM call dequantizes the weight once and runs
 // the bf16 tensor-core GEMM (measured crossover on B200).
 constexpr int64_t kDequantMinM = 128;
@@ -403,7 +404,7 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
   // waves of 256 x 256 units times their k steps, plus, when split, one write
   // and one read of the f32 partials and the reduction launch.
   const int ldp = w->n_tiles * nq::kPackRows;
-  g.bt = nq::gemm_bf16_block_t();
+  g.bt = g_gemm_unit_tokens ? g_gemm_unit_tokens : nq::gemm_bf16_block_t();
   g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
   const int tiles = g.grid_m * g.grid_n;
   double best = 1e300;
@@ -414,7 +415,8 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
     if (splits != sp) continue;
     const int64_t units = static_cast<int64_t>(tiles) * splits;
     const int64_t rounds = (units + g.pairs - 1) / g.pairs;
-    double t = static_cast<double>(rounds) * cps * kNsPerUnitStep;
+    // a k step of a unit scales with its token width (measured at 256)
+    double t = static_cast<double>(rounds) * cps * kNsPerUnitStep * g.bt / 256.0;
     if (splits > 1) t += 2.0 * splits * static_cast<double>(m) * ldp * 4.0 / kReduceBytesPerNs + kReduceLaunchNs;
     if (t < best) {
       best = t;
@@ -509,7 +511,7 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     p.ctl.status = ctx->status;
     p.ctl.wait_limit = g_wait_limit;
     ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
-    cudaError_t e = nq::launch_gemm_bf16(splitx, tm_w, tm_a, tm_alo, p, std::min(units, pairs), stream);
+    cudaError_t e = nq::launch_gemm_bf16(splitx, bt, tm_w, tm_a, tm_alo, p, std::min(units, pairs), stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   } else {
     nq::GemmParams p;
@@ -1025,6 +1027,13 @@ int nq_set_gemm_path(int path) {
   if (path != NQ_GEMM_AUTO && path != NQ_GEMM_FUSED && path != NQ_GEMM_DEQUANT)
     return fail(NQ_ERR_ARG, "unknown GEMM path %d", path);
   g_gemm_path = path;
+  return NQ_OK;
+}
+
+int nq_set_gemm_unit_tokens(int tokens) {
+  if (tokens != 0 && !nq::gemm_bf16_unit_ok(tokens))
+    return fail(NQ_ERR_ARG, "GEMM unit width %d (use 0, 64, 128 or 256)", tokens);
+  g_gemm_unit_tokens = tokens;
   return NQ_OK;
 }
 

@@ -33,28 +33,33 @@
 namespace nq {
 namespace {
 
-constexpr int kPT = 256;         // tokens per pair unit (MMA N)
-constexpr int kPTHalf = 128;     // token rows per CTA
+constexpr int kPTDefault = 256;  // tokens per pair unit (MMA N) unless set otherwise
 constexpr int kPW = 256;         // weight rows per pair unit (MMA M)
 constexpr int kEpiW = 16;        // epilogue warps: 4 column groups x 4 lane quarters
 constexpr int kThreads = 32 * (2 + kEpiW);  // 576
 constexpr int kEpi0 = 2;
-constexpr int kColsPerWarp = kPT / 4;  // 64
 constexpr int kAgreeBar = 9;     // named barrier of all epilogue warps (1..8: GLU pairs)
 
-template <bool SPLITX>
+// PT: tokens per pair unit (MMA N = PT, PT / 2 token rows per CTA).  256 is
+// the default; 128 and 64 give small-M calls more units instead of split K.
+template <bool SPLITX, int PT>
 struct Cfg {
-  static constexpr int kStages = SPLITX ? 4 : 6;
+  static_assert(PT == 64 || PT == 128 || PT == 256, "unit widths 64, 128, 256");
+  static constexpr int kPT = PT;
+  static constexpr int kPTHalf = PT / 2;       // token rows per CTA
+  static constexpr int kColsPerWarp = PT / 4;  // tokens per epilogue warp (4 column groups)
+  static_assert(kColsPerWarp % kEc == 0, "epilogue chunks");
+  static constexpr int kStages = SPLITX ? (PT == 256 ? 4 : 6) : (PT == 256 ? 6 : 8);
   static constexpr int kABytes = 128 * kPackK * 2;      // 16 KB of weight rows
-  static constexpr int kBBytes = kPTHalf * kPackK * 2;  // 16 KB per activation plane
+  static constexpr int kBBytes = kPTHalf * kPackK * 2;  // 4 / 8 / 16 KB per activation plane
   static constexpr int kStageBytes = kABytes + kBBytes * (SPLITX ? 2 : 1);
   static constexpr int kGluOffset = kStages * kStageBytes;
   static constexpr int kGluBytes = 8 * kEc * 32 * 4;    // 8 value/gate warp pairs
   static constexpr int kBarOffset = kGluOffset + kGluBytes;
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kBarOffset + kNumBars * 8 + 64;
-  static constexpr uint32_t kIdesc = idesc_bf16_f32(kPW, kPT);
-  static constexpr int kTmemCols = 512;  // D0 [0,256), D1 [256,512)
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(kPW, PT);
+  static constexpr int kTmemCols = 2 * PT;  // D0 [0, PT), D1 [PT, 2 PT)
   static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
@@ -74,12 +79,13 @@ __device__ __forceinline__ Unit decode_unit(const GemmBf16Params &p, int u) {
   return r;
 }
 
-template <bool SPLITX>
+template <bool SPLITX, int PT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                            const __grid_constant__ CUtensorMap tm_alo, const __grid_constant__ GemmBf16Params p) {
-  using C = Cfg<SPLITX>;
+  using C = Cfg<SPLITX, PT>;
   constexpr int kStages = C::kStages;
+  constexpr int kPT = C::kPT, kPTHalf = C::kPTHalf, kColsPerWarp = C::kColsPerWarp;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
@@ -324,11 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool SPLITX>
+template <bool SPLITX, int PT>
 cudaError_t launch_t(const CUtensorMap &w, const CUtensorMap &a_hi, const CUtensorMap &a_lo, const GemmBf16Params &p,
                      int pairs, cudaStream_t stream) {
-  using C = Cfg<SPLITX>;
-  auto kern = gemm_bf16_sm100_kernel<SPLITX>;
+  using C = Cfg<SPLITX, PT>;
+  auto kern = gemm_bf16_sm100_kernel<SPLITX, PT>;
   static bool attr_set[64] = {false};  // once per device (the attribute is per-context state)
   static int max_pairs[64] = {0};
   int dev = 0;
@@ -364,12 +370,21 @@ cudaError_t launch_t(const CUtensorMap &w, const CUtensorMap &a_hi, const CUtens
 
 }  // namespace
 
-int gemm_bf16_block_t() { return kPT; }
+int gemm_bf16_block_t() { return kPTDefault; }
 int gemm_bf16_block_w() { return kPW; }
+bool gemm_bf16_unit_ok(int tokens) { return tokens == 64 || tokens == 128 || tokens == 256; }
 
-cudaError_t launch_gemm_bf16(bool splitx, const CUtensorMap &w, const CUtensorMap &a_hi, const CUtensorMap &a_lo,
-                             const GemmBf16Params &p, int pairs, cudaStream_t stream) {
-  return splitx ? launch_t<true>(w, a_hi, a_lo, p, pairs, stream) : launch_t<false>(w, a_hi, a_lo, p, pairs, stream);
+cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w, const CUtensorMap &a_hi,
+                             const CUtensorMap &a_lo, const GemmBf16Params &p, int pairs, cudaStream_t stream) {
+  switch (unit_tokens * 2 + (splitx ? 1 : 0)) {
+    case 512: return launch_t<false, 256>(w, a_hi, a_lo, p, pairs, stream);
+    case 513: return launch_t<true, 256>(w, a_hi, a_lo, p, pairs, stream);
+    case 256: return launch_t<false, 128>(w, a_hi, a_lo, p, pairs, stream);
+    case 257: return launch_t<true, 128>(w, a_hi, a_lo, p, pairs, stream);
+    case 128: return launch_t<false, 64>(w, a_hi, a_lo, p, pairs, stream);
+    case 129: return launch_t<true, 64>(w, a_hi, a_lo, p, pairs, stream);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 }  // namespace nq

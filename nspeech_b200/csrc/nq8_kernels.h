@@ -111,14 +111,17 @@ struct GemmBf16Params {
   int splits;
   int cps;
   int grid_n;       // 256-row weight pair tiles
-  int grid_m;       // 256-token tiles
+  int grid_m;       // token tiles of the unit width
   float *partials;  // split-K only: [splits][M][n_rows] f32
   DevCtl ctl;
 };
-int gemm_bf16_block_t();     // tokens per pair unit
-int gemm_bf16_block_w();     // weight rows per pair unit
-cudaError_t launch_gemm_bf16(bool splitx, const CUtensorMap &w, const CUtensorMap &a_hi, const CUtensorMap &a_lo,
-                             const GemmBf16Params &p, int pairs, cudaStream_t stream);
+int gemm_bf16_block_t();              // default tokens per pair unit
+int gemm_bf16_block_w();              // weight rows per pair unit
+bool gemm_bf16_unit_ok(int tokens);   // unit widths the kernel is built for (64, 128, 256)
+// unit_tokens: tokens per pair unit (grid_m in p counts units of that width;
+// the token tensor maps have boxes of unit_tokens / 2 rows).
+cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w, const CUtensorMap &a_hi,
+                             const CUtensorMap &a_lo, const GemmBf16Params &p, int pairs, cudaStream_t stream);
 
 // Packed Q8_0 tiles -> bf16 [n_tiles * 128][kc * 64] (row-major, packed row
 // order), each element bf16(f32(d) * q).

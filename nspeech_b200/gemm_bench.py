@@ -121,6 +121,8 @@ def main() -> None:
     ap.add_argument("--keep-bf16", action="store_true",
                     help="give every weight a kept bf16 copy (nq_weight_keep_bf16), as the encoder does")
     ap.add_argument("--sweep-m", default="", help="comma-separated subset of the sweep's M values")
+    ap.add_argument("--unit-tokens", default="0",
+                    help="comma-separated GEMM unit widths to time each shape with (nq_set_gemm_unit_tokens; 0 = default)")
     a = ap.parse_args()
     torch.cuda.set_device(a.device)
     lib.init(a.device)
@@ -132,9 +134,14 @@ def main() -> None:
         jobs += [((m, k, n), sd, sd) for m in ms for k, n in CFG1_KN]
     if not jobs:
         ap.error("give --shape or --cfg1-sweep")
+    units = [int(v) for v in a.unit_tokens.split(",")]
     for (m, k, n), xd, yd in jobs:
-        print(json.dumps(time_shape(m, k, n, x_dtype=xd, y_dtype=yd, iters=a.iters, graph=a.graph,
-                                    keep_bf16=a.keep_bf16)), flush=True)
+        for u in units:
+            lib.check(lib.load().nq_set_gemm_unit_tokens(u))
+            r = time_shape(m, k, n, x_dtype=xd, y_dtype=yd, iters=a.iters, graph=a.graph, keep_bf16=a.keep_bf16)
+            r["unit_tokens"] = u
+            print(json.dumps(r), flush=True)
+    lib.check(lib.load().nq_set_gemm_unit_tokens(0))
 
 
 if __name__ == "__main__":

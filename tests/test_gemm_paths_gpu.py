@@ -151,3 +151,46 @@ def test_kept_bf16_copy_is_identical_and_skips_dequant(nq, oracle):
         c = w.linear(x, epilogue=epi, out_dtype=torch.float32)
         assert torch.equal(a, c)
     assert nq.status() == 0
+
+
+# Units of 64 / 128 tokens (nq_set_gemm_unit_tokens) in place of 256: MMA
+# N = 64 / 128, token tiles of 32 / 64 rows per CTA, 128 / 256 TMEM columns.
+# Partial token tiles (1100, 2100, 300, 129, 375 rows), GLU, f32 activations
+# (hi + lo planes) and a split-K shape (375 x 4096 -> 1024).  Without split K
+# every output is one unit's k-ordered sum, so it must equal the 256-token
+# result bit for bit.
+@pytest.mark.parametrize("unit", [64, 128])
+@pytest.mark.parametrize("m,k,n,epi,xdt", [(1100, 1024, 3072, 0, "bf16"), (2100, 1024, 1024, 1, "f32"),
+                                           (300, 640, 1920, 3, "bf16"), (129, 96, 130, 0, "bf16"),
+                                           (375, 4096, 1024, 0, "bf16")])
+def test_narrow_units_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
+    from nspeech_b200.fast_matmul import QWeight
+    L = nq.load()
+    glu = epi in (3, 4)
+    q = oracle.quantize_q8_0(oracle.normal(360 + n + k, (n, k), 0.0, 0.02))
+    bias = oracle.normal(361, (n,), 0.0, 0.01)
+    w = QWeight.from_q8_0(q, n, k, flags=nq.NQ_PACK_GLU if glu else 0)
+    x = oracle.normal(362 + m, (m, k))
+    if xdt == "bf16":
+        x = _bf16_round(x)
+    xt = torch.from_numpy(x).cuda().to(torch.float32 if xdt == "f32" else torch.bfloat16)
+    bt = torch.from_numpy(bias).cuda()
+    outs = {}
+    nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_DEQUANT))
+    nq.profile_enable(True)
+    try:
+        for u in (256, unit):
+            nq.check(L.nq_set_gemm_unit_tokens(u))
+            nq.profile_read(nq.NQ_KCLASS_REDUCE, True)
+            y = w.linear(xt, bias=bt, epilogue=epi, out_dtype=torch.float32).clone()
+            outs[u] = (y, nq.profile_read(nq.NQ_KCLASS_REDUCE, True)["launches"])
+    finally:
+        nq.profile_enable(False)
+        nq.check(L.nq_set_gemm_unit_tokens(0))
+        nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_AUTO))
+    y, red = outs[unit]
+    assert y.shape == (m, n // 2 if glu else n)
+    _check(oracle, y.cpu().numpy(), _ref(oracle, x, q, n, bias, epi), f"unit {unit} {m}x{k}x{n} epi={epi} {xdt}")
+    if red == 0 and outs[256][1] == 0:
+        assert torch.equal(y, outs[256][0]), f"unit {unit} differs from 256 without split K"
+    assert nq.status() == 0
