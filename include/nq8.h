@@ -324,10 +324,11 @@ int nq_set_wait_limit(int64_t cycles);
 int nq_set_gemm_path(int path);
 
 /* Tokens per 2-SM work unit of the dequantize-once (bf16 tcgen05) GEMM: 64,
- * 128 or 256, or 0 for the default (256).  No counterpart in the reference:
- * a B200 dispatch knob.  Narrower units give calls of a few thousand tokens
- * more units to spread over the SM pairs instead of splitting K.
- * Process-wide; returns NQ_ERR_ARG for other values. */
+ * 128, 256 or 512, or 0 for the default (256).  No counterpart in the
+ * reference: a B200 dispatch knob.  Narrower units give calls of a few
+ * thousand tokens more units; 512 (two MMAs per k slice on one weight tile)
+ * moves fewer bytes from L2 per FLOP, for bf16 activations only (f32
+ * activations keep 256).  Process-wide; returns NQ_ERR_ARG for other values. */
 int nq_set_gemm_unit_tokens(int tokens);
 
 /* Test hook for failure detection: launches a kernel that waits on an

@@ -405,6 +405,7 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
   // and one read of the f32 partials and the reduction launch.
   const int ldp = w->n_tiles * nq::kPackRows;
   g.bt = g_gemm_unit_tokens ? g_gemm_unit_tokens : nq::gemm_bf16_block_t();
+  if (g.bt > 256 && splitx) g.bt = 256;  // 512-token units take bf16 activations only
   g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
   const int tiles = g.grid_m * g.grid_n;
   double best = 1e300;
@@ -467,10 +468,10 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     a_ld = k_pad;
   }
   CUtensorMap tm_a, tm_alo;
-  rc = make_tmap(ctx, &tm_a, a_ptr, a_k, m, a_ld, bt / 2);
+  rc = make_tmap(ctx, &tm_a, a_ptr, a_k, m, a_ld, deq ? nq::gemm_bf16_token_box(bt) : bt / 2);
   if (rc) return rc;
   if (splitx) {
-    rc = make_tmap(ctx, &tm_alo, lo, a_k, m, a_ld, bt / 2);
+    rc = make_tmap(ctx, &tm_alo, lo, a_k, m, a_ld, deq ? nq::gemm_bf16_token_box(bt) : bt / 2);
     if (rc) return rc;
   } else {
     tm_alo = tm_a;
@@ -1032,7 +1033,7 @@ int nq_set_gemm_path(int path) {
 
 int nq_set_gemm_unit_tokens(int tokens) {
   if (tokens != 0 && !nq::gemm_bf16_unit_ok(tokens))
-    return fail(NQ_ERR_ARG, "GEMM unit width %d (use 0, 64, 128 or 256)", tokens);
+    return fail(NQ_ERR_ARG, "GEMM unit width %d (use 0, 64, 128, 256 or 512)", tokens);
   g_gemm_unit_tokens = tokens;
   return NQ_OK;
 }

@@ -40,27 +40,36 @@ constexpr int kThreads = 32 * (2 + kEpiW);  // 576
 constexpr int kEpi0 = 2;
 constexpr int kAgreeBar = 9;     // named barrier of all epilogue warps (1..8: GLU pairs)
 
-// PT: tokens per pair unit (MMA N = PT, PT / 2 token rows per CTA).  256 is
-// the default; 128 and 64 give small-M calls more units instead of split K.
+// PT: tokens per pair unit.  Up to 256 a unit is one MMA of N = PT per k
+// slice (PT / 2 token rows per CTA), with two TMEM accumulators so the
+// epilogue of one unit overlaps the next unit's main loop.  PT = 512 issues
+// two N = 256 MMAs per k slice on the same weight tile: 171 instead of 128
+// FLOP per byte moved from L2, with the whole TMEM as one accumulator.  256 is
+// the default; 128 and 64 give small-M calls more units.
 template <bool SPLITX, int PT>
 struct Cfg {
-  static_assert(PT == 64 || PT == 128 || PT == 256, "unit widths 64, 128, 256");
+  static_assert(PT == 64 || PT == 128 || PT == 256 || PT == 512, "unit widths 64, 128, 256, 512");
+  static_assert(!(SPLITX && PT == 512), "512-token units take bf16 activations only");
   static constexpr int kPT = PT;
-  static constexpr int kPTHalf = PT / 2;       // token rows per CTA
-  static constexpr int kColsPerWarp = PT / 4;  // tokens per epilogue warp (4 column groups)
+  static constexpr int kNB = PT > 256 ? 2 : 1;       // MMAs (token sub-tiles) per k slice
+  static constexpr int kMmaN = PT / kNB;             // N of each MMA
+  static constexpr int kSubRows = kMmaN / 2;         // token rows per CTA and sub-tile
+  static constexpr int kAccBufs = PT > 256 ? 1 : 2;  // TMEM accumulator buffers
+  static constexpr int kColsPerWarp = PT / 4;        // tokens per epilogue warp (4 column groups)
   static_assert(kColsPerWarp % kEc == 0, "epilogue chunks");
-  static constexpr int kStages = SPLITX ? (PT == 256 ? 4 : 6) : (PT == 256 ? 6 : 8);
-  static constexpr int kABytes = 128 * kPackK * 2;      // 16 KB of weight rows
-  static constexpr int kBBytes = kPTHalf * kPackK * 2;  // 4 / 8 / 16 KB per activation plane
+  static constexpr int kStages = PT == 512 ? 4 : SPLITX ? (PT == 256 ? 4 : 6) : (PT == 256 ? 6 : 8);
+  static constexpr int kABytes = 128 * kPackK * 2;          // 16 KB of weight rows
+  static constexpr int kSubBytes = kSubRows * kPackK * 2;   // one token sub-tile of one plane
+  static constexpr int kBBytes = kNB * kSubBytes;           // 4 / 8 / 16 / 32 KB per activation plane
   static constexpr int kStageBytes = kABytes + kBBytes * (SPLITX ? 2 : 1);
   static constexpr int kGluOffset = kStages * kStageBytes;
   static constexpr int kGluBytes = 8 * kEc * 32 * 4;    // 8 value/gate warp pairs
   static constexpr int kBarOffset = kGluOffset + kGluBytes;
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kBarOffset + kNumBars * 8 + 64;
-  static constexpr uint32_t kIdesc = idesc_bf16_f32(kPW, PT);
-  static constexpr int kTmemCols = 2 * PT;  // D0 [0, PT), D1 [PT, 2 PT)
-  static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0 && kBBytes % 1024 == 0, "swizzle alignment");
+  static constexpr uint32_t kIdesc = idesc_bf16_f32(kPW, kMmaN);
+  static constexpr int kTmemCols = kAccBufs * PT;  // D0 [0, PT) (, D1 [PT, 2 PT))
+  static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0 && kSubBytes % 1024 == 0, "swizzle alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
@@ -85,7 +94,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                            const __grid_constant__ CUtensorMap tm_alo, const __grid_constant__ GemmBf16Params p) {
   using C = Cfg<SPLITX, PT>;
   constexpr int kStages = C::kStages;
-  constexpr int kPT = C::kPT, kPTHalf = C::kPTHalf, kColsPerWarp = C::kColsPerWarp;
+  constexpr int kPT = C::kPT, kColsPerWarp = C::kColsPerWarp, kNB = C::kNB, kMmaN = C::kMmaN;
+  constexpr int kSubRows = C::kSubRows, kAccBufs = C::kAccBufs;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
   uint8_t *smem = smem_raw + (((raw_u32 + 1023u) & ~1023u) - raw_u32);
@@ -146,7 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int u = cl; u < n_units && ok; u += ncl) {
         const Unit un = decode_unit(p, u);
         const int wrow0 = un.ft * kPW + static_cast<int>(rank) * 128;
-        const int trow0 = un.tt * kPT + static_cast<int>(rank) * kPTHalf;
+        const int trow0 = un.tt * kPT + static_cast<int>(rank) * kSubRows;
         for (int i = 0; i < un.nk; ++i, ++g) {
           const int s = g % kStages;
           if (g >= kStages && !mbar_wait(empty(s), ((g / kStages) - 1) & 1, p.ctl.wait_limit, flags)) {
@@ -164,8 +174,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Weight rows past the matrix (odd tile count) and token rows past M
           // are zero-filled by the TMA unit.
           tma_load_2d_pair(smem_u32(stage_w(s)), &tm_w, bar, kx, wrow0);
-          tma_load_2d_pair(smem_u32(stage_b(s)), &tm_a, bar, kx, trow0);
-          if (SPLITX) tma_load_2d_pair(smem_u32(stage_blo(s)), &tm_alo, bar, kx, trow0);
+#pragma unroll
+          for (int t = 0; t < kNB; ++t) {  // token sub-tile t: unit tokens [t kMmaN, (t + 1) kMmaN)
+            tma_load_2d_pair(smem_u32(stage_b(s)) + t * C::kSubBytes, &tm_a, bar, kx, trow0 + t * kMmaN);
+            if (SPLITX)
+              tma_load_2d_pair(smem_u32(stage_blo(s)) + t * C::kSubBytes, &tm_alo, bar, kx, trow0 + t * kMmaN);
+          }
         }
       }
       // Drain: every copy into this CTA's shared memory has landed (the
@@ -185,8 +199,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int u = cl; u < n_units && ok; u += ncl, ++j) {
         const Unit un = decode_unit(p, u);
-        const int b = j & 1;
-        if (j >= 2 && !mbar_wait(accum_empty(b), ((j >> 1) - 1) & 1, p.ctl.wait_limit, flags)) {
+        const int b = kAccBufs == 2 ? (j & 1) : 0;
+        const int jb = kAccBufs == 2 ? (j >> 1) : j;  // use count of buffer b before this unit
+        if (j >= kAccBufs && !mbar_wait(accum_empty(b), (jb - 1) & 1, p.ctl.wait_limit, flags)) {
           if (!flags[0]) report(p.ctl, flags, kDevTimeoutMma);
           ok = false;
           break;
@@ -207,8 +222,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kPackK / 16; ++kk) {
             const uint64_t ad = sw128_kmajor_desc(a_addr + kk * 32);
-            umma2_bf16_ss(d_tmem, ad, sw128_kmajor_desc(b_addr + kk * 32), C::kIdesc, (i > 0 || kk > 0) ? 1u : 0u);
-            if (SPLITX) umma2_bf16_ss(d_tmem, ad, sw128_kmajor_desc(blo_addr + kk * 32), C::kIdesc, 1u);
+#pragma unroll
+            for (int t = 0; t < kNB; ++t) {  // sub-tile t accumulates into columns [t kMmaN, (t + 1) kMmaN)
+              const uint32_t dt = d_tmem + t * kMmaN;
+              const uint32_t boff = t * C::kSubBytes + kk * 32;
+              umma2_bf16_ss(dt, ad, sw128_kmajor_desc(b_addr + boff), C::kIdesc, (i > 0 || kk > 0) ? 1u : 0u);
+              if (SPLITX) umma2_bf16_ss(dt, ad, sw128_kmajor_desc(blo_addr + boff), C::kIdesc, 1u);
+            }
           }
           umma2_commit_both(empty(s));
         }
@@ -237,8 +257,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     int j = 0;
     for (int u = cl; u < n_units; u += ncl, ++j) {
       const Unit un = decode_unit(p, u);
-      const int b = j & 1;
-      bool ok = mbar_wait(accum_full(b), (j >> 1) & 1, p.ctl.wait_limit, flags);
+      const int b = kAccBufs == 2 ? (j & 1) : 0;
+      bool ok = mbar_wait(accum_full(b), (kAccBufs == 2 ? (j >> 1) : j) & 1, p.ctl.wait_limit, flags);
       ok = __all_sync(0xffffffffu, ok);
       // The GLU pairs share named barriers, so all epilogue warps agree on
       // giving up before any of them leaves the loop.
@@ -372,7 +392,8 @@ cudaError_t launch_t(const CUtensorMap &w, const CUtensorMap &a_hi, const CUtens
 
 int gemm_bf16_block_t() { return kPTDefault; }
 int gemm_bf16_block_w() { return kPW; }
-bool gemm_bf16_unit_ok(int tokens) { return tokens == 64 || tokens == 128 || tokens == 256; }
+bool gemm_bf16_unit_ok(int tokens) { return tokens == 64 || tokens == 128 || tokens == 256 || tokens == 512; }
+int gemm_bf16_token_box(int unit_tokens) { return (unit_tokens < 256 ? unit_tokens : 256) / 2; }
 
 cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w, const CUtensorMap &a_hi,
                              const CUtensorMap &a_lo, const GemmBf16Params &p, int pairs, cudaStream_t stream) {
@@ -383,6 +404,7 @@ cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w,
     case 257: return launch_t<true, 128>(w, a_hi, a_lo, p, pairs, stream);
     case 128: return launch_t<false, 64>(w, a_hi, a_lo, p, pairs, stream);
     case 129: return launch_t<true, 64>(w, a_hi, a_lo, p, pairs, stream);
+    case 1024: return launch_t<false, 512>(w, a_hi, a_lo, p, pairs, stream);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -117,9 +117,11 @@ struct GemmBf16Params {
 };
 int gemm_bf16_block_t();              // default tokens per pair unit
 int gemm_bf16_block_w();              // weight rows per pair unit
-bool gemm_bf16_unit_ok(int tokens);   // unit widths the kernel is built for (64, 128, 256)
+bool gemm_bf16_unit_ok(int tokens);   // unit widths the kernel is built for (64, 128, 256, 512)
+int gemm_bf16_token_box(int unit_tokens);  // token rows per TMA box (per CTA and sub-tile)
 // unit_tokens: tokens per pair unit (grid_m in p counts units of that width;
-// the token tensor maps have boxes of unit_tokens / 2 rows).
+// the token tensor maps have boxes of gemm_bf16_token_box(unit_tokens) rows).
+// 512 takes bf16 activations only (splitx false).
 cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w, const CUtensorMap &a_hi,
                              const CUtensorMap &a_lo, const GemmBf16Params &p, int pairs, cudaStream_t stream);
 

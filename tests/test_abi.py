@@ -37,9 +37,9 @@ def test_null_arguments_are_rejected_without_device_work():
     assert "null" in L.last_error()
     assert lib.nq_linear(None, None, 0, 1, 32, None, 0, None, 0, 32, None) == L.NQ_ERR_ARG
     assert lib.nq_set_wait_limit(0) == L.NQ_ERR_ARG
-    for bad in (-1, 1, 32, 100, 192, 512):
+    for bad in (-1, 1, 32, 100, 192, 1024):
         assert lib.nq_set_gemm_unit_tokens(bad) == L.NQ_ERR_ARG, bad
-    for ok in (64, 128, 256, 0):
+    for ok in (64, 128, 256, 512, 0):
         assert lib.nq_set_gemm_unit_tokens(ok) == L.NQ_OK, ok
     buf = ctypes.create_string_buffer(8)
     n = lib.nq_last_error(buf, len(buf))

@@ -153,17 +153,19 @@ def test_kept_bf16_copy_is_identical_and_skips_dequant(nq, oracle):
     assert nq.status() == 0
 
 
-# Units of 64 / 128 tokens (nq_set_gemm_unit_tokens) in place of 256: MMA
-# N = 64 / 128, token tiles of 32 / 64 rows per CTA, 128 / 256 TMEM columns.
+# Units of 64 / 128 / 512 tokens (nq_set_gemm_unit_tokens) in place of 256:
+# MMA N = 64 / 128 with token tiles of 32 / 64 rows per CTA, or two N = 256
+# MMAs per k slice on one weight tile (512; bf16 activations only, f32 keeps
+# 256).
 # Partial token tiles (1100, 2100, 300, 129, 375 rows), GLU, f32 activations
 # (hi + lo planes) and a split-K shape (375 x 4096 -> 1024).  Without split K
 # every output is one unit's k-ordered sum, so it must equal the 256-token
 # result bit for bit.
-@pytest.mark.parametrize("unit", [64, 128])
+@pytest.mark.parametrize("unit", [64, 128, 512])
 @pytest.mark.parametrize("m,k,n,epi,xdt", [(1100, 1024, 3072, 0, "bf16"), (2100, 1024, 1024, 1, "f32"),
                                            (300, 640, 1920, 3, "bf16"), (129, 96, 130, 0, "bf16"),
                                            (375, 4096, 1024, 0, "bf16")])
-def test_narrow_units_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
+def test_unit_widths_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
     from nspeech_b200.fast_matmul import QWeight
     L = nq.load()
     glu = epi in (3, 4)
