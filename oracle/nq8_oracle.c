@@ -121,6 +121,7 @@ static float bf16_round(float f) { return oq_bf16_to_f32(oq_f32_to_bf16(f)); }
  *   d stored as f16 (RNE). */
 void oq_quantize_q8_0(const float *x, int64_t n_rows, int64_t k, uint8_t *out) {
     int64_t nb = n_rows * (k / OQ_QK);
+#pragma omp parallel for schedule(static)
     for (int64_t b = 0; b < nb; b++) {
         const float *xb = x + b * OQ_QK;
         uint8_t *ob = out + b * OQ_BLOCK_BYTES;
@@ -143,6 +144,7 @@ void oq_quantize_q8_0(const float *x, int64_t n_rows, int64_t k, uint8_t *out) {
 /* w[n,k] = f32(d) * q (row-major [n_rows, k]). */
 void oq_dequant_q8_0(const uint8_t *blocks, int64_t n_rows, int64_t k, float *w) {
     int64_t nb = n_rows * (k / OQ_QK);
+#pragma omp parallel for schedule(static)
     for (int64_t b = 0; b < nb; b++) {
         const uint8_t *ib = blocks + b * OQ_BLOCK_BYTES;
         uint16_t dh;

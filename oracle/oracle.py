@@ -33,7 +33,7 @@ _i64 = ctypes.c_int64
 
 def build() -> str:
     """Compile the oracle with its Makefile (gcc) if it is missing or stale."""
-    srcs = [os.path.join(_HERE, s) for s in ("nq8_oracle.c", "encoder_oracle.c", "Makefile")]
+    srcs = [os.path.join(_HERE, s) for s in ("nq8_oracle.c", "encoder_oracle.c", "fbgemm_cpu.c", "Makefile")]
     if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < max(os.path.getmtime(s) for s in srcs):
         subprocess.run(["make", "-s", "-C", _HERE], check=True)
     return _LIB_PATH
@@ -62,6 +62,15 @@ def lib() -> ctypes.CDLL:
         L.oq_max_rel_err.restype = ctypes.c_double
         L.oq_fill_normal.argtypes = [ctypes.c_uint64, _f32p, _i64, ctypes.c_float, ctypes.c_float]
         L.oq_fill_uniform.argtypes = [ctypes.c_uint64, _f32p, _i64, ctypes.c_float, ctypes.c_float]
+        L.ofb_matmul_q8_0.argtypes = [_f32p, _i64, _i64, _u8p, _i64, ctypes.c_int, _f32p]
+        L.ofb_isa.restype = ctypes.c_int
+        L.ofb_force_isa.argtypes = [ctypes.c_int]
+        L.ofb_set_threads.argtypes = [ctypes.c_int]
+        L.ofb_max_threads.restype = ctypes.c_int
+        L.ofb_pack_q8_0.argtypes = [_u8p, _i64, _i64, ctypes.c_int]
+        L.ofb_pack_q8_0.restype = ctypes.c_void_p
+        L.ofb_free.argtypes = [ctypes.c_void_p]
+        L.ofb_linear.argtypes = [ctypes.c_void_p, _f32p, _i64, _i64, ctypes.c_void_p, _f32p, _i64]
         _lib = L
     return _lib
 
@@ -130,6 +139,58 @@ def matmul_fbgemm_bf16(x: np.ndarray, blocks: np.ndarray, n: int) -> np.ndarray:
     y = np.empty((m, n), dtype=np.float32)
     lib().oq_matmul_fbgemm_bf16(x, m, k, np.ascontiguousarray(blocks, dtype=np.uint8), n, y)
     return y
+
+
+def matmul_fbgemm_packed(x: np.ndarray, blocks: np.ndarray, n: int, bf16: bool = True) -> np.ndarray:
+    """The same product through fbgemm_cpu.c's packed AVX-512 / AVX2 kernels
+    (weights packed to bf16 once, FbgemmBf16Op's structure); bit-identical to
+    matmul_fbgemm_bf16 for bf16=True, exact f32 weights for bf16=False."""
+    x = _f32(x)
+    m, k = x.shape
+    y = np.empty((m, n), dtype=np.float32)
+    lib().ofb_matmul_q8_0(x, m, k, np.ascontiguousarray(blocks, dtype=np.uint8), n, 1 if bf16 else 0, y)
+    return y
+
+
+class PackedWeight:
+    """A Q8_0 weight dequantized and packed to bf16 once (MatMul::from_tensor,
+    src/fast_matmul.rs:191-208), multiplied by the packed CPU kernels
+    (FbgemmBf16Op::cpu_fwd, :138-167).  The CPU baseline's linear."""
+
+    def __init__(self, blocks: np.ndarray, n: int, k: int, bf16: bool = True):
+        self.n, self.k = n, k
+        self._h = lib().ofb_pack_q8_0(np.ascontiguousarray(blocks, dtype=np.uint8), n, k, 1 if bf16 else 0)
+
+    def __call__(self, x: np.ndarray, bias=None, out=None) -> np.ndarray:
+        x = _f32(x)
+        m = x.shape[0]
+        y = np.empty((m, self.n), np.float32) if out is None else out
+        b = None if bias is None else _f32(bias)
+        lib().ofb_linear(self._h, x, m, x.shape[1], None if b is None else b.ctypes.data, y, self.n)
+        return y
+
+    def __del__(self):
+        if getattr(self, "_h", None) and _lib is not None:
+            _lib.ofb_free(self._h)
+            self._h = None
+
+
+def set_threads(n: int) -> None:
+    """OpenMP threads of the CPU kernels (the CPU baseline's core count)."""
+    lib().ofb_set_threads(int(n))
+
+
+def max_threads() -> int:
+    return int(lib().ofb_max_threads())
+
+
+def cpu_isa() -> int:
+    """512 when the packed kernels run AVX-512, 256 for AVX2 + FMA."""
+    return int(lib().ofb_isa())
+
+
+def force_isa(isa: int) -> None:
+    lib().ofb_force_isa(int(isa))
 
 
 def matmul_qtiled(x: np.ndarray, blocks: np.ndarray, n: int) -> np.ndarray:
@@ -219,18 +280,60 @@ class _EncWeights(ctypes.Structure):
                 + [(n, _U8P) for n in ("pw3", "pw6", "lin")] + [("layers", ctypes.POINTER(_EncLayer))])
 
 
-def encoder_forward(cfg: dict, tensors: dict, mel: np.ndarray, weight_mode: int = 0) -> np.ndarray:
-    """Batch-1 FastConformer encoder forward (encoder_oracle.c) -> [T3, d_model].
+class EncoderModel:
+    """Batch-1 FastConformer encoder (encoder_oracle.c) with every linear packed
+    once, as the reference packs at load time; ``__call__`` runs one segment.
 
     ``tensors``: name -> f32 array for vectors, uint8 Q8_0 blocks [n, k/32*34]
     for the rank-2 / pointwise matrices (the names of remap_nemo_tensor_name).
     weight_mode 0: bf16-rounded dequantized weights (fast_matmul semantics);
     1: exact dequantized f32 weights (candle Linear).
     """
-    L = lib()
-    L.oq_encoder_forward.argtypes = [ctypes.POINTER(_EncCfg), ctypes.POINTER(_EncWeights), _f32p, ctypes.c_int, _f32p]
-    L.oq_encoder_forward.restype = ctypes.c_int
-    L.oq_encoder_set_weight_mode.argtypes = [ctypes.c_int]
+
+    def __init__(self, cfg: dict, tensors: dict, weight_mode: int = 0):
+        L = lib()
+        L.oq_encoder_prepare.argtypes = [ctypes.POINTER(_EncCfg), ctypes.POINTER(_EncWeights), ctypes.c_int]
+        L.oq_encoder_prepare.restype = ctypes.c_void_p
+        L.oq_encoder_run.argtypes = [ctypes.c_void_p, _f32p, ctypes.c_int, _f32p]
+        L.oq_encoder_run.restype = ctypes.c_int
+        L.oq_encoder_release.argtypes = [ctypes.c_void_p]
+        self.cfg = dict(cfg)
+        self._keep, self._c, self._w = _encoder_structs(cfg, tensors)
+        self._h = L.oq_encoder_prepare(ctypes.byref(self._c), ctypes.byref(self._w), int(weight_mode))
+
+    def __call__(self, mel: np.ndarray) -> np.ndarray:
+        mel = _f32(mel)
+        t_mel = mel.shape[0]
+        t3 = t_mel
+        for _ in range(3):
+            t3 = (t3 - 1) // 2 + 1
+        out = np.empty((t3, self.cfg["d_model"]), np.float32)
+        got = lib().oq_encoder_run(self._h, mel.reshape(-1), t_mel, out.reshape(-1))
+        assert got == t3
+        return out
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().oq_encoder_release(self._h)
+            self._h = None
+
+    def __del__(self):
+        if _lib is not None:
+            self.close()
+
+
+def encoder_forward(cfg: dict, tensors: dict, mel: np.ndarray, weight_mode: int = 0) -> np.ndarray:
+    """One-shot batch-1 encoder forward -> [T3, d_model] (see EncoderModel)."""
+    m = EncoderModel(cfg, tensors, weight_mode)
+    try:
+        return m(mel)
+    finally:
+        m.close()
+
+
+def _encoder_structs(cfg: dict, tensors: dict):
+    """ctypes config and weight table over the caller's arrays (kept alive by
+    the returned list)."""
     keep = []
 
     def f(name, default=None):
@@ -284,14 +387,5 @@ def encoder_forward(cfg: dict, tensors: dict, mel: np.ndarray, weight_mode: int 
                     pw3_b=f(sp + "layers.3.bias", zc), pw6_b=f(sp + "layers.6.bias", zc),
                     lin_b=f(sp + "linear.bias", zeros), pw3=q(sp + "layers.3.weight"), pw6=q(sp + "layers.6.weight"),
                     lin=q(sp + "linear.weight"), layers=layers)
-    mel = _f32(mel)
-    t_mel = mel.shape[0]
-    t3 = t_mel
-    for _ in range(3):
-        t3 = (t3 - 1) // 2 + 1
-    out = np.empty((t3, d), np.float32)
-    L.oq_encoder_set_weight_mode(weight_mode)
-    got = L.oq_encoder_forward(ctypes.byref(c), ctypes.byref(W), mel.reshape(-1), t_mel, out.reshape(-1))
-    assert got == t3
-    del keep
-    return out
+    keep.append(layers)
+    return keep, c, W
