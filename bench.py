@@ -1,30 +1,47 @@
 #!/usr/bin/env python
 """Parakeet FastConformer encoder RTFx on B200 through the nspeech Q8_0 path.
 
-Workload (the metric's multi-GPU configuration): per GPU,
-1024 synthetic VAD segments with durations U[2, 30] s (seed 4 + rank), as
-128-bin log-mel N(0, 1) at a 10 ms hop, length-bucketed into batches of <= 32
-padded segments, through the full 24-layer encoder (configs[1] architecture,
-random-init Q8_0 weights).  One step = every bucket of this rank once.  Ranks
-are independent (segment sharding, no collective on the data path; one
-all-reduce of the timings after the timed region): weak scaling.
-`--shard lpt` instead splits ONE job of --segments segments over the ranks
-(length buckets assigned by greedy longest-processing-time on the estimated
-bucket cost, nspeech_b200/shard.py): strong scaling.
+Workload (the metric's multi-GPU configuration): ONE job
+of 1024 synthetic VAD segments with durations U[2, 30] s (seed 4), as 128-bin
+log-mel N(0, 1) at a 10 ms hop (segment j's features from its own seed), through
+the full 24-layer encoder (configs[1] architecture, random-init Q8_0 weights).
+The job is cut into length buckets of <= 32 padded segments, and the buckets
+are split over the ranks by greedy longest-processing-time on the estimated
+bucket cost (nspeech_b200/shard.py): one process per GPU, no collective on the
+data path, strong scaling.  One step = every bucket of this rank once.
+`--shard weak` instead gives every rank its own 1024 segments (seed 4 + rank).
 
-    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--shard weak|lpt]
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference] [--shard lpt|weak]
     python bench.py --gemv [--gemv-shapes MxKxN,...] [--gemv-plain CALLS]
+    python bench.py --linear (--shape MxKxN ... | --cfg1-sweep) [--graph] [--keep-bf16] ...
 
 Prints one JSON line (rank 0).  `value`: RTFx = audio seconds of all ranks /
 max-over-ranks device time of K steps, inputs resident in HBM.  `e2e`: the
 same through the public host-buffer entry point (H2D of the mel features and
-D2H of the encoder output inside the timed region).
+D2H of the encoder output inside the timed region), over K steps.
+`cpu_baseline` (N = 1): the CPU restatement of the reference's path
+(oracle/encoder_oracle.c over oracle/fbgemm_cpu.c: weights packed to bf16 once,
+f32 activations, AVX-512 FMA, OpenMP) on a stratified sample of the same
+segments, at all host cores and at one core, plus the configs[0] linear set.
+`--impl reference` times that CPU path on the same sample per step.
 
-`--gemv` instead times the Q8_0 GEMV (M <= 16, the decode-step projections)
-alone: per shape, a CUDA graph of back-to-back nq_linear calls over enough
-weight copies to stream past L2, reported as device time per call and HBM
-GB/s (weight + x + y bytes) against the measured peak; one JSON line.
-`--gemv-plain CALLS` only makes CALLS plain calls per shape (for ncu).
+`--gemv` times the Q8_0 GEMV (M <= 16, the decode-step projections) alone:
+per shape, a CUDA graph of back-to-back nq_linear calls over enough weight
+copies to stream past L2, reported as device time per call and HBM GB/s
+(weight + x + y bytes) against the measured peak, and the configs[2] decode
+step; one JSON line.  `--gemv-plain CALLS` only makes CALLS plain calls per
+shape (for ncu).
+
+`--linear` times nq_linear per shape (M x K x N), one JSON line per shape:
+random Q8_0 weights rotated over enough copies to exceed the 126 MB L2, CUDA
+events over --iters back-to-back calls, or with --graph the device time per
+call of a CUDA graph of those calls; TFLOP/s and algorithmic GB/s
+(N*K*34/32 + M*K*sx + M*N*sy) against the bound that applies (HBM for
+M <= 125, tensor above).  --cfg1-sweep: the configs[0] block (K -> N:
+1024->4096, 4096->1024, 1024->3072, 1024->1024, 1024->2048, 1024->1024) at
+M in {1, 2, 4, 8, 16, 125, 1024, 2048, 4096, 12000}, f32 in and out, or bf16
+with --sweep-dtype bf16; --keep-bf16 gives every weight a kept bf16 copy as
+the encoder does; --kokoro adds the configs[3] Kokoro linears at M = 200.
 """
 from __future__ import annotations
 
@@ -58,18 +75,37 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--segments", type=int, default=1024)
     ap.add_argument("--max-batch", type=int, default=32)
-    ap.add_argument("--shard", choices=["weak", "lpt"], default="weak",
-                    help="weak: each rank runs its own --segments; lpt: one job of --segments split over the ranks")
+    ap.add_argument("--shard", choices=["weak", "lpt"], default="lpt",
+                    help="lpt: one job of --segments split over the ranks (strong scaling); "
+                         "weak: each rank runs its own --segments")
     ap.add_argument("--layers", type=int, default=24)
-    ap.add_argument("--e2e-steps", type=int, default=1)
+    ap.add_argument("--e2e-steps", type=int, default=0, help="steps of the e2e timing (0: --steps)")
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the buckets of a step alternate over")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--cpu-sample-s", type=float, default=10.0, help="audio seconds of the CPU-baseline sample")
+    ap.add_argument("--cpu-segments", type=int, default=16,
+                    help="segments of the CPU sample (stratified by length over the job) at all host cores")
+    ap.add_argument("--cpu-segments-one-core", type=int, default=2, help="segments of the one-core CPU sample")
+    ap.add_argument("--cpu-threads", type=int, default=0, help="CPU threads (0: all the host offers)")
     ap.add_argument("--gemv", action="store_true", help="time the Q8_0 GEMV alone instead of the encoder")
     ap.add_argument("--gemv-shapes", default="1x640x640,1x640x2560,1x2560x640,1x4096x4096,1x8192x8192,"
                     "1x640x32768,8x4096x4096,16x4096x4096,1x16384x16384")
     ap.add_argument("--gemv-plain", type=int, default=0, help="only make this many plain calls per shape")
     ap.add_argument("--no-decode-step", action="store_true", help="--gemv without the configs[2] decode step")
+    ap.add_argument("--linear", action="store_true", help="time nq_linear per shape instead of the encoder")
+    ap.add_argument("--shape", action="append", default=[], help="--linear: MxKxN")
+    ap.add_argument("--cfg1-sweep", action="store_true", help="--linear: the configs[0] block over the M sweep")
+    ap.add_argument("--kokoro", action="store_true", help="--linear: the configs[3] Kokoro linears at M = 200")
+    ap.add_argument("--sweep-dtype", choices=["f32", "bf16"], default="f32",
+                    help="--linear: activations in and out of the sweeps (f32: configs[0]; bf16: the encoder's)")
+    ap.add_argument("--x", choices=["bf16", "f32"], default="bf16", help="--linear: activation dtype of --shape")
+    ap.add_argument("--y", choices=["bf16", "f32"], default="bf16", help="--linear: output dtype of --shape")
+    ap.add_argument("--iters", type=int, default=20, help="--linear: calls per timing")
+    ap.add_argument("--graph", action="store_true", help="--linear: time a CUDA graph of the calls")
+    ap.add_argument("--keep-bf16", action="store_true", help="--linear: kept bf16 weight copies (as the encoder)")
+    ap.add_argument("--sweep-m", default="", help="--linear: comma-separated subset of the sweep's M values")
+    ap.add_argument("--unit-tokens", default="0",
+                    help="--linear: GEMM unit widths to time each shape with (nq_set_gemm_unit_tokens; 0 = default)")
+    ap.add_argument("--qtiled", action="store_true", help="--linear: weights with QTiled semantics (from_qtensor)")
     return ap.parse_args()
 
 
@@ -84,42 +120,72 @@ def peaks() -> dict:
 
 
 # ------------------------------------------------------------------ workload
-def make_buckets(rank: int, n_segments: int, max_batch: int, feat: int, shard: str = "weak", world: int = 1):
-    """This rank's padded buckets [(mel [B, T, feat], lengths)] and their audio seconds.
+def job_segments(n_segments: int, seed: int = 4):
+    """Mel frame counts of the configs[4] job: durations U[2, 30] s."""
+    from nspeech_b200 import synthetic as S
+    return [S.mel_frames(s) for s in S.segment_lengths_s(n_segments, 2.0, 30.0, seed=seed)]
 
-    shard "weak": the rank's own n_segments (seed 4 + rank), length-bucketed.
+
+def segment_mel(j: int, frames: int, feat: int, rank_seed: int = 0) -> np.ndarray:
+    """Log-mel features of segment j (its own seed: independent of the split)."""
+    return np.random.default_rng(100000 + 1000003 * rank_seed + j).standard_normal((frames, feat), dtype=np.float32)
+
+
+def plan_buckets(rank: int, world: int, n_segments: int, max_batch: int, shard: str):
+    """This rank's buckets as (segment indices, mel frame counts), and their mel seed.
+
     shard "lpt": one job of n_segments (seed 4) split over the ranks by
     nspeech_b200.shard (length buckets, greedy LPT on the estimated bucket
-    cost); a segment's features depend only on its index, not on the world size.
+    cost).  shard "weak": the rank's own n_segments (seed 4 + rank),
+    length-bucketed.
     """
-    from nspeech_b200 import synthetic as S
+    from nspeech_b200 import shard as SH
     if shard == "lpt":
-        from nspeech_b200 import shard as SH
-        secs = S.segment_lengths_s(n_segments, 2.0, 30.0, seed=4)
-        frames = [S.mel_frames(s) for s in secs]
-        buckets = []
-        for idx in SH.shard_segments(frames, max_batch, world, rank):
-            lens = [int(frames[j]) for j in idx]
-            mel = np.zeros((len(idx), max(lens), feat), np.float32)
-            for r, (j, L) in enumerate(zip(idx, lens)):
-                mel[r, :L] = np.random.default_rng(100000 + j).standard_normal((L, feat), dtype=np.float32)
-            buckets.append((mel, lens))
-        return buckets, float(sum(L for _, ls in buckets for L in ls)) * 0.01
-    secs = S.segment_lengths_s(n_segments, 2.0, 30.0, seed=4 + rank)
-    frames = np.array([S.mel_frames(s) for s in secs])
-    order = np.argsort(frames, kind="stable")
-    rng = np.random.default_rng(1000 + rank)
-    buckets = []
-    for i in range(0, n_segments, max_batch):
-        idx = order[i:i + max_batch]
-        lens = [int(frames[j]) for j in idx]
-        T = max(lens)
-        mel = np.zeros((len(idx), T, feat), np.float32)
-        for r, L in enumerate(lens):
-            mel[r, :L] = rng.standard_normal((L, feat), dtype=np.float32)
-        buckets.append((mel, lens))
-    audio_s = float(frames.sum()) * 0.01
-    return buckets, audio_s
+        frames = job_segments(n_segments, 4)
+        parts = SH.shard_segments(frames, max_batch, world, rank)
+        return [(idx, [int(frames[j]) for j in idx]) for idx in parts], 0
+    frames = job_segments(n_segments, 4 + rank)
+    return [(idx, [int(frames[j]) for j in idx]) for idx in SH.length_buckets(frames, max_batch)], rank
+
+
+def materialize(plan, feat: int, rank_seed: int):
+    """Padded bucket tensors [(mel [B, T, feat], lengths)] of a plan."""
+    out = []
+    for idx, lens in plan:
+        mel = np.zeros((len(idx), max(lens), feat), np.float32)
+        for r, (j, L) in enumerate(zip(idx, lens)):
+            mel[r, :L] = segment_mel(j, L, feat, rank_seed)
+        out.append((mel, lens))
+    return out
+
+
+def make_buckets(rank: int, n_segments: int, max_batch: int, feat: int, shard: str = "weak", world: int = 1):
+    """This rank's padded buckets [(mel [B, T, feat], lengths)] and their audio seconds."""
+    plan, rank_seed = plan_buckets(rank, world, n_segments, max_batch, shard)
+    buckets = materialize(plan, feat, rank_seed)
+    return buckets, float(sum(L for _, ls in buckets for L in ls)) * 0.01
+
+
+def workload_config(args, world: int, plan, spec) -> dict:
+    """The line's `config` (both arms report the same one)."""
+    from nspeech_b200.shard import encoder_frames
+    audio_s = sum(L for _, ls in plan for L in ls) * 0.01
+    segs = sum(len(ls) for _, ls in plan)
+    return {
+        "workload": (f"configs[4]: one job of {args.segments} VAD segments split over {world} GPU(s) "
+                     "(length buckets, greedy LPT)" if args.shard == "lpt" else
+                     f"configs[4]: {args.segments} VAD segments/GPU") +
+                    f", U[2,30] s, length-bucketed batches <= {args.max_batch}, "
+                    f"full {spec.n_layers}-layer encoder (configs[1] architecture)",
+        "model": f"Parakeet TDT 0.6B FastConformer encoder ({spec.n_layers} layers, d {spec.d_model}, "
+                 f"{spec.n_heads} heads, FFN {spec.d_model * spec.ff_mult}, conv {spec.conv_kernel})",
+        "segments_per_gpu": segs, "shard": args.shard, "max_batch": args.max_batch, "audio_s_per_gpu": audio_s,
+        "buckets": len(plan), "streams": max(1, args.streams),
+        "seq_len": max(encoder_frames(max(ls)) for _, ls in plan),
+        "global_batch": args.segments if args.shard == "lpt" else args.segments * world,
+        "parallelism": f"dp{world} (segment-sharded, no collective on the data path)",
+        "l2": "inputs larger than L2: 0.64 GB of Q8_0 weights stream per pass; activations up to 1.6 GB",
+    }
 
 
 def make_encoder(spec, seed=1):
@@ -183,47 +249,146 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------- CPU baseline
-def cpu_encoder_rtfx(spec, tensors, seconds: float, repeats: int = 1) -> dict:
-    """The CPU restatement of FastConformerEncoder::forward (oracle, a port:
-    the reference's Rust/candle/fbgemm build is not available) on one segment."""
+def cpu_info() -> dict:
+    from oracle import oracle as O
+    model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    return {"nproc": os.cpu_count(), "cpu_model": model, "isa": "avx512f" if O.cpu_isa() == 512 else "avx2+fma"}
+
+
+def cpu_sample(n_segments: int, n_take: int):
+    """n_take segments of the configs[4] job (seed 4), stratified by length:
+    the (i + 1/2) / n_take quantiles of the sorted durations."""
+    frames = job_segments(n_segments, 4)
+    order = sorted(range(len(frames)), key=lambda j: (frames[j], j))
+    return [(order[int((i + 0.5) * len(order) / n_take)], None) for i in range(n_take)], frames
+
+
+def cpu_model(spec, tensors):
+    """The CPU path restating the reference's Linux encoder with fast_matmul
+    linears: every Q8_0 weight dequantized and packed to bf16 once
+    (src/fast_matmul.rs:191-208), f32 activations (oracle/encoder_oracle.c,
+    oracle/fbgemm_cpu.c)."""
     from oracle import oracle as O
     q = {k: (O.quantize_q8_0(v.reshape(v.shape[0], -1)) if q8 else v) for k, (v, q8) in tensors.items()}
-    frames = int(round(seconds * 100))
-    mel = np.random.default_rng(7).standard_normal((frames, spec.feat_in), dtype=np.float32)
-    times = []
-    for _ in range(repeats):
+    return O.EncoderModel(spec.as_dict(), q, weight_mode=0)
+
+
+def cpu_encoder_pass(model, picks, frames, feat: int) -> tuple:
+    """Encode each picked segment (batch 1, as the reference): (audio s, wall s)."""
+    audio, wall = 0.0, 0.0
+    for j, _ in picks:
+        mel = segment_mel(j, frames[j], feat)
         t0 = time.perf_counter()
-        O.encoder_forward(spec.as_dict(), q, mel)
-        times.append(time.perf_counter() - t0)
-    t = min(times)
-    return {"value": frames * 0.01 / t, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"one {frames * 0.01:.1f} s segment through all {spec.n_layers} layers, "
-                      f"f32 activations, bf16-rounded Q8_0 weights (oracle/encoder_oracle.c, OpenMP)",
-            "seconds": t}
+        model(mel)
+        wall += time.perf_counter() - t0
+        audio += frames[j] * 0.01
+    return audio, wall
+
+
+def cpu_linear_set(threads: int, reps: int = 10) -> dict:
+    """configs[0] on the CPU path: the six linears of one block at M = 125,
+    f32 x ~ N(0, 1) (seed 0), Q8_0 weights N(0, 0.02), f32 bias N(0, 0.01);
+    3 warm-up and `reps` timed passes of the whole set (median, min, max)."""
+    from oracle import oracle as O
+    O.set_threads(threads)
+    m = 125
+    ws = []
+    for i, (k, n) in enumerate(CFG1_KN):
+        q = O.quantize_q8_0(O.normal(300 + i, (n, k), 0.0, 0.02))
+        ws.append((O.PackedWeight(q, n, k), O.normal(400 + i, (m, k)), O.normal(500 + i, (n,), 0.0, 0.01),
+                   np.empty((m, n), np.float32)))
+    flops = sum(2.0 * m * n * k for k, n in CFG1_KN)
+    times = []
+    for it in range(3 + reps):
+        t0 = time.perf_counter()
+        for w, x, b, y in ws:
+            w(x, b, out=y)
+        if it >= 3:
+            times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {"threads": threads, "m": m, "gflops": flops / med / 1e9, "ms_median": 1e3 * med,
+            "ms_min": 1e3 * min(times), "ms_max": 1e3 * max(times)}
+
+
+def cpu_baseline(args, spec, tensors) -> dict:
+    """RTFx of the CPU path on a stratified sample of the job at all host
+    cores and at one core, and the configs[0] linear set at both (BASELINE
+    CPU plan: pre-packed bf16 weights, f32 activations, AVX-512 widening + FMA,
+    OpenMP over 128-column tiles)."""
+    from oracle import oracle as O
+    threads = args.cpu_threads or O.max_threads()
+    model = cpu_model(spec, tensors)
+    picks, frames = cpu_sample(args.segments, args.cpu_segments)
+    O.set_threads(threads)
+    model(segment_mel(0, 200, spec.feat_in))  # warm-up
+    audio, wall = cpu_encoder_pass(model, picks, frames, spec.feat_in)
+    one = None
+    if args.cpu_segments_one_core > 0:
+        picks1, _ = cpu_sample(args.segments, args.cpu_segments_one_core)
+        O.set_threads(1)
+        a1, w1 = cpu_encoder_pass(model, picks1, frames, spec.feat_in)
+        one = {"value": a1 / w1, "cores": 1, "sample": f"{len(picks1)} segments, {a1:.1f} audio s"}
+    lin = [cpu_linear_set(threads), cpu_linear_set(1)]
+    O.set_threads(threads)
+    model.close()
+    return {"value": audio / wall, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{len(picks)} of the job's {args.segments} segments, stratified by length "
+                      f"({audio:.1f} audio s), batch 1, full {spec.n_layers}-layer encoder",
+            "path": "oracle/encoder_oracle.c + oracle/fbgemm_cpu.c: Q8_0 weights dequantized and packed to bf16 "
+                    "once, f32 activations, bf16 widened in registers + FMA (k-sequential f32 sums), OpenMP over "
+                    "48-row x 128-column tiles; attention as f32 GEMMs per (head, 32-query block)",
+            "one_core": one, "cfg1_linear_set": lin, **cpu_info()}
 
 
 def run_reference(args, rank: int, world: int) -> None:
+    """The reference's CPU path (the port; the Rust build is unavailable) on
+    the stratified sample of this arm's job, all host cores, per step."""
     if rank != 0:
         return
+    from oracle import oracle as O
     from nspeech_b200 import synthetic as S
     spec = S.EncoderSpec(n_layers=args.layers)
     tensors = S.encoder_tensors(spec, 1)
-    seg_s = 4.0
+    plan, _ = plan_buckets(0, world, args.segments, args.max_batch, args.shard)
+    threads = args.cpu_threads or O.max_threads()
+    model = cpu_model(spec, tensors)
+    del tensors
+    picks, frames = cpu_sample(args.segments, args.cpu_segments)
+    O.set_threads(threads)
     for _ in range(args.warmup):
-        cpu_encoder_rtfx(spec, tensors, seg_s)
-    t_total = 0.0
+        cpu_encoder_pass(model, picks, frames, spec.feat_in)
+    audio_step, t_total = 0.0, 0.0
     for _ in range(args.steps):
-        r = cpu_encoder_rtfx(spec, tensors, seg_s)
-        t_total += r["seconds"]
-    value = args.steps * seg_s / t_total
+        a, w = cpu_encoder_pass(model, picks, frames, spec.feat_in)
+        audio_step, t_total = a, t_total + w
+    value = args.steps * audio_step / t_total
+    one = None
+    if args.cpu_segments_one_core > 0:
+        picks1, _ = cpu_sample(args.segments, args.cpu_segments_one_core)
+        O.set_threads(1)
+        a1, w1 = cpu_encoder_pass(model, picks1, frames, spec.feat_in)
+        one = {"value": a1 / w1, "cores": 1, "sample": f"{len(picks1)} segments, {a1:.1f} audio s"}
+        O.set_threads(threads)
+    model.close()
+    sample = (f"{len(picks)} of the job's {args.segments} segments per step, stratified by length "
+              f"({audio_step:.1f} audio s), batch 1 (the reference's run_encoder), all host cores")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * t_total / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "configs[4] sample: one 4 s segment per step (CPU)", "model": "Parakeet TDT 0.6B encoder",
-                   "layers": spec.n_layers},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-                         "sample": f"one {seg_s} s segment per step, full encoder, oracle/encoder_oracle.c"},
+        "scaling": "strong" if args.shard == "lpt" else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) log-mel features, random-init Q8_0 weights",
+        "config": workload_config(args, world, plan, spec),
+        "audio_s_per_step": audio_step,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample,
+                         "one_core": one, **cpu_info()},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -258,9 +423,11 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     spec = S.EncoderSpec(n_layers=args.layers)
     enc, tensors = make_encoder(spec)
-    buckets, audio_s = make_buckets(rank, args.segments, args.max_batch, spec.feat_in, args.shard, world)
-    if not buckets:
+    plan, rank_seed = plan_buckets(rank, world, args.segments, args.max_batch, args.shard)
+    if not plan:
         raise SystemExit(f"rank {rank}: no buckets (--shard lpt needs at least one bucket per rank)")
+    buckets = materialize(plan, spec.feat_in, rank_seed)
+    audio_s = sum(L for _, ls in buckets for L in ls) * 0.01
 
     mel_dev, out_dev = [], []
     for mel, lens in buckets:
@@ -326,7 +493,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if lib.status() != 0:
         raise RuntimeError("device status reported a timeout during the timed region")
 
-    # ---- e2e: host buffers through nq_encoder_forward_host (pinned memory)
+    # ---- e2e: host buffers through nq_encoder_forward_host_async (pinned
+    # memory), K steps: each step's mel goes in and its encoder output comes
+    # back to host memory inside the timed region.
     host_in = [torch.from_numpy(m).pin_memory() for m, _ in buckets]
     host_out = [torch.empty(tuple(o.shape), dtype=torch.float32).pin_memory() for o in out_dev]
     torch.cuda.synchronize()
@@ -337,11 +506,12 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             enc.forward_host_async(hi.numpy(), lens, ho.numpy(), handles[j % len(handles)])
         enc.wait()  # every output of the step is in host memory
 
+    e2e_steps = args.e2e_steps or args.steps
     e2e_step()
     if dist:
         dist.barrier()
     t0 = time.perf_counter()
-    for _ in range(args.e2e_steps):
+    for _ in range(e2e_steps):
         e2e_step()
     t_e2e = time.perf_counter() - t0
     h2d = sum(m.nbytes for m, _ in buckets)
@@ -369,15 +539,15 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         pk = peaks()
         cpu = None
         if world == 1 and not args.no_cpu_baseline:
-            cpu = cpu_encoder_rtfx(spec, tensors, args.cpu_sample_s)
-            cpu.pop("seconds", None)
+            cpu = cpu_baseline(args, spec, tensors)
         achieved = gemm["flops"] / (gemm["ms"] / 1e3) / 1e12 if gemm["ms"] > 0 else 0.0
         peak_t = pk.get("bf16_tflops_sustained", pk.get("bf16_tflops"))
-        traffic = None
+        traffic, traffic_src = None, None
         tpath = os.path.join(ROOT, "profiles", "gemm_bf16_sm100_traffic.json")
         if os.path.exists(tpath):
             with open(tpath) as f:
-                traffic = json.load(f).get("traffic_bytes_per_launch")
+                tj = json.load(f)
+            traffic, traffic_src = tj.get("traffic_bytes_per_launch"), tj.get("source")
         line = {
             "metric": METRIC,
             "value": args.steps * audio_total / t_max,
@@ -387,32 +557,19 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "warmup": args.warmup,
             "ms_per_step": 1e3 * t_max / args.steps,
             "higher_is_better": True,
-            "scaling": "weak" if args.shard == "weak" else "strong",
+            "scaling": "strong" if args.shard == "lpt" else "weak",
             "vs_baseline": None,
             "dtype": "bf16",
             "data": "synthetic: seeded N(0,1) log-mel features, random-init Q8_0 weights",
-            "config": {
-                "workload": (f"configs[4]: {args.segments} VAD segments/GPU" if args.shard == "weak" else
-                             f"configs[4]: one job of {args.segments} VAD segments split over {world} GPU(s) "
-                             "(length buckets, greedy LPT)") +
-                            f", U[2,30] s, length-bucketed batches <= {args.max_batch}, "
-                            "full 24-layer encoder (configs[1] architecture)",
-                "model": "Parakeet TDT 0.6B FastConformer encoder (24 layers, d 1024, 8 heads, FFN 4096, conv 9)",
-                "segments_per_gpu": args.segments if args.shard == "weak" else sum(len(ls) for _, ls in buckets),
-                "shard": args.shard, "max_batch": args.max_batch, "audio_s_per_gpu": audio_s,
-                "buckets": len(buckets), "streams": len(streams),
-                "seq_len": max(out_frames(m.shape[1]) for m, _ in buckets),
-                "global_batch": args.segments * world if args.shard == "weak" else args.segments,
-                "parallelism": f"dp{world} (segment-sharded, no collective)",
-                "l2": "inputs larger than L2: 0.64 GB of Q8_0 weights stream per pass; activations up to 1.6 GB",
-            },
-            "e2e": {"value": args.e2e_steps * audio_total / te2e_max, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h,
+            "config": workload_config(args, world, plan, spec),
+            "e2e": {"value": e2e_steps * audio_total / te2e_max, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps,
                     "api": "nq_encoder_forward_host_async per bucket (buckets alternating over the streams) + "
-                           "nq_encoder_wait per step (pinned host buffers)"},
+                           "nq_encoder_wait per step (pinned host buffers); wall clock, max over ranks"},
             "roofline": {"kernel": "gemm_bf16_sm100_kernel (GEMM class; M < 128 calls use gemm_q8_sm100_kernel)",
                          "bound": "tensor", "achieved": achieved, "peak": peak_t,
                          "unit": "TFLOP/s", "frac": achieved / peak_t if peak_t else None, "traffic": traffic,
+                         "traffic_source": traffic_src,
                          "peak_source": f"{pk['source']} bf16_tflops_sustained",
                          "launches": gemm["launches"], "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"]),
                          "algorithmic_gflop_per_launch": gemm["flops"] / max(1, gemm["launches"]) / 1e9,
@@ -428,6 +585,108 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "cfg2_single_30s": {"ms": cfg2_ms, "rtfx": 30.0 / (cfg2_ms / 1e3)},
         }
         print(json.dumps(line), flush=True)
+
+
+# -------------------------------------------------------------------- linear
+CFG1_KN = [(1024, 4096), (4096, 1024), (1024, 3072), (1024, 1024), (1024, 2048), (1024, 1024)]
+CFG1_M = [1, 2, 4, 8, 16, 125, 1024, 2048, 4096, 12000]
+# configs[3] Kokoro linears (K -> N) at M = 200 phonemes: ALBERT Q/K/V/dense,
+# FFN and FFN output (src/kokoro/albert.rs:126-149), bert_encoder 768 -> 512
+# (src/kokoro/model.rs:84-87).
+KOKORO_KN = [(768, 768), (768, 2048), (2048, 768), (768, 512)]
+
+
+def _linear_weights(n: int, k: int, copies: int, rng, keep_bf16: bool = False, qtiled: bool = False) -> list:
+    from nspeech_b200 import lib
+    from nspeech_b200.fast_matmul import QWeight
+    out = []
+    for _ in range(copies):
+        q = rng.integers(-127, 128, size=(n, k // 32, 34), dtype=np.int64).astype(np.uint8)
+        d = (rng.random((n, k // 32)) * 1e-3 + 1e-4).astype(np.float16)
+        q[:, :, :2] = d.view(np.uint8).reshape(n, k // 32, 2)
+        w = QWeight.from_q8_0(q.reshape(n, -1), n, k, flags=lib.NQ_MODE_QTILED if qtiled else 0)
+        out.append(w.keep_bf16() if keep_bf16 else w)
+    return out
+
+
+def time_linear(m: int, k: int, n: int, x_dtype, y_dtype, iters: int = 20, seed: int = 0, graph: bool = False,
+                keep_bf16: bool = False, qtiled: bool = False) -> dict:
+    """Device time per nq_linear call of one shape (see the module docstring)."""
+    import torch
+    from nspeech_b200 import lib
+    rng = np.random.default_rng(seed)
+    wbytes = n * k * 34 / 32
+    # weights stream past L2 (the kept bf16 copy, when kept, is what the GEMM reads)
+    copies = int(min(32, max(1, np.ceil(300e6 / (n * k * 2 if keep_bf16 else wbytes)))))
+    ws = _linear_weights(n, k, copies, rng, keep_bf16, qtiled)
+    x = torch.randn(m, k, device="cuda").to(x_dtype)
+    y = torch.empty(m, n, device="cuda", dtype=y_dtype)
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        for i in range(max(3, copies)):  # also sizes the stream's workspace before any capture
+            ws[i % copies].linear(x, out=y)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(iters):
+                ws[i % copies].linear(x, out=y)
+        g.replay()
+        torch.cuda.synchronize()
+        reps = 5
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / (reps * iters) / 1e3
+        del g
+    else:
+        with torch.cuda.stream(stream):
+            e0.record()
+            for i in range(iters):
+                ws[i % copies].linear(x, out=y)
+            e1.record()
+        torch.cuda.synchronize()
+        t = e0.elapsed_time(e1) / iters / 1e3
+    if lib.status() != 0:
+        raise RuntimeError("device status reported a timeout")
+    byts = wbytes + m * k * x.element_size() + m * n * y.element_size()
+    pk = peaks()
+    tflops, gbs = 2 * m * n * k / t / 1e12, byts / t / 1e9
+    bound = "hbm" if m <= 125 else "tensor"
+    frac = gbs / pk["hbm_gbs"] if bound == "hbm" else tflops / pk["bf16_tflops"]
+    return {"m": m, "k": k, "n": n, "x": str(x_dtype).split(".")[-1], "y": str(y_dtype).split(".")[-1],
+            "us": round(t * 1e6, 2), "tflops": round(tflops, 1), "gbs": round(gbs, 1), "bound": bound,
+            "frac": round(frac, 3), "peak_source": pk["source"], "timing": "graph" if graph else "calls",
+            "weights": ("qtiled " if qtiled else "") + ("kept bf16 copy" if keep_bf16 else "q8_0")}
+
+
+def run_linear(args) -> None:
+    import torch
+    from nspeech_b200 import lib
+    torch.cuda.set_device(0)
+    lib.init(0)
+    dt = {"bf16": torch.bfloat16, "f32": torch.float32}
+    jobs = [(tuple(int(v) for v in s.lower().split("x")), dt[args.x], dt[args.y]) for s in args.shape]
+    sd = dt[args.sweep_dtype]
+    if args.cfg1_sweep:
+        ms = [int(v) for v in args.sweep_m.split(",")] if args.sweep_m else CFG1_M
+        jobs += [((m, k, n), sd, sd) for m in ms for k, n in CFG1_KN]
+    if args.kokoro:
+        jobs += [((200, k, n), sd, sd) for k, n in KOKORO_KN]
+    if not jobs:
+        raise SystemExit("--linear needs --shape, --cfg1-sweep or --kokoro")
+    units = [int(v) for v in args.unit_tokens.split(",")]
+    for (m, k, n), xd, yd in jobs:
+        for u in units:
+            lib.check(lib.load().nq_set_gemm_unit_tokens(u))
+            r = time_linear(m, k, n, xd, yd, iters=args.iters, graph=args.graph, keep_bf16=args.keep_bf16,
+                            qtiled=args.qtiled)
+            r["unit_tokens"] = u
+            print(json.dumps(r), flush=True)
+    lib.check(lib.load().nq_set_gemm_unit_tokens(0))
 
 
 def run_gemv_sweep(args) -> None:
@@ -575,6 +834,9 @@ def main():
         return
     if args.gemv:
         run_gemv_sweep(args)
+        return
+    if args.linear:
+        run_linear(args)
         return
     if world > 1:
         import torch

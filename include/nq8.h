@@ -67,6 +67,17 @@ extern "C" {
  * projection; they are interleaved per 128-row tile so that the GLU epilogues
  * fuse into the matmul.  Required for NQ_EPI_GLU_*; output width is N/2. */
 #define NQ_PACK_GLU 1
+/* Compute with the QTiled semantics of MatMul::from_qtensor
+ * (src/fast_matmul.rs:184, dispatched to QTiledOp at :212; QTiledOp::cpu_fwd
+ * :71-125 over tiled_matmul_inner :30-62): every nq_linear call quantizes the
+ * activation rows per 32 elements to Q8_0 (ggml rule: d = amax / 127,
+ * q = roundf(x / d), d rounded to f16) and computes
+ *   y[m, n] = sum over blocks b, in order, of ((float)sumi_b * d_w) * d_x
+ * with the exact int8 block dot products sumi_b, then bias and activation.
+ * Without the flag a weight computes FbgemmBf16Op's semantics (below).  Not
+ * combinable with NQ_PACK_GLU; nq_gemv_noalloc and nq_gemv_resadd_ln reject
+ * it. */
+#define NQ_MODE_QTILED 2
 
 /* ---- device status bits (nq_status) -------------------------------------- */
 #define NQ_DEV_TIMEOUT_PRODUCER 0x1
@@ -95,6 +106,10 @@ int nq_weight_from_q8_0(const void *blocks, int64_t n, int64_t k, int flags, nq_
 /* Upload a dequantized f32 [n, k] weight.  It is re-quantized to Q8_0 with
  * ggml semantics, which is lossless for tensors that came from Q8_0 (the only
  * way the reference calls it: new_mm, src/moonshine/encoder.rs:29-39).
+ * A tensor that does not round-trip exactly (any f32 weight not dequantized
+ * from Q8_0, NaN, infinities) is rejected with NQ_ERR_DTYPE: the reference's
+ * MatMul::from_tensor would keep it at bf16 precision, which a Q8_0 store
+ * cannot, so the call fails instead of silently losing precision.
  * Replaces MatMul::from_tensor (src/fast_matmul.rs:191-208). */
 int nq_weight_from_f32(const float *w, int64_t n, int64_t k, int flags, nq_weight **out);
 
@@ -331,9 +346,10 @@ int nq_set_gemm_path(int path);
  * activations keep 256).  Process-wide; returns NQ_ERR_ARG for other values. */
 int nq_set_gemm_unit_tokens(int tokens);
 
-/* Test hook for failure detection: launches a kernel that waits on an
- * mbarrier nothing arrives on, bounded by the wait limit; the kernel records
- * NQ_DEV_TIMEOUT_CONSUMER and returns, leaving the context usable. */
+/* DEBUG ONLY -- a test hook for failure detection, not part of the matmul
+ * API: launches a kernel that waits on an mbarrier nothing arrives on,
+ * bounded by the wait limit; the kernel records NQ_DEV_TIMEOUT_CONSUMER and
+ * returns, leaving the context usable.  No counterpart in the reference. */
 int nq_debug_wait_timeout(void *stream);
 
 #ifdef __cplusplus

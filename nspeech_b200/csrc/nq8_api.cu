@@ -160,7 +160,9 @@ int upload_packed(const uint8_t *blocks, int64_t n, int64_t k, int flags, nq_wei
 int check_weight_shape(int64_t n, int64_t k, int flags) {
   if (n <= 0 || k <= 0) return fail(NQ_ERR_SHAPE, "weight shape [%lld, %lld] must be positive", (long long)n, (long long)k);
   if (k % 32) return fail(NQ_ERR_SHAPE, "K=%lld is not a multiple of the Q8_0 block (32)", (long long)k);
-  if (flags & ~NQ_PACK_GLU) return fail(NQ_ERR_ARG, "unknown pack flags 0x%x", flags);
+  if (flags & ~(NQ_PACK_GLU | NQ_MODE_QTILED)) return fail(NQ_ERR_ARG, "unknown weight flags 0x%x", flags);
+  if ((flags & NQ_PACK_GLU) && (flags & NQ_MODE_QTILED))
+    return fail(NQ_ERR_UNSUPPORTED, "NQ_MODE_QTILED weights cannot be GLU-packed");
   if ((flags & NQ_PACK_GLU) && (n % 2)) return fail(NQ_ERR_SHAPE, "GLU weight needs an even N (got %lld)", (long long)n);
   if (n > (1LL << 31) || k > (1LL << 31)) return fail(NQ_ERR_SHAPE, "weight too large");
   return NQ_OK;
@@ -279,6 +281,20 @@ struct GemvResLn {
   float eps;
 };
 
+// Algorithmic FLOPs and bytes of `nprob` weights applied to M rows (the
+// profiler's per-launch figures): 2MNK, and N*K*34/32 + M*K*sx + M*N*sy + 4N.
+void linear_cost(const LinearArgs *args, int nprob, int64_t m, int x_dtype, int y_dtype, double *flops,
+                 double *bytes) {
+  *flops = 0;
+  *bytes = 0;
+  for (int i = 0; i < nprob; ++i) {
+    const nq_weight *w = args[i].w;
+    *flops += 2.0 * m * w->n * w->k;
+    *bytes += w->n * (w->k / 32) * 34.0 + m * w->k * (x_dtype == NQ_F32 ? 4.0 : 2.0) +
+              m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (args[i].bias ? 4.0 * w->n : 0.0);
+  }
+}
+
 int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
              int epilogue, int y_dtype, cudaStream_t stream, const GemvResLn *rl = nullptr) {
   const nq_weight *w0 = args[0].w;
@@ -349,12 +365,7 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
   double flops = 0, bytes = 0;
-  for (int i = 0; i < nprob; ++i) {
-    const nq_weight *w = args[i].w;
-    flops += 2.0 * m * w->n * w->k;
-    bytes += w->n * (w->k / 32) * 34.0 + m * w->k * (x_dtype == NQ_F32 ? 4.0 : 2.0) +
-             m * out_width(w) * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (args[i].bias ? 4.0 * w->n : 0.0);
-  }
+  linear_cost(args, nprob, m, x_dtype, y_dtype, &flops, &bytes);
   ProfScope ps(NQ_KCLASS_GEMV, stream, flops, bytes);
   cudaError_t e = nq::launch_gemv(p, plan.ctas, stream);
   if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
@@ -562,6 +573,45 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
   return NQ_OK;
 }
 
+// QTiled semantics (NQ_MODE_QTILED weights): quantize the activation rows to
+// Q8_0 once, then one int8 tensor-core launch per weight.
+int run_qtiled(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx,
+               int epilogue, int y_dtype, cudaStream_t stream) {
+  const int kc = args[0].w->kc;
+  for (int i = 1; i < nprob; ++i)
+    if (args[i].w->kc != kc) return fail(NQ_ERR_SHAPE, "weights sharing x must share K");
+  Workspace *ws = nullptr;
+  int rc = get_workspace(ctx, stream, nq::qtiled_x_bytes(m, kc), &ws);
+  if (rc) return rc;
+  int8_t *xq = reinterpret_cast<int8_t *>(ws->buf);
+  float *dx = reinterpret_cast<float *>(ws->buf + align_up(static_cast<size_t>(m) * kc * nq::kPackK, 256));
+  cudaError_t e = nq::launch_qtiled_quantize(x, x_dtype, ldx, m, args[0].w->k, kc, xq, dx, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "activation quantize launch");
+  for (int i = 0; i < nprob; ++i) {
+    const nq_weight *w = args[i].w;
+    nq::QtiledParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.w = w->dev;
+    p.n_tiles = w->n_tiles;
+    p.kc = kc;
+    p.N = w->n;
+    p.M = static_cast<int>(m);
+    p.xq = xq;
+    p.dx = dx;
+    p.bias = args[i].bias;
+    p.epi = epilogue;
+    p.y = args[i].y;
+    p.y_dtype = y_dtype;
+    p.ldy = args[i].ldy;
+    double flops = 0, bytes = 0;
+    linear_cost(&args[i], 1, m, x_dtype, y_dtype, &flops, &bytes);
+    ProfScope ps(m <= 16 ? NQ_KCLASS_GEMV : NQ_KCLASS_GEMM, stream, flops, bytes);
+    e = nq::launch_qtiled(p, stream);
+    if (e != cudaSuccess) return cuda_fail(e, "QTiled GEMM launch");
+  }
+  return NQ_OK;
+}
+
 int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, int64_t m, int64_t ldx, int epilogue,
                 int y_dtype, void *stream) {
   for (int i = 0; i < nprob; ++i) {
@@ -577,6 +627,11 @@ int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, i
     if (args[i].w->device != dev)
       return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", args[i].w->device, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool qtiled = (args[0].w->flags & NQ_MODE_QTILED) != 0;
+  for (int i = 1; i < nprob; ++i)
+    if (((args[i].w->flags & NQ_MODE_QTILED) != 0) != qtiled)
+      return fail(NQ_ERR_ARG, "weights sharing one call must all be NQ_MODE_QTILED or none");
+  if (qtiled) return run_qtiled(ctx, args, nprob, x, x_dtype, m, ldx, epilogue, y_dtype, s);
   if (m <= 16) return run_gemv(ctx, args, nprob, x, x_dtype, m, ldx, epilogue, y_dtype, s);
   for (int i = 0; i < nprob; ++i) {
     rc = run_gemm(ctx, args[i], x, x_dtype, m, ldx, epilogue, y_dtype, s);
@@ -623,6 +678,7 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 int linear_launches(const nq_weight *w, int64_t m, int x_dtype, bool aligned) {
   if (!w || m <= 0) return 0;
+  if (w->flags & NQ_MODE_QTILED) return 2;  // quantize x + the int8 GEMM
   if (m <= 16)  // GEMV + gemv_reduce (for up to three weights), after split_x unless x is read in place
     return x_dtype == NQ_BF16 && aligned && w->k % nq::kPackK == 0 ? 2 : 3;
   DeviceCtx *ctx = nullptr;
@@ -678,6 +734,12 @@ int nq_weight_from_f32(const float *wf, int64_t n, int64_t k, int flags, nq_weig
   if (rc) return rc;
   std::vector<uint8_t> blocks(static_cast<size_t>(n) * (k / 32) * 34);
   nq::quantize_q8_0(wf, n, k, blocks.data());
+  const int64_t bad = nq::q8_0_first_mismatch(wf, blocks.data(), n * k);
+  if (bad >= 0)
+    return fail(NQ_ERR_DTYPE,
+                "nq_weight_from_f32: element [%lld, %lld] = %g does not survive Q8_0 re-quantization; only "
+                "tensors dequantized from Q8_0 can be uploaded as f32 (the weights are stored as Q8_0)",
+                (long long)(bad / k), (long long)(bad % k), static_cast<double>(wf[bad]));
   return upload_packed(blocks.data(), n, k, flags, out);
 }
 
@@ -811,6 +873,7 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   int rc = validate(w, x, x_dtype, m, ldx, epilogue, y, y_dtype, ldy);
   if (rc) return rc;
   if (m > 16) return fail(NQ_ERR_SHAPE, "nq_gemv_noalloc serves M <= 16 rows (got %lld)", (long long)m);
+  if (w->flags & NQ_MODE_QTILED) return fail(NQ_ERR_UNSUPPORTED, "nq_gemv_noalloc: NQ_MODE_QTILED weight");
   if (m == 0) return NQ_OK;
   DeviceCtx *ctx = nullptr;
   int dev = 0;
@@ -880,8 +943,17 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   p.ctas = plan.ctas;
   p.ctl.status = ctx->status;
   p.ctl.wait_limit = g_wait_limit;
+  double flops = 0, bytes = 0;
+  LinearArgs la{w, bias, y, ldy};
+  linear_cost(&la, 1, m, x_dtype, y_dtype, &flops, &bytes);
+  ProfScope ps(NQ_KCLASS_GEMV, stream_, flops, bytes);
   cudaError_t e = nq::launch_gemv(p, plan.ctas, stream_);
-  if (e != cudaSuccess) return cuda_fail(e, "GEMV launch");
+  if (e != cudaSuccess) {
+    // The GEMV may have launched and bumped the shared work counter before
+    // its reduce (which re-arms it) failed to launch: zero it on the stream.
+    cudaMemsetAsync(sched, 0, sizeof(int), stream_);
+    return cuda_fail(e, "GEMV launch");
+  }
   return NQ_OK;
 }
 
@@ -893,6 +965,7 @@ int nq_gemv_resadd_ln(const nq_weight *w, const void *x, int x_dtype, int64_t m,
   if (!res_in || !res_out || !ln_gamma) return fail(NQ_ERR_ARG, "nq_gemv_resadd_ln: null residual or gamma");
   if (m > 16) return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln serves M <= 16 rows (got %lld)", (long long)m);
   if (w->flags & NQ_PACK_GLU) return fail(NQ_ERR_ARG, "nq_gemv_resadd_ln: GLU-packed weight");
+  if (w->flags & NQ_MODE_QTILED) return fail(NQ_ERR_UNSUPPORTED, "nq_gemv_resadd_ln: NQ_MODE_QTILED weight");
   if (w->n > nq::kGemvLnMaxN)
     return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln: N = %lld exceeds %d", (long long)w->n, nq::kGemvLnMaxN);
   if (ld_res < w->n) return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln: ld_res < N");

@@ -108,6 +108,43 @@ static uint16_t f32_to_f16(float f) {
 }
 
 // ggml quantize_row_q8_0_ref semantics: d = amax/127, q = roundf(x / d).
+static float f16_to_f32(uint16_t h) {
+  const uint32_t sign = (static_cast<uint32_t>(h) & 0x8000u) << 16;
+  uint32_t e = (h >> 10) & 0x1fu, m = h & 0x3ffu, x;
+  if (e == 0) {
+    if (m == 0) {
+      x = sign;
+    } else {
+      int sh = 0;
+      while (!(m & 0x400u)) {
+        m <<= 1;
+        ++sh;
+      }
+      x = sign | (static_cast<uint32_t>(113 - sh) << 23) | ((m & 0x3ffu) << 13);
+    }
+  } else if (e == 31) {
+    x = sign | 0x7f800000u | (m << 13);
+  } else {
+    x = sign | ((e + 112u) << 23) | (m << 13);
+  }
+  float f;
+  std::memcpy(&f, &x, 4);
+  return f;
+}
+
+int64_t q8_0_first_mismatch(const float *w, const uint8_t *blocks, int64_t count) {
+  for (int64_t b = 0; b < count / 32; ++b) {
+    uint16_t dh;
+    std::memcpy(&dh, blocks + b * 34, 2);
+    const float d = f16_to_f32(dh);
+    for (int j = 0; j < 32; ++j) {
+      const float v = d * static_cast<float>(static_cast<int8_t>(blocks[b * 34 + 2 + j]));
+      if (!(v == w[b * 32 + j])) return b * 32 + j;
+    }
+  }
+  return -1;
+}
+
 void quantize_q8_0(const float *w, int64_t n, int64_t k, uint8_t *blocks) {
   const int64_t nb = n * (k / 32);
   for (int64_t b = 0; b < nb; ++b) {

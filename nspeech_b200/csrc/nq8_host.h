@@ -31,6 +31,9 @@ void pack_q8_0(const uint8_t *blocks, int64_t n, int64_t k, int flags, uint8_t *
 void unpack_q8_0(const uint8_t *packed, int64_t n, int64_t k, int flags, uint8_t *blocks);
 // f32 [n][k] -> GGUF Q8_0 blocks (ggml quantize_row_q8_0_ref semantics).
 void quantize_q8_0(const float *w, int64_t n, int64_t k, uint8_t *blocks);
+// First element of w[0, count) whose Q8_0 block does not dequantize back to
+// it exactly (NaN never does), or -1.
+int64_t q8_0_first_mismatch(const float *w, const uint8_t *blocks, int64_t count);
 
 struct GgufTensor {
   std::string name;

@@ -152,6 +152,29 @@ cudaError_t launch_splitk_reduce(const SplitkReduceParams &p, cudaStream_t strea
 cudaError_t launch_split_x(const void *x, int x_dtype, int64_t ldx, int64_t M, int64_t K,
                            int64_t k_pad, __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t stream);
 
+// QTiled semantics (MatMul::from_qtensor, src/fast_matmul.rs:71-125): x
+// quantized per 32 to Q8_0, per-block int8 dot products scaled by both f16
+// scales and summed in block order (nq8_qtiled.cu).
+struct QtiledParams {
+  const uint8_t *w;  // packed tiles (not GLU-packed)
+  int n_tiles, kc;
+  int64_t N;
+  int M;
+  const int8_t *xq;  // [M][kc * 64] quantized activations
+  const float *dx;   // [M][kc * 2] their Q8_0 scales (f16 values)
+  const float *bias;
+  int epi;           // NONE, SILU, GELU_ERF or RELU
+  void *y;
+  int y_dtype;
+  int64_t ldy;
+};
+// Workspace bytes of the quantized activations of M rows (int8 rows, then the
+// f32 scales at the returned offset's 256-byte-aligned split).
+size_t qtiled_x_bytes(int64_t M, int kc);
+cudaError_t launch_qtiled_quantize(const void *x, int x_dtype, int64_t ldx, int64_t M, int64_t K, int kc, int8_t *xq,
+                                   float *dx, cudaStream_t stream);
+cudaError_t launch_qtiled(const QtiledParams &p, cudaStream_t stream);
+
 cudaError_t launch_wait_timeout_probe(DevCtl ctl, cudaStream_t stream);
 
 }  // namespace nq

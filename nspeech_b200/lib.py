@@ -40,6 +40,7 @@ NQ_EPI_RELU = 5
 
 NQ_PACK_DEFAULT = 0
 NQ_PACK_GLU = 1
+NQ_MODE_QTILED = 2
 
 
 class NqError(RuntimeError):

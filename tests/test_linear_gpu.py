@@ -20,6 +20,10 @@ CONTRACT_TOL = 1e-2   # north-star bound (row-rms-normalised max relative error)
 EXPECT_TOL = 2e-3     # what the hi/lo f32 path and bf16-exact weights deliver
 
 CFG1_SHAPES = [(1024, 4096), (4096, 1024), (1024, 3072), (1024, 1024), (1024, 2048), (1024, 1024)]
+# configs[3] Kokoro linears (K -> N) at M = 200 phonemes: ALBERT Q/K/V/dense
+# 768 -> 768, FFN 768 -> 2048 (GELU-erf), FFN output 2048 -> 768
+# (src/kokoro/albert.rs:126-149), bert_encoder 768 -> 512 (src/kokoro/model.rs:84-87).
+KOKORO_SHAPES = [(768, 768, 0), (768, 2048, 2), (2048, 768, 0), (768, 512, 0)]
 
 
 @pytest.fixture(scope="module")
@@ -82,6 +86,27 @@ def test_cfg1_block_shapes(nq, oracle, k, n, xdt):
         x = _bf16_round(x)
     got = _run(w, x, torch.float32 if xdt == "f32" else torch.bfloat16, bias=bias)
     err = _check(oracle, got, _ref(oracle, x, q, n, bias), f"cfg1 {k}->{n} {xdt}")
+    assert err <= EXPECT_TOL
+
+
+@pytest.mark.parametrize("k,n,epi", KOKORO_SHAPES)
+@pytest.mark.parametrize("xdt", ["f32", "bf16"])
+@pytest.mark.parametrize("keep", [False, True])
+def test_kokoro_shapes(nq, oracle, k, n, epi, xdt, keep):
+    """200 phoneme rows, f32 bias N(0, 0.01), both GEMM paths (the
+    fused-dequantize kernel below 128 rows is not reached at M = 200: Q8_0
+    tiles dequantized per call, or a kept bf16 copy)."""
+    from nspeech_b200.fast_matmul import QWeight
+    x = oracle.normal(3, (200, k), 0.0, 1.0)
+    q = oracle.quantize_q8_0(oracle.normal(3000 + k + n, (n, k), 0.0, 0.02))
+    bias = oracle.normal(8, (n,), 0.0, 0.01)
+    w = QWeight.from_q8_0(q, n, k)
+    if keep:
+        w.keep_bf16()
+    if xdt == "bf16":
+        x = _bf16_round(x)
+    got = _run(w, x, torch.float32 if xdt == "f32" else torch.bfloat16, bias=bias, epi=epi)
+    err = _check(oracle, got, _ref(oracle, x, q, n, bias, epi), f"kokoro {k}->{n} {xdt} keep={keep}")
     assert err <= EXPECT_TOL
 
 
@@ -190,12 +215,15 @@ def test_matmul_mirror_api(nq, oracle):
     a = MatMul.from_qtensor(q, n, k)
     b = MatMul.from_tensor(deq)  # dequantized f32, as new_mm passes it
     assert np.array_equal(b.weight.to_q8_0(), q)  # lossless re-quantization
+    assert np.array_equal(a.weight.to_q8_0(), q)
     x = oracle.normal(51, (2, 3, k))
     xt = torch.from_numpy(x).cuda()
     ya, yb = a.forward(xt), b.forward(xt)
-    assert ya.shape == (2, 3, n)
-    assert torch.equal(ya, yb)
-    _check(oracle, ya.reshape(6, n).cpu().numpy(), _ref(oracle, x.reshape(6, k), q, n), "MatMul")
+    assert ya.shape == yb.shape == (2, 3, n)
+    # from_qtensor: QTiledOp's semantics, bit-identical to the oracle's order
+    assert np.array_equal(ya.reshape(6, n).cpu().numpy(), oracle.matmul_qtiled(x.reshape(6, k), q, n))
+    # from_tensor: FbgemmBf16Op's semantics
+    _check(oracle, yb.reshape(6, n).cpu().numpy(), _ref(oracle, x.reshape(6, k), q, n), "MatMul")
     with pytest.raises(MatMulError, match="not contiguous"):
         a.forward(xt.transpose(0, 1))
     with pytest.raises(MatMulError, match="only one dimension"):
@@ -204,6 +232,87 @@ def test_matmul_mirror_api(nq, oracle):
         a.forward(xt[..., :512].contiguous())
     with pytest.raises(MatMulError, match="only supports f32"):
         a.forward(xt.to(torch.bfloat16))
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 1024), (3, 96, 130), (16, 640, 2560), (17, 1024, 4096),
+                                   (125, 4096, 1024), (200, 768, 2048), (1000, 160, 200)])
+@pytest.mark.parametrize("xdt", ["f32", "bf16"])
+def test_qtiled_mode_bit_identical_to_oracle(nq, oracle, m, k, n, xdt):
+    """NQ_MODE_QTILED weights (MatMul::from_qtensor): x quantized per 32 to
+    Q8_0 on the GPU, exact int8 block sums, f32 scaling in block order --
+    bit-identical to REF_QTILED (oracle/nq8_oracle.c) on the same inputs."""
+    from nspeech_b200.fast_matmul import QWeight
+    q = oracle.quantize_q8_0(oracle.normal(70 + n, (n, k), 0.0, 0.02))
+    w = QWeight.from_q8_0(q, n, k, flags=nq.NQ_MODE_QTILED)
+    x = oracle.normal(71 + m, (m, k))
+    if xdt == "bf16":
+        x = _bf16_round(x)
+    got = _run(w, x, torch.float32 if xdt == "f32" else torch.bfloat16)
+    ref = oracle.matmul_qtiled(x, q, n)
+    assert np.array_equal(got, ref), float(np.abs(got - ref).max())
+    # against the exact product: the activation quantization is the difference
+    assert oracle.max_rel_err(got, oracle.matmul_exact(x, q, n), 1.0) < 5e-2
+
+
+@pytest.mark.parametrize("epi", [0, 1, 2, 5])
+def test_qtiled_mode_bias_epilogue_and_edges(nq, oracle, epi):
+    from nspeech_b200.fast_matmul import QWeight
+    k, n, m = 640, 1000, 33
+    xs = oracle.normal(81, (m, k))
+    xs[3, :32] = 0.0          # an all-zero block: d = 0
+    xs[4, 64:96] = 1e-30      # tiny values: f16 scale underflows to 0
+    xs[5, 96:128] = 127.0     # d = 1 exactly
+    xs[6, 128:160] = np.linspace(-0.5, 0.5, 32)  # rounding ties
+    q = oracle.quantize_q8_0(oracle.normal(82, (n, k), 0.0, 0.05))
+    bias = oracle.normal(83, (n,), 0.0, 0.1)
+    w = QWeight.from_q8_0(q, n, k, flags=nq.NQ_MODE_QTILED)
+    got = _run(w, xs, bias=bias, epi=epi)
+    raw = oracle.matmul_qtiled(xs, q, n).astype(np.float64)
+    ref = oracle.epilogue(raw, bias, epi)
+    assert oracle.max_rel_err(got, ref, 1.0) < 1e-6
+    # bf16 output
+    got_b = _run(w, xs, bias=bias, epi=epi, out_dtype=torch.bfloat16)
+    assert oracle.max_rel_err(got_b, ref, 1.0) < 5e-3
+    assert nq.status() == 0
+
+
+def test_qtiled_mode_rejections(nq, oracle):
+    from nspeech_b200 import lib
+    from nspeech_b200.fast_matmul import QWeight
+    q = oracle.quantize_q8_0(oracle.normal(84, (256, 256), 0.0, 0.05))
+    with pytest.raises(lib.NqError) as e:
+        QWeight.from_q8_0(q, 256, 256, flags=nq.NQ_MODE_QTILED | nq.NQ_PACK_GLU)
+    assert e.value.code == nq.NQ_ERR_UNSUPPORTED
+    w = QWeight.from_q8_0(q, 256, 256, flags=nq.NQ_MODE_QTILED)
+    x = torch.zeros((1, 256), device="cuda")
+    y = torch.zeros((1, 256), device="cuda")
+    L = nq.load()
+    rc = L.nq_gemv_noalloc(w.handle, x.data_ptr(), 0, 1, 256, None, 0, y.data_ptr(), 0, 256, None)
+    assert rc == nq.NQ_ERR_UNSUPPORTED
+    plain = QWeight.from_q8_0(q, 256, 256)
+    import ctypes
+    outs = [torch.zeros((1, 256), device="cuda") for _ in range(3)]
+    rc = L.nq_gemv_qkv_splitk(w.handle, plain.handle, w.handle, x.data_ptr(), 0, *[o.data_ptr() for o in outs], 0,
+                              ctypes.c_void_p(0))
+    assert rc == nq.NQ_ERR_ARG  # one call mixes the two semantics
+
+
+def test_from_f32_rejects_non_q8_tensor(nq, oracle):
+    """MatMul::from_tensor on an f32 tensor that is not a Q8_0 dequantization:
+    the Q8_0 store cannot keep it, so the upload fails (NQ_ERR_DTYPE) instead
+    of silently re-quantizing."""
+    from nspeech_b200 import lib
+    from nspeech_b200.fast_matmul import MatMul, QWeight
+    w = oracle.normal(85, (64, 128), 0.0, 0.02)
+    with pytest.raises(lib.NqError) as e:
+        QWeight.from_f32(w)
+    assert e.value.code == nq.NQ_ERR_DTYPE and "re-quantization" in str(e.value)
+    deq = oracle.dequant_q8_0(oracle.quantize_q8_0(w), 64, 128)
+    assert np.array_equal(QWeight.from_f32(deq).to_q8_0(), oracle.quantize_q8_0(w))
+    bad = deq.copy()
+    bad[7, 9] = np.nan
+    with pytest.raises(lib.NqError):
+        MatMul.from_tensor(bad)
 
 
 def test_weight_roundtrip_and_fuse(nq, oracle):

@@ -1,11 +1,14 @@
-"""nq_gemv_noalloc (static-scratch split-K GEMV) against nq_linear.
+"""nq_gemv_noalloc (static-scratch split-K GEMV) against nq_linear and the
+CPU oracle.
 
 Runs through the C ABI: the same weight and activations go through the
 existing entry point (nq_linear, workspace scratch) and through
 nq_gemv_noalloc (static device scratch); outputs must agree within the
 linear contract's tolerance, on two calls in a row (the second call reuses
-the array the first one left behind).  Collected last, and self-contained so
-it also passes alone in a fresh process (its first call sets up the scratch).
+the array the first one left behind), and both must match the reference's
+FbgemmBf16Op semantics computed by the oracle.  Collected last, and
+self-contained so it also passes alone in a fresh process (its first call
+sets up the scratch).
 """
 import ctypes
 
@@ -53,12 +56,14 @@ def _call(L, fn, w, x, m, bias, epi, y, y_dtype):
                                            (16, 1024, 1024, 0, False), (1, 640, 1024, 4, True),
                                            (9, 2048, 3072, 2, False)])
 @pytest.mark.parametrize("xdt", [torch.float32, torch.bfloat16])
-def test_noalloc_matches_linear_twice(nq, m, k, n, epi, glu, xdt):
+def test_noalloc_matches_linear_twice(nq, oracle, m, k, n, epi, glu, xdt):
     L = nq.load()
     rng = np.random.default_rng(m * 31 + k + n)
     w = _weight(nq, rng, n, k, flags=nq.NQ_PACK_GLU if glu else 0)
+    blocks = w.to_q8_0()
     n_out = n // 2 if glu else n
-    bias = torch.from_numpy(rng.standard_normal(n).astype(np.float32) * 0.1).cuda()
+    bias_np = rng.standard_normal(n).astype(np.float32) * 0.1
+    bias = torch.from_numpy(bias_np).cuda()
     ref = torch.empty((m, n_out), device="cuda")
     for call in range(2):
         x = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda().to(xdt)
@@ -69,7 +74,34 @@ def test_noalloc_matches_linear_twice(nq, m, k, n, epi, glu, xdt):
         g, r = got.cpu().numpy(), ref.cpu().numpy()
         assert np.isfinite(g).all(), call
         assert _rel(g, r) <= TOL, (call, _rel(g, r))
+        # the reference's semantics on the same inputs (bf16 x as its values)
+        want = oracle.epilogue(oracle.matmul_fbgemm_bf16(x.float().cpu().numpy(), blocks, n).astype(np.float64),
+                               bias_np, epi)
+        assert oracle.max_rel_err(g, want, 1.0) <= TOL, (call, oracle.max_rel_err(g, want, 1.0))
     assert nq.status() == 0
+
+
+def test_noalloc_is_profiled_like_linear(nq):
+    """One nq_gemv_noalloc call is one GEMV-class launch in the library's
+    profiler, with the same algorithmic FLOPs and bytes as nq_linear's."""
+    L = nq.load()
+    rng = np.random.default_rng(9)
+    w = _weight(nq, rng, 1024, 1024)
+    x = torch.from_numpy(rng.standard_normal((2, 1024)).astype(np.float32)).cuda()
+    y = torch.empty((2, 1024), device="cuda")
+    nq.check(_call(L, L.nq_linear, w, x, 2, None, 0, y, 0))  # workspace sized outside the profile
+    torch.cuda.synchronize()
+    nq.profile_read(nq.NQ_KCLASS_GEMV, reset=True)
+    nq.profile_enable(True)
+    try:
+        nq.check(_call(L, L.nq_linear, w, x, 2, None, 0, y, 0))
+        a = nq.profile_read(nq.NQ_KCLASS_GEMV, reset=True)
+        nq.check(_call(L, L.nq_gemv_noalloc, w, x, 2, None, 0, y, 0))
+        b = nq.profile_read(nq.NQ_KCLASS_GEMV, reset=True)
+    finally:
+        nq.profile_enable(False)
+    assert a["launches"] == b["launches"] == 1
+    assert a["flops"] == b["flops"] and a["bytes"] == b["bytes"]
 
 
 def test_noalloc_rejects_oversized_and_wide(nq):
