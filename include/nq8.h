@@ -283,7 +283,9 @@ int nq_encoder_forward_host(nq_encoder *enc, const float *mel_host, const int32_
  * run on the encoder's own copy streams and overlap the forwards of the
  * neighbouring calls (two device staging slots, event-ordered).  mel_host and
  * out_host must be pinned host memory and stay untouched until
- * nq_encoder_wait returns; out_lengths is filled before this returns. */
+ * nq_encoder_wait returns; out_lengths is filled before this returns.
+ * Calls from several threads are serialized by the encoder (they share its
+ * two staging slots). */
 int nq_encoder_forward_host_async(nq_encoder *enc, const float *mel_host, const int32_t *lengths, int batch,
                                   int t_mel, float *out_host, int32_t *out_lengths, void *stream);
 /* Block until every queued nq_encoder_forward_host_async output is in host memory. */

@@ -38,9 +38,16 @@ struct DevBuf {
   ~DevBuf() {
     if (p) cudaFree(p);
   }
-  int ensure(size_t want) {
+  // Grow to `want` bytes.  Work queued on `st` (the stream that uses the
+  // buffer) may still read the old allocation: synchronize it before the free.
+  int ensure(size_t want, cudaStream_t st = nullptr) {
     if (bytes >= want) return NQ_OK;
-    if (p) cudaFree(p);
+    if (p) {
+      cudaError_t e = cudaStreamSynchronize(st);
+      if (e != cudaSuccess)
+        return api_fail(NQ_ERR_CUDA, std::string("cudaStreamSynchronize(arena growth): ") + cudaGetErrorString(e));
+      cudaFree(p);
+    }
     p = nullptr;
     bytes = 0;
     cudaError_t e = cudaMalloc(&p, want);
@@ -116,6 +123,9 @@ struct nq_encoder {
   HostSlot host_slots[2];
   cudaStream_t h2d_stream = nullptr, d2h_stream = nullptr;
   int host_next = 0;
+  // Serializes nq_encoder_forward_host_async callers (slot choice, the lazy
+  // stream creation and the enqueue of one call's copies and forward).
+  std::mutex host_mu;
 
   ~nq_encoder() {
     if (h2d_stream) cudaStreamSynchronize(h2d_stream);
@@ -365,32 +375,33 @@ Arena *arena_for(nq_encoder *e, cudaStream_t st) {
   return a.get();
 }
 
-int ensure_arena(nq_encoder *e, Arena &A, const Shapes &s) {
+int ensure_arena(nq_encoder *e, Arena &A, const Shapes &s, cudaStream_t st) {
   const size_t M = s.M, D = s.D, ff = static_cast<size_t>(D) * e->cfg.ff_mult;
   const size_t P = 2 * static_cast<size_t>(s.T3) - 1;
-  NQ_TRY(A.x.ensure(M * D * 4));
-  NQ_TRY(A.h.ensure(M * D * 2));
-  NQ_TRY(A.t.ensure(M * ff * 2));
-  NQ_TRY(A.u.ensure(M * D * 2));
-  NQ_TRY(A.u32.ensure(M * D * 4));
-  NQ_TRY(A.qkv.ensure(M * 3 * D * 2));
-  NQ_TRY(A.pos.ensure(P * D * 2));
-  NQ_TRY(A.krel.ensure(P * D * e->cfg.n_layers * 2));
-  NQ_TRY(A.att.ensure(M * D * 2));
-  NQ_TRY(A.g.ensure(M * D * 2));
-  NQ_TRY(A.c.ensure(M * D * 2));
-  if (!nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C)) NQ_TRY(A.s1.ensure(static_cast<size_t>(s.B) * s.T1 * s.F1 * s.C * 2));
-  NQ_TRY(A.s2a.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
-  NQ_TRY(A.s2b.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2));
-  NQ_TRY(A.s3a.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
-  NQ_TRY(A.s3b.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
-  NQ_TRY(A.flat.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2));
+  NQ_TRY(A.x.ensure(M * D * 4, st));
+  NQ_TRY(A.h.ensure(M * D * 2, st));
+  NQ_TRY(A.t.ensure(M * ff * 2, st));
+  NQ_TRY(A.u.ensure(M * D * 2, st));
+  NQ_TRY(A.u32.ensure(M * D * 4, st));
+  NQ_TRY(A.qkv.ensure(M * 3 * D * 2, st));
+  NQ_TRY(A.pos.ensure(P * D * 2, st));
+  NQ_TRY(A.krel.ensure(P * D * e->cfg.n_layers * 2, st));
+  NQ_TRY(A.att.ensure(M * D * 2, st));
+  NQ_TRY(A.g.ensure(M * D * 2, st));
+  NQ_TRY(A.c.ensure(M * D * 2, st));
+  if (!nq::enc::conv0_dw_s2_supported(s.F, s.F1, s.C))
+    NQ_TRY(A.s1.ensure(static_cast<size_t>(s.B) * s.T1 * s.F1 * s.C * 2, st));
+  NQ_TRY(A.s2a.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2, st));
+  NQ_TRY(A.s2b.ensure(static_cast<size_t>(s.B) * s.T2 * s.F2 * s.C * 2, st));
+  NQ_TRY(A.s3a.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2, st));
+  NQ_TRY(A.s3b.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2, st));
+  NQ_TRY(A.flat.ensure(static_cast<size_t>(s.B) * s.T3 * s.F3 * s.C * 2, st));
   if (A.lens_cap < s.B) {
     for (int i = 0; i < Arena::kLenSlots; ++i) {
       if (A.lens_done[i]) NQ_CUDA(cudaEventSynchronize(A.lens_done[i]));
       if (A.lens_host[i]) cudaFreeHost(A.lens_host[i]);
       NQ_CUDA(cudaMallocHost(&A.lens_host[i], static_cast<size_t>(4) * s.B * sizeof(int)));
-      NQ_TRY(A.lens[i].ensure(static_cast<size_t>(4) * s.B * sizeof(int)));
+      NQ_TRY(A.lens[i].ensure(static_cast<size_t>(4) * s.B * sizeof(int), st));
       if (!A.lens_done[i]) NQ_CUDA(cudaEventCreateWithFlags(&A.lens_done[i], cudaEventDisableTiming));
     }
     A.lens_cap = s.B;
@@ -404,7 +415,7 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
             int32_t *out_lengths, cudaStream_t st) {
   const Shapes s = shapes(e, batch, t_mel);
   Arena &A = *arena_for(e, st);
-  NQ_TRY(ensure_arena(e, A, s));
+  NQ_TRY(ensure_arena(e, A, s, st));
   const int slot = A.lens_next;
   A.lens_next = (slot + 1) % Arena::kLenSlots;
   NQ_CUDA(cudaEventSynchronize(A.lens_done[slot]));  // its previous upload has been consumed
@@ -594,6 +605,7 @@ int nq_encoder_forward_host_async(nq_encoder *enc, const float *mel_host, const 
   if (!enc->ready) return api_fail(NQ_ERR_ARG, "encoder not finalized");
   if (batch < 1 || t_mel < 1) return api_fail(NQ_ERR_SHAPE, "batch and t_mel must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::lock_guard<std::mutex> lk(enc->host_mu);
   if (!enc->h2d_stream) {
     NQ_CUDA(cudaStreamCreateWithFlags(&enc->h2d_stream, cudaStreamNonBlocking));
     NQ_CUDA(cudaStreamCreateWithFlags(&enc->d2h_stream, cudaStreamNonBlocking));
@@ -608,8 +620,8 @@ int nq_encoder_forward_host_async(nq_encoder *enc, const float *mel_host, const 
   if (hs.in.bytes < in_bytes || hs.out.bytes < out_bytes) {
     // growing a slot frees its buffers: let its previous use finish first
     if (hs.used) NQ_CUDA(cudaEventSynchronize(hs.d2h_done));
-    NQ_TRY(hs.in.ensure(in_bytes));
-    NQ_TRY(hs.out.ensure(out_bytes));
+    NQ_TRY(hs.in.ensure(in_bytes, enc->d2h_stream));
+    NQ_TRY(hs.out.ensure(out_bytes, enc->d2h_stream));
   }
   // The slot's previous forward must have consumed its input, and its
   // previous output must have left for the host, before they are overwritten.

@@ -142,6 +142,33 @@ def test_batched_segments_equal_single(nq, oracle):
         _compare(oracle, out[i, :olens[i]], ref, f"batched seg {i} len {L}", 0.05)
 
 
+def test_arena_growth_without_host_sync(nq, oracle):
+    """A small bucket then larger ones on the same stream, queued without a
+    host synchronize between them: the arena grows (its old buffers are freed
+    only after the stream drained) and every output matches its own forward."""
+    from nspeech_b200 import synthetic as S
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=1, sub_channels=64)
+    q = _model(oracle, spec, seed=13)
+    shapes = [(1, 120), (4, 700), (8, 1000)]
+    mels = [torch.from_numpy(oracle.normal(60 + i, (b, t, 128))).cuda() for i, (b, t) in enumerate(shapes)]
+    ref_enc = _gpu_encoder(spec, q)
+    refs = []
+    for m in mels:  # separate forwards, synchronized one by one
+        o, _ = ref_enc.forward(m)
+        torch.cuda.synchronize()
+        refs.append(o.clone())
+    enc = _gpu_encoder(spec, q)  # fresh arenas: every shape above grows them
+    s = torch.cuda.Stream()
+    outs = []
+    with torch.cuda.stream(s):
+        for m in mels:
+            o, _ = enc.forward(m)
+            outs.append(o)
+    torch.cuda.synchronize()
+    for o, r in zip(outs, refs):
+        assert torch.equal(o, r)
+
+
 def test_forward_host_matches_device(nq, oracle):
     from nspeech_b200 import synthetic as S
     spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=1, sub_channels=64)
@@ -277,8 +304,8 @@ def test_forwards_on_two_streams_match_one_stream(nq, oracle):
 
 
 # ------------------------------------------------ configs[1] at full size
-CFG1_TOL = 0.08          # row-rms relative error after 24 layers of bf16 activations
-CFG1_MAX_EXCLUDED = 0.5  # near-tie frames (oracle top-2 margin <= 4x max abs error)
+CFG1_TOL = 0.04           # row-rms relative error after 24 layers of bf16 activations (measured 0.020)
+CFG1_MAX_EXCLUDED = 0.25  # near-tie frames (oracle top-2 margin <= 4x max abs error; measured 10%)
 
 
 @pytest.fixture(scope="module")
@@ -295,7 +322,7 @@ def full_model(nq, oracle):
     enc.free()
 
 
-def test_cfg1_full_encoder_matches_oracle(full_model, oracle):
+def test_cfg1_full_encoder_matches_oracle(nq, full_model, oracle):
     """30 s of audio (3000 mel frames, N(0, 1), seed 1) through all
     24 layers, batch 1."""
     spec, enc, ref = full_model
@@ -320,8 +347,14 @@ def test_cfg1_full_encoder_padded_batch(full_model, oracle):
         mel[i, :L] = oracle.normal(50 + i, (L, spec.feat_in))
     out, olens = enc.forward(torch.from_numpy(mel).cuda(), lens)
     out = out.cpu().numpy()
+    excluded = 0
     for i, L in enumerate(lens):
         assert olens[i] == out_frames(L)
         assert not out[i, olens[i]:].any()
-        _compare(oracle, out[i, :olens[i]], ref(mel[i, :L]), f"cfg1 batch seg {i} len {L}", CFG1_TOL,
-                 CFG1_MAX_EXCLUDED)
+        y = ref(mel[i, :L])
+        # short segments have few frames: the near-tie ceiling applies to the batch
+        _compare(oracle, out[i, :olens[i]], y, f"cfg1 batch seg {i} len {L}", CFG1_TOL, 0.4)
+        abs_err = float(np.abs(out[i, :olens[i]] - y).max())
+        srt = np.sort(y, axis=1)
+        excluded += int(((srt[:, -1] - srt[:, -2]) <= 4 * abs_err).sum())
+    assert excluded <= CFG1_MAX_EXCLUDED * sum(olens), (excluded, sum(olens))
