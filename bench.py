@@ -106,6 +106,8 @@ def parse_args():
     ap.add_argument("--unit-tokens", default="0",
                     help="--linear: GEMM unit widths to time each shape with (nq_set_gemm_unit_tokens; 0 = default)")
     ap.add_argument("--qtiled", action="store_true", help="--linear: weights with QTiled semantics (from_qtensor)")
+    ap.add_argument("--tail-split", type=int, default=0,
+                    help="--linear: nq_set_gemm_tail_split mode (0 cost model, 1 off, >= 2 pieces)")
     return ap.parse_args()
 
 
@@ -679,14 +681,17 @@ def run_linear(args) -> None:
     if not jobs:
         raise SystemExit("--linear needs --shape, --cfg1-sweep or --kokoro")
     units = [int(v) for v in args.unit_tokens.split(",")]
+    lib.check(lib.load().nq_set_gemm_tail_split(args.tail_split))
     for (m, k, n), xd, yd in jobs:
         for u in units:
             lib.check(lib.load().nq_set_gemm_unit_tokens(u))
             r = time_linear(m, k, n, xd, yd, iters=args.iters, graph=args.graph, keep_bf16=args.keep_bf16,
                             qtiled=args.qtiled)
             r["unit_tokens"] = u
+            r["tail_split"] = args.tail_split
             print(json.dumps(r), flush=True)
     lib.check(lib.load().nq_set_gemm_unit_tokens(0))
+    lib.check(lib.load().nq_set_gemm_tail_split(0))
 
 
 def run_gemv_sweep(args) -> None:

@@ -341,12 +341,20 @@ int nq_set_wait_limit(int64_t cycles);
 int nq_set_gemm_path(int path);
 
 /* Tokens per 2-SM work unit of the dequantize-once (bf16 tcgen05) GEMM: 64,
- * 128, 256 or 512, or 0 for the default (256).  No counterpart in the
- * reference: a B200 dispatch knob.  Narrower units give calls of a few
- * thousand tokens more units; 512 (two MMAs per k slice on one weight tile)
- * moves fewer bytes from L2 per FLOP, for bf16 activations only (f32
- * activations keep 256).  Process-wide; returns NQ_ERR_ARG for other values. */
+ * 128 or 256, or 0 for the default (256).  No counterpart in the reference: a
+ * B200 dispatch knob.  Narrower units give calls of a few thousand tokens
+ * more units.  Process-wide; returns NQ_ERR_ARG for other values. */
 int nq_set_gemm_unit_tokens(int tokens);
+
+/* Tail split of the dequantize-once GEMM.  No counterpart in the reference: a
+ * B200 dispatch knob.  When a call's 256 x 256 output tiles leave the last
+ * round of SM pairs partly idle, the tiles of that round are cut into k
+ * pieces that run on the idle pairs; the last piece of each tile to finish
+ * adds the pieces in piece order (deterministic) and writes the output, in
+ * the same launch.  0 (default): a cost model decides per call; 1: never;
+ * 2..16: that many pieces whenever a partial round exists (tests).  Results
+ * differ from the unsplit sums only by f32 summation order.  Process-wide. */
+int nq_set_gemm_tail_split(int mode);
 
 /* DEBUG ONLY -- a test hook for failure detection, not part of the matmul
  * API: launches a kernel that waits on an mbarrier nothing arrives on,

@@ -65,6 +65,7 @@ std::mutex g_init_mu;
 long long g_wait_limit = 1LL << 31;
 int g_gemm_path = NQ_GEMM_AUTO;
 int g_gemm_unit_tokens = 0;  // 0: the kernel's default unit width
+int g_tail_split = 0;        // 0: cost model, 1: off, >= 2: that many pieces when a tail exists
 // Token count from which a GEMM call dequantizes the weight once and runs
 // the bf16 tensor-core GEMM (measured crossover on B200).
 constexpr int64_t kDequantMinM = 128;
@@ -74,6 +75,12 @@ constexpr int64_t kDequantMinM = 128;
 constexpr double kNsPerUnitStep = 390.0;
 constexpr double kReduceBytesPerNs = 5000.0;
 constexpr double kReduceLaunchNs = 3000.0;
+// Tail split: each piece stores 128 KB of f32 accumulators per CTA and the last
+// piece reads every piece back (L2-resident), modelled per piece.
+constexpr double kTailFixupNsPerPiece = 700.0;
+// Workspace counters: slot 0 is the GEMV work counter; the tail split's
+// per-(tile, CTA, warp group) counters start here.
+constexpr size_t kTailCounterBase = 64;
 thread_local std::string t_err;
 
 int fail(int code, const char *fmt, ...) {
@@ -380,6 +387,8 @@ struct GemmPlan {
   bool split_x;    // activations staged to bf16 planes first (f32, or unaligned bf16)
   int bt;          // tokens per pair unit
   int grid_m, grid_n, splits, cps, pairs;
+  int full_units = 0, tail_pieces = 1, tail_cps = 0;  // K3 tail split (tail_pieces > 1)
+  int tail_tiles() const { return tail_pieces > 1 ? grid_m * grid_n - full_units : 0; }
   int launches() const { return 1 + (deq && !cached ? 1 : 0) + (splits > 1 ? 1 : 0) + (split_x ? 1 : 0); }
 };
 
@@ -416,7 +425,6 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
   // and one read of the f32 partials and the reduction launch.
   const int ldp = w->n_tiles * nq::kPackRows;
   g.bt = g_gemm_unit_tokens ? g_gemm_unit_tokens : nq::gemm_bf16_block_t();
-  if (g.bt > 256 && splitx) g.bt = 256;  // 512-token units take bf16 activations only
   g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
   const int tiles = g.grid_m * g.grid_n;
   double best = 1e300;
@@ -434,6 +442,33 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
       best = t;
       g.splits = splits;
       g.cps = cps;
+    }
+  }
+  // Tail split (256-token units): the R full rounds run whole tiles, the L
+  // tiles of the last, partial round run as S k pieces on S x L <= pairs
+  // pairs, and the last piece of each tile sums them (no extra launch).
+  const int R = tiles / g.pairs, L = tiles - R * g.pairs;
+  g.full_units = tiles;
+  if (g.bt == 256 && g_tail_split != 1 && L > 0) {
+    const int s_cap = std::min(std::min(g.pairs / L, kc / 2), 16);
+    double best_tail = 1e300;
+    int pick = 1, pick_cps = kc;
+    for (int sp = 2; sp <= s_cap; ++sp) {
+      const int cps = (kc + sp - 1) / sp;
+      if ((kc + cps - 1) / cps != sp) continue;
+      const double t = (static_cast<double>(R) * kc + cps) * kNsPerUnitStep + (sp + 1) * kTailFixupNsPerPiece;
+      if (g_tail_split >= 2 ? sp == g_tail_split : t < best_tail) {
+        best_tail = t;
+        pick = sp;
+        pick_cps = cps;
+      }
+    }
+    if (pick > 1 && (g_tail_split >= 2 || best_tail < best)) {
+      g.splits = 1;
+      g.cps = kc;
+      g.tail_pieces = pick;
+      g.tail_cps = pick_cps;
+      g.full_units = R * g.pairs;
     }
   }
   return g;
@@ -456,15 +491,21 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
   const int splits = plan.splits, cps = plan.cps;
   const int ldp = w->n_tiles * nq::kPackRows;  // rows of partials / of the dequantized weight
 
-  // Workspace: [activation planes][dequantized weight][split-K partials].
+  // Workspace: [activation planes][dequantized weight][split-K partials]
+  // [tail-split pieces].
   size_t xbytes = 0;
   if (!direct) xbytes = align_up(static_cast<size_t>(m) * k_pad * 2, 1024) * (splitx ? 2 : 1);
   const size_t wbytes = deq && !plan.cached ? align_up(static_cast<size_t>(ldp) * k_pad * 2, 1024) : 0;
-  const size_t part_bytes = splits > 1 ? static_cast<size_t>(splits) * m * ldp * sizeof(float) : 0;
+  const size_t part_bytes = splits > 1 ? align_up(static_cast<size_t>(splits) * m * ldp * sizeof(float), 256) : 0;
+  // one piece: 2 CTAs x 16 epilogue warps x (bt / 4) tokens x 32 rows of f32
+  const size_t tail_bytes = static_cast<size_t>(plan.tail_tiles()) * plan.tail_pieces * 2 * 16 * (bt / 4) * 32 * 4;
+  if (kTailCounterBase + static_cast<size_t>(plan.tail_tiles()) * 2 * 16 > kCounterSlots)
+    return fail(NQ_ERR_SHAPE, "tail split needs more counters than the workspace holds");
   Workspace *ws = nullptr;
-  int rc = get_workspace(ctx, stream, xbytes + wbytes + part_bytes, &ws);
+  int rc = get_workspace(ctx, stream, xbytes + wbytes + part_bytes + tail_bytes, &ws);
   if (rc) return rc;
   float *partials = splits > 1 ? reinterpret_cast<float *>(ws->buf + xbytes + wbytes) : nullptr;
+  float *tail_part = tail_bytes ? reinterpret_cast<float *>(ws->buf + xbytes + wbytes + part_bytes) : nullptr;
 
   const void *a_ptr = x;
   int64_t a_k = w->k, a_ld = ldx;
@@ -520,10 +561,16 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     p.grid_n = grid_n;
     p.grid_m = grid_m;
     p.partials = partials;
+    p.full_units = plan.full_units;
+    p.tail_pieces = plan.tail_pieces;
+    p.tail_cps = plan.tail_cps;
+    p.tail_part = tail_part;
+    p.tail_cnt = ws->counters + kTailCounterBase;
     p.ctl.status = ctx->status;
     p.ctl.wait_limit = g_wait_limit;
+    const int work_units = plan.tail_pieces > 1 ? plan.full_units + plan.tail_tiles() * plan.tail_pieces : units;
     ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
-    cudaError_t e = nq::launch_gemm_bf16(splitx, bt, tm_w, tm_a, tm_alo, p, std::min(units, pairs), stream);
+    cudaError_t e = nq::launch_gemm_bf16(splitx, bt, tm_w, tm_a, tm_alo, p, std::min(work_units, pairs), stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
   } else {
     nq::GemmParams p;
@@ -1106,8 +1153,14 @@ int nq_set_gemm_path(int path) {
 
 int nq_set_gemm_unit_tokens(int tokens) {
   if (tokens != 0 && !nq::gemm_bf16_unit_ok(tokens))
-    return fail(NQ_ERR_ARG, "GEMM unit width %d (use 0, 64, 128, 256 or 512)", tokens);
+    return fail(NQ_ERR_ARG, "GEMM unit width %d (use 0, 64, 128 or 256)", tokens);
   g_gemm_unit_tokens = tokens;
+  return NQ_OK;
+}
+
+int nq_set_gemm_tail_split(int mode) {
+  if (mode < 0 || mode > 16) return fail(NQ_ERR_ARG, "tail split mode %d (0 auto, 1 off, 2..16 pieces)", mode);
+  g_tail_split = mode;
   return NQ_OK;
 }
 

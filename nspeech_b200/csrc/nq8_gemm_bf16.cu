@@ -24,6 +24,13 @@
 //               column group; bias + activation (GLU through shared memory
 //               between the value and gate warps of a column group); split-K
 //               partials are raw f32 sums for splitk_reduce.
+// Tail split: when the tiles leave the last round of pairs partly idle, the
+// tiles of that round are cut into k pieces run by different pairs.  A piece
+// stores its raw accumulator (L2-resident scratch) and bumps a counter per
+// (tile, CTA, epilogue warp); the warp that arrives last sums the pieces in
+// piece order and applies the epilogue.  Nothing waits for another CTA, so a
+// grid that is only partly resident (another stream's kernels hold SMs)
+// cannot deadlock, and the sums do not depend on arrival order.
 // Every mbarrier wait is bounded; on give-up the kernel records a status bit,
 // drains, frees TMEM and returns.
 #include "nq8_common.cuh"
@@ -40,27 +47,24 @@ constexpr int kThreads = 32 * (2 + kEpiW);  // 576
 constexpr int kEpi0 = 2;
 constexpr int kAgreeBar = 9;     // named barrier of all epilogue warps (1..8: GLU pairs)
 
-// PT: tokens per pair unit.  Up to 256 a unit is one MMA of N = PT per k
-// slice (PT / 2 token rows per CTA), with two TMEM accumulators so the
-// epilogue of one unit overlaps the next unit's main loop.  PT = 512 issues
-// two N = 256 MMAs per k slice on the same weight tile: 171 instead of 128
-// FLOP per byte moved from L2, with the whole TMEM as one accumulator.  256 is
-// the default; 128 and 64 give small-M calls more units.
+// PT: tokens per pair unit: one MMA of N = PT per k slice (PT / 2 token rows
+// per CTA), with two TMEM accumulators so the epilogue of one unit overlaps
+// the next unit's main loop.  256 is the default; 128 and 64 give small-M
+// calls more units.
 template <bool SPLITX, int PT>
 struct Cfg {
-  static_assert(PT == 64 || PT == 128 || PT == 256 || PT == 512, "unit widths 64, 128, 256, 512");
-  static_assert(!(SPLITX && PT == 512), "512-token units take bf16 activations only");
+  static_assert(PT == 64 || PT == 128 || PT == 256, "unit widths 64, 128, 256");
   static constexpr int kPT = PT;
-  static constexpr int kNB = PT > 256 ? 2 : 1;       // MMAs (token sub-tiles) per k slice
-  static constexpr int kMmaN = PT / kNB;             // N of each MMA
+  static constexpr int kNB = 1;                      // MMAs (token sub-tiles) per k slice
+  static constexpr int kMmaN = PT;                   // N of each MMA
   static constexpr int kSubRows = kMmaN / 2;         // token rows per CTA and sub-tile
-  static constexpr int kAccBufs = PT > 256 ? 1 : 2;  // TMEM accumulator buffers
+  static constexpr int kAccBufs = 2;                 // TMEM accumulator buffers
   static constexpr int kColsPerWarp = PT / 4;        // tokens per epilogue warp (4 column groups)
   static_assert(kColsPerWarp % kEc == 0, "epilogue chunks");
-  static constexpr int kStages = PT == 512 ? 4 : SPLITX ? (PT == 256 ? 4 : 6) : (PT == 256 ? 6 : 8);
+  static constexpr int kStages = SPLITX ? (PT == 256 ? 4 : 6) : (PT == 256 ? 6 : 8);
   static constexpr int kABytes = 128 * kPackK * 2;          // 16 KB of weight rows
   static constexpr int kSubBytes = kSubRows * kPackK * 2;   // one token sub-tile of one plane
-  static constexpr int kBBytes = kNB * kSubBytes;           // 4 / 8 / 16 / 32 KB per activation plane
+  static constexpr int kBBytes = kNB * kSubBytes;           // 4 / 8 / 16 KB per activation plane
   static constexpr int kStageBytes = kABytes + kBBytes * (SPLITX ? 2 : 1);
   static constexpr int kGluOffset = kStages * kStageBytes;
   static constexpr int kGluBytes = 8 * kEc * 32 * 4;    // 8 value/gate warp pairs
@@ -68,23 +72,42 @@ struct Cfg {
   static constexpr int kNumBars = 2 * kStages + 4;
   static constexpr int kSmemBytes = 1024 /*align slack*/ + kBarOffset + kNumBars * 8 + 64;
   static constexpr uint32_t kIdesc = idesc_bf16_f32(kPW, kMmaN);
-  static constexpr int kTmemCols = kAccBufs * PT;  // D0 [0, PT) (, D1 [PT, 2 PT))
+  static constexpr int kTmemCols = kAccBufs * PT;  // D0 [0, PT), D1 [PT, 2 PT)
   static_assert(kStageBytes % 1024 == 0 && kABytes % 1024 == 0 && kSubBytes % 1024 == 0, "swizzle alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
 };
 
 struct Unit {
   int ft, tt, split, kc0, nk;
+  int tail;    // tail tile index (tiles past full_units), or -1
+  int piece;   // k piece of a tail tile
 };
+__device__ __forceinline__ int num_units(const GemmBf16Params &p) {
+  const int tiles = p.grid_n * p.grid_m;
+  return p.tail_pieces > 1 ? p.full_units + (tiles - p.full_units) * p.tail_pieces : tiles * p.splits;
+}
 __device__ __forceinline__ Unit decode_unit(const GemmBf16Params &p, int u) {
   Unit r;
-  const int per_split = p.grid_n * p.grid_m;
-  r.split = u / per_split;
-  const int rem = u - r.split * per_split;
-  r.tt = rem / p.grid_n;
-  r.ft = rem - r.tt * p.grid_n;
-  r.kc0 = r.split * p.cps;
-  r.nk = max(min(r.kc0 + p.cps, p.kc_total) - r.kc0, 0);
+  int tile;
+  r.tail = -1;
+  r.piece = 0;
+  if (p.tail_pieces > 1 && u >= p.full_units) {
+    const int w = u - p.full_units;
+    r.tail = w / p.tail_pieces;
+    r.piece = w - r.tail * p.tail_pieces;
+    tile = p.full_units + r.tail;
+    r.split = 0;
+    r.kc0 = r.piece * p.tail_cps;
+    r.nk = max(min(r.kc0 + p.tail_cps, p.kc_total) - r.kc0, 0);
+  } else {
+    const int per_split = p.grid_n * p.grid_m;
+    r.split = u / per_split;
+    tile = u - r.split * per_split;
+    r.kc0 = r.split * p.cps;
+    r.nk = max(min(r.kc0 + p.cps, p.kc_total) - r.kc0, 0);
+  }
+  r.tt = tile / p.grid_n;
+  r.ft = tile - r.tt * p.grid_n;
   return r;
 }
 
@@ -105,7 +128,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t rank = cluster_ctarank();  // 0: leader (issues the pair MMA), 1: peer
   const int cl = blockIdx.x >> 1;
   const int ncl = gridDim.x >> 1;
-  const int n_units = p.grid_n * p.grid_m * p.splits;
+  const int n_units = num_units(p);
 
   auto stage_w = [&](int s) { return smem + s * C::kStageBytes; };
   auto stage_b = [&](int s) { return smem + s * C::kStageBytes + C::kABytes; };
@@ -284,7 +307,73 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int x = 0; x < kEc; ++x) v[x] = __uint_as_float(r[x]);
       };
-      if (p.splits > 1) {
+      if (un.tail >= 0) {
+        // Tail piece: the raw accumulator goes to scratch and this warp
+        // group's counter is bumped; the group that arrives last sums every
+        // piece in piece order and runs the epilogue.  GLU value and gate
+        // warps count together (the last of the two finishes both halves).
+        const int grp = p.glu ? pr : e;
+        const int expect = (p.glu ? 2 : 1) * p.tail_pieces;
+        auto region = [&](int piece, int warp_e) {
+          return p.tail_part + (((static_cast<size_t>(un.tail) * p.tail_pieces + piece) * 2 + rank) * kEpiW + warp_e) *
+                                   (static_cast<size_t>(kColsPerWarp) * 32);
+        };
+        float *mine = region(un.piece, e);
+        for (int col = 0; col < cols; col += kEc) {
+          float v[kEc];
+          fetch(col, v);
+#pragma unroll
+          for (int x = 0; x < kEc; ++x) __stcg(mine + (col + x) * 32 + lane, v[x]);
+        }
+        __threadfence();
+        __syncwarp();
+        int *cnt = p.tail_cnt + (un.tail * 2 + static_cast<int>(rank)) * kEpiW + grp;
+        int old = 0;
+        if (lane == 0) {
+          old = atomicAdd(cnt, 1);
+          __threadfence();
+        }
+        __syncwarp();
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (old == expect - 1) {
+          if (lane == 0) *cnt = 0;  // every piece has counted: re-arm for the next call
+          auto sum_pieces = [&](int warp_e, int col, float (&v)[kEc]) {
+#pragma unroll
+            for (int x = 0; x < kEc; ++x) v[x] = __ldcg(region(0, warp_e) + (col + x) * 32 + lane);
+            for (int s2 = 1; s2 < p.tail_pieces; ++s2) {
+              const float *r = region(s2, warp_e);
+#pragma unroll
+              for (int x = 0; x < kEc; ++x) v[x] += __ldcg(r + (col + x) * 32 + lane);
+            }
+          };
+          if (!p.glu) {
+            const bool nvalid = n < p.N;
+            const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
+            for (int col = 0; col < cols && nvalid; col += kEc) {
+              float v[kEc];
+              sum_pieces(e, col, v);
+              const int valid = p.M - (m0 + col);
+              store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
+            }
+          } else {
+            const int ev = cg * 4 + (q & 1), eg = ev + 2;  // the pair's value and gate warps
+            const int64_t jcol = static_cast<int64_t>(tile) * 64 + (frow & 63);
+            const bool jvalid = jcol < p.n_out;
+            const float bv = (p.bias && jvalid) ? p.bias[jcol] : 0.f;
+            const float bg = (p.bias && jvalid) ? p.bias[p.n_out + jcol] : 0.f;
+            for (int col = 0; col < cols && jvalid; col += kEc) {
+              float v[kEc], gv[kEc];
+              sum_pieces(ev, col, v);
+              sum_pieces(eg, col, gv);
+#pragma unroll
+              for (int x = 0; x < kEc; ++x) gv[x] += bg;
+              const int valid = p.M - (m0 + col);
+              store_glu_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + jcol, p.ldy, valid, v,
+                            bv, gv);
+            }
+          }
+        }
+      } else if (p.splits > 1) {
         const bool nvalid = n < p.n_rows;
         float *part = p.partials + (static_cast<size_t>(un.split) * p.M + m0) * p.n_rows + n;
         for (int col = 0; col < cols; col += kEc) {
@@ -392,7 +481,7 @@ cudaError_t launch_t(const CUtensorMap &w, const CUtensorMap &a_hi, const CUtens
 
 int gemm_bf16_block_t() { return kPTDefault; }
 int gemm_bf16_block_w() { return kPW; }
-bool gemm_bf16_unit_ok(int tokens) { return tokens == 64 || tokens == 128 || tokens == 256 || tokens == 512; }
+bool gemm_bf16_unit_ok(int tokens) { return tokens == 64 || tokens == 128 || tokens == 256; }
 int gemm_bf16_token_box(int unit_tokens) { return (unit_tokens < 256 ? unit_tokens : 256) / 2; }
 
 cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w, const CUtensorMap &a_hi,
@@ -404,7 +493,6 @@ cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w,
     case 257: return launch_t<true, 128>(w, a_hi, a_lo, p, pairs, stream);
     case 128: return launch_t<false, 64>(w, a_hi, a_lo, p, pairs, stream);
     case 129: return launch_t<true, 64>(w, a_hi, a_lo, p, pairs, stream);
-    case 1024: return launch_t<false, 512>(w, a_hi, a_lo, p, pairs, stream);
     default: return cudaErrorInvalidValue;
   }
 }

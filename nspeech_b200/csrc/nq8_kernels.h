@@ -113,15 +113,25 @@ struct GemmBf16Params {
   int grid_n;       // 256-row weight pair tiles
   int grid_m;       // token tiles of the unit width
   float *partials;  // split-K only: [splits][M][n_rows] f32
+  // Tail split (splits == 1 only): tiles [0, full_units) run whole; each
+  // later tile runs as tail_pieces units of tail_cps k chunks on different
+  // pairs.  A piece stores its raw accumulator to tail_part and counts on
+  // tail_cnt; the last piece to arrive sums all pieces in piece order and
+  // applies the epilogue (so results do not depend on arrival order), then
+  // re-arms the counter.  tail_pieces <= 1: no tail split.
+  int full_units;
+  int tail_pieces;
+  int tail_cps;
+  float *tail_part;  // [tail tiles][pieces][2 CTAs][16 warps][unit tokens / 4][32] f32
+  int *tail_cnt;     // [tail tiles][2 CTAs][16] counters, zero between calls
   DevCtl ctl;
 };
 int gemm_bf16_block_t();              // default tokens per pair unit
 int gemm_bf16_block_w();              // weight rows per pair unit
-bool gemm_bf16_unit_ok(int tokens);   // unit widths the kernel is built for (64, 128, 256, 512)
+bool gemm_bf16_unit_ok(int tokens);   // unit widths the kernel is built for (64, 128, 256)
 int gemm_bf16_token_box(int unit_tokens);  // token rows per TMA box (per CTA and sub-tile)
 // unit_tokens: tokens per pair unit (grid_m in p counts units of that width;
 // the token tensor maps have boxes of gemm_bf16_token_box(unit_tokens) rows).
-// 512 takes bf16 activations only (splitx false).
 cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w, const CUtensorMap &a_hi,
                              const CUtensorMap &a_lo, const GemmBf16Params &p, int pairs, cudaStream_t stream);
 

@@ -111,6 +111,7 @@ SIGNATURES = {
     "nq_launch_counter": (_I, [ctypes.POINTER(_I64), _I]),
     "nq_set_gemm_path": (_I, [_I]),
     "nq_set_gemm_unit_tokens": (_I, [_I]),
+    "nq_set_gemm_tail_split": (_I, [_I]),
     "nq_set_wait_limit": (_I, [_I64]),
     "nq_debug_wait_timeout": (_I, [_P]),
 }

@@ -39,8 +39,13 @@ def test_null_arguments_are_rejected_without_device_work():
     assert lib.nq_set_wait_limit(0) == L.NQ_ERR_ARG
     for bad in (-1, 1, 32, 100, 192, 1024):
         assert lib.nq_set_gemm_unit_tokens(bad) == L.NQ_ERR_ARG, bad
-    for ok in (64, 128, 256, 512, 0):
+    assert lib.nq_set_gemm_unit_tokens(512) == L.NQ_ERR_ARG
+    for ok in (64, 128, 256, 0):
         assert lib.nq_set_gemm_unit_tokens(ok) == L.NQ_OK, ok
+    for bad in (-1, 17):
+        assert lib.nq_set_gemm_tail_split(bad) == L.NQ_ERR_ARG, bad
+    for ok in (1, 2, 16, 0):
+        assert lib.nq_set_gemm_tail_split(ok) == L.NQ_OK, ok
     buf = ctypes.create_string_buffer(8)
     n = lib.nq_last_error(buf, len(buf))
     assert n > 0 and len(buf.value) == min(n, 7)

@@ -153,15 +153,13 @@ def test_kept_bf16_copy_is_identical_and_skips_dequant(nq, oracle):
     assert nq.status() == 0
 
 
-# Units of 64 / 128 / 512 tokens (nq_set_gemm_unit_tokens) in place of 256:
-# MMA N = 64 / 128 with token tiles of 32 / 64 rows per CTA, or two N = 256
-# MMAs per k slice on one weight tile (512; bf16 activations only, f32 keeps
-# 256).
+# Units of 64 / 128 tokens (nq_set_gemm_unit_tokens) in place of 256:
+# MMA N = 64 / 128 with token tiles of 32 / 64 rows per CTA.
 # Partial token tiles (1100, 2100, 300, 129, 375 rows), GLU, f32 activations
 # (hi + lo planes) and a split-K shape (375 x 4096 -> 1024).  Without split K
-# every output is one unit's k-ordered sum, so it must equal the 256-token
-# result bit for bit.
-@pytest.mark.parametrize("unit", [64, 128, 512])
+# (and with the tail split off) every output is one unit's k-ordered sum, so
+# it must equal the 256-token result bit for bit.
+@pytest.mark.parametrize("unit", [64, 128])
 @pytest.mark.parametrize("m,k,n,epi,xdt", [(1100, 1024, 3072, 0, "bf16"), (2100, 1024, 1024, 1, "f32"),
                                            (300, 640, 1920, 3, "bf16"), (129, 96, 130, 0, "bf16"),
                                            (375, 4096, 1024, 0, "bf16")])
@@ -179,6 +177,7 @@ def test_unit_widths_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
     bt = torch.from_numpy(bias).cuda()
     outs = {}
     nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_DEQUANT))
+    nq.check(L.nq_set_gemm_tail_split(1))
     nq.profile_enable(True)
     try:
         for u in (256, unit):
@@ -189,6 +188,7 @@ def test_unit_widths_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
     finally:
         nq.profile_enable(False)
         nq.check(L.nq_set_gemm_unit_tokens(0))
+        nq.check(L.nq_set_gemm_tail_split(0))
         nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_AUTO))
     y, red = outs[unit]
     assert y.shape == (m, n // 2 if glu else n)
@@ -196,3 +196,46 @@ def test_unit_widths_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
     if red == 0 and outs[256][1] == 0:
         assert torch.equal(y, outs[256][0]), f"unit {unit} differs from 256 without split K"
     assert nq.status() == 0
+
+
+# Tail split of the bf16 GEMM (nq_set_gemm_tail_split): the tiles of the last,
+# partial round of SM pairs run as k pieces whose last arrival sums them in
+# piece order.  Shapes with a partial round: 2048 x 4096 -> 1024 (32 tiles, no
+# full round), 1024^3 (16 tiles), 12000 x 1024 -> 4096 (752 tiles: 10 full
+# rounds + 12), a GLU weight with an odd tile count, partial token tiles, and
+# f32 activations.  Checked against the oracle, against the unsplit result
+# (summation order only) and for bit-identical repeats.
+@pytest.mark.parametrize("m,k,n,epi,xdt,pieces", [(2048, 4096, 1024, 0, "bf16", 2), (1024, 1024, 1024, 1, "bf16", 4),
+                                                  (12000, 1024, 4096, 0, "bf16", 6), (300, 640, 1920, 3, "bf16", 5),
+                                                  (2100, 1024, 1024, 2, "f32", 2), (1000, 1024, 1000, 0, "bf16", 3)])
+@pytest.mark.parametrize("keep", [False, True])
+def test_tail_split_matches_oracle_and_unsplit(nq, oracle, m, k, n, epi, xdt, pieces, keep):
+    from nspeech_b200.fast_matmul import QWeight
+    L = nq.load()
+    glu = epi in (3, 4)
+    q = oracle.quantize_q8_0(oracle.normal(370 + n + k, (n, k), 0.0, 0.02))
+    bias = oracle.normal(371, (n,), 0.0, 0.01)
+    w = QWeight.from_q8_0(q, n, k, flags=nq.NQ_PACK_GLU if glu else 0)
+    if keep:
+        w.keep_bf16()
+    x = oracle.normal(372 + m, (m, k))
+    if xdt == "bf16":
+        x = _bf16_round(x)
+    xt = torch.from_numpy(x).cuda().to(torch.float32 if xdt == "f32" else torch.bfloat16)
+    bt = torch.from_numpy(bias).cuda()
+    nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_DEQUANT))
+    try:
+        nq.check(L.nq_set_gemm_tail_split(1))
+        ref = w.linear(xt, bias=bt, epilogue=epi, out_dtype=torch.float32).clone()
+        nq.check(L.nq_set_gemm_tail_split(pieces))
+        a = w.linear(xt, bias=bt, epilogue=epi, out_dtype=torch.float32).clone()
+        b = w.linear(xt, bias=bt, epilogue=epi, out_dtype=torch.float32).clone()
+    finally:
+        nq.check(L.nq_set_gemm_tail_split(0))
+        nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_AUTO))
+    torch.cuda.synchronize()
+    assert nq.status() == 0
+    assert torch.equal(a, b), "tail split is not reproducible"
+    tag = f"tail {pieces} {m}x{k}x{n} epi={epi} {xdt} keep={keep}"
+    _check(oracle, a.cpu().numpy(), _ref(oracle, x, q, n, bias, epi), tag)
+    assert oracle.max_rel_err(a.cpu().numpy(), ref.cpu().numpy().astype(np.float64), 1.0) < 1e-4, tag
