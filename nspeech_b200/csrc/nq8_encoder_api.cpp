@@ -590,8 +590,8 @@ int nq_encoder_forward_host(nq_encoder *enc, const float *mel_host, const int32_
   const size_t in_bytes = static_cast<size_t>(batch) * t_mel * enc->cfg.feat_in * sizeof(float);
   const size_t out_bytes = static_cast<size_t>(batch) * nq_encoder_out_frames(t_mel) * enc->cfg.d_model * sizeof(float);
   Arena &A = *arena_for(enc, st);
-  NQ_TRY(A.mel_in.ensure(in_bytes));
-  NQ_TRY(A.out_buf.ensure(out_bytes));
+  NQ_TRY(A.mel_in.ensure(in_bytes, st));
+  NQ_TRY(A.out_buf.ensure(out_bytes, st));
   NQ_CUDA(cudaMemcpyAsync(A.mel_in.p, mel_host, in_bytes, cudaMemcpyHostToDevice, st));
   NQ_TRY(forward(enc, A.mel_in.as<float>(), lengths, batch, t_mel, A.out_buf.as<float>(), out_lengths, st));
   NQ_CUDA(cudaMemcpyAsync(out_host, A.out_buf.p, out_bytes, cudaMemcpyDeviceToHost, st));

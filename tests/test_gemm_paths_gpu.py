@@ -96,21 +96,27 @@ def test_paths_ragged(nq, oracle, path, m, n, k):
 
 
 def test_paths_split_k_deterministic(nq, oracle, path):
-    """Shapes with few output tiles split K; the reduction sums splits in order."""
+    """Shapes with few output tiles split K; the reduction sums splits in order.
+    (The tail split, which would take these shapes in the bf16 GEMM, is off.)"""
     from nspeech_b200.fast_matmul import QWeight
-    for (m, k, n) in [(40, 4096, 1024), (375, 4096, 1024), (300, 4096, 256)]:
-        q = oracle.quantize_q8_0(oracle.normal(330 + m, (n, k), 0.0, 0.02))
-        w = QWeight.from_q8_0(q, n, k)
-        x = torch.from_numpy(oracle.normal(331, (m, k))).cuda()
-        nq.profile_enable(True)
-        nq.profile_read(nq.NQ_KCLASS_REDUCE, True)
-        a = w.linear(x).clone()
-        b = w.linear(x).clone()
-        red = nq.profile_read(nq.NQ_KCLASS_REDUCE, True)
+    nq.check(nq.load().nq_set_gemm_tail_split(1))
+    try:
+        for (m, k, n) in [(40, 4096, 1024), (375, 4096, 1024), (300, 4096, 256)]:
+            q = oracle.quantize_q8_0(oracle.normal(330 + m, (n, k), 0.0, 0.02))
+            w = QWeight.from_q8_0(q, n, k)
+            x = torch.from_numpy(oracle.normal(331, (m, k))).cuda()
+            nq.profile_enable(True)
+            nq.profile_read(nq.NQ_KCLASS_REDUCE, True)
+            a = w.linear(x).clone()
+            b = w.linear(x).clone()
+            red = nq.profile_read(nq.NQ_KCLASS_REDUCE, True)
+            nq.profile_enable(False)
+            assert red["launches"] == 2, (m, k, n, red)
+            assert torch.equal(a, b)
+            _check(oracle, a.cpu().numpy(), _ref(oracle, x.cpu().numpy(), q, n), f"{path} split {m}x{k}x{n}")
+    finally:
         nq.profile_enable(False)
-        assert red["launches"] == 2, (m, k, n, red)
-        assert torch.equal(a, b)
-        _check(oracle, a.cpu().numpy(), _ref(oracle, x.cpu().numpy(), q, n), f"{path} split {m}x{k}x{n}")
+        nq.check(nq.load().nq_set_gemm_tail_split(0))
 
 
 def test_auto_path_selection(nq, oracle):
