@@ -190,13 +190,23 @@ def workload_config(args, world: int, plan, spec) -> dict:
     }
 
 
-def make_encoder(spec, seed=1):
+def make_encoder(spec, seed=1, timings=None):
+    """The GPU encoder with seeded random weights; `timings` (dict) receives the
+    wall seconds of generating the f32 tensors, staging them (the library
+    quantizes them to Q8_0 with ggml's rule) and nq_encoder_finalize (repack,
+    upload, kept bf16 copies)."""
     from nspeech_b200 import synthetic as S
     from nspeech_b200.encoder import ParakeetEncoder
+    t0 = time.perf_counter()
     enc = ParakeetEncoder(spec, device=int(os.environ.get("LOCAL_RANK", 0)))
     tensors = S.encoder_tensors(spec, seed)
+    t1 = time.perf_counter()
     enc.load_tensors(tensors)
+    t2 = time.perf_counter()
     enc.finalize()
+    t3 = time.perf_counter()
+    if timings is not None:
+        timings.update({"generate_s": t1 - t0, "stage_and_quantize_s": t2 - t1, "finalize_s": t3 - t2})
     return enc, tensors
 
 
@@ -424,7 +434,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
         import torch.distributed as dist
     torch.cuda.set_device(local_rank)
     spec = S.EncoderSpec(n_layers=args.layers)
-    enc, tensors = make_encoder(spec)
+    load_t = {}
+    enc, tensors = make_encoder(spec, timings=load_t)
     plan, rank_seed = plan_buckets(rank, world, args.segments, args.max_batch, args.shard)
     if not plan:
         raise SystemExit(f"rank {rank}: no buckets (--shard lpt needs at least one bucket per rank)")
@@ -585,6 +596,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             "gpu_launches": launches_timed,
             "gpu_launches_expected": launches_per_step * args.steps,
             "cfg2_single_30s": {"ms": cfg2_ms, "rtfx": 30.0 / (cfg2_ms / 1e3)},
+            "load": dict(load_t, note="per process, before the timed region; excluded from value"),
         }
         print(json.dumps(line), flush=True)
 

@@ -76,8 +76,10 @@ constexpr double kNsPerUnitStep = 390.0;
 constexpr double kReduceBytesPerNs = 5000.0;
 constexpr double kReduceLaunchNs = 3000.0;
 // Tail split: each piece stores 128 KB of f32 accumulators per CTA and the last
-// piece reads every piece back (L2-resident), modelled per piece.
-constexpr double kTailFixupNsPerPiece = 700.0;
+// piece reads every piece back from L2 (about 130 GB/s per SM), modelled per
+// piece; measured on B200 from 1024^3 (no split 10.5 us, 4 pieces 15.3 us)
+// and 2048 x 4096 -> 1024 (28.2 us, 2 pieces 22.8 us).
+constexpr double kTailFixupNsPerPiece = 2200.0;
 // Workspace counters: slot 0 is the GEMV work counter; the tail split's
 // per-(tile, CTA, warp group) counters start here.
 constexpr size_t kTailCounterBase = 64;

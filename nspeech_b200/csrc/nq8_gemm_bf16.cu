@@ -356,7 +356,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
             }
           } else {
-            const int ev = cg * 4 + (q & 1), eg = ev + 2;  // the pair's value and gate warps
+            // epilogue warp index of lane quarter qq in this column group
+            // (warp w reads quarter w & 3; e = w - kEpi0)
+            auto quarter_warp = [&](int qq) { return cg * 4 + ((qq - kEpi0) & 3); };
+            const int ev = quarter_warp(q & 1), eg = quarter_warp((q & 1) + 2);  // value and gate warps
             const int64_t jcol = static_cast<int64_t>(tile) * 64 + (frow & 63);
             const bool jvalid = jcol < p.n_out;
             const float bv = (p.bias && jvalid) ? p.bias[jcol] : 0.f;

@@ -211,8 +211,11 @@ def test_unit_widths_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
 # rounds + 12), a GLU weight with an odd tile count, partial token tiles, and
 # f32 activations.  Checked against the oracle, against the unsplit result
 # (summation order only) and for bit-identical repeats.
+# Every case has pieces x (tiles of the partial round) <= 74 SM pairs, so the
+# forced split runs (checked: the sums differ from the unsplit ones).
 @pytest.mark.parametrize("m,k,n,epi,xdt,pieces", [(2048, 4096, 1024, 0, "bf16", 2), (1024, 1024, 1024, 1, "bf16", 4),
-                                                  (12000, 1024, 4096, 0, "bf16", 6), (300, 640, 1920, 3, "bf16", 5),
+                                                  (12000, 1024, 4096, 0, "bf16", 6), (300, 640, 1920, 3, "bf16", 4),
+                                                  (100, 1024, 2048, 3, "bf16", 8), (200, 640, 5120, 4, "f32", 3),
                                                   (2100, 1024, 1024, 2, "f32", 2), (1000, 1024, 1000, 0, "bf16", 3)])
 @pytest.mark.parametrize("keep", [False, True])
 def test_tail_split_matches_oracle_and_unsplit(nq, oracle, m, k, n, epi, xdt, pieces, keep):
@@ -242,6 +245,7 @@ def test_tail_split_matches_oracle_and_unsplit(nq, oracle, m, k, n, epi, xdt, pi
     torch.cuda.synchronize()
     assert nq.status() == 0
     assert torch.equal(a, b), "tail split is not reproducible"
+    assert not torch.equal(a, ref), "the forced tail split did not run"
     tag = f"tail {pieces} {m}x{k}x{n} epi={epi} {xdt} keep={keep}"
     _check(oracle, a.cpu().numpy(), _ref(oracle, x, q, n, bias, epi), tag)
     assert oracle.max_rel_err(a.cpu().numpy(), ref.cpu().numpy().astype(np.float64), 1.0) < 1e-4, tag
