@@ -391,11 +391,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if (!p.glu) {
         const bool nvalid = n < p.N;
         const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
+        // bf16 rows whose 32 features of this warp all exist: paired 4-byte stores
+        const bool paired = p.y_dtype == 1 && (p.ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 3) == 0 &&
+                            static_cast<int64_t>(tile) * kPackRows + 32 * q + 32 <= p.N;
         for (int col = 0; col < cols; col += kEc) {
           float v[kEc];
           fetch(col, v);
-          if (!nvalid) continue;
           const int valid = p.M - (m0 + col);
+          if (paired && valid >= kEc) {
+            store_pair_act(p.epi, static_cast<__nv_bfloat16 *>(p.y) + static_cast<int64_t>(m0 + col) * p.ldy + (n & ~1LL),
+                           p.ldy, lane, v, bn);
+            continue;
+          }
+          if (!nvalid) continue;
           store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
         }
       } else {

@@ -164,6 +164,40 @@ __device__ __forceinline__ void store_act(int epi, int y_dtype, void *y, int64_t
     default: store_col<__nv_bfloat16, kEpiRelu>(yb, ldy, valid, v, b); break;
   }
 }
+// bf16 output of kEc tokens from a warp whose lanes hold 32 consecutive
+// output features (lane parity = feature parity, all 32 valid, all kEc tokens
+// valid).  Lanes pair up through one shuffle per token pair so that every
+// store writes two adjacent features (4 bytes): the even lane stores tokens
+// [0, kEc/2), the odd lane tokens [kEc/2, kEc).  `pair_base` is the element
+// offset of token 0 and the pair's even feature.  Half the store
+// instructions of store_col, the same values.
+template <int EPI>
+__device__ __forceinline__ void store_pair_bf16(__nv_bfloat16 *pair_base, int64_t ldy, int lane, const float (&v)[kEc],
+                                                float b) {
+  float a[kEc];
+#pragma unroll
+  for (int e = 0; e < kEc; ++e) a[e] = act_t<EPI>(v[e] + b);
+  const bool odd = lane & 1;
+#pragma unroll
+  for (int x = 0; x < kEc / 2; ++x) {
+    const float send = odd ? a[x] : a[kEc / 2 + x];
+    const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+    const float lo = odd ? recv : a[x];
+    const float hi = odd ? a[kEc / 2 + x] : recv;
+    const int tok = odd ? kEc / 2 + x : x;
+    *reinterpret_cast<__nv_bfloat162 *>(pair_base + tok * ldy) = __floats2bfloat162_rn(lo, hi);
+  }
+}
+__device__ __forceinline__ void store_pair_act(int epi, __nv_bfloat16 *pair_base, int64_t ldy, int lane,
+                                               const float (&v)[kEc], float b) {
+  switch (epi) {
+    case kEpiSilu: store_pair_bf16<kEpiSilu>(pair_base, ldy, lane, v, b); break;
+    case kEpiGeluErf: store_pair_bf16<kEpiGeluErf>(pair_base, ldy, lane, v, b); break;
+    case kEpiRelu: store_pair_bf16<kEpiRelu>(pair_base, ldy, lane, v, b); break;
+    default: store_pair_bf16<kEpiNone>(pair_base, ldy, lane, v, b); break;
+  }
+}
+
 __device__ __forceinline__ void store_glu_act(int epi, int y_dtype, void *y, int64_t off, int64_t ldy, int valid,
                                               const float (&v)[kEc], float b, const float (&g)[kEc]) {
   float *yf = static_cast<float *>(y) + off;
