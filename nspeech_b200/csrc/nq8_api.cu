@@ -568,6 +568,7 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     p.tail_cps = plan.tail_cps;
     p.tail_part = tail_part;
     p.tail_cnt = ws->counters + kTailCounterBase;
+    p.w_static = plan.cached ? 1 : 0;
     p.ctl.status = ctx->status;
     p.ctl.wait_limit = g_wait_limit;
     const int work_units = plan.tail_pieces > 1 ? plan.full_units + plan.tail_tiles() * plan.tail_pieces : units;

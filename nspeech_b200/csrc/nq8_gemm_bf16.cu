@@ -165,6 +165,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   cluster_sync_all();  // both CTAs' barriers exist before anyone signals across the pair
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // A weight that no preceding kernel writes (a kept bf16 copy) streams its
+  // first ring stages before the dependency wait, during the previous
+  // kernel's tail; the token halves of those stages follow after the wait.
+  int pre = 0;
+  if (warp == 0 && lane == 0 && p.w_static) {
+    prefetch_tmap(&tm_w);
+    for (int u = cl; u < n_units && pre < kStages; u += ncl) {
+      const Unit un = decode_unit(p, u);
+      const int wrow0 = un.ft * kPW + static_cast<int>(rank) * 128;
+      for (int i = 0; i < un.nk && pre < kStages; ++i, ++pre) {
+        if (rank == 0) mbar_arrive_expect_tx(full(pre), 2 * C::kStageBytes);
+        tma_load_2d_pair(smem_u32(stage_w(pre)), &tm_w, map_rank(full(pre), 0), (un.kc0 + i) * kPackK, wrow0);
+      }
+    }
+  }
   pdl_wait();  // barriers and TMEM are set up; now wait for the predecessor's data
   pdl_trigger();
 
@@ -191,12 +206,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * C::kStageBytes);
           const uint32_t bar = map_rank(full(s), 0);
           const int kx = (un.kc0 + i) * kPackK;
           // Weight rows past the matrix (odd tile count) and token rows past M
           // are zero-filled by the TMA unit.
-          tma_load_2d_pair(smem_u32(stage_w(s)), &tm_w, bar, kx, wrow0);
+          if (g >= pre) {  // else its expect_tx and weight load were issued before the wait
+            if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * C::kStageBytes);
+            tma_load_2d_pair(smem_u32(stage_w(s)), &tm_w, bar, kx, wrow0);
+          }
 #pragma unroll
           for (int t = 0; t < kNB; ++t) {  // token sub-tile t: unit tokens [t kMmaN, (t + 1) kMmaN)
             tma_load_2d_pair(smem_u32(stage_b(s)) + t * C::kSubBytes, &tm_a, bar, kx, trow0 + t * kMmaN);
@@ -206,10 +223,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // Drain: every copy into this CTA's shared memory has landed (the
-      // leader's full barrier, or the commit of the MMA that read it).
+      // leader's full barrier, or the commit of the MMA that read it).  Stages
+      // whose weight half went out before the dependency wait count too.
       volatile int no_abort = 0;
-      for (int s = 0; s < kStages && s < g; ++s) {
-        const int last = s + kStages * ((g - 1 - s) / kStages);
+      const int issued = g > pre ? g : pre;
+      for (int s = 0; s < kStages && s < issued; ++s) {
+        const int last = s + kStages * ((issued - 1 - s) / kStages);
         const bool done = rank == 0 ? mbar_wait(full(s), (last / kStages) & 1, p.ctl.wait_limit, &no_abort)
                                     : mbar_wait(empty(s), (last / kStages) & 1, p.ctl.wait_limit, &no_abort);
         if (!done) atomicOr(p.ctl.status, kDevTimeoutDrain);

@@ -124,6 +124,7 @@ struct GemmBf16Params {
   int tail_cps;
   float *tail_part;  // [tail tiles][pieces][2 CTAs][16 warps][unit tokens / 4][32] f32
   int *tail_cnt;     // [tail tiles][2 CTAs][16] counters, zero between calls
+  int w_static;      // the weight is not written by any kernel of this stream (kept bf16 copy)
   DevCtl ctl;
 };
 int gemm_bf16_block_t();              // default tokens per pair unit
