@@ -103,13 +103,15 @@ const char *nq_version(void);
  * (src/moonshine/gpu_encoder.rs:33-35). */
 int nq_weight_from_q8_0(const void *blocks, int64_t n, int64_t k, int flags, nq_weight **out);
 
-/* Upload a dequantized f32 [n, k] weight.  It is re-quantized to Q8_0 with
- * ggml semantics, which is lossless for tensors that came from Q8_0 (the only
- * way the reference calls it: new_mm, src/moonshine/encoder.rs:29-39).
- * A tensor that does not round-trip exactly (any f32 weight not dequantized
- * from Q8_0, NaN, infinities) is rejected with NQ_ERR_DTYPE: the reference's
- * MatMul::from_tensor would keep it at bf16 precision, which a Q8_0 store
- * cannot, so the call fails instead of silently losing precision.
+/* Upload an f32 [n, k] weight.  A tensor dequantized from Q8_0 (the way the
+ * reference calls it: new_mm, src/moonshine/encoder.rs:29-39) re-quantizes
+ * losslessly and is stored as Q8_0.  Any other finite tensor is kept at bf16
+ * precision (round to nearest even), as the reference's PackedMatrixBf16
+ * packing does: a bf16-only weight, which every nq_linear call runs on the
+ * bf16 tensor-core GEMM (M <= 16 included) and which has no Q8_0 form
+ * (nq_weight_to_q8_0, nq_weights_fuse, nq_gemv_noalloc, nq_gemv_resadd_ln
+ * and NQ_MODE_QTILED reject it).  Either way y = x . bf16(W)^T with f32
+ * accumulation.  NaN or infinite elements fail with NQ_ERR_DTYPE.
  * Replaces MatMul::from_tensor (src/fast_matmul.rs:191-208). */
 int nq_weight_from_f32(const float *w, int64_t n, int64_t k, int flags, nq_weight **out);
 

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -33,6 +34,10 @@ struct nq_weight {
   // order (nq_weight_keep_bf16): the dequantize-once GEMM reads it instead of
   // dequantizing per call.
   __nv_bfloat16 *bf16 = nullptr;
+  // bf16-only weight (no Q8_0 tiles, dev == nullptr): an f32 tensor that is not
+  // a Q8_0 dequantization kept at bf16 precision (MatMul::from_tensor's
+  // packing), or a transposed conv weight.  Every call runs the bf16 GEMM.
+  bool bf16_only = false;
 };
 
 namespace {
@@ -161,6 +166,34 @@ int upload_packed(const uint8_t *blocks, int64_t n, int64_t k, int flags, nq_wei
   if (e != cudaSuccess) {
     cudaFree(w->dev);
     return cuda_fail(e, "cudaMemcpy(weight)");
+  }
+  *out = w.release();
+  return NQ_OK;
+}
+
+// A bf16-only weight from f32 values [n, k] (rounded to bf16, packed row order).
+int upload_bf16_only(const float *wf, int64_t n, int64_t k, int flags, nq_weight **out) {
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  int rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  std::unique_ptr<nq_weight> w(new nq_weight);
+  w->device = dev;
+  w->n = n;
+  w->k = k;
+  w->flags = flags;
+  w->n_tiles = nq::pack_n_tiles(n, flags);
+  w->kc = nq::pack_k_chunks(k);
+  w->bf16_only = true;
+  const size_t elems = static_cast<size_t>(w->n_tiles) * nq::kPackRows * w->kc * nq::kPackK;
+  std::vector<uint16_t> host(elems);
+  nq::pack_bf16_rows(wf, n, k, flags, host.data());
+  cudaError_t e = cudaMalloc(&w->bf16, elems * 2);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(bf16 weight)");
+  e = cudaMemcpy(w->bf16, host.data(), elems * 2, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(w->bf16);
+    return cuda_fail(e, "cudaMemcpy(bf16 weight)");
   }
   *out = w.release();
   return NQ_OK;
@@ -403,7 +436,7 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
   // A weight with a kept bf16 copy needs no dequantize pass: K3 on the copy
   // is the faster path down to small M as well (M = 125, 1024 -> 4096:
   // 10.0 vs 14.9 us for the fused kernel).
-  g.deq = g_gemm_path == NQ_GEMM_DEQUANT ||
+  g.deq = w->bf16_only || g_gemm_path == NQ_GEMM_DEQUANT ||
           (g_gemm_path == NQ_GEMM_AUTO && (m >= kDequantMinM || w->bf16 != nullptr));
   g.cached = g.deq && w->bf16 != nullptr;
   g.split_x = !direct;
@@ -682,7 +715,9 @@ int linear_impl(const LinearArgs *args, int nprob, const void *x, int x_dtype, i
     if (((args[i].w->flags & NQ_MODE_QTILED) != 0) != qtiled)
       return fail(NQ_ERR_ARG, "weights sharing one call must all be NQ_MODE_QTILED or none");
   if (qtiled) return run_qtiled(ctx, args, nprob, x, x_dtype, m, ldx, epilogue, y_dtype, s);
-  if (m <= 16) return run_gemv(ctx, args, nprob, x, x_dtype, m, ldx, epilogue, y_dtype, s);
+  bool any_bf16_only = false;
+  for (int i = 0; i < nprob; ++i) any_bf16_only = any_bf16_only || args[i].w->bf16_only;
+  if (m <= 16 && !any_bf16_only) return run_gemv(ctx, args, nprob, x, x_dtype, m, ldx, epilogue, y_dtype, s);
   for (int i = 0; i < nprob; ++i) {
     rc = run_gemm(ctx, args[i], x, x_dtype, m, ldx, epilogue, y_dtype, s);
     if (rc) return rc;
@@ -729,7 +764,7 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 int linear_launches(const nq_weight *w, int64_t m, int x_dtype, bool aligned) {
   if (!w || m <= 0) return 0;
   if (w->flags & NQ_MODE_QTILED) return 2;  // quantize x + the int8 GEMM
-  if (m <= 16)  // GEMV + gemv_reduce (for up to three weights), after split_x unless x is read in place
+  if (m <= 16 && !w->bf16_only)  // GEMV + gemv_reduce (for up to three weights), after split_x unless x is read in place
     return x_dtype == NQ_BF16 && aligned && w->k % nq::kPackK == 0 ? 2 : 3;
   DeviceCtx *ctx = nullptr;
   int dev = 0;
@@ -785,12 +820,18 @@ int nq_weight_from_f32(const float *wf, int64_t n, int64_t k, int flags, nq_weig
   std::vector<uint8_t> blocks(static_cast<size_t>(n) * (k / 32) * 34);
   nq::quantize_q8_0(wf, n, k, blocks.data());
   const int64_t bad = nq::q8_0_first_mismatch(wf, blocks.data(), n * k);
-  if (bad >= 0)
+  if (bad < 0) return upload_packed(blocks.data(), n, k, flags, out);
+  // Not a Q8_0 dequantization: keep it at bf16 precision, as the reference's
+  // PackedMatrixBf16 does.  QTiled semantics need Q8_0 blocks.
+  if (flags & NQ_MODE_QTILED)
     return fail(NQ_ERR_DTYPE,
-                "nq_weight_from_f32: element [%lld, %lld] = %g does not survive Q8_0 re-quantization; only "
-                "tensors dequantized from Q8_0 can be uploaded as f32 (the weights are stored as Q8_0)",
-                (long long)(bad / k), (long long)(bad % k), static_cast<double>(wf[bad]));
-  return upload_packed(blocks.data(), n, k, flags, out);
+                "nq_weight_from_f32: element [%lld, %lld] = %g is not a Q8_0 value; NQ_MODE_QTILED needs Q8_0 "
+                "weights", (long long)(bad / k), (long long)(bad % k), static_cast<double>(wf[bad]));
+  for (int64_t i = 0; i < n * k; ++i)
+    if (!std::isfinite(wf[i]))
+      return fail(NQ_ERR_DTYPE, "nq_weight_from_f32: element [%lld, %lld] is not finite", (long long)(i / k),
+                  (long long)(i % k));
+  return upload_bf16_only(wf, n, k, flags, out);
 }
 
 int nq_weight_from_gguf(const char *path, const char *tensor_name, int flags, nq_weight **out) {
@@ -830,6 +871,7 @@ int nq_gguf_tensor_info(const char *path, const char *tensor_name, int *ggml_typ
 
 int nq_weight_to_q8_0(const nq_weight *w, void *blocks_out) {
   if (!w || !blocks_out) return fail(NQ_ERR_ARG, "null argument");
+  if (w->bf16_only) return fail(NQ_ERR_UNSUPPORTED, "a bf16-only weight has no Q8_0 blocks");
   std::vector<uint8_t> host(w->bytes);
   cudaError_t e = cudaMemcpy(host.data(), w->dev, w->bytes, cudaMemcpyDeviceToHost);
   if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(weight readback)");
@@ -843,6 +885,7 @@ int nq_weights_fuse(const nq_weight *const *ws, int count, int flags, nq_weight 
   for (int i = 0; i < count; ++i) {
     if (!ws[i]) return fail(NQ_ERR_ARG, "null weight %d", i);
     if (ws[i]->flags & NQ_PACK_GLU) return fail(NQ_ERR_UNSUPPORTED, "cannot fuse GLU-packed weights");
+    if (ws[i]->bf16_only) return fail(NQ_ERR_UNSUPPORTED, "cannot fuse bf16-only weights");
     if (k < 0) k = ws[i]->k;
     if (ws[i]->k != k) return fail(NQ_ERR_SHAPE, "fused weights must share K");
     n_total += ws[i]->n;
@@ -875,6 +918,7 @@ int nq_weight_keep_bf16(nq_weight *w, int keep) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if (cur != w->device) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, cur);
   if (!keep) {
+    if (w->bf16_only) return fail(NQ_ERR_UNSUPPORTED, "the bf16 copy is a bf16-only weight's only copy");
     if (w->bf16) {
       e = cudaDeviceSynchronize();  // no launch in flight may still read it
       if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize(drop bf16 copy)");
@@ -907,7 +951,7 @@ void nq_weight_free(nq_weight *w) {
   cudaGetDevice(&cur);
   if (cur != w->device) cudaSetDevice(w->device);
   if (w->bf16) cudaFree(w->bf16);
-  cudaFree(w->dev);
+  if (w->dev) cudaFree(w->dev);
   if (cur != w->device) cudaSetDevice(cur);
   delete w;
 }
@@ -924,6 +968,7 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   if (rc) return rc;
   if (m > 16) return fail(NQ_ERR_SHAPE, "nq_gemv_noalloc serves M <= 16 rows (got %lld)", (long long)m);
   if (w->flags & NQ_MODE_QTILED) return fail(NQ_ERR_UNSUPPORTED, "nq_gemv_noalloc: NQ_MODE_QTILED weight");
+  if (w->bf16_only) return fail(NQ_ERR_UNSUPPORTED, "nq_gemv_noalloc: bf16-only weight");
   if (m == 0) return NQ_OK;
   DeviceCtx *ctx = nullptr;
   int dev = 0;
@@ -1016,6 +1061,7 @@ int nq_gemv_resadd_ln(const nq_weight *w, const void *x, int x_dtype, int64_t m,
   if (m > 16) return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln serves M <= 16 rows (got %lld)", (long long)m);
   if (w->flags & NQ_PACK_GLU) return fail(NQ_ERR_ARG, "nq_gemv_resadd_ln: GLU-packed weight");
   if (w->flags & NQ_MODE_QTILED) return fail(NQ_ERR_UNSUPPORTED, "nq_gemv_resadd_ln: NQ_MODE_QTILED weight");
+  if (w->bf16_only) return fail(NQ_ERR_UNSUPPORTED, "nq_gemv_resadd_ln: bf16-only weight");
   if (w->n > nq::kGemvLnMaxN)
     return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln: N = %lld exceeds %d", (long long)w->n, nq::kGemvLnMaxN);
   if (ld_res < w->n) return fail(NQ_ERR_SHAPE, "nq_gemv_resadd_ln: ld_res < N");

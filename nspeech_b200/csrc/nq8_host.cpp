@@ -57,6 +57,25 @@ void pack_q8_0(const uint8_t *blocks, int64_t n, int64_t k, int flags, uint8_t *
     }
 }
 
+static uint16_t f32_to_bf16(float f) {
+  uint32_t x;
+  std::memcpy(&x, &f, 4);
+  if ((x & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((x >> 16) | 0x40u);
+  x += 0x7fffu + ((x >> 16) & 1u);
+  return static_cast<uint16_t>(x >> 16);
+}
+
+void pack_bf16_rows(const float *w, int64_t n, int64_t k, int flags, uint16_t *out) {
+  const int tiles = pack_n_tiles(n, flags);
+  const int64_t k_pad = static_cast<int64_t>(pack_k_chunks(k)) * kPackK;
+  for (int t = 0; t < tiles; ++t)
+    for (int r = 0; r < kPackRows; ++r) {
+      uint16_t *dst = out + (static_cast<int64_t>(t) * kPackRows + r) * k_pad;
+      const int64_t sr = src_row(n, flags, t, r);
+      for (int64_t c = 0; c < k_pad; ++c) dst[c] = (sr >= 0 && c < k) ? f32_to_bf16(w[sr * k + c]) : 0;
+    }
+}
+
 void unpack_q8_0(const uint8_t *packed, int64_t n, int64_t k, int flags, uint8_t *blocks) {
   const int tiles = pack_n_tiles(n, flags);
   const int kc = pack_k_chunks(k);

@@ -29,6 +29,9 @@ int pack_k_chunks(int64_t k);
 // GGUF Q8_0 blocks [n][k/32] x 34 B  <->  tiles [n_tiles][kc] x 8704 B.
 void pack_q8_0(const uint8_t *blocks, int64_t n, int64_t k, int flags, uint8_t *out);
 void unpack_q8_0(const uint8_t *packed, int64_t n, int64_t k, int flags, uint8_t *blocks);
+// f32 [n][k] -> bf16 (round to nearest even) rows in packed row order,
+// [n_tiles * 128][kc * 64], zero past n and k: the layout of a kept bf16 copy.
+void pack_bf16_rows(const float *w, int64_t n, int64_t k, int flags, uint16_t *out);
 // f32 [n][k] -> GGUF Q8_0 blocks (ggml quantize_row_q8_0_ref semantics).
 void quantize_q8_0(const float *w, int64_t n, int64_t k, uint8_t *blocks);
 // First element of w[0, count) whose Q8_0 block does not dequantize back to

@@ -12,8 +12,8 @@ arithmetic is kept:
   semantics (:71-125, dispatch :212);
 * ``MatMul.from_tensor`` (fast_matmul.rs:191-208) receives the dequantized f32
   weight (``new_mm``, src/moonshine/encoder.rs:29-39) and re-quantizes it to
-  Q8_0, which is lossless for Q8_0-derived tensors (anything else is rejected
-  with NQ_ERR_DTYPE rather than stored at lower precision); ``forward``
+  Q8_0, which is lossless for Q8_0-derived tensors; any other tensor is kept
+  at bf16 precision (a bf16-only weight), like PackedMatrixBf16; ``forward``
   computes ``y = x . bf16(W)^T`` with f32 accumulation, FbgemmBf16Op's
   semantics (:138-167);
 * ``MatMul.forward`` (fast_matmul.rs:210-226, checks of :138-167) flattens the

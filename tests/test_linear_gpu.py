@@ -297,22 +297,48 @@ def test_qtiled_mode_rejections(nq, oracle):
     assert rc == nq.NQ_ERR_ARG  # one call mixes the two semantics
 
 
-def test_from_f32_rejects_non_q8_tensor(nq, oracle):
-    """MatMul::from_tensor on an f32 tensor that is not a Q8_0 dequantization:
-    the Q8_0 store cannot keep it, so the upload fails (NQ_ERR_DTYPE) instead
-    of silently re-quantizing."""
+def test_from_f32_keeps_bf16_for_non_q8_tensor(nq, oracle):
+    """MatMul::from_tensor on an f32 tensor that is not a Q8_0 dequantization
+    keeps it at bf16 precision, as the reference's PackedMatrixBf16 packing
+    does (src/fast_matmul.rs:191-208): y = x . bf16(W)^T with f32 accumulation
+    at every M (such a weight has no Q8_0 tiles; the bf16 GEMM serves all M).
+    A Q8_0-derived tensor is still stored as Q8_0 (lossless)."""
     from nspeech_b200 import lib
     from nspeech_b200.fast_matmul import MatMul, QWeight
-    w = oracle.normal(85, (64, 128), 0.0, 0.02)
+    n, k = 300, 640
+    w = oracle.normal(85, (n, k), 0.0, 0.02)
+    qw = QWeight.from_f32(w)
+    wb = _bf16_round(w).astype(np.float64)
+    bias = oracle.normal(86, (n,), 0.0, 0.01)
+    for m in (1, 5, 16, 17, 200):
+        x = oracle.normal(87 + m, (m, k))
+        got = _run(qw, x, bias=bias, epi=1)
+        ref = oracle.epilogue(x.astype(np.float64) @ wb.T, bias, 1)
+        assert _check(oracle, got, ref, f"bf16-only m={m}") <= EXPECT_TOL
+        gotb = _run(qw, _bf16_round(x), torch.bfloat16)
+        refb = _bf16_round(x).astype(np.float64) @ wb.T
+        assert _check(oracle, gotb, refb, f"bf16-only bf16 x m={m}") <= EXPECT_TOL
     with pytest.raises(lib.NqError) as e:
-        QWeight.from_f32(w)
-    assert e.value.code == nq.NQ_ERR_DTYPE and "re-quantization" in str(e.value)
-    deq = oracle.dequant_q8_0(oracle.quantize_q8_0(w), 64, 128)
-    assert np.array_equal(QWeight.from_f32(deq).to_q8_0(), oracle.quantize_q8_0(w))
-    bad = deq.copy()
+        qw.to_q8_0()
+    assert e.value.code == nq.NQ_ERR_UNSUPPORTED
+    with pytest.raises(lib.NqError) as e:
+        qw.keep_bf16(False)
+    assert e.value.code == nq.NQ_ERR_UNSUPPORTED
+    with pytest.raises(lib.NqError) as e:
+        QWeight.from_f32(w, flags=nq.NQ_MODE_QTILED)
+    assert e.value.code == nq.NQ_ERR_DTYPE
+    bad = w.copy()
     bad[7, 9] = np.nan
-    with pytest.raises(lib.NqError):
+    with pytest.raises(lib.NqError) as e:
         MatMul.from_tensor(bad)
+    assert e.value.code == nq.NQ_ERR_DTYPE
+    deq = oracle.dequant_q8_0(oracle.quantize_q8_0(w), n, k)
+    assert np.array_equal(QWeight.from_f32(deq).to_q8_0(), oracle.quantize_q8_0(w))
+    # the MatMul mirror keeps the reference's f32 contract on such a weight
+    mm = MatMul.from_tensor(w)
+    x = oracle.normal(90, (2, 3, k))
+    y = mm.forward(torch.from_numpy(x).cuda()).cpu().numpy().reshape(6, n)
+    assert _check(oracle, y, x.reshape(6, k).astype(np.float64) @ wb.T, "MatMul bf16-only") <= EXPECT_TOL
 
 
 def test_weight_roundtrip_and_fuse(nq, oracle):
