@@ -107,7 +107,7 @@ def parse_args():
                     help="--linear: GEMM unit widths to time each shape with (nq_set_gemm_unit_tokens; 0 = default)")
     ap.add_argument("--qtiled", action="store_true", help="--linear: weights with QTiled semantics (from_qtensor)")
     ap.add_argument("--tail-split", type=int, default=0,
-                    help="--linear: nq_set_gemm_tail_split mode (0 cost model, 1 off, >= 2 pieces)")
+                    help="nq_set_gemm_tail_split mode of the GEMMs (0 cost model, 1 off, >= 2 pieces)")
     return ap.parse_args()
 
 
@@ -433,6 +433,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     if world > 1:
         import torch.distributed as dist
     torch.cuda.set_device(local_rank)
+    lib.init(local_rank)
+    lib.check(lib.load().nq_set_gemm_tail_split(args.tail_split))
     spec = S.EncoderSpec(n_layers=args.layers)
     load_t = {}
     enc, tensors = make_encoder(spec, timings=load_t)

@@ -214,6 +214,53 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
                     const float *bias, int epilogue, void *y, int y_dtype, int64_t ldy,
                     void *stream);
 
+/* ---- Kokoro conv1d / conv_transpose1d (configs 4) -------------------------
+ * One sequence, NCW layouts as the reference's decoder: x is [c_in][ldx]
+ * (channel rows of >= t_in elements), y is [c_out][ldy].  x_leaky is the
+ * slope of a leaky ReLU applied to x on load (1.0 = none), the fused
+ * leaky_relu + conv variants of the reference (conv1d_lrelu001,
+ * conv_transpose1d_lrelu).  bias (f32 [c_out], nullable) and epilogue
+ * (NONE, SILU, GELU_ERF, RELU) apply to the output. */
+
+/* Output frames of a conv1d: (t_in + 2 padding - dilation (kernel - 1) - 1) /
+ * stride + 1, or a negative NQ_ERR_* code. */
+int64_t nq_conv1d_out_len(int64_t t_in, int kernel, int stride, int padding, int dilation);
+
+/* y[co][t] = act(bias[co] + sum over ci, j of W[co, ci * kernel + j] *
+ * leaky(x[ci][t * stride - padding + j * dilation])), zero padding.  `w` is
+ * the conv weight in its GGUF 2-D form [c_out, c_in * kernel] (n = c_out,
+ * k = c_in * kernel): a Q8_0 weight, or a bf16-only one from
+ * nq_weight_from_f32 when c_in * kernel is not a multiple of 32.  Lowered as
+ * im2col -> nq_linear (tensor cores) -> transpose to NCW, the reference's GPU
+ * lowering (im2col + matmul_bias).  Scratch: a per-stream conv workspace
+ * (grows with cudaMalloc on first use of a size).  Replaces
+ * KokoroGpuBackend::conv1d / conv1d_k / conv1d_lrelu001 / im2col +
+ * matmul_bias (src/kokoro/gpu_backend.rs:59-110; kernels conv1d_k and
+ * im2col_conv1d, kernels/kokoro_kernels.py:182,426). */
+int nq_conv1d(const nq_weight *w, const void *x, int x_dtype, int64_t c_in, int64_t t_in, int64_t ldx, int kernel,
+              int stride, int padding, int dilation, float x_leaky, const float *bias, int epilogue, void *y,
+              int y_dtype, int64_t ldy, void *stream);
+
+/* Output frames of a conv_transpose1d: (t_in - 1) stride - 2 padding + kernel
+ * + output_padding, or a negative NQ_ERR_* code. */
+int64_t nq_conv_transpose1d_out_len(int64_t t_in, int kernel, int stride, int padding, int output_padding);
+
+/* The weight of a conv_transpose1d from its (dequantized) values in the
+ * reference's layout [c_in][c_out][kernel] (ConvTranspose1d, groups 1),
+ * stored transposed as a bf16-only weight [c_out * kernel, c_in] (values
+ * rounded to bf16, the fast_matmul packing). */
+int nq_conv_transpose1d_weight(const float *w, int64_t c_in, int64_t c_out, int kernel, nq_weight **out);
+
+/* y[co][t] = act(bias[co] + sum over ci, j with t = ti * stride - padding + j
+ * of W[ci][co][j] * leaky(x[ci][ti])): one GEMM to the columns
+ * [t_in][c_out * kernel] (f32), then an overlap-add that sums each output's
+ * taps in ascending j (deterministic).  Replaces
+ * KokoroGpuBackend::conv_transpose1d / conv_transpose1d_lrelu
+ * (src/kokoro/gpu_backend.rs:72-81; decoder.rs generator.ups). */
+int nq_conv_transpose1d(const nq_weight *w, const void *x, int x_dtype, int64_t c_in, int64_t t_in, int64_t ldx,
+                        int kernel, int stride, int padding, int output_padding, float x_leaky, const float *bias,
+                        int epilogue, void *y, int y_dtype, int64_t ldy, void *stream);
+
 /* ---- FastConformer encoder (the caller of the Q8_0 path for configs 2/5) ---
  * Mirrors FastConformerConfig (src/parakeet/fast_conformer.rs:31-45) and
  * FastConformerEncoder::forward (:1072-1104, blocks :967-999): dw-striding

@@ -63,6 +63,9 @@ struct DeviceCtx {
   EncodeTiledFn encode = nullptr;
   std::mutex mu;
   std::map<cudaStream_t, Workspace> ws;
+  // Scratch of the conv entry points (im2col rows, GEMM outputs), separate from
+  // `ws` so that the GEMM's own workspace growth cannot free it mid-call.
+  std::map<cudaStream_t, Workspace> conv_ws;
 };
 
 DeviceCtx g_ctx[kMaxDevices];
@@ -116,10 +119,10 @@ int current_ctx(DeviceCtx **out, int *dev_out) {
 }
 
 // Grow-only workspace for `stream`; counters are zeroed once at allocation
-// and re-armed by the kernels.
-int get_workspace(DeviceCtx *ctx, cudaStream_t stream, size_t bytes, Workspace **out) {
+// and re-armed by the kernels.  `conv` selects the conv entry points' scratch.
+int get_workspace(DeviceCtx *ctx, cudaStream_t stream, size_t bytes, Workspace **out, bool conv = false) {
   std::lock_guard<std::mutex> lk(ctx->mu);
-  Workspace &w = ctx->ws[stream];
+  Workspace &w = (conv ? ctx->conv_ws : ctx->ws)[stream];
   if (!w.counters) {
     cudaError_t e = cudaMalloc(&w.counters, kCounterSlots * sizeof(int));
     if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(workspace counters)");
@@ -815,6 +818,16 @@ int nq_weight_from_q8_0(const void *blocks, int64_t n, int64_t k, int flags, nq_
 
 int nq_weight_from_f32(const float *wf, int64_t n, int64_t k, int flags, nq_weight **out) {
   if (!wf || !out) return fail(NQ_ERR_ARG, "null argument");
+  if (k > 0 && k % 32 != 0 && !(flags & NQ_MODE_QTILED)) {
+    // no Q8_0 form (blocks of 32 along K): a bf16-only weight
+    int rc = check_weight_shape(n, (k + 31) / 32 * 32, flags);
+    if (rc) return rc;
+    for (int64_t i = 0; i < n * k; ++i)
+      if (!std::isfinite(wf[i]))
+        return fail(NQ_ERR_DTYPE, "nq_weight_from_f32: element [%lld, %lld] is not finite", (long long)(i / k),
+                    (long long)(i % k));
+    return upload_bf16_only(wf, n, k, flags, out);
+  }
   int rc = check_weight_shape(n, k, flags);
   if (rc) return rc;
   std::vector<uint8_t> blocks(static_cast<size_t>(n) * (k / 32) * 34);
@@ -960,6 +973,128 @@ int nq_linear(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t
               void *y, int y_dtype, int64_t ldy, void *stream) {
   LinearArgs a{w, bias, y, ldy};
   return linear_impl(&a, 1, x, x_dtype, m, ldx, epilogue, y_dtype, stream);
+}
+
+int64_t nq_conv1d_out_len(int64_t t_in, int kernel, int stride, int padding, int dilation) {
+  if (t_in < 1 || kernel < 1 || stride < 1 || padding < 0 || dilation < 1) return NQ_ERR_ARG;
+  const int64_t span = static_cast<int64_t>(dilation) * (kernel - 1) + 1;
+  if (t_in + 2 * padding < span) return NQ_ERR_SHAPE;
+  return (t_in + 2 * padding - span) / stride + 1;
+}
+
+int64_t nq_conv_transpose1d_out_len(int64_t t_in, int kernel, int stride, int padding, int output_padding) {
+  if (t_in < 1 || kernel < 1 || stride < 1 || padding < 0 || output_padding < 0) return NQ_ERR_ARG;
+  const int64_t t = (t_in - 1) * stride - 2 * padding + kernel + output_padding;
+  return t < 1 ? NQ_ERR_SHAPE : t;
+}
+
+int nq_conv1d(const nq_weight *w, const void *x, int x_dtype, int64_t c_in, int64_t t_in, int64_t ldx, int kernel,
+              int stride, int padding, int dilation, float x_leaky, const float *bias, int epilogue, void *y,
+              int y_dtype, int64_t ldy, void *stream) {
+  if (!w || !x || !y) return fail(NQ_ERR_ARG, "null argument");
+  if (x_dtype != NQ_F32 && x_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "x dtype %d unsupported", x_dtype);
+  if (y_dtype != NQ_F32 && y_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "y dtype %d unsupported", y_dtype);
+  if (w->flags & NQ_PACK_GLU) return fail(NQ_ERR_UNSUPPORTED, "nq_conv1d: GLU-packed weight");
+  if (epilogue == NQ_EPI_GLU_SIGMOID || epilogue == NQ_EPI_GLU_SILU)
+    return fail(NQ_ERR_UNSUPPORTED, "nq_conv1d: GLU epilogue");
+  if (c_in < 1 || kernel < 1 || w->k != c_in * kernel)
+    return fail(NQ_ERR_SHAPE, "nq_conv1d: weight K = %lld is not c_in (%lld) x kernel (%d)", (long long)w->k,
+                (long long)c_in, kernel);
+  if (ldx < t_in) return fail(NQ_ERR_SHAPE, "nq_conv1d: ldx < t_in");
+  const int64_t t_out = nq_conv1d_out_len(t_in, kernel, stride, padding, dilation);
+  if (t_out < 0) return fail(static_cast<int>(t_out), "nq_conv1d: no output frames (t_in %lld)", (long long)t_in);
+  if (ldy < t_out) return fail(NQ_ERR_SHAPE, "nq_conv1d: ldy < output length %lld", (long long)t_out);
+  if (t_out > (1 << 30) || c_in * t_in > (1LL << 40)) return fail(NQ_ERR_SHAPE, "nq_conv1d: too large");
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  int rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  if (w->device != dev) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // im2col rows in x's precision (f32 rows go through the GEMM's hi/lo path),
+  // the GEMM's token-major output in y's.
+  const int64_t k_pad = static_cast<int64_t>(w->kc) * nq::kPackK;
+  const size_t esz = x_dtype == NQ_F32 ? 4 : 2, ysz = y_dtype == NQ_F32 ? 4 : 2;
+  const size_t rows_bytes = align_up(static_cast<size_t>(t_out) * k_pad * esz, 256);
+  const size_t out_bytes = align_up(static_cast<size_t>(t_out) * w->n * ysz, 256);
+  Workspace *ws = nullptr;
+  rc = get_workspace(ctx, s, rows_bytes + out_bytes, &ws, true);
+  if (rc) return rc;
+  void *rows = ws->buf;
+  void *ytmp = ws->buf + rows_bytes;
+  cudaError_t e = nq::launch_im2col(x, x_dtype, ldx, static_cast<int>(c_in), static_cast<int>(t_in), kernel, stride,
+                                    padding, dilation, x_leaky, static_cast<int>(t_out), k_pad, x_dtype, rows, s);
+  if (e != cudaSuccess) return cuda_fail(e, "im2col launch");
+  LinearArgs a{w, bias, ytmp, w->n};
+  rc = linear_impl(&a, 1, rows, x_dtype, t_out, k_pad, epilogue, y_dtype, stream);
+  if (rc) return rc;
+  e = nq::launch_transpose_out(ytmp, y_dtype, w->n, static_cast<int>(t_out), static_cast<int>(w->n), y, y_dtype, ldy,
+                               s);
+  if (e != cudaSuccess) return cuda_fail(e, "conv output transpose launch");
+  return NQ_OK;
+}
+
+int nq_conv_transpose1d_weight(const float *w, int64_t c_in, int64_t c_out, int kernel, nq_weight **out) {
+  if (!w || !out) return fail(NQ_ERR_ARG, "null argument");
+  if (c_in < 1 || c_out < 1 || kernel < 1) return fail(NQ_ERR_SHAPE, "nq_conv_transpose1d_weight: bad shape");
+  // [c_in][c_out][K] -> rows (co, j) of c_in: the GEMM weight [c_out * K, c_in]
+  const int64_t n = c_out * kernel;
+  std::vector<float> t(static_cast<size_t>(n) * c_in);
+  for (int64_t ci = 0; ci < c_in; ++ci)
+    for (int64_t r = 0; r < n; ++r) {
+      const float v = w[ci * n + r];
+      if (!std::isfinite(v)) return fail(NQ_ERR_DTYPE, "nq_conv_transpose1d_weight: non-finite element");
+      t[r * c_in + ci] = v;
+    }
+  int rc = check_weight_shape(n, (c_in + 31) / 32 * 32, 0);
+  if (rc) return rc;
+  return upload_bf16_only(t.data(), n, c_in, 0, out);
+}
+
+int nq_conv_transpose1d(const nq_weight *w, const void *x, int x_dtype, int64_t c_in, int64_t t_in, int64_t ldx,
+                        int kernel, int stride, int padding, int output_padding, float x_leaky, const float *bias,
+                        int epilogue, void *y, int y_dtype, int64_t ldy, void *stream) {
+  if (!w || !x || !y) return fail(NQ_ERR_ARG, "null argument");
+  if (x_dtype != NQ_F32 && x_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "x dtype %d unsupported", x_dtype);
+  if (y_dtype != NQ_F32 && y_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "y dtype %d unsupported", y_dtype);
+  if (epilogue < NQ_EPI_NONE || epilogue > NQ_EPI_RELU || epilogue == NQ_EPI_GLU_SIGMOID ||
+      epilogue == NQ_EPI_GLU_SILU)
+    return fail(NQ_ERR_UNSUPPORTED, "nq_conv_transpose1d: epilogue %d", epilogue);
+  if (kernel < 1 || w->k != c_in || w->n % kernel != 0 || (w->flags & NQ_PACK_GLU))
+    return fail(NQ_ERR_SHAPE, "nq_conv_transpose1d: weight [%lld, %lld] is not [c_out * %d, c_in %lld]",
+                (long long)w->n, (long long)w->k, kernel, (long long)c_in);
+  if (ldx < t_in) return fail(NQ_ERR_SHAPE, "nq_conv_transpose1d: ldx < t_in");
+  const int64_t t_out = nq_conv_transpose1d_out_len(t_in, kernel, stride, padding, output_padding);
+  if (t_out < 0) return fail(static_cast<int>(t_out), "nq_conv_transpose1d: no output frames");
+  if (ldy < t_out) return fail(NQ_ERR_SHAPE, "nq_conv_transpose1d: ldy < output length %lld", (long long)t_out);
+  if (t_out > (1 << 30) || c_in * t_in > (1LL << 40)) return fail(NQ_ERR_SHAPE, "nq_conv_transpose1d: too large");
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  int rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  if (w->device != dev) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t c_out = w->n / kernel;
+  const int64_t k_pad = static_cast<int64_t>(w->kc) * nq::kPackK;
+  const size_t esz = x_dtype == NQ_F32 ? 4 : 2;
+  const size_t rows_bytes = align_up(static_cast<size_t>(t_in) * k_pad * esz, 256);
+  const size_t cols_bytes = align_up(static_cast<size_t>(t_in) * w->n * 4, 256);
+  Workspace *ws = nullptr;
+  rc = get_workspace(ctx, s, rows_bytes + cols_bytes, &ws, true);
+  if (rc) return rc;
+  void *rows = ws->buf;
+  float *cols = reinterpret_cast<float *>(ws->buf + rows_bytes);
+  // token-major input rows: the im2col of a 1-tap, stride-1 conv
+  cudaError_t e = nq::launch_im2col(x, x_dtype, ldx, static_cast<int>(c_in), static_cast<int>(t_in), 1, 1, 0, 1,
+                                    x_leaky, static_cast<int>(t_in), k_pad, x_dtype, rows, s);
+  if (e != cudaSuccess) return cuda_fail(e, "conv_transpose input transpose launch");
+  LinearArgs a{w, nullptr, cols, w->n};
+  rc = linear_impl(&a, 1, rows, x_dtype, t_in, k_pad, NQ_EPI_NONE, NQ_F32, stream);
+  if (rc) return rc;
+  e = nq::launch_col2im(cols, w->n, static_cast<int>(t_in), static_cast<int>(c_out), kernel, stride, padding,
+                        static_cast<int>(t_out), bias, epilogue, y, y_dtype, ldy, s);
+  if (e != cudaSuccess) return cuda_fail(e, "col2im launch");
+  return NQ_OK;
 }
 
 int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, int64_t ldx, const float *bias,

@@ -186,6 +186,18 @@ cudaError_t launch_qtiled_quantize(const void *x, int x_dtype, int64_t ldx, int6
                                    float *dx, cudaStream_t stream);
 cudaError_t launch_qtiled(const QtiledParams &p, cudaStream_t stream);
 
+// conv1d / conv_transpose1d glue (nq8_conv.cu).
+// rows[t][e] = leaky(x[e / K][t * stride - pad + (e % K) * dil]) for e < c_in * K,
+// zero up to ld; x NCW with row stride ldx; a_dtype 0 f32, 1 bf16.
+cudaError_t launch_im2col(const void *x, int x_dtype, int64_t ldx, int c_in, int t_in, int K, int stride, int pad,
+                          int dil, float slope, int t_out, int64_t ld, int a_dtype, void *rows, cudaStream_t s);
+// y[c][t] = src[t][c] (NCW output from token-major rows).
+cudaError_t launch_transpose_out(const void *src, int src_dtype, int64_t lds, int rows_t, int cols_c, void *y,
+                                 int y_dtype, int64_t ldy, cudaStream_t s);
+// conv_transpose1d overlap-add of GEMM columns cols[t_in][c_out * K] (f32).
+cudaError_t launch_col2im(const float *cols, int64_t ldc, int t_in, int c_out, int K, int stride, int pad, int t_out,
+                          const float *bias, int epi, void *y, int y_dtype, int64_t ldy, cudaStream_t s);
+
 cudaError_t launch_wait_timeout_probe(DevCtl ctl, cudaStream_t stream);
 
 }  // namespace nq

@@ -106,6 +106,12 @@ SIGNATURES = {
     "nq_last_error": (_I, [ctypes.c_char_p, _I]),
     "nq_status": (_I, [_P, ctypes.POINTER(_I)]),
     "nq_gemv_noalloc": (_I, [_P, _P, _I, _I64, _I64, _P, _I, _P, _I, _I64, _P]),
+    "nq_conv1d_out_len": (_I64, [_I64, _I, _I, _I, _I]),
+    "nq_conv1d": (_I, [_P, _P, _I, _I64, _I64, _I64, _I, _I, _I, _I, ctypes.c_float, _P, _I, _P, _I, _I64, _P]),
+    "nq_conv_transpose1d_out_len": (_I64, [_I64, _I, _I, _I, _I]),
+    "nq_conv_transpose1d_weight": (_I, [_P, _I64, _I64, _I, ctypes.POINTER(_P)]),
+    "nq_conv_transpose1d": (_I, [_P, _P, _I, _I64, _I64, _I64, _I, _I, _I, _I, ctypes.c_float, _P, _I, _P, _I, _I64,
+                                 _P]),
     "nq_gemv_resadd_ln": (_I, [_P, _P, _I, _I64, _I64, _P, _P, _P, _I64, _P, _P, ctypes.c_float, _P, _I, _I64, _P]),
     "nq_weight_keep_bf16": (_I, [_P, _I]),
     "nq_launch_counter": (_I, [ctypes.POINTER(_I64), _I]),

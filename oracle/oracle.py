@@ -389,3 +389,50 @@ def _encoder_structs(cfg: dict, tensors: dict):
                     lin=q(sp + "linear.weight"), layers=layers)
     keep.append(layers)
     return keep, c, W
+
+
+# ------------------------------------------------------------ Kokoro convs
+def _leaky(x: np.ndarray, slope: float) -> np.ndarray:
+    return np.where(x >= 0, x, x * slope)
+
+
+def conv1d_ref(x, w, bias=None, stride: int = 1, padding: int = 0, dilation: int = 1, x_leaky: float = 1.0):
+    """Conv1d of one NCW sequence in float64 (candle Tensor::conv1d as the
+    Kokoro decoder calls it, src/kokoro/decoder.rs:154-773; the Triton conv1d_k
+    / im2col_conv1d of kernels/kokoro_kernels.py:182,426):
+    y[co, t] = bias[co] + sum_{ci, j} w[co, ci, j] * leaky(x)[ci, t*stride - padding + j*dilation],
+    zero padding.  x [C_in, T_in], w [C_out, C_in, K] -> [C_out, T_out]."""
+    x = _leaky(np.asarray(x, np.float64), x_leaky)
+    w = np.asarray(w, np.float64)
+    c_in, t_in = x.shape
+    c_out, _, k = w.shape
+    t_out = (t_in + 2 * padding - dilation * (k - 1) - 1) // stride + 1
+    xp = np.zeros((c_in, t_in + 2 * padding + stride), np.float64)
+    xp[:, padding:padding + t_in] = x
+    cols = np.stack([xp[:, j * dilation: j * dilation + (t_out - 1) * stride + 1: stride] for j in range(k)], axis=1)
+    y = np.einsum("oik,ikt->ot", w, cols)
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)[:, None]
+    return y
+
+
+def conv_transpose1d_ref(x, w, bias=None, stride: int = 1, padding: int = 0, output_padding: int = 0,
+                         x_leaky: float = 1.0):
+    """ConvTranspose1d (groups 1) of one NCW sequence in float64 (candle
+    Tensor::conv_transpose1d, the generator upsampling of src/kokoro/
+    decoder.rs:432-470,752): every input frame ti adds w[ci, co, :] * x[ci, ti]
+    at output frames ti*stride - padding + j.  x [C_in, T_in], w [C_in, C_out, K]
+    -> [C_out, (T_in - 1)*stride - 2*padding + K + output_padding]."""
+    x = _leaky(np.asarray(x, np.float64), x_leaky)
+    w = np.asarray(w, np.float64)
+    c_in, t_in = x.shape
+    _, c_out, k = w.shape
+    t_out = (t_in - 1) * stride - 2 * padding + k + output_padding
+    full = np.zeros((c_out, (t_in - 1) * stride + k + output_padding), np.float64)
+    contrib = np.einsum("it,iok->tok", x, w)  # [T_in, C_out, K]
+    for ti in range(t_in):
+        full[:, ti * stride: ti * stride + k] += contrib[ti]
+    y = full[:, padding: padding + t_out]
+    if bias is not None:
+        y = y + np.asarray(bias, np.float64)[:, None]
+    return y

@@ -113,3 +113,34 @@ def test_packed_cpu_kernels_bit_identical(oracle, m, n, k):
         oracle.force_isa(isa)
     exact = oracle.matmul_exact(x, q, n)
     assert oracle.max_rel_err(oracle.matmul_fbgemm_packed(x, q, n, bf16=False), exact, 1.0) < 1e-5
+
+
+@pytest.mark.parametrize("cin,cout,k,stride,pad,dil,leaky", [(128, 128, 3, 1, 1, 1, 1.0), (64, 64, 11, 1, 25, 5, 0.1),
+                                                            (128, 22, 7, 1, 3, 1, 0.01), (1, 1, 3, 2, 1, 1, 1.0),
+                                                            (512, 64, 1, 1, 0, 1, 1.0)])
+def test_conv1d_oracle_matches_torch(oracle, cin, cout, k, stride, pad, dil, leaky):
+    """The Kokoro conv1d restatement against torch.nn.functional.conv1d (f64)."""
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(cin + k)
+    x = rng.standard_normal((cin, 97))
+    w = rng.standard_normal((cout, cin, k)) * 0.1
+    b = rng.standard_normal(cout)
+    y = oracle.conv1d_ref(x, w, b, stride, pad, dil, leaky)
+    xt = torch.from_numpy(np.where(x >= 0, x, x * leaky))[None]
+    ref = torch.nn.functional.conv1d(xt, torch.from_numpy(w), torch.from_numpy(b), stride, pad, dil)[0].numpy()
+    assert y.shape == ref.shape
+    np.testing.assert_allclose(y, ref, rtol=1e-12, atol=1e-12)
+
+
+@pytest.mark.parametrize("cin,cout,k,stride,pad,opad", [(512, 256, 20, 10, 5, 0), (256, 128, 12, 6, 3, 0),
+                                                         (64, 64, 3, 2, 1, 1)])
+def test_conv_transpose1d_oracle_matches_torch(oracle, cin, cout, k, stride, pad, opad):
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(cin + k)
+    x = rng.standard_normal((cin, 23))
+    w = rng.standard_normal((cin, cout, k)) * 0.1
+    b = rng.standard_normal(cout)
+    y = oracle.conv_transpose1d_ref(x, w, b, stride, pad, opad, 0.1)
+    xt = torch.from_numpy(np.where(x >= 0, x, x * 0.1))[None]
+    ref = torch.nn.functional.conv_transpose1d(xt, torch.from_numpy(w), torch.from_numpy(b), stride, pad, opad)[0]
+    np.testing.assert_allclose(y, ref.numpy(), rtol=1e-12, atol=1e-12)
