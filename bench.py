@@ -106,6 +106,9 @@ def parse_args():
     ap.add_argument("--unit-tokens", default="0",
                     help="--linear: GEMM unit widths to time each shape with (nq_set_gemm_unit_tokens; 0 = default)")
     ap.add_argument("--qtiled", action="store_true", help="--linear: weights with QTiled semantics (from_qtensor)")
+    ap.add_argument("--conv", action="store_true",
+                    help="time the Kokoro generator's conv1d / conv_transpose1d shapes (nq_conv*) instead")
+    ap.add_argument("--conv-frames", type=int, default=300, help="--conv: decoder frames (80 Hz) of the utterance")
     ap.add_argument("--tail-split", type=int, default=0,
                     help="nq_set_gemm_tail_split mode of the GEMMs (0 cost model, 1 off, >= 2 pieces)")
     return ap.parse_args()
@@ -708,6 +711,81 @@ def run_linear(args) -> None:
     lib.check(lib.load().nq_set_gemm_tail_split(0))
 
 
+# configs[3] Kokoro ISTFTNet generator convolutions for an utterance of F
+# decoder frames (upsample rates 10 and 6; src/kokoro/decoder.rs generator):
+# (name, kind, c_in, c_out, K, stride, padding, dilation, T_in as a multiple of F)
+KOKORO_CONVS = [
+    ("ups.0", "t", 512, 256, 20, 10, 5, 1, 1),
+    ("resblock 256 k3 d1", "c", 256, 256, 3, 1, 1, 1, 10),
+    ("resblock 256 k7 d3", "c", 256, 256, 7, 1, 9, 3, 10),
+    ("resblock 256 k11 d5", "c", 256, 256, 11, 1, 25, 5, 10),
+    ("ups.1", "t", 256, 128, 12, 6, 3, 1, 10),
+    ("resblock 128 k3 d1", "c", 128, 128, 3, 1, 1, 1, 60),
+    ("resblock 128 k11 d5", "c", 128, 128, 11, 1, 25, 5, 60),
+    ("conv_post", "c", 128, 22, 7, 1, 3, 1, 60),
+]
+
+
+def run_conv_sweep(args) -> None:
+    """Device time per nq_conv1d / nq_conv_transpose1d call (CUDA graph of
+    back-to-back calls, bf16 NCW input and output, seeded weights: Q8_0 for
+    conv1d, the [C_in, C_out, K] values for conv_transpose1d), with the
+    convolution's FLOPs (2 * C_out * C_in * K * T_out, conv_transpose:
+    2 * C_in * C_out * K * T_in) against the measured bf16 peak."""
+    import torch
+    from nspeech_b200 import conv as C, lib
+    from nspeech_b200.fast_matmul import QWeight
+    torch.cuda.set_device(0)
+    lib.init(0)
+    pk = peaks()
+    rng = np.random.default_rng(0)
+    rows = []
+    for name, kind, cin, cout, k, stride, pad, dil, tmul in KOKORO_CONVS:
+        t_in = args.conv_frames * tmul
+        x = torch.randn(cin, t_in, device="cuda").to(torch.bfloat16)
+        if kind == "c":
+            if (cin * k) % 32 == 0:  # random Q8_0 blocks of the GGUF form [C_out, C_in * K]
+                w = _linear_weights(cout, cin * k, 1, rng, keep_bf16=True)[0]
+            else:  # left in f32 by the quantizer: kept at bf16 precision
+                w = QWeight.from_f32((rng.standard_normal((cout, cin * k)) * 0.05).astype(np.float32))
+            t_out = C.conv1d_out_len(t_in, k, stride, pad, dil)
+            flops = 2.0 * cout * cin * k * t_out
+            call = lambda: C.conv1d(x, w, None, k, stride, pad, dil, out=y)  # noqa: E731
+        else:
+            w = C.ConvTransposeWeight.from_f32((rng.standard_normal((cin, cout, k)) * 0.05).astype(np.float32))
+            t_out = C.conv_transpose1d_out_len(t_in, k, stride, pad)
+            flops = 2.0 * cin * cout * k * t_in
+            call = lambda: C.conv_transpose1d(x, w, None, stride, pad, out=y)  # noqa: E731
+        y = torch.empty(cout, t_out, device="cuda", dtype=torch.bfloat16)
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            call()  # scratch sized before capture
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        iters = 10
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(iters):
+                call()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (5 * iters)
+        rows.append({"conv": name, "c_in": cin, "c_out": cout, "k": k, "stride": stride, "t_in": t_in,
+                     "t_out": t_out, "us": round(us, 2), "tflops": round(flops / us / 1e6, 1),
+                     "frac_bf16_peak": round(flops / us / 1e6 / pk["bf16_tflops"], 3)})
+        del g
+    if lib.status() != 0:
+        raise RuntimeError("device status bits set after the conv sweep")
+    print(json.dumps({"metric": "Kokoro generator conv1d / conv_transpose1d (nq_conv*), bf16 NCW",
+                      "frames": args.conv_frames, "peak_bf16_tflops": pk["bf16_tflops"],
+                      "peak_source": pk.get("source", "measured"), "convs": rows}), flush=True)
+
+
 def run_gemv_sweep(args) -> None:
     """Graph-timed Q8_0 GEMV per shape (synthetic Q8_0 weights, bf16 x and y)."""
     import torch
@@ -856,6 +934,9 @@ def main():
         return
     if args.linear:
         run_linear(args)
+        return
+    if args.conv:
+        run_conv_sweep(args)
         return
     if world > 1:
         import torch
