@@ -9,10 +9,30 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <thread>
+#include <vector>
 
 namespace nq {
+
+// Run fn(lo, hi) over [0, n) on up to the host's hardware threads, in
+// contiguous ranges (each index in exactly one range).  Small ranges run
+// inline.
+template <class Fn>
+static void parallel_ranges(int64_t n, int64_t min_per_thread, Fn fn) {
+  const int64_t hw = std::max(1u, std::thread::hardware_concurrency());
+  const int64_t parts = std::min<int64_t>(hw, std::max<int64_t>(1, n / std::max<int64_t>(1, min_per_thread)));
+  if (parts <= 1) {
+    fn(int64_t{0}, n);
+    return;
+  }
+  std::vector<std::thread> th;
+  const int64_t step = (n + parts - 1) / parts;
+  for (int64_t lo = 0; lo < n; lo += step) th.emplace_back(fn, lo, std::min(n, lo + step));
+  for (auto &t : th) t.join();
+}
 
 // ------------------------------------------------------------------ layout
 int pack_n_tiles(int64_t n, int flags) {
@@ -38,7 +58,9 @@ void pack_q8_0(const uint8_t *blocks, int64_t n, int64_t k, int flags, uint8_t *
   const int kc = pack_k_chunks(k);
   const int64_t kb = k / 32;
   std::memset(out, 0, static_cast<size_t>(tiles) * kc * kTileBytes);
-  for (int t = 0; t < tiles; ++t)
+  // tiles are independent (each writes its own kc chunks)
+  parallel_ranges(tiles, 64, [&](int64_t t0, int64_t t1) {
+  for (int t = static_cast<int>(t0); t < t1; ++t)
     for (int r = 0; r < kPackRows; ++r) {
       const int64_t sr = src_row(n, flags, t, r);
       if (sr < 0) continue;
@@ -55,6 +77,7 @@ void pack_q8_0(const uint8_t *blocks, int64_t n, int64_t k, int flags, uint8_t *
         }
       }
     }
+  });
 }
 
 static uint16_t f32_to_bf16(float f) {
@@ -166,7 +189,9 @@ int64_t q8_0_first_mismatch(const float *w, const uint8_t *blocks, int64_t count
 
 void quantize_q8_0(const float *w, int64_t n, int64_t k, uint8_t *blocks) {
   const int64_t nb = n * (k / 32);
-  for (int64_t b = 0; b < nb; ++b) {
+  // blocks are independent
+  parallel_ranges(nb, 1 << 15, [&](int64_t b0, int64_t b1) {
+  for (int64_t b = b0; b < b1; ++b) {
     const float *xb = w + b * 32;
     uint8_t *ob = blocks + b * 34;
     float amax = 0.f;
@@ -177,6 +202,7 @@ void quantize_q8_0(const float *w, int64_t n, int64_t k, uint8_t *blocks) {
     std::memcpy(ob, &dh, 2);
     for (int j = 0; j < 32; ++j) ob[2 + j] = static_cast<uint8_t>(static_cast<int8_t>(std::roundf(xb[j] * id)));
   }
+  });
 }
 
 // --------------------------------------------------------------------- GGUF
