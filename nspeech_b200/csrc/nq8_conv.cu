@@ -32,25 +32,45 @@ __device__ __forceinline__ float leaky(float v, float slope) { return v >= 0.f ?
 
 // rows[t][e] for e < c_in * K: x[ci][t * stride - pad + j * dil] with
 // ci = e / K, j = e % K (zero outside [0, t_in)); zero for e in [c_in * K, ld).
+// A thread writes 8 consecutive elements of one row (one 16-byte store for
+// bf16 rows, two for f32), walking (ci, j) incrementally; ld % 8 == 0.
 __global__ void im2col_kernel(const void *__restrict__ x, int x_dtype, int64_t ldx, int c_in, int t_in, int K,
                               int stride, int pad, int dil, float slope, int t_out, int64_t ld, int a_dtype,
                               void *__restrict__ rows) {
   pdl_wait();
   pdl_trigger();
-  const int64_t total = static_cast<int64_t>(t_out) * ld;
   const int ck = c_in * K;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int t = static_cast<int>(i / ld);
-    const int e = static_cast<int>(i - static_cast<int64_t>(t) * ld);
-    float v = 0.f;
-    if (e < ck) {
-      const int ci = e / K, j = e - ci * K;
-      const int ti = t * stride - pad + j * dil;
-      if (ti >= 0 && ti < t_in) v = leaky(load_x(x, x_dtype, static_cast<int64_t>(ci) * ldx + ti), slope);
+  for (int t = blockIdx.y; t < t_out; t += gridDim.y) {
+    const int tbase = t * stride - pad;
+    for (int64_t e0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; e0 < ld;
+         e0 += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
+      float v[8];
+      int ci = static_cast<int>(e0 / K), j = static_cast<int>(e0 - static_cast<int64_t>(ci) * K);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        v[q] = 0.f;
+        if (e0 + q < ck) {
+          const int ti = tbase + j * dil;
+          if (ti >= 0 && ti < t_in) v[q] = leaky(load_x(x, x_dtype, static_cast<int64_t>(ci) * ldx + ti), slope);
+        }
+        if (++j == K) {
+          j = 0;
+          ++ci;
+        }
+      }
+      if (a_dtype == 0) {
+        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(rows) + static_cast<int64_t>(t) * ld + e0);
+        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
+        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+      } else {
+        uint4 pk;
+        pk.x = pack_bf16x2(v[0], v[1]);
+        pk.y = pack_bf16x2(v[2], v[3]);
+        pk.z = pack_bf16x2(v[4], v[5]);
+        pk.w = pack_bf16x2(v[6], v[7]);
+        *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(rows) + static_cast<int64_t>(t) * ld + e0) = pk;
+      }
     }
-    if (a_dtype == 0) static_cast<float *>(rows)[i] = v;
-    else static_cast<__nv_bfloat16 *>(rows)[i] = __float2bfloat16_rn(v);
   }
 }
 
@@ -117,10 +137,12 @@ int grid_for(int64_t total, int threads) {
 
 cudaError_t launch_im2col(const void *x, int x_dtype, int64_t ldx, int c_in, int t_in, int K, int stride, int pad,
                           int dil, float slope, int t_out, int64_t ld, int a_dtype, void *rows, cudaStream_t s) {
-  const int64_t total = static_cast<int64_t>(t_out) * ld;
-  if (total == 0) return cudaSuccess;
-  return launch_pdl(im2col_kernel, dim3(grid_for(total, 256)), dim3(256), 0, s, 1, x, x_dtype, ldx, c_in, t_in, K,
-                    stride, pad, dil, slope, t_out, ld, a_dtype, rows);
+  if (t_out == 0 || ld == 0) return cudaSuccess;
+  if (ld % 8) return cudaErrorInvalidValue;
+  const int threads = 128;
+  const dim3 grid(static_cast<unsigned>((ld / 8 + threads - 1) / threads), static_cast<unsigned>(std::min(t_out, 65535)));
+  return launch_pdl(im2col_kernel, grid, dim3(threads), 0, s, 1, x, x_dtype, ldx, c_in, t_in, K, stride, pad, dil,
+                    slope, t_out, ld, a_dtype, rows);
 }
 
 cudaError_t launch_transpose_out(const void *src, int src_dtype, int64_t lds, int rows_t, int cols_c, void *y,
