@@ -63,7 +63,7 @@ sys.path.insert(0, ROOT)
 METRIC = "Parakeet encoder RTFx (audio s/s) at 1/2/4/8 B200; Q8_0 GEMM % of peak"
 UNIT = "audio s/s"
 # libnq8 kernel classes timed by its event profiler (include/nq8.h NQ_KCLASS_*).
-KCLASSES = {"gemm": 0, "gemv": 1, "dequant": 2, "reduce": 3}
+KCLASSES = {"gemm": 0, "gemv": 1, "dequant": 2, "reduce": 3, "attention": 4}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
@@ -111,6 +111,8 @@ def parse_args():
     ap.add_argument("--conv-frames", type=int, default=300, help="--conv: decoder frames (80 Hz) of the utterance")
     ap.add_argument("--tail-split", type=int, default=0,
                     help="nq_set_gemm_tail_split mode of the GEMMs (0 cost model, 1 off, >= 2 pieces)")
+    ap.add_argument("--attention", choices=["tcgen05", "mma_sync"], default="tcgen05",
+                    help="encoder attention kernel (nq_set_attention_kernel)")
     return ap.parse_args()
 
 
@@ -185,7 +187,7 @@ def workload_config(args, world: int, plan, spec) -> dict:
         "model": f"Parakeet TDT 0.6B FastConformer encoder ({spec.n_layers} layers, d {spec.d_model}, "
                  f"{spec.n_heads} heads, FFN {spec.d_model * spec.ff_mult}, conv {spec.conv_kernel})",
         "segments_per_gpu": segs, "shard": args.shard, "max_batch": args.max_batch, "audio_s_per_gpu": audio_s,
-        "buckets": len(plan), "streams": max(1, args.streams),
+        "buckets": len(plan), "streams": max(1, args.streams), "attention": args.attention,
         "seq_len": max(encoder_frames(max(ls)) for _, ls in plan),
         "global_batch": args.segments if args.shard == "lpt" else args.segments * world,
         "parallelism": f"dp{world} (segment-sharded, no collective on the data path)",
@@ -438,6 +440,8 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     torch.cuda.set_device(local_rank)
     lib.init(local_rank)
     lib.check(lib.load().nq_set_gemm_tail_split(args.tail_split))
+    lib.check(lib.load().nq_set_attention_kernel(
+        lib.NQ_ATTENTION_TCGEN05 if args.attention == "tcgen05" else lib.NQ_ATTENTION_MMA_SYNC))
     spec = S.EncoderSpec(n_layers=args.layers)
     load_t = {}
     enc, tensors = make_encoder(spec, timings=load_t)

@@ -354,6 +354,9 @@ void nq_encoder_free(nq_encoder *enc);
 #define NQ_KCLASS_GEMV 1    /* GEMV (M <= 16), its partial-sum pass included */
 #define NQ_KCLASS_DEQUANT 2 /* Q8_0 -> bf16 weight pass of the large-M GEMM */
 #define NQ_KCLASS_REDUCE 3  /* split-K reduction after a split GEMM */
+#define NQ_KCLASS_ATTENTION 4 /* encoder relative-position attention; FLOPs
+                               * 6 B Tp^2 D (QK^T, the relative band, PV over
+                               * padded frames), bytes q, k, v, rel. keys, out */
 int nq_profile_enable(int on);
 /* Synchronizes the recorded events and reports for one class: launches,
  * summed device ms, summed algorithmic FLOPs (2MNK) and bytes
@@ -404,6 +407,16 @@ int nq_set_gemm_unit_tokens(int tokens);
  * 2..16: that many pieces whenever a partial round exists (tests).  Results
  * differ from the unsplit sums only by f32 summation order.  Process-wide. */
 int nq_set_gemm_tail_split(int mode);
+
+/* Which kernel runs the encoder's relative-position attention.  No
+ * counterpart in the reference: a B200 dispatch knob.  TCGEN05 (default):
+ * tcgen05 MMAs with the scores and the output in tensor memory; MMA_SYNC:
+ * the earlier warp-level mma.sync kernel (kept for comparison).  Both compute
+ * the same attention; results differ by f32 / bf16 rounding only.
+ * Process-wide; returns NQ_ERR_ARG for other values. */
+#define NQ_ATTENTION_TCGEN05 0
+#define NQ_ATTENTION_MMA_SYNC 1
+int nq_set_attention_kernel(int kernel);
 
 /* DEBUG ONLY -- a test hook for failure detection, not part of the matmul
  * API: launches a kernel that waits on an mbarrier nothing arrives on,

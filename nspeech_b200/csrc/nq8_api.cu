@@ -20,6 +20,8 @@
 #include <vector>
 
 #include "../../include/nq8.h"
+#include "nq8_attention.h"
+#include "nq8_encoder.h"
 #include "nq8_host.h"
 #include "nq8_kernels.h"
 
@@ -73,6 +75,7 @@ std::mutex g_init_mu;
 long long g_wait_limit = 1LL << 31;
 int g_gemm_path = NQ_GEMM_AUTO;
 int g_gemm_unit_tokens = 0;  // 0: the kernel's default unit width
+int g_attention_kernel = NQ_ATTENTION_TCGEN05;
 int g_tail_split = 0;        // 0: cost model, 1: off, >= 2: that many pieces when a tail exists
 // Token count from which a GEMM call dequantizes the weight once and runs
 // the bf16 tensor-core GEMM (measured crossover on B200).
@@ -608,6 +611,7 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     p.ctl.status = ctx->status;
     p.ctl.wait_limit = g_wait_limit;
     const int work_units = plan.tail_pieces > 1 ? plan.full_units + plan.tail_tiles() * plan.tail_pieces : units;
+    p.pair_stores = work_units <= pairs ? 1 : 0;
     ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
     cudaError_t e = nq::launch_gemm_bf16(splitx, bt, tm_w, tm_a, tm_alo, p, std::min(work_units, pairs), stream);
     if (e != cudaSuccess) return cuda_fail(e, "GEMM launch");
@@ -773,6 +777,42 @@ int linear_launches(const nq_weight *w, int64_t m, int x_dtype, bool aligned) {
   int dev = 0;
   const int sm = current_ctx(&ctx, &dev) == NQ_OK ? ctx->sm_count : kSmCountB200;
   return plan_gemm(sm, w, m, x_dtype, x_dtype == NQ_BF16 && aligned).launches();
+}
+
+int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_t ldr, const float *bias_u,
+                     const float *bias_v, const int *len, int B, int Tp, int H, int D, __nv_bfloat16 *out,
+                     cudaStream_t s) {
+  DeviceCtx *ctx = nullptr;
+  int rc = current_ctx(&ctx, nullptr);
+  if (rc) return rc;
+  if (H <= 0 || D != H * 128 || Tp <= 0 || B <= 0 || ldr < D || ldr % 8)
+    return fail(NQ_ERR_SHAPE, "attention shape B=%d Tp=%d H=%d D=%d ldr=%lld", B, Tp, H, D, (long long)ldr);
+  const double tok = static_cast<double>(B) * Tp;
+  ProfScope ps(NQ_KCLASS_ATTENTION, s, 6.0 * tok * Tp * D, (tok * 4.0 + 2.0 * Tp - 1.0) * D * 2.0);
+  if (g_attention_kernel == NQ_ATTENTION_MMA_SYNC) {
+    const cudaError_t e = enc::relpos_attention(qkv, krel, ldr, bias_u, bias_v, len, B, Tp, H, D, out, s);
+    if (e != cudaSuccess) return cuda_fail(e, "relpos_attention launch");
+    return NQ_OK;
+  }
+  CUtensorMap tm_qkv, tm_rel;
+  rc = make_tmap(ctx, &tm_qkv, qkv, 3 * static_cast<int64_t>(D), static_cast<int64_t>(B) * Tp, 3 * static_cast<int64_t>(D), 64);
+  if (rc) return rc;
+  rc = make_tmap(ctx, &tm_rel, krel, D, 2 * static_cast<int64_t>(Tp) - 1, ldr, 64);
+  if (rc) return rc;
+  AttnTcParams p;
+  p.qkv = qkv;
+  p.bias_u = bias_u;
+  p.bias_v = bias_v;
+  p.len = len;
+  p.out = out;
+  p.Tp = Tp;
+  p.D = D;
+  p.rel_col0 = 0;
+  p.sl2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
+  p.ctl = DevCtl{ctx->status, g_wait_limit};
+  const cudaError_t e = launch_relpos_attention_tc(tm_qkv, tm_rel, p, B, H, s);
+  if (e != cudaSuccess) return cuda_fail(e, "relpos_attention_tc launch");
+  return NQ_OK;
 }
 }  // namespace nq
 
@@ -1345,6 +1385,13 @@ int nq_set_gemm_unit_tokens(int tokens) {
 int nq_set_gemm_tail_split(int mode) {
   if (mode < 0 || mode > 16) return fail(NQ_ERR_ARG, "tail split mode %d (0 auto, 1 off, 2..16 pieces)", mode);
   g_tail_split = mode;
+  return NQ_OK;
+}
+
+int nq_set_attention_kernel(int kernel) {
+  if (kernel != NQ_ATTENTION_TCGEN05 && kernel != NQ_ATTENTION_MMA_SYNC)
+    return fail(NQ_ERR_ARG, "attention kernel %d (0 tcgen05, 1 mma.sync)", kernel);
+  g_attention_kernel = kernel;
   return NQ_OK;
 }
 

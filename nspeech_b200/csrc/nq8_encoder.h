@@ -37,4 +37,12 @@ cudaError_t relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel
 cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, float *out, cudaStream_t s);
 
 }  // namespace enc
+
+// The encoder's attention on the kernel nq_set_attention_kernel selects: the
+// tcgen05 kernel (nq8_attention.cu, tensor maps encoded on the current
+// device) or enc::relpos_attention; timed as NQ_KCLASS_ATTENTION when
+// profiling.  Same arguments as enc::relpos_attention; returns an NQ_* code.
+int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_t ldr, const float *bias_u,
+                     const float *bias_v, const int *len, int B, int Tp, int H, int D, __nv_bfloat16 *out,
+                     cudaStream_t s);
 }  // namespace nq

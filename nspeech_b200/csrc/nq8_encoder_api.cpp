@@ -475,9 +475,9 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 0.5f, M, D, L.ln_mha_g, L.ln_mha_b, nullptr, nullptr, h, eps, st));
     // MHSA with relative positions -> norm_conv
     NQ_TRY(nq_linear(L.qkv, h, NQ_BF16, M, D, L.qkv_b, NQ_EPI_NONE, A.qkv.p, NQ_BF16, 3 * D, stv));
-    NQ_K(nq::enc::relpos_attention(A.qkv.as<__nv_bfloat16>(), A.krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
-                                   static_cast<int64_t>(c.n_layers) * D, L.bias_u, L.bias_v, L3,
-                                   s.B, Tp, H, D, A.att.as<__nv_bfloat16>(), st));
+    NQ_TRY(nq::relpos_attention(A.qkv.as<__nv_bfloat16>(), A.krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
+                                static_cast<int64_t>(c.n_layers) * D, L.bias_u, L.bias_v, L3, s.B, Tp, H, D,
+                                A.att.as<__nv_bfloat16>(), st));
     NQ_TRY(nq_linear(L.o, A.att.p, NQ_BF16, M, D, L.o_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_conv_g, L.ln_conv_b, nullptr, nullptr, h, eps, st));
     // Conv module -> norm_feed_forward2

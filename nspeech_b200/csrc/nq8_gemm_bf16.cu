@@ -410,8 +410,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else if (!p.glu) {
         const bool nvalid = n < p.N;
         const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
-        // bf16 rows whose 32 features of this warp all exist: paired 4-byte stores
-        const bool paired = p.y_dtype == 1 && (p.ldy & 1) == 0 && (reinterpret_cast<uintptr_t>(p.y) & 3) == 0 &&
+        // bf16 rows whose 32 features of this warp all exist: paired 4-byte
+        // stores (half the store instructions for one shuffle per token pair;
+        // they pay when the epilogue is exposed, and cost ~1% of a multi-round
+        // call, where it overlaps the next unit's main loop)
+        const bool paired = p.pair_stores && p.y_dtype == 1 && (p.ldy & 1) == 0 &&
+                            (reinterpret_cast<uintptr_t>(p.y) & 3) == 0 &&
                             static_cast<int64_t>(tile) * kPackRows + 32 * q + 32 <= p.N;
         for (int col = 0; col < cols; col += kEc) {
           float v[kEc];

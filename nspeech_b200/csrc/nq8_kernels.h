@@ -125,6 +125,8 @@ struct GemmBf16Params {
   float *tail_part;  // [tail tiles][pieces][2 CTAs][16 warps][unit tokens / 4][32] f32
   int *tail_cnt;     // [tail tiles][2 CTAs][16] counters, zero between calls
   int w_static;      // the weight is not written by any kernel of this stream (kept bf16 copy)
+  int pair_stores;   // bf16 epilogue through lane pairs (4-byte stores); the host sets it when
+                     // every unit runs in one round, where each unit's epilogue is exposed
   DevCtl ctl;
 };
 int gemm_bf16_block_t();              // default tokens per pair unit

@@ -42,6 +42,9 @@ NQ_PACK_DEFAULT = 0
 NQ_PACK_GLU = 1
 NQ_MODE_QTILED = 2
 
+NQ_ATTENTION_TCGEN05 = 0
+NQ_ATTENTION_MMA_SYNC = 1
+
 
 class NqError(RuntimeError):
     """A non-zero status from libnq8 (carries the code and the library message)."""
@@ -118,6 +121,7 @@ SIGNATURES = {
     "nq_set_gemm_path": (_I, [_I]),
     "nq_set_gemm_unit_tokens": (_I, [_I]),
     "nq_set_gemm_tail_split": (_I, [_I]),
+    "nq_set_attention_kernel": (_I, [_I]),
     "nq_set_wait_limit": (_I, [_I64]),
     "nq_debug_wait_timeout": (_I, [_P]),
 }
@@ -172,6 +176,7 @@ NQ_KCLASS_GEMM = 0
 NQ_KCLASS_GEMV = 1
 NQ_KCLASS_DEQUANT = 2
 NQ_KCLASS_REDUCE = 3
+NQ_KCLASS_ATTENTION = 4
 NQ_GEMM_AUTO = 0
 NQ_GEMM_FUSED = 1
 NQ_GEMM_DEQUANT = 2
@@ -194,4 +199,8 @@ def profile_read(kclass: int, reset: bool = True) -> dict:
     ms, fl, by = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
     check(load().nq_profile_read(kclass, ctypes.byref(n), ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(by),
                                  1 if reset else 0))
-    return {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}
+    out = {"launches": n.value, "ms": ms.value, "flops": fl.value, "bytes": by.value}
+    if ms.value > 0:
+        out["tflops"] = fl.value / ms.value / 1e9
+        out["gbs"] = by.value / ms.value / 1e6
+    return out

@@ -117,6 +117,35 @@ def test_encoder_ragged_mel_bins_matches_oracle(nq, oracle, sub):
     _compare(oracle, out[0].cpu().numpy(), ref, f"encoder F88 sub{sub} T333", 0.05)
 
 
+# Encoder frames 1, 64, 65, 129, 300 and 513 (mel frames 8x): one partial key
+# tile, exact tile multiples, a ragged last tile, two and three query tiles,
+# and nine key tiles (the relative-key ring of the tcgen05 kernel wraps twice).
+@pytest.mark.parametrize("t_mel", [8, 512, 520, 1032, 2400, 4104])
+def test_attention_kernels_match_oracle(nq, oracle, t_mel):
+    """Both attention kernels (tcgen05, mma.sync) inside the encoder against
+    the oracle, and against each other."""
+    from nspeech_b200 import synthetic as S
+    L = nq.load()
+    spec = S.EncoderSpec(d_model=512, n_heads=4, n_layers=1, sub_channels=64)
+    q = _model(oracle, spec, seed=8)
+    enc = _gpu_encoder(spec, q)
+    mel = oracle.normal(5, (t_mel, 128))
+    ref = oracle.encoder_forward(spec.as_dict(), _oracle_tensors(q), mel)
+    outs = {}
+    try:
+        for kern in (nq.NQ_ATTENTION_MMA_SYNC, nq.NQ_ATTENTION_TCGEN05):
+            nq.check(L.nq_set_attention_kernel(kern))
+            out, lens = enc.forward(torch.from_numpy(mel)[None].cuda())
+            torch.cuda.synchronize()
+            assert lens == [ref.shape[0]]
+            outs[kern] = out[0].cpu().numpy()
+            _compare(oracle, outs[kern], ref, f"attention kernel {kern} T{t_mel}", 0.05)
+    finally:
+        nq.check(L.nq_set_attention_kernel(nq.NQ_ATTENTION_TCGEN05))
+    assert oracle.max_rel_err(outs[nq.NQ_ATTENTION_TCGEN05], outs[nq.NQ_ATTENTION_MMA_SYNC].astype(np.float64), 1.0) < 2e-2
+    assert nq.status() == 0
+
+
 def test_batched_segments_equal_single(nq, oracle):
     """A padded batch of segments reproduces each segment's own forward."""
     from nspeech_b200 import synthetic as S
