@@ -779,9 +779,18 @@ int linear_launches(const nq_weight *w, int64_t m, int x_dtype, bool aligned) {
   return plan_gemm(sm, w, m, x_dtype, x_dtype == NQ_BF16 && aligned).launches();
 }
 
+bool attention_tc(int Tp) { return g_attention_kernel == NQ_ATTENTION_TCGEN05 && Tp <= attention_tc_max_tp(); }
+
+int relpos_bias(const __nv_bfloat16 *krel, const float *vmu, int nrel, int n_layers, int D, float *vrel,
+                cudaStream_t s) {
+  const cudaError_t e = launch_relpos_bias(krel, vmu, nrel, n_layers, D, vrel, s);
+  if (e != cudaSuccess) return cuda_fail(e, "relpos_bias launch");
+  return NQ_OK;
+}
+
 int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_t ldr, const float *bias_u,
-                     const float *bias_v, const int *len, int B, int Tp, int H, int D, __nv_bfloat16 *out,
-                     cudaStream_t s) {
+                     const float *bias_v, const float *vrel, const int *len, int B, int Tp, int H, int D,
+                     __nv_bfloat16 *out, cudaStream_t s) {
   DeviceCtx *ctx = nullptr;
   int rc = current_ctx(&ctx, nullptr);
   if (rc) return rc;
@@ -789,7 +798,7 @@ int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_
     return fail(NQ_ERR_SHAPE, "attention shape B=%d Tp=%d H=%d D=%d ldr=%lld", B, Tp, H, D, (long long)ldr);
   const double tok = static_cast<double>(B) * Tp;
   ProfScope ps(NQ_KCLASS_ATTENTION, s, 6.0 * tok * Tp * D, (tok * 4.0 + 2.0 * Tp - 1.0) * D * 2.0);
-  if (g_attention_kernel == NQ_ATTENTION_MMA_SYNC) {
+  if (!attention_tc(Tp) || !vrel) {
     const cudaError_t e = enc::relpos_attention(qkv, krel, ldr, bias_u, bias_v, len, B, Tp, H, D, out, s);
     if (e != cudaSuccess) return cuda_fail(e, "relpos_attention launch");
     return NQ_OK;
@@ -802,7 +811,7 @@ int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_
   AttnTcParams p;
   p.qkv = qkv;
   p.bias_u = bias_u;
-  p.bias_v = bias_v;
+  p.vrel = vrel;
   p.len = len;
   p.out = out;
   p.Tp = Tp;

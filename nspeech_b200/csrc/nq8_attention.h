@@ -17,7 +17,7 @@ namespace nq {
 struct AttnTcParams {
   const __nv_bfloat16 *qkv;
   const float *bias_u;  // [D]
-  const float *bias_v;  // [D]
+  const float *vrel;    // [H][2 Tp - 1]: (v_h - u_h) . r_p of this layer (launch_relpos_bias)
   const int *len;       // [B] valid frames per segment
   __nv_bfloat16 *out;
   int Tp;
@@ -27,8 +27,15 @@ struct AttnTcParams {
   DevCtl ctl;
 };
 
-size_t attention_tc_smem_bytes();
+// Largest padded segment length (encoder frames) the kernel takes.
+int attention_tc_max_tp();
+size_t attention_tc_smem_bytes(int Tp);
 cudaError_t launch_relpos_attention_tc(const CUtensorMap &tm_qkv, const CUtensorMap &tm_rel, const AttnTcParams &p,
                                        int B, int H, cudaStream_t stream);
+// vrel[li][h][p] = vmu[li][h hd : +hd] . krel[p][li D + h hd : +hd] for every
+// layer li and head h; krel [nrel][n_layers D] bf16, vmu [n_layers][D] f32
+// (bias_v - bias_u), vrel [n_layers][D / hd][nrel] f32.
+cudaError_t launch_relpos_bias(const __nv_bfloat16 *krel, const float *vmu, int nrel, int n_layers, int D,
+                               float *vrel, cudaStream_t stream);
 
 }  // namespace nq

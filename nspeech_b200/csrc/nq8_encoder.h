@@ -40,9 +40,14 @@ cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, fl
 
 // The encoder's attention on the kernel nq_set_attention_kernel selects: the
 // tcgen05 kernel (nq8_attention.cu, tensor maps encoded on the current
-// device) or enc::relpos_attention; timed as NQ_KCLASS_ATTENTION when
-// profiling.  Same arguments as enc::relpos_attention; returns an NQ_* code.
+// device) when attention_tc(Tp), else enc::relpos_attention; timed as
+// NQ_KCLASS_ATTENTION when profiling.  The tcgen05 kernel also takes vrel,
+// this layer's [H][2 Tp - 1] table of (v - u) . r from relpos_bias.  Return
+// NQ_* codes.
+bool attention_tc(int Tp);
+int relpos_bias(const __nv_bfloat16 *krel, const float *vmu, int nrel, int n_layers, int D, float *vrel,
+                cudaStream_t s);
 int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_t ldr, const float *bias_u,
-                     const float *bias_v, const int *len, int B, int Tp, int H, int D, __nv_bfloat16 *out,
-                     cudaStream_t s);
+                     const float *bias_v, const float *vrel, const int *len, int B, int Tp, int H, int D,
+                     __nv_bfloat16 *out, cudaStream_t s);
 }  // namespace nq

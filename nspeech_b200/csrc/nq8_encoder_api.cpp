@@ -74,7 +74,7 @@ struct Layer {
 // batch ints) travel, each slot reused only after its previous copy
 // completed.
 struct Arena {
-  DevBuf x, h, t, u, u32, qkv, pos, krel, att, g, c, s1, s2a, s2b, s3a, s3b, flat, mel_in, out_buf;
+  DevBuf x, h, t, u, u32, qkv, pos, krel, vrel, att, g, c, s1, s2a, s2b, s3a, s3b, flat, mel_in, out_buf;
   static constexpr int kLenSlots = 4;
   DevBuf lens[kLenSlots];
   int *lens_host[kLenSlots] = {nullptr, nullptr, nullptr, nullptr};
@@ -107,6 +107,9 @@ struct nq_encoder {
   // they depend only on the positions, so one GEMM per forward serves all
   // layers (krel holds [2T-1][n_layers * d]).
   nq_weight *rel_all = nullptr;
+  // bias_v - bias_u of every layer, [n_layers][d] f32: with the stacked
+  // relative keys it gives each layer's (v - u) . r table (relpos_bias).
+  float *vmu_all = nullptr;
   // Activation arenas, one per stream (created on a stream's first forward):
   // forwards on one stream reuse its arena in stream order; forwards on
   // different streams have their own and may run concurrently.
@@ -335,6 +338,19 @@ int finalize(nq_encoder *e) {
     NQ_TRY(nq_weights_fuse(rels.data(), static_cast<int>(rels.size()), 0, &e->rel_all));
     e->weights.push_back(e->rel_all);
   }
+  {
+    std::vector<float> vmu(static_cast<size_t>(c.n_layers) * d), bu(d), bv(d);
+    for (int i = 0; i < c.n_layers; ++i) {
+      NQ_CUDA(cudaMemcpy(bu.data(), e->layers[i].bias_u, d * sizeof(float), cudaMemcpyDeviceToHost));
+      NQ_CUDA(cudaMemcpy(bv.data(), e->layers[i].bias_v, d * sizeof(float), cudaMemcpyDeviceToHost));
+      for (int64_t j = 0; j < d; ++j) vmu[i * d + j] = bv[j] - bu[j];
+    }
+    void *pv = nullptr;
+    NQ_CUDA(cudaMalloc(&pv, vmu.size() * sizeof(float)));
+    e->dev_allocs.push_back(pv);
+    NQ_CUDA(cudaMemcpy(pv, vmu.data(), vmu.size() * sizeof(float), cudaMemcpyHostToDevice));
+    e->vmu_all = static_cast<float *>(pv);
+  }
   NQ_TRY(nq_weight_keep_bf16(e->pw3, 1));
   NQ_TRY(nq_weight_keep_bf16(e->pw6, 1));
   NQ_TRY(nq_weight_keep_bf16(e->lin, 1));
@@ -386,6 +402,7 @@ int ensure_arena(nq_encoder *e, Arena &A, const Shapes &s, cudaStream_t st) {
   NQ_TRY(A.qkv.ensure(M * 3 * D * 2, st));
   NQ_TRY(A.pos.ensure(P * D * 2, st));
   NQ_TRY(A.krel.ensure(P * D * e->cfg.n_layers * 2, st));
+  if (nq::attention_tc(s.T3)) NQ_TRY(A.vrel.ensure(P * (D / 128) * e->cfg.n_layers * 4, st));
   NQ_TRY(A.att.ensure(M * D * 2, st));
   NQ_TRY(A.g.ensure(M * D * 2, st));
   NQ_TRY(A.c.ensure(M * D * 2, st));
@@ -466,6 +483,9 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
   // relative keys of every layer: krel[p][li * D + :] = pos[p] . W_rel(li)^T
   NQ_TRY(nq_linear(e->rel_all, A.pos.p, NQ_BF16, 2 * Tp - 1, D, nullptr, NQ_EPI_NONE, A.krel.p, NQ_BF16,
                    static_cast<int64_t>(c.n_layers) * D, stv));
+  // (v - u) . r of every layer, head and relative row (tcgen05 attention)
+  const bool att_tc = nq::attention_tc(Tp);
+  if (att_tc) NQ_TRY(nq::relpos_bias(A.krel.as<__nv_bfloat16>(), e->vmu_all, 2 * Tp - 1, c.n_layers, D, A.vrel.as<float>(), st));
 
   for (int li = 0; li < c.n_layers; ++li) {
     const Layer &L = e->layers[li];
@@ -476,8 +496,9 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
     // MHSA with relative positions -> norm_conv
     NQ_TRY(nq_linear(L.qkv, h, NQ_BF16, M, D, L.qkv_b, NQ_EPI_NONE, A.qkv.p, NQ_BF16, 3 * D, stv));
     NQ_TRY(nq::relpos_attention(A.qkv.as<__nv_bfloat16>(), A.krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
-                                static_cast<int64_t>(c.n_layers) * D, L.bias_u, L.bias_v, L3, s.B, Tp, H, D,
-                                A.att.as<__nv_bfloat16>(), st));
+                                static_cast<int64_t>(c.n_layers) * D, L.bias_u, L.bias_v,
+                                att_tc ? A.vrel.as<float>() + static_cast<size_t>(li) * H * (2 * Tp - 1) : nullptr,
+                                L3, s.B, Tp, H, D, A.att.as<__nv_bfloat16>(), st));
     NQ_TRY(nq_linear(L.o, A.att.p, NQ_BF16, M, D, L.o_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
     NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_conv_g, L.ln_conv_b, nullptr, nullptr, h, eps, st));
     // Conv module -> norm_feed_forward2
@@ -662,6 +683,7 @@ int nq_encoder_launch_count(const nq_encoder *enc, int batch, int t_mel) {
   n += lin(enc->pw6, static_cast<int64_t>(s.B) * s.T3 * s.F3, s.C);
   n += lin(enc->lin, M, static_cast<int64_t>(s.F3) * s.C);
   n += lin(enc->rel_all, 2 * Tp - 1, s.D);  // every layer's relative keys
+  if (nq::attention_tc(Tp)) n += 1;          // their (v - u) . r table
   for (const Layer &L : enc->layers) {
     n += 6;  // 4 LN, attention, depthwise conv
     n += lin(L.ff1_w1, M, s.D) + lin(L.ff1_w2, M, s.D * enc->cfg.ff_mult) + lin(L.qkv, M, s.D) +

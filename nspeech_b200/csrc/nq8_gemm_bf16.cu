@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) {
         if (rank == 0) mbar_arrive(accum_empty(b));
-        else mbar_arrive_remote(map_rank(accum_empty(b), 0));
+        else mbar_arrive_remote_relaxed(map_rank(accum_empty(b), 0));  // TMEM reads done; stores need no release
       }
     }
   }

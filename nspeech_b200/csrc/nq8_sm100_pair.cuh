@@ -30,6 +30,13 @@ __device__ __forceinline__ uint32_t map_rank(uint32_t saddr, uint32_t rank) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Relaxed remote arrive: signals only that this thread's earlier tcgen05 work
+// is done (ordered by tcgen05.fence::before_thread_sync), with no release of
+// its ordinary memory writes -- the release form waits for the thread's
+// epilogue stores to become visible to the cluster first.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 
 // ---------------------------------------------------------------- tcgen05 x2
 __device__ __forceinline__ void tmem_alloc2(uint32_t dst_smem, uint32_t ncols) {
