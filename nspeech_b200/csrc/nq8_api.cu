@@ -810,16 +810,16 @@ int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_
   if (rc) return rc;
   AttnTcParams p;
   p.qkv = qkv;
-  p.bias_u = bias_u;
   p.vrel = vrel;
   p.len = len;
   p.out = out;
+  p.B = B;
   p.Tp = Tp;
   p.D = D;
   p.rel_col0 = 0;
   p.sl2 = static_cast<float>(1.4426950408889634 / std::sqrt(128.0));
   p.ctl = DevCtl{ctx->status, g_wait_limit};
-  const cudaError_t e = launch_relpos_attention_tc(tm_qkv, tm_rel, p, B, H, s);
+  const cudaError_t e = launch_relpos_attention_tc(tm_qkv, tm_rel, p, ctx->sm_count, s);
   if (e != cudaSuccess) return cuda_fail(e, "relpos_attention_tc launch");
   return NQ_OK;
 }

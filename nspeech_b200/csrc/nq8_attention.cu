@@ -12,33 +12,40 @@
 // a per-relative-row number vrel[h][p] = (v_h - u_h) . r_p (f32, computed once
 // per forward for all layers by relpos_bias_kernel).
 //
-// CTA = one (128 query rows, head, segment); 320 threads:
+// Persistent CTAs (one per SM): a work item is one (128 query rows, head,
+// segment); CTA c takes items c, c + grid, ...  All tiles of a CTA's items
+// form one sequence, so the loads and the S / band MMAs of an item's first
+// tile overlap the previous item's last tile and epilogue.  320 threads:
 //   warps 0-7  softmax: warp w owns TMEM lanes [32 (w % 4), +32) (query
 //              rows) and keys [32 (w / 4), +32) of every 64-key tile; the two
-//              warps of a row exchange row maxima through shared memory.
-//   warp 8     TMA producers: lane 0 Q and K, lane 1 V, lane 2 relative
-//              keys, each waiting only on its own ring; owns the TMEM columns.
+//              warps of a row share one parked row and exchange row maxima.
+//   warp 8     TMA producers: lane 0 K, lane 1 V, lane 2 relative keys,
+//              lane 3 Q, each waiting only on its own ring; owns the TMEM.
 //   warp 9     MMA issuer (one elected thread).
+// q arrives with u already added (the encoder folds u into the q projection's
+// bias), so Q is an MMA operand straight from its TMA tile.
 // TMEM (512 columns, f32):
 //   [0, 128)   O accumulator                 (128 rows x hd)
-//   [128, 256) S = (q+u) K^T, two 64-column buffers (tile t in buffer t % 2)
+//   [128, 256) S = (q+u) K^T, two 64-column buffers (tile tau in buffer tau % 2)
 //   [256, 512) band = (q+u) R^T ring: 4 chunks of 64 relative rows.
-// Tile t needs relative rows [64t, 64t + 191) of the CTA's window (base row
-// P0 = Tp - 1 - i0 - 127); tile 0 computes chunks 0..2, tile t >= 1 only the
-// new chunk t + 2, so every relative row is multiplied once per CTA (the
-// reference's full [T, 2T-1] product costs twice the QK^T work; this costs
-// the same as QK^T).  Each softmax thread reads the 64 ring columns its
-// diagonal band touches, adds vrel, parks them in its own shared-memory row
-// and gathers band[i][jl - il + 127] for its 32 scores.
+// Tile t of an item needs relative rows [64t, 64t + 191) of the item's
+// window (base row P0 = Tp - 1 - i0 - 127); its tile 0 computes chunks 0..2,
+// tile t >= 1 only the new chunk t + 2, so every relative row is multiplied
+// once per item (the reference's full [T, 2T-1] product costs twice the
+// QK^T work; this costs the same as QK^T).  The two softmax threads of a row
+// park the 96 ring columns the row's diagonal band touches (plus vrel) in
+// the row's shared-memory line and each gathers band[i][jl - il + 127] for
+// its 32 scores.
 // P = exp2(s - m) goes to shared memory as bf16 (K-major, 128-byte swizzle)
 // and O += P V runs with V as an MN-major operand straight from its TMA tile.
 // O is rescaled only when a row maximum grows by more than 2^8 (the
 // exponentials stay <= 256; the final O / l is unchanged by the choice of
-// reference maximum).
+// reference maximum).  Items whose query rows all lie past the segment's
+// length (padding) are written as zeros.
 // Every wait is bounded (DevCtl); on give-up the roles record a kDev* bit,
 // drain their copies and MMAs, free TMEM and return.  A softmax warp that
-// gives up keeps stepping through its tiles without touching TMEM, so the
-// named barrier it shares with its partner warp is always reached.
+// gives up keeps stepping through its items without touching TMEM, so the
+// named barriers it shares with the other softmax warps are always reached.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -65,15 +72,16 @@ constexpr uint32_t kBox = 8192;    // one [64 x 64] SW128 box
 constexpr uint32_t kOffQ = 0;                  // [128 rows x 128] bf16(q + u): two 16 KB column halves
 constexpr uint32_t kOffK = 32768;              // 2 slots
 constexpr uint32_t kOffV = kOffK + 2 * kTile;  // 2 slots
-constexpr uint32_t kOffR = kOffV + 2 * kTile;  // 2 slots of 64 relative rows
-constexpr uint32_t kOffP = kOffR + 2 * kTile;  // [128 rows x 64 keys] bf16
-constexpr int kParkPitch = 68;                 // floats per parked row (conflict-free)
-constexpr uint32_t kOffPark = kOffP + kTile;   // one row per softmax thread
-constexpr uint32_t kOffRed = kOffPark + kSoftThreads * kParkPitch * 4;
+constexpr int kRSlots = 3;                     // relative-key ring: tile 0 of an item takes three chunks
+constexpr uint32_t kOffR = kOffV + 2 * kTile;
+constexpr uint32_t kOffP = kOffR + kRSlots * kTile;  // [128 rows x 64 keys] bf16
+constexpr int kParkPitch = 100;                      // floats per parked row (conflict-free)
+constexpr uint32_t kOffPark = kOffP + kTile;         // one row per query row: 96 band values
+constexpr uint32_t kOffRed = kOffPark + kBQ * kParkPitch * 4;
 constexpr uint32_t kRedBytes = (2 * 2 + 2) * kBQ * 4;  // row maxima [tile parity][key half][row], sums [half][row]
 constexpr uint32_t kOffBar = kOffRed + kRedBytes;
-constexpr int kNumBars = 22;
-constexpr uint32_t kOffVr = kOffBar + 256;     // vrel over the CTA's window (f32), sized per launch
+constexpr int kNumBars = 24;
+constexpr uint32_t kOffVr = kOffBar + 256;     // vrel over an item's window (f32), sized per launch
 constexpr uint32_t kSmemMax = 232448;
 constexpr uint32_t kAlignSlack = 1024;
 
@@ -84,9 +92,9 @@ constexpr uint32_t kTmBD = 256;
 constexpr uint32_t kTmCols = 512;
 
 // Barriers.
-constexpr int kBarKFull = 0, kBarKEmpty = 2, kBarVFull = 4, kBarVEmpty = 6, kBarRFull = 8, kBarREmpty = 10;
-constexpr int kBarSFull = 12, kBarSFree = 14, kBarPReady = 16, kBarPvDone = 17, kBarQFull = 18, kBarQReady = 19,
-              kBarMmaDone = 20, kBarR2Full = 21;
+constexpr int kBarKFull = 0, kBarKEmpty = 2, kBarVFull = 4, kBarVEmpty = 6, kBarRFull = 8, kBarREmpty = 11;
+constexpr int kBarSFull = 14, kBarSFree = 16, kBarPReady = 18, kBarPvDone = 19, kBarQFull = 20, kBarQFree = 21,
+              kBarOFree = 22, kBarMmaDone = 23;
 static_assert(kNumBars * 8 + 8 <= 256, "barrier block");
 
 constexpr uint32_t kIdescS = idesc_bf16_f32(128, 64);                // K-major A and B
@@ -144,6 +152,25 @@ __device__ __forceinline__ void park32(float *row, int col, const uint32_t (&r)[
                          __uint_as_float(r[4 * x + 2]) + b[x].z, __uint_as_float(r[4 * x + 3]) + b[x].w);
 }
 
+// One work item: query rows [i0, i0 + 128) of head h in segment b, with nt
+// key tiles (0: nothing to compute, rows written as zeros).
+struct Item {
+  int b, h, i0, L, nt;
+};
+__device__ __forceinline__ Item item_of(const AttnTcParams &p, int it) {
+  const int nq = (p.Tp + kBQ - 1) / kBQ;
+  const int heads = p.D / kHd;
+  Item r;
+  const int qt = it % nq;
+  const int bh = it / nq;
+  r.h = bh % heads;
+  r.b = bh / heads;
+  r.i0 = qt * kBQ;
+  r.L = max(0, min(__ldg(p.len + r.b), p.Tp));
+  r.nt = r.i0 < r.L ? (r.L + kBK - 1) / kBK : 0;
+  return r;
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     relpos_attention_tc_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_rel,
                                const __grid_constant__ AttnTcParams p) {
@@ -159,10 +186,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int b = blockIdx.z;
-  const int h = blockIdx.y;
-  const int i0 = blockIdx.x * kBQ;
   const long long lim = p.ctl.wait_limit;
+  const int n_items = ((p.Tp + kBQ - 1) / kBQ) * (p.D / kHd) * p.B;
+  const int Tp = p.Tp;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < 2; ++s) {
@@ -170,17 +196,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kBarKEmpty + s), 1);
       mbar_init(bar(kBarVFull + s), 1);
       mbar_init(bar(kBarVEmpty + s), 1);
-      mbar_init(bar(kBarRFull + s), 1);
-      mbar_init(bar(kBarREmpty + s), 1);
       mbar_init(bar(kBarSFull + s), 1);
       mbar_init(bar(kBarSFree + s), kSoftThreads);
+    }
+    for (int s = 0; s < kRSlots; ++s) {
+      mbar_init(bar(kBarRFull + s), 1);
+      mbar_init(bar(kBarREmpty + s), 1);
     }
     mbar_init(bar(kBarPReady), kSoftThreads);
     mbar_init(bar(kBarPvDone), 1);
     mbar_init(bar(kBarQFull), 1);
-    mbar_init(bar(kBarQReady), kSoftThreads);
+    mbar_init(bar(kBarQFree), 1);
+    mbar_init(bar(kBarOFree), kSoftThreads);
     mbar_init(bar(kBarMmaDone), 1);
-    mbar_init(bar(kBarR2Full), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -195,92 +223,88 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_wait();  // barriers and TMEM are set up; now wait for the predecessor's data
   pdl_trigger();
 
-  const int Tp = p.Tp;
-  const int L = max(0, min(p.len[b], Tp));
-  const int nt = (L + kBK - 1) / kBK;
-  const int row0 = b * Tp;                 // first qkv row of the segment
-  const int P0 = Tp - 1 - i0 - (kBQ - 1);  // relative row of window column 0
-
   if (warp == kProdWarp) {
-    if (lane < 3 && nt > 0) {
+    if (lane < 4) {
       // ------------------------------------------------------------ producers
-      // One lane per ring, each waiting only on its own ring's slots: lane 0
-      // Q and K, lane 1 V, lane 2 the relative keys.
+      // Lane 0 K tiles, lane 1 V tiles, lane 2 relative-key chunks (0 .. nt + 1
+      // of each item), lane 3 Q (one per item, once the previous item's last
+      // S / band MMAs have read the buffer).
       const int which = lane;
       if (which == 0) {
         prefetch_tmap(&tm_qkv);
         prefetch_tmap(&tm_rel);
-        // Q rows [i0, i0 + 128): four [64 x 64] boxes (rows past the segment
-        // belong to the next one or are zero-filled; their outputs are not stored)
-        mbar_arrive_expect_tx(bar(kBarQFull), 2 * kTile);
-#pragma unroll
-        for (int half = 0; half < 2; ++half)
-#pragma unroll
-          for (int rh = 0; rh < 2; ++rh)
-            tma_load_2d(sbase + kOffQ + half * 16384 + rh * kBox, &tm_qkv, bar(kBarQFull), h * kHd + 64 * half,
-                        row0 + i0 + 64 * rh);
       }
-      const int full0 = which == 0 ? kBarKFull : which == 1 ? kBarVFull : kBarRFull;
-      const uint32_t slot0 = which == 0 ? kOffK : which == 1 ? kOffV : kOffR;
+      const int nslots = which == 2 ? kRSlots : which == 3 ? 1 : 2;
+      const int full0 = which == 0 ? kBarKFull : which == 1 ? kBarVFull : which == 2 ? kBarRFull : kBarQFull;
+      const int empty0 = which == 0 ? kBarKEmpty : which == 1 ? kBarVEmpty : which == 2 ? kBarREmpty : kBarQFree;
+      const uint32_t slot0 = which == 0 ? kOffK : which == 1 ? kOffV : which == 2 ? kOffR : kOffQ;
       const CUtensorMap *map = which == 2 ? &tm_rel : &tm_qkv;
-      const int x = which == 0 ? p.D + h * kHd : which == 1 ? 2 * p.D + h * kHd : p.rel_col0 + h * kHd;
-      // K and V: tile k; relative keys: chunks 0, 1, then 3 .. nt + 1 through
-      // the ring, and chunk 2 (tile 0's third) into the P buffer, which stays
-      // unused until softmax 0 has waited for the MMA that reads it.
-      const int count = which == 2 ? nt + 1 : nt;
-      int n = 0;
-      bool r2 = false;
-      for (int k = 0; k < count; ++k) {
-        if (which == 2 && k == 2 && !r2) {
-          mbar_arrive_expect_tx(bar(kBarR2Full), kTile);
-          tma_load_2d(sbase + kOffP, &tm_rel, bar(kBarR2Full), x, P0 + 2 * kBK);
-          tma_load_2d(sbase + kOffP + kBox, &tm_rel, bar(kBarR2Full), x + 64, P0 + 2 * kBK);
-          r2 = true;
+      int n = 0;  // loads issued
+      bool ok = true;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const Item w = item_of(p, it);
+        if (w.nt == 0) continue;
+        const int row0 = w.b * Tp;
+        const int P0 = Tp - 1 - w.i0 - (kBQ - 1);
+        const int x = which == 0 ? p.D + w.h * kHd : which == 1 ? 2 * p.D + w.h * kHd
+                    : which == 2 ? p.rel_col0 + w.h * kHd : w.h * kHd;
+        const int count = which == 2 ? w.nt + 2 : which == 3 ? 1 : w.nt;
+        for (int k = 0; k < count; ++k) {
+          const int s = n % nslots;
+          const int use = n / nslots;
+          if (use > 0 && !mbar_wait(bar(empty0 + s), (use - 1) & 1, lim, abort_flag)) {
+            if (!*abort_flag) report(p.ctl, abort_flag, kDevTimeoutProducer);
+            ok = false;
+            break;
+          }
+          if (*abort_flag) {
+            ok = false;
+            break;
+          }
+          const uint32_t full = bar(full0 + s);
+          const uint32_t dst = sbase + slot0 + s * kTile;
+          if (which == 3) {
+            // Q rows [i0, i0 + 128): four [64 x 64] boxes (rows past the segment
+            // belong to the next one or are zero-filled; their outputs are not stored)
+            mbar_arrive_expect_tx(full, 2 * kTile);
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+#pragma unroll
+              for (int rh = 0; rh < 2; ++rh)
+                tma_load_2d(dst + half * 16384 + rh * kBox, map, full, x + 64 * half, row0 + w.i0 + 64 * rh);
+          } else {
+            const int y = which == 2 ? P0 + kBK * k : row0 + k * kBK;
+            mbar_arrive_expect_tx(full, kTile);
+            tma_load_2d(dst, map, full, x, y);
+            tma_load_2d(dst + kBox, map, full, x + 64, y);
+          }
+          ++n;
         }
-        const int y = which == 2 ? P0 + kBK * (k < 2 ? k : k + 1) : row0 + k * kBK;
-        const int s = n & 1;
-        const int use = n >> 1;
-        if (use > 0 && !mbar_wait(bar(full0 + 2 + s), (use - 1) & 1, lim, abort_flag)) {
-          if (!*abort_flag) report(p.ctl, abort_flag, kDevTimeoutProducer);
-          break;
-        }
-        if (*abort_flag) break;
-        const uint32_t full = bar(full0 + s);
-        const uint32_t dst = sbase + slot0 + s * kTile;
-        mbar_arrive_expect_tx(full, kTile);
-        tma_load_2d(dst, map, full, x, y);
-        tma_load_2d(dst + kBox, map, full, x + 64, y);
-        ++n;
-      }
-      if (which == 2 && count == 2 && n == 2 && !r2) {  // nt == 1: chunk 2 after the loop
-        mbar_arrive_expect_tx(bar(kBarR2Full), kTile);
-        tma_load_2d(sbase + kOffP, &tm_rel, bar(kBarR2Full), x, P0 + 2 * kBK);
-        tma_load_2d(sbase + kOffP + kBox, &tm_rel, bar(kBarR2Full), x + 64, P0 + 2 * kBK);
-        r2 = true;
       }
       // Drain: every copy this lane issued into shared memory has landed.
       volatile int no_abort = 0;
-      if (which == 0 && !mbar_wait(bar(kBarQFull), 0, lim, &no_abort)) atomicOr(p.ctl.status, kDevTimeoutDrain);
-      if (r2 && !mbar_wait(bar(kBarR2Full), 0, lim, &no_abort)) atomicOr(p.ctl.status, kDevTimeoutDrain);
-      for (int s = 0; s < 2; ++s) {
-        const int uses = (n - s + 1) >> 1;
+      for (int s = 0; s < nslots; ++s) {
+        const int uses = n > s ? (n - 1 - s) / nslots + 1 : 0;
         if (uses > 0 && !mbar_wait(bar(full0 + s), (uses - 1) & 1, lim, &no_abort))
           atomicOr(p.ctl.status, kDevTimeoutDrain);
       }
     }
   } else if (warp == kMmaWarp) {
-    if (lane == 0 && nt > 0) {
+    if (lane == 0) {
       // ------------------------------------------------------------ MMA
       bool ok = true;
+      bool issued = false;
       auto wait = [&](int i, int parity) -> bool {
         if (mbar_wait(bar(i), parity, lim, abort_flag)) return !*abort_flag;
         if (!*abort_flag) report(p.ctl, abort_flag, kDevTimeoutMma);
         return false;
       };
       const uint32_t qa = sbase + kOffQ;
-      // O += P V_tau: P [128 x 64 keys] K-major, V [64 keys x 128 hd] MN-major.
-      auto pv = [&](int tau) -> bool {
+      // O += P V of global tile tau (local tile t of the kq-th item with work):
+      // P [128 x 64 keys] K-major, V [64 keys x 128 hd] MN-major.
+      auto pv = [&](int tau, int t, int kq) -> bool {
         const int s = tau & 1;
+        if (t == 0 && kq > 0 && !wait(kBarOFree, (kq - 1) & 1)) return false;  // previous item's O read
         if (!wait(kBarPReady, tau & 1) || !wait(kBarVFull + s, (tau >> 1) & 1)) return false;
         tc_fence_after();
         const uint32_t pa = sbase + kOffP, va = sbase + kOffV + s * kTile;
@@ -289,7 +313,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
             umma_bf16(tmem + kTmO + 64 * nh, sw128_kmajor_desc(pa + kk * 32), sw128_mn_desc(va + nh * kBox + kk * 2048, 1024),
-                      kIdescPV, (tau > 0 || kk > 0) ? 1u : 0u);
+                      kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
         umma_commit(bar(kBarVEmpty + s));
         umma_commit(bar(kBarPvDone));
         return true;
@@ -302,136 +326,149 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_bf16(d, sw128_kmajor_desc(qa + ko), sw128_kmajor_desc(bt + kb), kIdescS, kk > 0 ? 1u : 0u);
         }
       };
-      ok = wait(kBarQReady, 0);
-      tc_fence_after();
-      int ng = 0;  // relative-key chunks consumed from the ring
-      for (int t = 0; t < nt && ok; ++t) {
-        const int sb = t & 1;
-        // S buffer sb and ring chunk (t + 2) % 4 were last read by softmax t - 2.
-        if (t >= 2 && !(ok = wait(kBarSFree + sb, ((t >> 1) - 1) & 1))) break;
-        if (!(ok = wait(kBarKFull + sb, (t >> 1) & 1))) break;
-        tc_fence_after();
-        qk(tmem + kTmS + 64 * sb, sbase + kOffK + sb * kTile);
-        umma_commit(bar(kBarKEmpty + sb));
-        for (int g = (t == 0 ? 0 : t + 2); g < t + 3 && ok; ++g) {
-          if (t == 0 && g == 2) {  // tile 0's third chunk sits in the P buffer
-            if (!(ok = wait(kBarR2Full, 0))) break;
-            tc_fence_after();
-            qk(tmem + kTmBD + 64 * 2, sbase + kOffP);
-            continue;
-          }
-          const int rs = ng & 1;
-          if (!(ok = wait(kBarRFull + rs, (ng >> 1) & 1))) break;
-          tc_fence_after();
-          qk(tmem + kTmBD + 64 * (g & 3), sbase + kOffR + rs * kTile);
-          umma_commit(bar(kBarREmpty + rs));
-          ++ng;
+      int tau = 0, ng = 0, kq = 0, g0 = 0;  // tiles, ring chunks consumed, items with work, chunk base
+      int prev_tau = -1, prev_t = 0, prev_kq = 0;
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const Item w = item_of(p, it);
+        if (w.nt == 0) continue;
+        // The previous item's last PV goes first: its epilogue (which waits
+        // for it) then overlaps this item's first S / band MMAs, and nothing
+        // here waits for this item's loads before it.
+        if (prev_tau >= 0) {
+          if (!(ok = pv(prev_tau, prev_t, prev_kq))) break;
+          prev_tau = -1;
         }
-        if (!ok) break;
-        umma_commit(bar(kBarSFull + sb));
-        if (t >= 1) ok = pv(t - 1);
+        if (!(ok = wait(kBarQFull, kq & 1))) break;
+        for (int t = 0; t < w.nt && ok; ++t, ++tau) {
+          const int sb = tau & 1;
+          // S buffer sb was last read by softmax tau - 2; a first tile also
+          // overwrites ring chunks the previous tile (tau - 1) still reads.
+          if (t == 0 && tau >= 1) {
+            if (!(ok = wait(kBarSFree + ((tau - 1) & 1), ((tau - 1) >> 1) & 1))) break;
+          } else if (tau >= 2) {
+            if (!(ok = wait(kBarSFree + sb, ((tau >> 1) - 1) & 1))) break;
+          }
+          if (!(ok = wait(kBarKFull + sb, (tau >> 1) & 1))) break;
+          tc_fence_after();
+          qk(tmem + kTmS + 64 * sb, sbase + kOffK + sb * kTile);
+          issued = true;
+          umma_commit(bar(kBarKEmpty + sb));
+          for (int c = (t == 0 ? 0 : t + 2); c < t + 3 && ok; ++c, ++ng) {
+            const int rs = ng % kRSlots;
+            if (!(ok = wait(kBarRFull + rs, (ng / kRSlots) & 1))) break;
+            tc_fence_after();
+            qk(tmem + kTmBD + 64 * ((g0 + c) & 3), sbase + kOffR + rs * kTile);
+            umma_commit(bar(kBarREmpty + rs));
+          }
+          if (!ok) break;
+          if (t == w.nt - 1) umma_commit(bar(kBarQFree));  // every MMA reading this Q is issued
+          umma_commit(bar(kBarSFull + sb));
+          if (prev_tau >= 0 && !(ok = pv(prev_tau, prev_t, prev_kq))) break;
+          prev_tau = tau;
+          prev_t = t;
+          prev_kq = kq;
+        }
+        g0 += w.nt + 2;
+        ++kq;
       }
-      if (ok) pv(nt - 1);
+      if (ok && prev_tau >= 0) pv(prev_tau, prev_t, prev_kq);
       // Every MMA issued by this thread completes before TMEM is freed.
-      volatile int no_abort = 0;
-      umma_commit(bar(kBarMmaDone));
-      if (!mbar_wait(bar(kBarMmaDone), 0, lim, &no_abort)) atomicOr(p.ctl.status, kDevTimeoutDrain);
+      if (issued) {
+        volatile int no_abort = 0;
+        umma_commit(bar(kBarMmaDone));
+        if (!mbar_wait(bar(kBarMmaDone), 0, lim, &no_abort)) atomicOr(p.ctl.status, kDevTimeoutDrain);
+      }
     }
   } else {
     // -------------------------------------------------------------- softmax
     const int q4 = warp & 3;             // TMEM lane quarter
     const int kh = warp >> 2;            // key half of every tile
-    const int il = 32 * q4 + lane;       // query row within the CTA == TMEM lane
-    const int i = i0 + il;
+    const int il = 32 * q4 + lane;       // query row within the item == TMEM lane
     const int pair_bar = 1 + q4;         // named barrier of warps q4 and q4 + 4
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q4) << 16);
     float *red_max = reinterpret_cast<float *>(smem + kOffRed);  // [2][2][128]
     float *red_l = red_max + 4 * kBQ;                            // [2][128]
-    __nv_bfloat16 *orow = p.out + (static_cast<int64_t>(row0) + i) * p.D + h * kHd + 64 * kh;
-    if (nt == 0) {
-      if (i < Tp)
-        for (int c8 = 0; c8 < 8; ++c8) reinterpret_cast<uint4 *>(orow)[c8] = make_uint4(0u, 0u, 0u, 0u);
-    } else {
-      // vrel over the window: relative rows P0 + [0, W), zero outside the table.
-      const int W = vr_window(nt);
-      const int nrel = 2 * Tp - 1;
-      const float *vrel = p.vrel + static_cast<int64_t>(h) * nrel;
+    float *park = reinterpret_cast<float *>(smem + kOffPark) + il * kParkPitch;  // shared by the row's two threads
+    const int nrel = 2 * Tp - 1;
+    const float sl2 = p.sl2;
+    bool dead = false;  // warp-uniform: a wait gave up; no TMEM access from here on
+    auto wait_all = [&](int i_bar, int parity, int bit) -> bool {
+      if (dead) return false;
+      bool ok = mbar_wait(bar(i_bar), parity, lim, abort_flag) && !*abort_flag;
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0 && !*abort_flag) report(p.ctl, abort_flag, bit);
+      return ok;
+    };
+    int tau = 0, g0 = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      const Item w = item_of(p, it);
+      const int i = w.i0 + il;
+      const int row0 = w.b * Tp;
+      // The previous item's parked rows, vrel window and staged outputs are
+      // no longer read by any softmax warp.
+      named_bar_sync(5, kSoftThreads);
+      if (w.nt == 0) {
+        if (i < Tp) {
+          uint4 *orow = reinterpret_cast<uint4 *>(p.out + (static_cast<int64_t>(row0) + i) * p.D + w.h * kHd + 64 * kh);
+          for (int c8 = 0; c8 < 8; ++c8) orow[c8] = make_uint4(0u, 0u, 0u, 0u);
+        }
+        continue;
+      }
+      // vrel over the item's window: relative rows P0 + [0, W), zero outside the table.
+      const int P0 = Tp - 1 - w.i0 - (kBQ - 1);
+      const int W = vr_window(w.nt);
+      const float *vrel = p.vrel + static_cast<int64_t>(w.h) * nrel;
       for (int x = threadIdx.x; x < W; x += kSoftThreads) {
         const int pr = P0 + x;
         vr_s[x] = (pr >= 0 && pr < nrel) ? __ldg(vrel + pr) : 0.f;
       }
-      // bf16(q + u) in place: this thread's row, columns [64 kh, 64 kh + 64).
-      {
-        float4 bu[16];
-        const float4 *u4 = reinterpret_cast<const float4 *>(p.bias_u + h * kHd + 64 * kh);
-#pragma unroll
-        for (int x = 0; x < 16; ++x) bu[x] = __ldg(u4 + x);
-        const bool okq = __all_sync(0xffffffffu, mbar_wait(bar(kBarQFull), 0, lim, abort_flag));
-        if (okq) {
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            uint4 *a = reinterpret_cast<uint4 *>(smem + kOffQ + kh * 16384 + sw128_offset(il, c));
-            const uint4 v = *a;
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-            uint32_t o[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float4 bb = bu[2 * c + (e >> 1)];
-              const float b0 = (e & 1) ? bb.z : bb.x, b1 = (e & 1) ? bb.w : bb.y;
-              o[e] = pack_bf16x2(bf16_bits_to_f32(w[e] & 0xFFFFu) + b0, bf16_bits_to_f32(w[e] >> 16) + b1);
-            }
-            *a = make_uint4(o[0], o[1], o[2], o[3]);
-          }
-        } else if (lane == 0 && !*abort_flag) {
-          report(p.ctl, abort_flag, kDevTimeoutConsumer);
-        }
-        fence_proxy_async_smem();
-      }
-      named_bar_sync(5, kSoftThreads);  // vr_s written by every softmax thread
-      mbar_arrive(bar(kBarQReady));
-      float *park = reinterpret_cast<float *>(smem + kOffPark) + threadIdx.x * kParkPitch;
-      const float sl2 = p.sl2;
+      named_bar_sync(5, kSoftThreads);
       float m_use = -INFINITY, l_part = 0.f;
-      bool dead = false;  // warp-uniform: a wait gave up; no TMEM access from here on
-      auto wait_all = [&](int i_bar, int parity, int bit) -> bool {
-        if (dead) return false;
-        bool ok = mbar_wait(bar(i_bar), parity, lim, abort_flag) && !*abort_flag;
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok && lane == 0 && !*abort_flag) report(p.ctl, abort_flag, bit);
-        return ok;
-      };
-      for (int t = 0; t < nt; ++t) {
-        const int sb = t & 1;
+      for (int t = 0; t < w.nt; ++t, ++tau) {
+        const int sb = tau & 1;
         float s[32];
         float tmax = -INFINITY;
-        if (wait_all(kBarSFull + sb, (t >> 1) & 1, kDevTimeoutConsumer)) {
+        // Band chunks (32 columns) of this row: window chunks kc0 .. kc0 + 2
+        // (ring chunk (2 g0 + kc) % 8); the key-half-0 thread parks the first
+        // two, the key-half-1 thread the third.
+        const int kc0 = 2 * t + 3 - q4;
+        const bool live = wait_all(kBarSFull + sb, (tau >> 1) & 1, kDevTimeoutConsumer);
+        if (!live) dead = true;
+        uint32_t rs[32];
+        if (live) {
           tc_fence_after();
-          // Band chunks (32 columns) of this warp: window chunk kc (column
-          // 32 kc) is ring chunk kc % 8; thread `lane` reads window offsets
-          // 32 kc + (31 - lane) + jl.
-          const int kc = 2 * t + 3 - q4 + kh;
-          uint32_t ra[32], rb[32], rs[32];
-          tmem_ld32(tl + kTmBD + 32 * (kc & 7), ra);
-          tmem_ld32(tl + kTmBD + 32 * ((kc + 1) & 7), rb);
+          uint32_t ra[32], rb[32];
+          if (kh == 0) {
+            tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kc0) & 7), ra);
+            tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kc0 + 1) & 7), rb);
+          } else {
+            tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kc0 + 2) & 7), ra);
+          }
           tmem_ld32(tl + kTmS + 64 * sb + 32 * kh, rs);
           tmem_ld_wait();
           tc_fence_before();
           mbar_arrive(bar(kBarSFree + sb));  // S buffer and this tile's ring reads are done
-          park32(park, 0, ra, vr_s + 32 * kc);
-          park32(park, 32, rb, vr_s + 32 * (kc + 1));
+          if (kh == 0) {
+            park32(park, 0, ra, vr_s + 32 * kc0);
+            park32(park, 32, rb, vr_s + 32 * (kc0 + 1));
+          } else {
+            park32(park, 64, ra, vr_s + 32 * (kc0 + 2));
+          }
+        }
+        named_bar_sync(pair_bar, 64);  // the row's 96 band values are parked
+        if (live) {
+          const int off = 31 + 32 * kh - lane;
           const int jbase = t * kBK + 32 * kh;
 #pragma unroll
           for (int jl = 0; jl < 32; ++jl) {
-            float v = (__uint_as_float(rs[jl]) + park[31 - lane + jl]) * sl2;
-            v = jbase + jl < L ? v : -INFINITY;
+            float v = (__uint_as_float(rs[jl]) + park[off + jl]) * sl2;
+            v = jbase + jl < w.L ? v : -INFINITY;
             s[jl] = v;
             tmax = fmaxf(tmax, v);
           }
-        } else {
-          dead = true;
         }
         // Row maximum over both key halves (the partner warp holds the other).
-        float *rm = red_max + (t & 1) * 2 * kBQ;
+        float *rm = red_max + (tau & 1) * 2 * kBQ;
         rm[kh * kBQ + il] = tmax;
         named_bar_sync(pair_bar, 64);
         tmax = fmaxf(rm[kBQ + il], rm[il]);  // same order in both warps
@@ -446,8 +483,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           factor = ex2(m_use - tmax);
           m_use = tmax;
         }
-        // PV_{t-1} has finished: O is stable and the P buffer is free.
-        if (t >= 1 && !wait_all(kBarPvDone, (t - 1) & 1, kDevTimeoutConsumer)) dead = true;
+        // PV of the previous tile has finished: O is stable and the P buffer
+        // is free (an item's first tile follows the previous item's epilogue,
+        // which waited for it).
+        if (t >= 1 && !wait_all(kBarPvDone, (tau - 1) & 1, kDevTimeoutConsumer)) dead = true;
         if (dead) continue;
         if (t >= 1) {
           tc_fence_after();
@@ -480,40 +519,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(bar(kBarPReady));
       }
-      if (!wait_all(kBarPvDone, (nt - 1) & 1, kDevTimeoutEpilogue)) dead = true;
+      // ---- item epilogue: O / l as bf16, through this row's parked line
+      if (!wait_all(kBarPvDone, (tau - 1) & 1, kDevTimeoutEpilogue)) dead = true;
       red_l[kh * kBQ + il] = l_part;
       named_bar_sync(pair_bar, 64);
       if (!dead) {
         tc_fence_after();
         const float l_sum = red_l[il] + red_l[kBQ + il];  // same order in both warps
         const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        uint32_t oa[32], ob[32];
+        tmem_ld32(tl + kTmO + 64 * kh, oa);
+        tmem_ld32(tl + kTmO + 64 * kh + 32, ob);
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(bar(kBarOFree));  // the next item's first PV may overwrite O
         // This thread's 64 outputs (row il, columns [64 kh, +64)) as bf16 into
-        // its own park row, then the warp stores its 32 rows 128 bytes at a time.
-        uint4 *stage = reinterpret_cast<uint4 *>(park);
-#pragma unroll 1
-        for (int x = 0; x < 2; ++x) {
-          uint32_t o[32];
-          tmem_ld32(tl + kTmO + 64 * kh + 32 * x, o);
-          tmem_ld_wait();
+        // bytes [128 kh, +128) of its row's parked line, then the warp stores
+        // its 32 rows 128 bytes at a time.
+        uint4 *stage = reinterpret_cast<uint4 *>(park) + 8 * kh;
+        auto put = [&](int c, const uint32_t (&o)[32]) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c)
-            stage[4 * x + c] = make_uint4(
-                pack_bf16x2(__uint_as_float(o[8 * c + 0]) * inv, __uint_as_float(o[8 * c + 1]) * inv),
-                pack_bf16x2(__uint_as_float(o[8 * c + 2]) * inv, __uint_as_float(o[8 * c + 3]) * inv),
-                pack_bf16x2(__uint_as_float(o[8 * c + 4]) * inv, __uint_as_float(o[8 * c + 5]) * inv),
-                pack_bf16x2(__uint_as_float(o[8 * c + 6]) * inv, __uint_as_float(o[8 * c + 7]) * inv));
-        }
+          for (int q = 0; q < 4; ++q)
+            stage[c + q] = make_uint4(pack_bf16x2(__uint_as_float(o[8 * q + 0]) * inv, __uint_as_float(o[8 * q + 1]) * inv),
+                                      pack_bf16x2(__uint_as_float(o[8 * q + 2]) * inv, __uint_as_float(o[8 * q + 3]) * inv),
+                                      pack_bf16x2(__uint_as_float(o[8 * q + 4]) * inv, __uint_as_float(o[8 * q + 5]) * inv),
+                                      pack_bf16x2(__uint_as_float(o[8 * q + 6]) * inv, __uint_as_float(o[8 * q + 7]) * inv));
+        };
+        put(0, oa);
+        put(4, ob);
         __syncwarp();
-        const uint4 *wstage = reinterpret_cast<const uint4 *>(smem + kOffPark) + (32 * warp) * (kParkPitch / 4);
+        const uint4 *wstage = reinterpret_cast<const uint4 *>(smem + kOffPark) + (32 * q4) * (kParkPitch / 4) + 8 * kh;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int r = 4 * k + (lane >> 3);  // row within the warp
-          const int ri = i0 + 32 * q4 + r;
+          const int ri = w.i0 + 32 * q4 + r;
           if (ri < Tp)
-            reinterpret_cast<uint4 *>(p.out + (static_cast<int64_t>(row0) + ri) * p.D + h * kHd + 64 * kh)[lane & 7] =
+            reinterpret_cast<uint4 *>(p.out + (static_cast<int64_t>(row0) + ri) * p.D + w.h * kHd + 64 * kh)[lane & 7] =
                 wstage[r * (kParkPitch / 4) + (lane & 7)];
         }
       }
+      g0 += w.nt + 2;
     }
   }
   __syncwarp();
@@ -565,8 +610,8 @@ size_t attention_tc_smem_bytes(int Tp) {
 }
 
 cudaError_t launch_relpos_attention_tc(const CUtensorMap &tm_qkv, const CUtensorMap &tm_rel, const AttnTcParams &p,
-                                       int B, int H, cudaStream_t stream) {
-  if (p.D != H * kHd || p.Tp <= 0 || B <= 0 || p.Tp > attention_tc_max_tp() || !p.vrel) return cudaErrorInvalidValue;
+                                       int sm_count, cudaStream_t stream) {
+  if (p.D % kHd || p.Tp <= 0 || p.B <= 0 || p.Tp > attention_tc_max_tp() || !p.vrel) return cudaErrorInvalidValue;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -577,8 +622,9 @@ cudaError_t launch_relpos_attention_tc(const CUtensorMap &tm_qkv, const CUtensor
     attr_set[dev] = true;
   }
   const size_t smem = attention_tc_smem_bytes(p.Tp);
-  dim3 grid((p.Tp + kBQ - 1) / kBQ, H, B);
-  return launch_pdl(relpos_attention_tc_kernel, grid, dim3(kThreads), smem, stream, 1, tm_qkv, tm_rel, p);
+  const int items = ((p.Tp + kBQ - 1) / kBQ) * (p.D / kHd) * p.B;
+  const int grid = items < sm_count ? items : sm_count;  // persistent: one CTA per SM
+  return launch_pdl(relpos_attention_tc_kernel, dim3(grid), dim3(kThreads), smem, stream, 1, tm_qkv, tm_rel, p);
 }
 
 cudaError_t launch_relpos_bias(const __nv_bfloat16 *krel, const float *vmu, int nrel, int n_layers, int D,

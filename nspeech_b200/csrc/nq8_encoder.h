@@ -41,9 +41,11 @@ cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, fl
 // The encoder's attention on the kernel nq_set_attention_kernel selects: the
 // tcgen05 kernel (nq8_attention.cu, tensor maps encoded on the current
 // device) when attention_tc(Tp), else enc::relpos_attention; timed as
-// NQ_KCLASS_ATTENTION when profiling.  The tcgen05 kernel also takes vrel,
-// this layer's [H][2 Tp - 1] table of (v - u) . r from relpos_bias.  Return
-// NQ_* codes.
+// NQ_KCLASS_ATTENTION when profiling.  The q columns of qkv hold q + u (the
+// encoder folds u into the q projection's bias); the tcgen05 kernel takes
+// vrel, this layer's [H][2 Tp - 1] table of (v - u) . r from relpos_bias, and
+// enc::relpos_attention gets bias_u = 0 and bias_v = v - u.  Return NQ_*
+// codes.
 bool attention_tc(int Tp);
 int relpos_bias(const __nv_bfloat16 *krel, const float *vmu, int nrel, int n_layers, int D, float *vrel,
                 cudaStream_t s);

@@ -110,6 +110,7 @@ struct nq_encoder {
   // bias_v - bias_u of every layer, [n_layers][d] f32: with the stacked
   // relative keys it gives each layer's (v - u) . r table (relpos_bias).
   float *vmu_all = nullptr;
+  float *zero_d = nullptr;  // [d] zeros: the mma.sync attention's u (already in q)
   // Activation arenas, one per stream (created on a stream's first forward):
   // forwards on one stream reuse its arena in stream order; forwards on
   // different streams have their own and may run concurrently.
@@ -339,17 +340,29 @@ int finalize(nq_encoder *e) {
     e->weights.push_back(e->rel_all);
   }
   {
-    std::vector<float> vmu(static_cast<size_t>(c.n_layers) * d), bu(d), bv(d);
+    // u moves into the q projection's bias (q + u comes out of the QKV GEMM,
+    // rounded once); attention keeps v - u: (q + v) . r = (q + u) . r + (v - u) . r.
+    std::vector<float> vmu(static_cast<size_t>(c.n_layers) * d), bu(d), bv(d), bq(3 * d);
     for (int i = 0; i < c.n_layers; ++i) {
-      NQ_CUDA(cudaMemcpy(bu.data(), e->layers[i].bias_u, d * sizeof(float), cudaMemcpyDeviceToHost));
-      NQ_CUDA(cudaMemcpy(bv.data(), e->layers[i].bias_v, d * sizeof(float), cudaMemcpyDeviceToHost));
-      for (int64_t j = 0; j < d; ++j) vmu[i * d + j] = bv[j] - bu[j];
+      Layer &L = e->layers[i];
+      NQ_CUDA(cudaMemcpy(bu.data(), L.bias_u, d * sizeof(float), cudaMemcpyDeviceToHost));
+      NQ_CUDA(cudaMemcpy(bv.data(), L.bias_v, d * sizeof(float), cudaMemcpyDeviceToHost));
+      NQ_CUDA(cudaMemcpy(bq.data(), L.qkv_b, 3 * d * sizeof(float), cudaMemcpyDeviceToHost));
+      for (int64_t j = 0; j < d; ++j) {
+        vmu[i * d + j] = bv[j] - bu[j];
+        bq[j] += bu[j];
+      }
+      NQ_CUDA(cudaMemcpy(L.qkv_b, bq.data(), 3 * d * sizeof(float), cudaMemcpyHostToDevice));
     }
-    void *pv = nullptr;
+    void *pv = nullptr, *pz = nullptr;
     NQ_CUDA(cudaMalloc(&pv, vmu.size() * sizeof(float)));
     e->dev_allocs.push_back(pv);
     NQ_CUDA(cudaMemcpy(pv, vmu.data(), vmu.size() * sizeof(float), cudaMemcpyHostToDevice));
     e->vmu_all = static_cast<float *>(pv);
+    NQ_CUDA(cudaMalloc(&pz, d * sizeof(float)));
+    e->dev_allocs.push_back(pz);
+    NQ_CUDA(cudaMemset(pz, 0, d * sizeof(float)));
+    e->zero_d = static_cast<float *>(pz);
   }
   NQ_TRY(nq_weight_keep_bf16(e->pw3, 1));
   NQ_TRY(nq_weight_keep_bf16(e->pw6, 1));
@@ -496,7 +509,7 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
     // MHSA with relative positions -> norm_conv
     NQ_TRY(nq_linear(L.qkv, h, NQ_BF16, M, D, L.qkv_b, NQ_EPI_NONE, A.qkv.p, NQ_BF16, 3 * D, stv));
     NQ_TRY(nq::relpos_attention(A.qkv.as<__nv_bfloat16>(), A.krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
-                                static_cast<int64_t>(c.n_layers) * D, L.bias_u, L.bias_v,
+                                static_cast<int64_t>(c.n_layers) * D, e->zero_d, e->vmu_all + static_cast<size_t>(li) * D,
                                 att_tc ? A.vrel.as<float>() + static_cast<size_t>(li) * H * (2 * Tp - 1) : nullptr,
                                 L3, s.B, Tp, H, D, A.att.as<__nv_bfloat16>(), st));
     NQ_TRY(nq_linear(L.o, A.att.p, NQ_BF16, M, D, L.o_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
