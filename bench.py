@@ -570,6 +570,9 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
             with open(tpath) as f:
                 tj = json.load(f)
             traffic, traffic_src = tj.get("traffic_bytes_per_launch"), tj.get("source")
+            if traffic is None and tj.get("traffic_bytes_per_gflop") and gemm["launches"]:
+                # scaled to this run's average launch by its algorithmic GFLOP
+                traffic = tj["traffic_bytes_per_gflop"] * gemm["flops"] / gemm["launches"] / 1e9
         line = {
             "metric": METRIC,
             "value": args.steps * audio_total / t_max,

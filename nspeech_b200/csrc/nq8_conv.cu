@@ -32,43 +32,73 @@ __device__ __forceinline__ float leaky(float v, float slope) { return v >= 0.f ?
 
 // rows[t][e] for e < c_in * K: x[ci][t * stride - pad + j * dil] with
 // ci = e / K, j = e % K (zero outside [0, t_in)); zero for e in [c_in * K, ld).
-// A thread writes 8 consecutive elements of one row (one 16-byte store for
-// bf16 rows, two for f32), walking (ci, j) incrementally; ld % 8 == 0.
-__global__ void im2col_kernel(const void *__restrict__ x, int x_dtype, int64_t ldx, int c_in, int t_in, int K,
-                              int stride, int pad, int dil, float slope, int t_out, int64_t ld, int a_dtype,
-                              void *__restrict__ rows) {
+// A block covers tt output rows and the channel chunk [ci0, ci0 + cb): the
+// cb x W input window it reads (W = (tt - 1) stride + (K - 1) dil + 1
+// samples) is staged once in shared memory -- loads coalesced along time,
+// leaky ReLU and zero padding applied -- and each row's segment
+// [ci0 K, (ci0 + cb) K) is written 8 elements (16 bytes of bf16) per thread.
+// The block of the last chunk also zero-fills [c_in K, ld).  ld % 8 == 0 and
+// cb K % 8 == 0 unless cb == c_in keep every 8-element group aligned.
+constexpr int kIcTTMax = 32;
+__global__ void __launch_bounds__(256) im2col_kernel(const void *__restrict__ x, int x_dtype, int64_t ldx, int c_in,
+                                                     int t_in, int K, int stride, int pad, int dil, float slope,
+                                                     int t_out, int64_t ld, int a_dtype, void *__restrict__ rows, int cb,
+                                                     int tt, int W, int pitch) {
   pdl_wait();
   pdl_trigger();
-  const int ck = c_in * K;
-  for (int t = blockIdx.y; t < t_out; t += gridDim.y) {
-    const int tbase = t * stride - pad;
-    for (int64_t e0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) * 8; e0 < ld;
-         e0 += static_cast<int64_t>(gridDim.x) * blockDim.x * 8) {
+  extern __shared__ float sx[];  // [cb][pitch]
+  const int ci0 = blockIdx.x * cb;
+  const int cbn = min(cb, c_in - ci0);
+  for (int t0 = blockIdx.y * tt; t0 < t_out; t0 += gridDim.y * tt) {
+    const int tb = t0 * stride - pad;
+    __syncthreads();  // the previous tile's window is no longer read
+    for (int idx = threadIdx.x; idx < cbn * W; idx += blockDim.x) {
+      const int cl = idx / W, w = idx - cl * W;
+      const int ti = tb + w;
+      sx[cl * pitch + w] =
+          (ti >= 0 && ti < t_in) ? leaky(load_x(x, x_dtype, static_cast<int64_t>(ci0 + cl) * ldx + ti), slope) : 0.f;
+    }
+    __syncthreads();
+    const int seg = cbn * K;                            // this chunk's elements of a row
+    const int64_t e_base = static_cast<int64_t>(ci0) * K;
+    const int64_t seg_w = ci0 + cbn == c_in ? ld - e_base : seg;  // the last chunk also pads the row
+    const int rows_here = min(tt, t_out - t0);
+    const int groups = static_cast<int>((seg_w + 7) / 8);
+    for (int g = threadIdx.x; g < rows_here * groups; g += blockDim.x) {
+      const int r = g / groups;
+      const int q = (g - r * groups) * 8;  // first element of the group within the segment
       float v[8];
-      int ci = static_cast<int>(e0 / K), j = static_cast<int>(e0 - static_cast<int64_t>(ci) * K);
+      int cl = q / K, j = q - cl * K;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        v[q] = 0.f;
-        if (e0 + q < ck) {
-          const int ti = tbase + j * dil;
-          if (ti >= 0 && ti < t_in) v[q] = leaky(load_x(x, x_dtype, static_cast<int64_t>(ci) * ldx + ti), slope);
-        }
+      for (int u = 0; u < 8; ++u) {
+        v[u] = q + u < seg ? sx[cl * pitch + r * stride + j * dil] : 0.f;
         if (++j == K) {
           j = 0;
-          ++ci;
+          ++cl;
         }
       }
+      const int64_t o = static_cast<int64_t>(t0 + r) * ld + e_base + q;
+      const int n = seg_w - q < 8 ? static_cast<int>(seg_w - q) : 8;
       if (a_dtype == 0) {
-        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(rows) + static_cast<int64_t>(t) * ld + e0);
-        dst[0] = make_float4(v[0], v[1], v[2], v[3]);
-        dst[1] = make_float4(v[4], v[5], v[6], v[7]);
+        float *dst = static_cast<float *>(rows) + o;
+        if (n == 8) {
+          reinterpret_cast<float4 *>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+          reinterpret_cast<float4 *>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+        } else {
+          for (int u = 0; u < n; ++u) dst[u] = v[u];
+        }
       } else {
-        uint4 pk;
-        pk.x = pack_bf16x2(v[0], v[1]);
-        pk.y = pack_bf16x2(v[2], v[3]);
-        pk.z = pack_bf16x2(v[4], v[5]);
-        pk.w = pack_bf16x2(v[6], v[7]);
-        *reinterpret_cast<uint4 *>(static_cast<__nv_bfloat16 *>(rows) + static_cast<int64_t>(t) * ld + e0) = pk;
+        __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(rows) + o;
+        if (n == 8) {
+          uint4 pk;
+          pk.x = pack_bf16x2(v[0], v[1]);
+          pk.y = pack_bf16x2(v[2], v[3]);
+          pk.z = pack_bf16x2(v[4], v[5]);
+          pk.w = pack_bf16x2(v[6], v[7]);
+          *reinterpret_cast<uint4 *>(dst) = pk;
+        } else {
+          for (int u = 0; u < n; ++u) dst[u] = __float2bfloat16_rn(v[u]);
+        }
       }
     }
   }
@@ -139,10 +169,26 @@ cudaError_t launch_im2col(const void *x, int x_dtype, int64_t ldx, int c_in, int
                           int dil, float slope, int t_out, int64_t ld, int a_dtype, void *rows, cudaStream_t s) {
   if (t_out == 0 || ld == 0) return cudaSuccess;
   if (ld % 8) return cudaErrorInvalidValue;
-  const int threads = 128;
-  const dim3 grid(static_cast<unsigned>((ld / 8 + threads - 1) / threads), static_cast<unsigned>(std::min(t_out, 65535)));
-  return launch_pdl(im2col_kernel, grid, dim3(threads), 0, s, 1, x, x_dtype, ldx, c_in, t_in, K, stride, pad, dil,
-                    slope, t_out, ld, a_dtype, rows);
+  if (static_cast<int64_t>(K - 1) * dil > 8192 || stride > 64) return cudaErrorInvalidValue;
+  // Channel chunk: 64 (a multiple of 8, so chunk boundaries keep rows 8-aligned)
+  // or all of c_in.  Time tile: 32 rows, halved (to 8) until the grid has
+  // about four blocks per SM, so the window loads of some blocks overlap the
+  // stores of others.
+  const int cb0 = c_in <= 64 ? c_in : 64;
+  const int chunks0 = (c_in + cb0 - 1) / cb0;
+  int tt = kIcTTMax;
+  while (tt > 8 && static_cast<int64_t>(chunks0) * ((t_out + tt - 1) / tt) < 4 * 148) tt /= 2;
+  const int W = (tt - 1) * stride + (K - 1) * dil + 1;
+  const int pitch = W | 1;  // odd: the taps of consecutive elements spread over the banks
+  int cb = cb0;  // halved while its window exceeds 48 KB
+  while (cb > 8 && static_cast<size_t>(cb) * pitch * 4 > 48 * 1024) cb /= 2;
+  if (cb < c_in && (cb * K) % 8) return cudaErrorInvalidValue;
+  const size_t smem = static_cast<size_t>(cb) * pitch * 4;
+  if (smem > 48 * 1024) return cudaErrorInvalidValue;
+  const dim3 grid(static_cast<unsigned>((c_in + cb - 1) / cb),
+                  static_cast<unsigned>(std::min((t_out + tt - 1) / tt, 65535)));
+  return launch_pdl(im2col_kernel, grid, dim3(256), smem, s, 1, x, x_dtype, ldx, c_in, t_in, K, stride, pad, dil,
+                    slope, t_out, ld, a_dtype, rows, cb, tt, W, pitch);
 }
 
 cudaError_t launch_transpose_out(const void *src, int src_dtype, int64_t lds, int rows_t, int cols_c, void *y,
