@@ -11,9 +11,9 @@ segments splits over GPUs with no exchange on the data path:
    B x T x (1 + ATTN_PER_FRAME x T), with T the padded encoder frames.
    - The first term is the per-token work: Q8_0 GEMMs, LayerNorm, convs.
    - The second is attention, which grows as T^2.
-   - ``ATTN_PER_FRAME`` comes from one B200 step of the configs[4] workload:
-     attention ~54 ms of 430 ms, with sum(B T) = 216,032 and
-     sum(B T^2) = 56.0 M.
+   - ``ATTN_PER_FRAME`` comes from one B200 step of the configs[4] workload
+     with the tcgen05 attention kernel: attention ~40 ms of 447 ms, with
+     sum(B T) = 216,032 and sum(B T^2) = 56.0 M.
 3. ``assign_lpt`` is greedy longest-processing-time. Buckets go out in
    decreasing cost, each to the rank with the least cost so far; ties go to
    the lower rank, and equal costs keep the lower bucket index first. It is
@@ -28,7 +28,7 @@ from __future__ import annotations
 import heapq
 from typing import Dict, List, Optional, Sequence
 
-ATTN_PER_FRAME = 5.5e-4
+ATTN_PER_FRAME = 3.8e-4
 
 
 def encoder_frames(mel_frames: int) -> int:
