@@ -436,7 +436,11 @@ __global__ void __launch_bounds__(32 * kReduceWarps) gemv_reduce_kernel(const __
 // slot order + bias; res_out = res_in + y (f32, stored); then the row's mean
 // and variance (fixed-order block sums) and out = (res_out - mean) * rstd *
 // gamma + beta.  The first CTA re-arms the GEMV's work counter.
-constexpr int kLnThreads = 256;
+// 1024 threads: rows of up to 1024 outputs (the decoders' d_model) give each
+// thread one output, whose unit partials it sums with 16 loads in flight --
+// the call is a chain of dependent L2 round trips, so parallelism is what
+// sets its latency.
+constexpr int kLnThreads = 1024;
 constexpr int kLnPerThread = kGemvLnMaxN / kLnThreads;
 
 __device__ __forceinline__ float block_sum_fixed(float v, float *red) {
@@ -471,17 +475,24 @@ __global__ void __launch_bounds__(kLnThreads) gemv_reduce_resadd_ln_kernel(const
     const int n = threadIdx.x + i * kLnThreads;
     float a = 0.f;
     if (n < N) {
-      // slots in index order, eight loads in flight
+      // slots in index order, sixteen loads in flight
       const float *q = src + n;
       int j = 0;
-      for (; j + 8 <= p.upt; j += 8) {
-        float t[8];
+      for (; j + 16 <= p.upt; j += 16) {
+        float t[16];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) t[e] = __ldcg(q + (j + e) * slot_stride);
+        for (int e = 0; e < 16; ++e) t[e] = __ldcg(q + (j + e) * slot_stride);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) a += t[e];
+        for (int e = 0; e < 16; ++e) a += t[e];
       }
-      for (; j < p.upt; ++j) a += __ldcg(q + j * slot_stride);
+      if (j < p.upt) {
+        float t[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) t[e] = j + e < p.upt ? __ldcg(q + (j + e) * slot_stride) : 0.f;
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          if (j + e < p.upt) a += t[e];
+      }
       if (pr.bias) a += pr.bias[n];
       a += rin[n];
       rout[n] = a;
