@@ -18,7 +18,7 @@
 // tile overlap the previous item's last tile and epilogue.  320 threads:
 //   warps 0-7  softmax: warp w owns TMEM lanes [32 (w % 4), +32) (query
 //              rows) and keys [32 (w / 4), +32) of every 64-key tile; the two
-//              warps of a row share one parked row and exchange row maxima.
+//              warps of a row exchange row maxima through shared memory.
 //   warp 8     TMA producers: lane 0 K, lane 1 V, lane 2 relative keys,
 //              lane 3 Q, each waiting only on its own ring; owns the TMEM.
 //   warp 9     MMA issuer (one elected thread).
@@ -32,10 +32,11 @@
 // window (base row P0 = Tp - 1 - i0 - 127); its tile 0 computes chunks 0..2,
 // tile t >= 1 only the new chunk t + 2, so every relative row is multiplied
 // once per item (the reference's full [T, 2T-1] product costs twice the
-// QK^T work; this costs the same as QK^T).  The two softmax threads of a row
-// park the 96 ring columns the row's diagonal band touches (plus vrel) in
-// the row's shared-memory line and each gathers band[i][jl - il + 127] for
-// its 32 scores.
+// QK^T work; this costs the same as QK^T).  Each softmax thread loads the
+// two 32-column ring chunks its row's diagonal band touches for its 32 keys,
+// adds vrel, and shifts them by (31 - lane) in registers with a five-stage
+// barrel shift (selects only), so band[i][jl - il + 127] lines up with its
+// scores without a trip through shared memory.
 // P = exp2(s - m) goes to shared memory as bf16 (K-major, 128-byte swizzle)
 // and O += P V runs with V as an MN-major operand straight from its TMA tile.
 // O is rescaled only when a row maximum grows by more than 2^8 (the
@@ -75,8 +76,8 @@ constexpr uint32_t kOffV = kOffK + 2 * kTile;  // 2 slots
 constexpr int kRSlots = 3;                     // relative-key ring: tile 0 of an item takes three chunks
 constexpr uint32_t kOffR = kOffV + 2 * kTile;
 constexpr uint32_t kOffP = kOffR + kRSlots * kTile;  // [128 rows x 64 keys] bf16
-constexpr int kParkPitch = 100;                      // floats per parked row (conflict-free)
-constexpr uint32_t kOffPark = kOffP + kTile;         // one row per query row: 96 band values
+constexpr int kParkPitch = 100;                      // floats per staging row (conflict-free)
+constexpr uint32_t kOffPark = kOffP + kTile;         // output staging: one row per query row
 constexpr uint32_t kOffRed = kOffPark + kBQ * kParkPitch * 4;
 constexpr uint32_t kRedBytes = (2 * 2 + 2) * kBQ * 4;  // row maxima [tile parity][key half][row], sums [half][row]
 constexpr uint32_t kOffBar = kOffRed + kRedBytes;
@@ -135,21 +136,6 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
-}
-
-// 32 TMEM words plus 32 vrel values -> this thread's parked row, floats
-// [col, col + 32).  Plain shared-memory accesses (no asm memory clobber), so
-// the compiler overlaps the broadcast vrel loads with the stores.
-__device__ __forceinline__ void park32(float *row, int col, const uint32_t (&r)[32], const float *vr) {
-  float4 *dst = reinterpret_cast<float4 *>(row + col);
-  const float4 *src = reinterpret_cast<const float4 *>(vr);  // same address in every lane: broadcast
-  float4 b[8];
-#pragma unroll
-  for (int x = 0; x < 8; ++x) b[x] = src[x];
-#pragma unroll
-  for (int x = 0; x < 8; ++x)
-    dst[x] = make_float4(__uint_as_float(r[4 * x]) + b[x].x, __uint_as_float(r[4 * x + 1]) + b[x].y,
-                         __uint_as_float(r[4 * x + 2]) + b[x].z, __uint_as_float(r[4 * x + 3]) + b[x].w);
 }
 
 // One work item: query rows [i0, i0 + 128) of head h in segment b, with nt
@@ -388,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q4) << 16);
     float *red_max = reinterpret_cast<float *>(smem + kOffRed);  // [2][2][128]
     float *red_l = red_max + 4 * kBQ;                            // [2][128]
-    float *park = reinterpret_cast<float *>(smem + kOffPark) + il * kParkPitch;  // shared by the row's two threads
+    float *park = reinterpret_cast<float *>(smem + kOffPark) + il * kParkPitch;  // the row's output staging line
     const int nrel = 2 * Tp - 1;
     const float sl2 = p.sl2;
     bool dead = false;  // warp-uniform: a wait gave up; no TMEM access from here on
@@ -434,34 +420,46 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kc0 = 2 * t + 3 - q4;
         const bool live = wait_all(kBarSFull + sb, (tau >> 1) & 1, kDevTimeoutConsumer);
         if (!live) dead = true;
-        uint32_t rs[32];
         if (live) {
           tc_fence_after();
-          uint32_t ra[32], rb[32];
-          if (kh == 0) {
-            tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kc0) & 7), ra);
-            tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kc0 + 1) & 7), rb);
-          } else {
-            tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kc0 + 2) & 7), ra);
-          }
+          // This thread's band values: window offsets (31 - lane) + 32 kh + jl,
+          // inside the two 32-column chunks kcA, kcA + 1 (ring chunk
+          // (2 g0 + kc) % 8), plus vrel of the same window columns.
+          const int kcA = kc0 + kh;
+          uint32_t a[64], rs[32];
+          tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kcA) & 7), *reinterpret_cast<uint32_t(*)[32]>(a));
+          tmem_ld32(tl + kTmBD + 32 * ((2 * g0 + kcA + 1) & 7), *reinterpret_cast<uint32_t(*)[32]>(a + 32));
           tmem_ld32(tl + kTmS + 64 * sb + 32 * kh, rs);
           tmem_ld_wait();
           tc_fence_before();
           mbar_arrive(bar(kBarSFree + sb));  // S buffer and this tile's ring reads are done
-          if (kh == 0) {
-            park32(park, 0, ra, vr_s + 32 * kc0);
-            park32(park, 32, rb, vr_s + 32 * (kc0 + 1));
-          } else {
-            park32(park, 64, ra, vr_s + 32 * (kc0 + 2));
+          float f[64];
+          const float4 *vr4 = reinterpret_cast<const float4 *>(vr_s + 32 * kcA);  // same address in every lane
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            const float4 b = vr4[x];
+            f[4 * x] = __uint_as_float(a[4 * x]) + b.x;
+            f[4 * x + 1] = __uint_as_float(a[4 * x + 1]) + b.y;
+            f[4 * x + 2] = __uint_as_float(a[4 * x + 2]) + b.z;
+            f[4 * x + 3] = __uint_as_float(a[4 * x + 3]) + b.w;
           }
-        }
-        named_bar_sync(pair_bar, 64);  // the row's 96 band values are parked
-        if (live) {
-          const int off = 31 + 32 * kh - lane;
+          // rel_shift in registers: f[jl] <- f[jl + 31 - lane], a five-stage
+          // barrel shift (selects only; register indices stay static).
+          const int sh = 31 - lane;
+#pragma unroll
+          for (int i = 0; i < 48; ++i) f[i] = (sh & 16) ? f[i + 16] : f[i];
+#pragma unroll
+          for (int i = 0; i < 40; ++i) f[i] = (sh & 8) ? f[i + 8] : f[i];
+#pragma unroll
+          for (int i = 0; i < 36; ++i) f[i] = (sh & 4) ? f[i + 4] : f[i];
+#pragma unroll
+          for (int i = 0; i < 34; ++i) f[i] = (sh & 2) ? f[i + 2] : f[i];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = (sh & 1) ? f[i + 1] : f[i];
           const int jbase = t * kBK + 32 * kh;
 #pragma unroll
           for (int jl = 0; jl < 32; ++jl) {
-            float v = (__uint_as_float(rs[jl]) + park[off + jl]) * sl2;
+            float v = (__uint_as_float(rs[jl]) + f[jl]) * sl2;
             v = jbase + jl < w.L ? v : -INFINITY;
             s[jl] = v;
             tmax = fmaxf(tmax, v);
