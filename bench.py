@@ -104,7 +104,8 @@ def parse_args():
     ap.add_argument("--keep-bf16", action="store_true", help="--linear: kept bf16 weight copies (as the encoder)")
     ap.add_argument("--sweep-m", default="", help="--linear: comma-separated subset of the sweep's M values")
     ap.add_argument("--unit-tokens", default="0",
-                    help="--linear: GEMM unit widths to time each shape with (nq_set_gemm_unit_tokens; 0 = default)")
+                    help="GEMM unit width (nq_set_gemm_unit_tokens; 0 = the cost model's choice); "
+                         "--linear: comma-separated widths to time each shape with")
     ap.add_argument("--qtiled", action="store_true", help="--linear: weights with QTiled semantics (from_qtensor)")
     ap.add_argument("--conv", action="store_true",
                     help="time the Kokoro generator's conv1d / conv_transpose1d shapes (nq_conv*) instead")
@@ -188,6 +189,7 @@ def workload_config(args, world: int, plan, spec) -> dict:
                  f"{spec.n_heads} heads, FFN {spec.d_model * spec.ff_mult}, conv {spec.conv_kernel})",
         "segments_per_gpu": segs, "shard": args.shard, "max_batch": args.max_batch, "audio_s_per_gpu": audio_s,
         "buckets": len(plan), "streams": max(1, args.streams), "attention": args.attention,
+        "gemm_unit_tokens": int(args.unit_tokens.split(",")[0]) or "auto",
         "seq_len": max(encoder_frames(max(ls)) for _, ls in plan),
         "global_batch": args.segments if args.shard == "lpt" else args.segments * world,
         "parallelism": f"dp{world} (segment-sharded, no collective on the data path)",
@@ -442,6 +444,7 @@ def run_ours(args, rank: int, world: int, local_rank: int) -> None:
     lib.check(lib.load().nq_set_gemm_tail_split(args.tail_split))
     lib.check(lib.load().nq_set_attention_kernel(
         lib.NQ_ATTENTION_TCGEN05 if args.attention == "tcgen05" else lib.NQ_ATTENTION_MMA_SYNC))
+    lib.check(lib.load().nq_set_gemm_unit_tokens(int(args.unit_tokens.split(",")[0])))
     spec = S.EncoderSpec(n_layers=args.layers)
     load_t = {}
     enc, tensors = make_encoder(spec, timings=load_t)

@@ -393,9 +393,10 @@ int nq_set_wait_limit(int64_t cycles);
 int nq_set_gemm_path(int path);
 
 /* Tokens per 2-SM work unit of the dequantize-once (bf16 tcgen05) GEMM: 64,
- * 128 or 256, or 0 for the default (256).  No counterpart in the reference: a
- * B200 dispatch knob.  Narrower units give calls of a few thousand tokens
- * more units.  Process-wide; returns NQ_ERR_ARG for other values. */
+ * 128 or 256, or 0 (default) for a per-call choice by a cost model (narrower
+ * units give calls with few 256-token tiles more units for the SM pairs).
+ * No counterpart in the reference: a B200 dispatch knob.  Process-wide;
+ * returns NQ_ERR_ARG for other values. */
 int nq_set_gemm_unit_tokens(int tokens);
 
 /* Tail split of the dequantize-once GEMM.  No counterpart in the reference: a
@@ -405,7 +406,9 @@ int nq_set_gemm_unit_tokens(int tokens);
  * adds the pieces in piece order (deterministic) and writes the output, in
  * the same launch.  0 (default): a cost model decides per call; 1: never;
  * 2..16: that many pieces whenever a partial round exists (tests).  Results
- * differ from the unsplit sums only by f32 summation order.  Process-wide. */
+ * differ from the unsplit sums only by f32 summation order.  A forced piece
+ * count also selects 256-token units (the tail split's width) unless
+ * nq_set_gemm_unit_tokens sets one.  Process-wide. */
 int nq_set_gemm_tail_split(int mode);
 
 /* Which kernel runs the encoder's relative-position attention.  No

@@ -423,15 +423,79 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
 // ------------------------------------------------------------------ GEMM
 // How one GEMM call (M > 16) is carried out.
 struct GemmPlan {
-  bool deq;        // dequantize-once path (dequant_tiles + K3), else fused K1
-  bool cached;     // deq with the weight's kept bf16 copy: no dequantize launch
-  bool split_x;    // activations staged to bf16 planes first (f32, or unaligned bf16)
-  int bt;          // tokens per pair unit
-  int grid_m, grid_n, splits, cps, pairs;
+  bool deq = false;      // dequantize-once path (dequant_tiles + K3), else fused K1
+  bool cached = false;   // deq with the weight's kept bf16 copy: no dequantize launch
+  bool split_x = false;  // activations staged to bf16 planes first (f32, or unaligned bf16)
+  int bt = 256;          // tokens per pair unit
+  int grid_m = 0, grid_n = 0, splits = 1, cps = 0, pairs = 1;
   int full_units = 0, tail_pieces = 1, tail_cps = 0;  // K3 tail split (tail_pieces > 1)
   int tail_tiles() const { return tail_pieces > 1 ? grid_m * grid_n - full_units : 0; }
   int launches() const { return 1 + (deq && !cached ? 1 : 0) + (splits > 1 ? 1 : 0) + (split_x ? 1 : 0); }
 };
+
+// Measured time of one 64-wide k step of a pair unit in a full wave, by unit
+// width: it barely shrinks with the width, because the unit's 256-row weight
+// tile (32 KB per pair and step) streams whole whatever the token count.
+double unit_step_ns(int bt) { return bt >= 256 ? kNsPerUnitStep : bt >= 128 ? 360.0 : 330.0; }
+
+// The bf16 GEMM (K3) at unit width bt: split-K or tail split with the least
+// estimated time.  Full waves of units times their k steps, plus, when split,
+// one write and one read of the f32 partials and the reduction launch; the
+// tail split (256-token units) runs the R full rounds whole and cuts the L
+// tiles of the last, partial round into S k pieces on S x L <= pairs pairs,
+// the last piece of each tile summing them (no extra launch).  Returns the
+// estimate.
+double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp) {
+  GemmPlan &g = *gp;
+  g.bt = bt;
+  g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
+  const int tiles = g.grid_m * g.grid_n;
+  const double step = unit_step_ns(bt);
+  double best = 1e300;
+  const int max_splits = std::max(1, std::min(8, kc / 4));
+  for (int sp = 1; sp <= max_splits; ++sp) {
+    const int cps = (kc + sp - 1) / sp;
+    const int splits = (kc + cps - 1) / cps;
+    if (splits != sp) continue;
+    const int64_t units = static_cast<int64_t>(tiles) * splits;
+    const int64_t rounds = (units + g.pairs - 1) / g.pairs;
+    double t = static_cast<double>(rounds) * cps * step;
+    if (splits > 1) t += 2.0 * splits * static_cast<double>(m) * ldp * 4.0 / kReduceBytesPerNs + kReduceLaunchNs;
+    if (t < best) {
+      best = t;
+      g.splits = splits;
+      g.cps = cps;
+    }
+  }
+  const int R = tiles / g.pairs, L = tiles - R * g.pairs;
+  g.full_units = tiles;
+  g.tail_pieces = 1;
+  g.tail_cps = 0;
+  if (g.bt == 256 && g_tail_split != 1 && L > 0) {
+    const int s_cap = std::min(std::min(g.pairs / L, kc / 2), 16);
+    double best_tail = 1e300;
+    int pick = 1, pick_cps = kc;
+    for (int sp = 2; sp <= s_cap; ++sp) {
+      const int cps = (kc + sp - 1) / sp;
+      if ((kc + cps - 1) / cps != sp) continue;
+      const double t = (static_cast<double>(R) * kc + cps) * step + (sp + 1) * kTailFixupNsPerPiece;
+      if (g_tail_split >= 2 ? sp == g_tail_split : t < best_tail) {
+        best_tail = t;
+        pick = sp;
+        pick_cps = cps;
+      }
+    }
+    if (pick > 1 && (g_tail_split >= 2 || best_tail < best)) {
+      g.splits = 1;
+      g.cps = kc;
+      g.tail_pieces = pick;
+      g.tail_cps = pick_cps;
+      g.full_units = R * g.pairs;
+      best = best_tail;
+    }
+  }
+  return best;
+}
 
 // The fused kernel (K1) re-dequantizes the weight for every 192-token tile
 // and is issue-bound; the dequantize-once path is tensor-bound and wins from
@@ -461,58 +525,25 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
     g.splits = (kc + g.cps - 1) / g.cps;
     return g;
   }
-  // bf16 GEMM: pick the split factor with the least estimated time: full
-  // waves of 256 x 256 units times their k steps, plus, when split, one write
-  // and one read of the f32 partials and the reduction launch.
   const int ldp = w->n_tiles * nq::kPackRows;
-  g.bt = g_gemm_unit_tokens ? g_gemm_unit_tokens : nq::gemm_bf16_block_t();
-  g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
-  const int tiles = g.grid_m * g.grid_n;
-  double best = 1e300;
-  const int max_splits = std::max(1, std::min(8, kc / 4));
-  for (int sp = 1; sp <= max_splits; ++sp) {
-    const int cps = (kc + sp - 1) / sp;
-    const int splits = (kc + cps - 1) / cps;
-    if (splits != sp) continue;
-    const int64_t units = static_cast<int64_t>(tiles) * splits;
-    const int64_t rounds = (units + g.pairs - 1) / g.pairs;
-    // a k step of a unit scales with its token width (measured at 256)
-    double t = static_cast<double>(rounds) * cps * kNsPerUnitStep * g.bt / 256.0;
-    if (splits > 1) t += 2.0 * splits * static_cast<double>(m) * ldp * 4.0 / kReduceBytesPerNs + kReduceLaunchNs;
-    if (t < best) {
-      best = t;
-      g.splits = splits;
-      g.cps = cps;
+  if (g_gemm_unit_tokens || g_tail_split >= 2) {  // a forced tail split runs on 256-token units
+    plan_bf16_width(&g, g_gemm_unit_tokens ? g_gemm_unit_tokens : 256, m, kc, ldp);
+    return g;
+  }
+  // Unit width: the one with the least estimated time.  Narrow units give a
+  // call with few 256-token tiles more units for the SM pairs, at a k step
+  // that costs nearly as much (the weight tile streams whole either way).
+  GemmPlan best_plan = g;
+  double best_t = 1e300;
+  for (int bt : {256, 128, 64}) {
+    GemmPlan c = g;
+    const double t = plan_bf16_width(&c, bt, m, kc, ldp);
+    if (t < best_t) {
+      best_t = t;
+      best_plan = c;
     }
   }
-  // Tail split (256-token units): the R full rounds run whole tiles, the L
-  // tiles of the last, partial round run as S k pieces on S x L <= pairs
-  // pairs, and the last piece of each tile sums them (no extra launch).
-  const int R = tiles / g.pairs, L = tiles - R * g.pairs;
-  g.full_units = tiles;
-  if (g.bt == 256 && g_tail_split != 1 && L > 0) {
-    const int s_cap = std::min(std::min(g.pairs / L, kc / 2), 16);
-    double best_tail = 1e300;
-    int pick = 1, pick_cps = kc;
-    for (int sp = 2; sp <= s_cap; ++sp) {
-      const int cps = (kc + sp - 1) / sp;
-      if ((kc + cps - 1) / cps != sp) continue;
-      const double t = (static_cast<double>(R) * kc + cps) * kNsPerUnitStep + (sp + 1) * kTailFixupNsPerPiece;
-      if (g_tail_split >= 2 ? sp == g_tail_split : t < best_tail) {
-        best_tail = t;
-        pick = sp;
-        pick_cps = cps;
-      }
-    }
-    if (pick > 1 && (g_tail_split >= 2 || best_tail < best)) {
-      g.splits = 1;
-      g.cps = kc;
-      g.tail_pieces = pick;
-      g.tail_cps = pick_cps;
-      g.full_units = R * g.pairs;
-    }
-  }
-  return g;
+  return best_plan;
 }
 
 bool direct_bf16(const void *x, int x_dtype, int64_t ldx) {
