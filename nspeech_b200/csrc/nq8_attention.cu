@@ -76,9 +76,9 @@ constexpr uint32_t kOffV = kOffK + 2 * kTile;  // 2 slots
 constexpr int kRSlots = 3;                     // relative-key ring: tile 0 of an item takes three chunks
 constexpr uint32_t kOffR = kOffV + 2 * kTile;
 constexpr uint32_t kOffP = kOffR + kRSlots * kTile;  // [128 rows x 64 keys] bf16
-constexpr int kParkPitch = 100;                      // floats per staging row (conflict-free)
-constexpr uint32_t kOffPark = kOffP + kTile;         // output staging: one row per query row
-constexpr uint32_t kOffRed = kOffPark + kBQ * kParkPitch * 4;
+constexpr int kStagePitch = 100;                     // floats per staging row (conflict-free)
+constexpr uint32_t kOffStage = kOffP + kTile;        // output staging: one row per query row
+constexpr uint32_t kOffRed = kOffStage + kBQ * kStagePitch * 4;
 constexpr uint32_t kRedBytes = (2 * 2 + 2) * kBQ * 4;  // row maxima [tile parity][key half][row], sums [half][row]
 constexpr uint32_t kOffBar = kOffRed + kRedBytes;
 constexpr int kNumBars = 24;
@@ -374,7 +374,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tl = tmem + (static_cast<uint32_t>(32 * q4) << 16);
     float *red_max = reinterpret_cast<float *>(smem + kOffRed);  // [2][2][128]
     float *red_l = red_max + 4 * kBQ;                            // [2][128]
-    float *park = reinterpret_cast<float *>(smem + kOffPark) + il * kParkPitch;  // the row's output staging line
+    float *stage_row = reinterpret_cast<float *>(smem + kOffStage) + il * kStagePitch;  // the row's output staging line
     const int nrel = 2 * Tp - 1;
     const float sl2 = p.sl2;
     bool dead = false;  // warp-uniform: a wait gave up; no TMEM access from here on
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Item w = item_of(p, it);
       const int i = w.i0 + il;
       const int row0 = w.b * Tp;
-      // The previous item's parked rows, vrel window and staged outputs are
+      // The previous item's vrel window and staged outputs are
       // no longer read by any softmax warp.
       named_bar_sync(5, kSoftThreads);
       if (w.nt == 0) {
@@ -415,8 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float s[32];
         float tmax = -INFINITY;
         // Band chunks (32 columns) of this row: window chunks kc0 .. kc0 + 2
-        // (ring chunk (2 g0 + kc) % 8); the key-half-0 thread parks the first
-        // two, the key-half-1 thread the third.
+        // (ring chunk (2 g0 + kc) % 8); the key-half-0 thread reads the first
+        // two, the key-half-1 thread the last two.
         const int kc0 = 2 * t + 3 - q4;
         const bool live = wait_all(kBarSFull + sb, (tau >> 1) & 1, kDevTimeoutConsumer);
         if (!live) dead = true;
@@ -517,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(bar(kBarPReady));
       }
-      // ---- item epilogue: O / l as bf16, through this row's parked line
+      // ---- item epilogue: O / l as bf16, through this row's staging line
       if (!wait_all(kBarPvDone, (tau - 1) & 1, kDevTimeoutEpilogue)) dead = true;
       red_l[kh * kBQ + il] = l_part;
       named_bar_sync(pair_bar, 64);
@@ -532,9 +532,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         mbar_arrive(bar(kBarOFree));  // the next item's first PV may overwrite O
         // This thread's 64 outputs (row il, columns [64 kh, +64)) as bf16 into
-        // bytes [128 kh, +128) of its row's parked line, then the warp stores
+        // bytes [128 kh, +128) of its row's staging line, then the warp stores
         // its 32 rows 128 bytes at a time.
-        uint4 *stage = reinterpret_cast<uint4 *>(park) + 8 * kh;
+        uint4 *stage = reinterpret_cast<uint4 *>(stage_row) + 8 * kh;
         auto put = [&](int c, const uint32_t (&o)[32]) {
 #pragma unroll
           for (int q = 0; q < 4; ++q)
@@ -546,14 +546,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         put(0, oa);
         put(4, ob);
         __syncwarp();
-        const uint4 *wstage = reinterpret_cast<const uint4 *>(smem + kOffPark) + (32 * q4) * (kParkPitch / 4) + 8 * kh;
+        const uint4 *wstage = reinterpret_cast<const uint4 *>(smem + kOffStage) + (32 * q4) * (kStagePitch / 4) + 8 * kh;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const int r = 4 * k + (lane >> 3);  // row within the warp
           const int ri = w.i0 + 32 * q4 + r;
           if (ri < Tp)
             reinterpret_cast<uint4 *>(p.out + (static_cast<int64_t>(row0) + ri) * p.D + w.h * kHd + 64 * kh)[lane & 7] =
-                wstage[r * (kParkPitch / 4) + (lane & 7)];
+                wstage[r * (kStagePitch / 4) + (lane & 7)];
         }
       }
       g0 += w.nt + 2;
