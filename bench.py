@@ -767,28 +767,41 @@ def run_conv_sweep(args) -> None:
             flops = 2.0 * cin * cout * k * t_in
             call = lambda: C.conv_transpose1d(x, w, None, stride, pad, out=y)  # noqa: E731
         y = torch.empty(cout, t_out, device="cuda", dtype=torch.bfloat16)
-        s = torch.cuda.Stream()
-        with torch.cuda.stream(s):
-            call()  # scratch sized before capture
-        torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        iters = 10
-        with torch.cuda.graph(g, stream=s):
-            for _ in range(iters):
-                call()
-        g.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(5):
+        implicit = kind == "c" and stride == 1 and cin % 64 == 0 and t_out > 16
+
+        def graph_us():
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                call()  # scratch sized (and the weight's tap-major copy built) before capture
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            iters = 10
+            with torch.cuda.graph(g, stream=s):
+                for _ in range(iters):
+                    call()
             g.replay()
-        e1.record()
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) * 1e3 / (5 * iters)
-        rows.append({"conv": name, "c_in": cin, "c_out": cout, "k": k, "stride": stride, "t_in": t_in,
-                     "t_out": t_out, "us": round(us, 2), "tflops": round(flops / us / 1e6, 1),
-                     "frac_bf16_peak": round(flops / us / 1e6 / pk["bf16_tflops"], 3)})
-        del g
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(5):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            del g
+            return e0.elapsed_time(e1) * 1e3 / (5 * iters)
+
+        us = graph_us()
+        row = {"conv": name, "c_in": cin, "c_out": cout, "k": k, "stride": stride, "t_in": t_in,
+               "t_out": t_out, "path": "implicit" if implicit else ("im2col" if kind == "c" else "col2im"),
+               "us": round(us, 2), "tflops": round(flops / us / 1e6, 1),
+               "frac_bf16_peak": round(flops / us / 1e6 / pk["bf16_tflops"], 3)}
+        if implicit:  # the same call through the im2col lowering, for comparison
+            lib.check(lib.load().nq_set_conv_path(lib.NQ_CONV_IM2COL))
+            try:
+                row["us_im2col"] = round(graph_us(), 2)
+            finally:
+                lib.check(lib.load().nq_set_conv_path(lib.NQ_CONV_AUTO))
+        rows.append(row)
     if lib.status() != 0:
         raise RuntimeError("device status bits set after the conv sweep")
     print(json.dumps({"metric": "Kokoro generator conv1d / conv_transpose1d (nq_conv*), bf16 NCW",

@@ -232,7 +232,11 @@ int64_t nq_conv1d_out_len(int64_t t_in, int kernel, int stride, int padding, int
  * k = c_in * kernel): a Q8_0 weight, or a bf16-only one from
  * nq_weight_from_f32 when c_in * kernel is not a multiple of 32.  Lowered as
  * im2col -> nq_linear (tensor cores) -> transpose to NCW, the reference's GPU
- * lowering (im2col + matmul_bias).  Scratch: a per-stream conv workspace
+ * lowering (im2col + matmul_bias), or, for stride-1 convs with c_in a multiple
+ * of 64 and more than 16 output frames, as an implicit GEMM over a tap-major
+ * bf16 copy of the weight (nq_set_conv_path).  That copy is built and kept on
+ * the first such call with the weight, which therefore must not run under
+ * stream capture (NQ_ERR_UNSUPPORTED).  Scratch: a per-stream conv workspace
  * (grows with cudaMalloc on first use of a size).  Replaces
  * KokoroGpuBackend::conv1d / conv1d_k / conv1d_lrelu001 / im2col +
  * matmul_bias (src/kokoro/gpu_backend.rs:59-110; kernels conv1d_k and
@@ -420,6 +424,18 @@ int nq_set_gemm_tail_split(int mode);
 #define NQ_ATTENTION_TCGEN05 0
 #define NQ_ATTENTION_MMA_SYNC 1
 int nq_set_attention_kernel(int kernel);
+
+/* How nq_conv1d lowers a convolution.  No counterpart in the reference: a
+ * B200 dispatch knob.  AUTO (default): stride-1 convs whose c_in is a multiple
+ * of 64 with more than 16 output frames run as an implicit GEMM (token-major
+ * input planes, the weight's tap-major bf16 copy, shifted-row loads, NCW
+ * output from the GEMM epilogue); other convs as im2col + nq_linear +
+ * transpose.  IM2COL forces the second form (tests compare the two).
+ * Results differ by f32 summation order only.  Process-wide; returns
+ * NQ_ERR_ARG for other values. */
+#define NQ_CONV_AUTO 0
+#define NQ_CONV_IM2COL 1
+int nq_set_conv_path(int path);
 
 /* DEBUG ONLY -- a test hook for failure detection, not part of the matmul
  * API: launches a kernel that waits on an mbarrier nothing arrives on,

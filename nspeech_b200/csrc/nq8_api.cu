@@ -40,6 +40,12 @@ struct nq_weight {
   // a Q8_0 dequantization kept at bf16 precision (MatMul::from_tensor's
   // packing), or a transposed conv weight.  Every call runs the bf16 GEMM.
   bool bf16_only = false;
+  // Tap-major bf16 copy for the implicit conv1d, [n_tiles * 128][tap_k *
+  // tap_cin] with element (r, j tap_cin + ci) = W[r, ci tap_k + j]: built on the
+  // first nq_conv1d call that takes that path, freed with the weight.
+  mutable __nv_bfloat16 *tap = nullptr;
+  mutable int64_t tap_cin = 0;
+  mutable int tap_k = 0;
 };
 
 namespace {
@@ -77,6 +83,8 @@ int g_gemm_path = NQ_GEMM_AUTO;
 int g_gemm_unit_tokens = 0;  // 0: the kernel's default unit width
 int g_attention_kernel = NQ_ATTENTION_TCGEN05;
 int g_tail_split = 0;        // 0: cost model, 1: off, >= 2: that many pieces when a tail exists
+int g_conv_path = NQ_CONV_AUTO;
+std::mutex g_tap_mu;         // builds of weights' tap-major copies
 // Token count from which a GEMM call dequantizes the weight once and runs
 // the bf16 tensor-core GEMM (measured crossover on B200).
 constexpr int64_t kDequantMinM = 128;
@@ -445,14 +453,14 @@ double unit_step_ns(int bt) { return bt >= 256 ? kNsPerUnitStep : bt >= 128 ? 36
 // tiles of the last, partial round into S k pieces on S x L <= pairs pairs,
 // the last piece of each tile summing them (no extra launch).  Returns the
 // estimate.
-double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp) {
+double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp, bool splitk = true) {
   GemmPlan &g = *gp;
   g.bt = bt;
   g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
   const int tiles = g.grid_m * g.grid_n;
   const double step = unit_step_ns(bt);
   double best = 1e300;
-  const int max_splits = std::max(1, std::min(8, kc / 4));
+  const int max_splits = splitk ? std::max(1, std::min(8, kc / 4)) : 1;
   for (int sp = 1; sp <= max_splits; ++sp) {
     const int cps = (kc + sp - 1) / sp;
     const int splits = (kc + cps - 1) / cps;
@@ -497,6 +505,29 @@ double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp) {
   return best;
 }
 
+// Unit width of a bf16 GEMM call: the one with the least estimated time,
+// unless a width or a tail split is forced.  Narrow units give a call with
+// few 256-token tiles more units for the SM pairs, at a k step that costs
+// nearly as much (the weight tile streams whole either way).
+GemmPlan plan_bf16(const GemmPlan &g0, int64_t m, int kc, int ldp, bool splitk) {
+  GemmPlan g = g0;
+  if (g_gemm_unit_tokens || g_tail_split >= 2) {  // a forced tail split runs on 256-token units
+    plan_bf16_width(&g, g_gemm_unit_tokens ? g_gemm_unit_tokens : 256, m, kc, ldp, splitk);
+    return g;
+  }
+  GemmPlan best_plan = g;
+  double best_t = 1e300;
+  for (int bt : {256, 128, 64}) {
+    GemmPlan c = g;
+    const double t = plan_bf16_width(&c, bt, m, kc, ldp, splitk);
+    if (t < best_t) {
+      best_t = t;
+      best_plan = c;
+    }
+  }
+  return best_plan;
+}
+
 // The fused kernel (K1) re-dequantizes the weight for every 192-token tile
 // and is issue-bound; the dequantize-once path is tensor-bound and wins from
 // kDequantMinM tokens (measured on B200), unless a path is forced.
@@ -525,25 +556,7 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
     g.splits = (kc + g.cps - 1) / g.cps;
     return g;
   }
-  const int ldp = w->n_tiles * nq::kPackRows;
-  if (g_gemm_unit_tokens || g_tail_split >= 2) {  // a forced tail split runs on 256-token units
-    plan_bf16_width(&g, g_gemm_unit_tokens ? g_gemm_unit_tokens : 256, m, kc, ldp);
-    return g;
-  }
-  // Unit width: the one with the least estimated time.  Narrow units give a
-  // call with few 256-token tiles more units for the SM pairs, at a k step
-  // that costs nearly as much (the weight tile streams whole either way).
-  GemmPlan best_plan = g;
-  double best_t = 1e300;
-  for (int bt : {256, 128, 64}) {
-    GemmPlan c = g;
-    const double t = plan_bf16_width(&c, bt, m, kc, ldp);
-    if (t < best_t) {
-      best_t = t;
-      best_plan = c;
-    }
-  }
-  return best_plan;
+  return plan_bf16(g, m, kc, w->n_tiles * nq::kPackRows, true);
 }
 
 bool direct_bf16(const void *x, int x_dtype, int64_t ldx) {
@@ -691,6 +704,142 @@ int run_gemm(DeviceCtx *ctx, const LinearArgs &a, const void *x, int x_dtype, in
     cudaError_t e = nq::launch_splitk_reduce(r, stream);
     if (e != cudaSuccess) return cuda_fail(e, "split-K reduce launch");
   }
+  return NQ_OK;
+}
+
+// The tap-major copy of a conv weight for (c_in, kernel), built once on
+// `stream` (dequantizing Q8_0 tiles into scratch first when the weight keeps
+// no bf16 copy) and synchronized, so every stream may read it afterwards.
+int ensure_tap_copy(const nq_weight *w, int64_t c_in, int kernel, cudaStream_t stream, const __nv_bfloat16 **out) {
+  std::lock_guard<std::mutex> lk(g_tap_mu);
+  if (w->tap && w->tap_cin == c_in && w->tap_k == kernel) {
+    *out = w->tap;
+    return NQ_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &cs);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(NQ_ERR_UNSUPPORTED,
+                "nq_conv1d: the first call with a weight builds its tap-major copy and cannot run under stream "
+                "capture; call it once before capturing");
+  const int rows = w->n_tiles * nq::kPackRows;
+  const int64_t k_pad = static_cast<int64_t>(w->kc) * nq::kPackK;
+  const __nv_bfloat16 *src = w->bf16;
+  __nv_bfloat16 *tmp = nullptr, *dst = nullptr;
+  if (!src) {
+    e = cudaMalloc(&tmp, static_cast<size_t>(rows) * k_pad * 2);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(conv weight dequantize scratch)");
+    e = nq::launch_dequant_tiles(w->dev, w->n_tiles, w->kc, tmp, stream);
+    if (e != cudaSuccess) {
+      cudaFree(tmp);
+      return cuda_fail(e, "weight dequantize launch");
+    }
+    src = tmp;
+  }
+  e = cudaMalloc(&dst, static_cast<size_t>(rows) * kernel * c_in * 2);
+  if (e == cudaSuccess) e = nq::launch_conv_tap_weight(src, k_pad, rows, static_cast<int>(c_in), kernel, dst, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (tmp) cudaFree(tmp);
+  if (e != cudaSuccess) {
+    if (dst) cudaFree(dst);
+    return cuda_fail(e, "conv weight tap-major copy");
+  }
+  if (w->tap) {  // a copy for another (c_in, kernel) view of the same weight
+    e = cudaDeviceSynchronize();  // no launch in flight may still read it
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize(replace tap-major copy)");
+    cudaFree(w->tap);
+  }
+  w->tap = dst;
+  w->tap_cin = c_in;
+  w->tap_k = kernel;
+  *out = dst;
+  return NQ_OK;
+}
+
+// Implicit-GEMM conv1d (stride 1, channels in whole 64-wide k chunks): the
+// input goes to token-major bf16 planes once (leaky ReLU applied), and the
+// bf16 GEMM reads, for k chunk (tap j, channels c), the planes' rows shifted
+// by j dilation - padding (zero outside the input), against the weight's
+// tap-major copy; its epilogue writes the NCW output directly.  No im2col
+// rows and no output transpose.  Split-K is not used (the tail split is).
+int conv1d_implicit(DeviceCtx *ctx, const nq_weight *w, const void *x, int x_dtype, int64_t c_in, int64_t t_in,
+                    int64_t ldx, int kernel, int padding, int dilation, float x_leaky, const float *bias, int epilogue,
+                    void *y, int y_dtype, int64_t ldy, int64_t t_out, cudaStream_t stream) {
+  const __nv_bfloat16 *wt = nullptr;
+  int rc = ensure_tap_copy(w, c_in, kernel, stream, &wt);
+  if (rc) return rc;
+  const bool splitx = x_dtype == NQ_F32;
+  const int kc = static_cast<int>(kernel * c_in / nq::kPackK);
+  const int ldp = w->n_tiles * nq::kPackRows;
+  GemmPlan g;
+  g.deq = true;
+  g.cached = true;
+  g.pairs = std::max(1, ctx->sm_count / 2);
+  g.grid_n = (w->n_tiles + 1) / 2;
+  const GemmPlan plan = plan_bf16(g, t_out, kc, ldp, false);
+  const int bt = plan.bt;
+  const size_t plane = align_up(static_cast<size_t>(t_in) * c_in * 2, 1024);
+  const size_t tail_bytes = static_cast<size_t>(plan.tail_tiles()) * plan.tail_pieces * 2 * 16 * (bt / 4) * 32 * 4;
+  if (kTailCounterBase + static_cast<size_t>(plan.tail_tiles()) * 2 * 16 > kCounterSlots)
+    return fail(NQ_ERR_SHAPE, "tail split needs more counters than the workspace holds");
+  Workspace *ws = nullptr;
+  rc = get_workspace(ctx, stream, plane * (splitx ? 2 : 1) + tail_bytes, &ws, true);
+  if (rc) return rc;
+  __nv_bfloat16 *hi = reinterpret_cast<__nv_bfloat16 *>(ws->buf);
+  __nv_bfloat16 *lo = splitx ? reinterpret_cast<__nv_bfloat16 *>(ws->buf + plane) : nullptr;
+  float *tail_part = tail_bytes ? reinterpret_cast<float *>(ws->buf + plane * (splitx ? 2 : 1)) : nullptr;
+  cudaError_t e = nq::launch_conv_tokens(x, x_dtype, ldx, static_cast<int>(c_in), static_cast<int>(t_in), x_leaky,
+                                         hi, lo, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "conv input launch");
+  CUtensorMap tm_w, tm_a, tm_alo;
+  rc = make_tmap(ctx, &tm_w, wt, static_cast<int64_t>(kc) * nq::kPackK, ldp, static_cast<int64_t>(kc) * nq::kPackK,
+                 nq::gemm_bf16_block_w() / 2);
+  if (rc) return rc;
+  rc = make_tmap(ctx, &tm_a, hi, c_in, t_in, c_in, nq::gemm_bf16_token_box(bt));
+  if (rc) return rc;
+  if (splitx) {
+    rc = make_tmap(ctx, &tm_alo, lo, c_in, t_in, c_in, nq::gemm_bf16_token_box(bt));
+    if (rc) return rc;
+  } else {
+    tm_alo = tm_a;
+  }
+  nq::GemmBf16Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.N = w->n;
+  p.n_rows = ldp;
+  p.n_out = w->n;
+  p.M = static_cast<int>(t_out);
+  p.kc_total = kc;
+  p.bias = bias;
+  p.epi = epilogue;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  p.ldy = ldy;
+  p.splits = 1;
+  p.cps = kc;
+  p.grid_n = plan.grid_n;
+  p.grid_m = plan.grid_m;
+  p.full_units = plan.full_units;
+  p.tail_pieces = plan.tail_pieces;
+  p.tail_cps = plan.tail_cps;
+  p.tail_part = tail_part;
+  p.tail_cnt = ws->counters + kTailCounterBase;
+  p.w_static = 1;
+  p.conv_cpt = static_cast<int>(c_in / nq::kPackK);
+  p.conv_dil = dilation;
+  p.conv_pad = padding;
+  p.y_cm = 1;
+  p.ctl.status = ctx->status;
+  p.ctl.wait_limit = g_wait_limit;
+  const int work_units = plan.tail_pieces > 1 ? plan.full_units + plan.tail_tiles() * plan.tail_pieces
+                                              : plan.grid_m * plan.grid_n;
+  const double flops = 2.0 * t_out * w->n * c_in * kernel;
+  const double bytes = static_cast<double>(ldp) * kc * nq::kPackK * 2 + t_in * c_in * (splitx ? 4.0 : 2.0) +
+                       t_out * w->n * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (bias ? 4.0 * w->n : 0.0);
+  ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
+  e = nq::launch_gemm_bf16(splitx, bt, tm_w, tm_a, tm_alo, p, std::min(work_units, plan.pairs), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "implicit conv GEMM launch");
   return NQ_OK;
 }
 
@@ -1045,6 +1194,7 @@ void nq_weight_free(nq_weight *w) {
   if (cur != w->device) cudaSetDevice(w->device);
   if (w->bf16) cudaFree(w->bf16);
   if (w->dev) cudaFree(w->dev);
+  if (w->tap) cudaFree(w->tap);
   if (cur != w->device) cudaSetDevice(cur);
   delete w;
 }
@@ -1091,6 +1241,9 @@ int nq_conv1d(const nq_weight *w, const void *x, int x_dtype, int64_t c_in, int6
   if (rc) return rc;
   if (w->device != dev) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (g_conv_path == NQ_CONV_AUTO && stride == 1 && c_in % nq::kPackK == 0 && t_out > 16 && !(w->flags & NQ_MODE_QTILED))
+    return conv1d_implicit(ctx, w, x, x_dtype, c_in, t_in, ldx, kernel, padding, dilation, x_leaky, bias, epilogue, y,
+                           y_dtype, ldy, t_out, s);
   // im2col rows in x's precision (f32 rows go through the GEMM's hi/lo path),
   // the GEMM's token-major output in y's.
   const int64_t k_pad = static_cast<int64_t>(w->kc) * nq::kPackK;
@@ -1425,6 +1578,13 @@ int nq_set_gemm_unit_tokens(int tokens) {
 int nq_set_gemm_tail_split(int mode) {
   if (mode < 0 || mode > 16) return fail(NQ_ERR_ARG, "tail split mode %d (0 auto, 1 off, 2..16 pieces)", mode);
   g_tail_split = mode;
+  return NQ_OK;
+}
+
+int nq_set_conv_path(int path) {
+  if (path != NQ_CONV_AUTO && path != NQ_CONV_IM2COL)
+    return fail(NQ_ERR_ARG, "conv path %d (0 auto, 1 im2col)", path);
+  g_conv_path = path;
   return NQ_OK;
 }
 

@@ -104,6 +104,56 @@ __global__ void __launch_bounds__(256) im2col_kernel(const void *__restrict__ x,
   }
 }
 
+// Token-major operand planes of the implicit conv1d: hi[t][c] =
+// bf16(leaky(x[c][t])), lo[t][c] = bf16(v - hi) (f32 x only).  A block moves
+// a 64-channel x 32-frame tile through shared memory: loads coalesced along
+// time, stores of whole 128-byte channel rows per frame.
+__global__ void __launch_bounds__(256) conv_tokens_kernel(const void *__restrict__ x, int x_dtype, int64_t ldx, int c_in,
+                                                          int t_in, float slope, __nv_bfloat16 *__restrict__ hi,
+                                                          __nv_bfloat16 *__restrict__ lo) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float tile[64][33];
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 64;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int c = ty; c < 64; c += 8) {
+    const int t = t0 + tx;
+    tile[c][tx] = t < t_in ? leaky(load_x(x, x_dtype, static_cast<int64_t>(c0 + c) * ldx + t), slope) : 0.f;
+  }
+  __syncthreads();
+  for (int r = ty; r < 32; r += 8) {
+    const int t = t0 + r;
+    if (t >= t_in) break;
+    const float v0 = tile[2 * tx][r], v1 = tile[2 * tx + 1][r];
+    const uint32_t h = pack_bf16x2(v0, v1);
+    const int64_t o = static_cast<int64_t>(t) * c_in + c0 + 2 * tx;
+    *reinterpret_cast<uint32_t *>(hi + o) = h;
+    if (lo) *reinterpret_cast<uint32_t *>(lo + o) = pack_bf16x2(v0 - bf16_bits_to_f32(h & 0xffffu), v1 - bf16_bits_to_f32(h >> 16));
+  }
+}
+
+// dst[r][j c_in + ci] = src[r][ci K + j]: eight consecutive destination
+// elements (one 16-byte store) per thread.
+__global__ void conv_tap_weight_kernel(const __nv_bfloat16 *__restrict__ src, int64_t ld_src, int rows, int c_in, int K,
+                                       __nv_bfloat16 *__restrict__ dst) {
+  const int64_t ld_dst = static_cast<int64_t>(K) * c_in;
+  const int64_t groups = static_cast<int64_t>(rows) * (ld_dst / 8);
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = g / (ld_dst / 8);
+    const int64_t e0 = (g - r * (ld_dst / 8)) * 8;
+    const int j = static_cast<int>(e0 / c_in);
+    const int ci0 = static_cast<int>(e0 - static_cast<int64_t>(j) * c_in);
+    const __nv_bfloat16 *s = src + r * ld_src + static_cast<int64_t>(ci0) * K + j;
+    uint16_t v[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) v[u] = reinterpret_cast<const uint16_t *>(s)[static_cast<int64_t>(u) * K];
+    *reinterpret_cast<uint4 *>(dst + r * ld_dst + e0) =
+        make_uint4(v[0] | (uint32_t(v[1]) << 16), v[2] | (uint32_t(v[3]) << 16), v[4] | (uint32_t(v[5]) << 16),
+                   v[6] | (uint32_t(v[7]) << 16));
+  }
+}
+
 // y[c][t] (ldy) = src[t][c] (lds): 32 x 32 tiles through shared memory.
 __global__ void transpose_out_kernel(const void *__restrict__ src, int src_dtype, int64_t lds, int rows_t, int cols_c,
                                      void *__restrict__ y, int y_dtype, int64_t ldy) {
@@ -189,6 +239,23 @@ cudaError_t launch_im2col(const void *x, int x_dtype, int64_t ldx, int c_in, int
                   static_cast<unsigned>(std::min((t_out + tt - 1) / tt, 65535)));
   return launch_pdl(im2col_kernel, grid, dim3(256), smem, s, 1, x, x_dtype, ldx, c_in, t_in, K, stride, pad, dil,
                     slope, t_out, ld, a_dtype, rows, cb, tt, W, pitch);
+}
+
+cudaError_t launch_conv_tokens(const void *x, int x_dtype, int64_t ldx, int c_in, int t_in, float slope,
+                               __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t s) {
+  if (t_in == 0) return cudaSuccess;
+  if (c_in % 64) return cudaErrorInvalidValue;
+  const dim3 grid((t_in + 31) / 32, c_in / 64);
+  return launch_pdl(conv_tokens_kernel, grid, dim3(256), 0, s, 1, x, x_dtype, ldx, c_in, t_in, slope, hi, lo);
+}
+
+cudaError_t launch_conv_tap_weight(const __nv_bfloat16 *src, int64_t ld_src, int rows, int c_in, int K,
+                                   __nv_bfloat16 *dst, cudaStream_t s) {
+  if (c_in % 8) return cudaErrorInvalidValue;
+  const int64_t groups = static_cast<int64_t>(rows) * K * c_in / 8;
+  if (groups == 0) return cudaSuccess;
+  conv_tap_weight_kernel<<<grid_for(groups, 256), 256, 0, s>>>(src, ld_src, rows, c_in, K, dst);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_transpose_out(const void *src, int src_dtype, int64_t lds, int rows_t, int cols_c, void *y,

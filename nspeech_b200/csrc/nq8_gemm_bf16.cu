@@ -208,17 +208,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t bar = map_rank(full(s), 0);
           const int kx = (un.kc0 + i) * kPackK;
+          int ax = kx, arow = trow0;  // token operand coordinates
+          if (p.conv_cpt) {
+            const int c = un.kc0 + i;
+            const int tap = c / p.conv_cpt;
+            ax = (c - tap * p.conv_cpt) * kPackK;
+            arow = trow0 + tap * p.conv_dil - p.conv_pad;
+          }
           // Weight rows past the matrix (odd tile count) and token rows past M
-          // are zero-filled by the TMA unit.
+          // (conv: outside the input) are zero-filled by the TMA unit.
           if (g >= pre) {  // else its expect_tx and weight load were issued before the wait
             if (rank == 0) mbar_arrive_expect_tx(full(s), 2 * C::kStageBytes);
             tma_load_2d_pair(smem_u32(stage_w(s)), &tm_w, bar, kx, wrow0);
           }
 #pragma unroll
           for (int t = 0; t < kNB; ++t) {  // token sub-tile t: unit tokens [t kMmaN, (t + 1) kMmaN)
-            tma_load_2d_pair(smem_u32(stage_b(s)) + t * C::kSubBytes, &tm_a, bar, kx, trow0 + t * kMmaN);
+            tma_load_2d_pair(smem_u32(stage_b(s)) + t * C::kSubBytes, &tm_a, bar, ax, arow + t * kMmaN);
             if (SPLITX)
-              tma_load_2d_pair(smem_u32(stage_blo(s)) + t * C::kSubBytes, &tm_alo, bar, kx, trow0 + t * kMmaN);
+              tma_load_2d_pair(smem_u32(stage_blo(s)) + t * C::kSubBytes, &tm_alo, bar, ax, arow + t * kMmaN);
           }
         }
       }
@@ -296,6 +303,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (quarters 2, 3); warps (q, cg) and (q + 2, cg) form pair `pr`.
     const int pr = (q & 1) * 4 + cg;
     float *gbuf = glu_s + pr * (kEc * 32);
+    // channel-major runs start at token multiples of kEc: 16-byte vector
+    // stores when every row start is 16-byte aligned
+    const int esz = p.y_dtype == 0 ? 4 : 2;
+    const bool y_vec = p.y_cm && (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && ((p.ldy * esz) & 15) == 0;
     int j = 0;
     for (int u = cl; u < n_units; u += ncl, ++j) {
       const Unit un = decode_unit(p, u);
@@ -318,6 +329,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int cols = max(0, min(kColsPerWarp, ((p.M - m0 + kEc - 1) / kEc) * kEc));
       const int tile = 2 * un.ft + static_cast<int>(rank);
       const int64_t n = static_cast<int64_t>(tile) * kPackRows + frow;  // packed row
+      // kEc tokens [tok, tok + kEc) of output feature f (bias b, epilogue
+      // applied): a token-major column, or a channel-major run.
+      auto emit = [&](int tok, int64_t f, const float (&v)[kEc], float b) {
+        const int valid = p.M - tok;
+        if (p.y_cm)
+          store_run_act(p.epi, p.y_dtype, p.y, f * p.ldy + tok, valid, y_vec, v, b);
+        else
+          store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(tok) * p.ldy + f, p.ldy, valid, v, b);
+      };
       auto fetch = [&](int col, float (&v)[kEc]) {
         uint32_t r[kEc];
         __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
@@ -371,8 +391,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int col = 0; col < cols && nvalid; col += kEc) {
               float v[kEc];
               sum_pieces(e, col, v);
-              const int valid = p.M - (m0 + col);
-              store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
+              emit(m0 + col, n, v, bn);
             }
           } else {
             // epilogue warp index of lane quarter qq in this column group
@@ -414,7 +433,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // stores (half the store instructions for one shuffle per token pair;
         // they pay when the epilogue is exposed, and cost ~1% of a multi-round
         // call, where it overlaps the next unit's main loop)
-        const bool paired = p.pair_stores && p.y_dtype == 1 && (p.ldy & 1) == 0 &&
+        const bool paired = p.pair_stores && !p.y_cm && p.y_dtype == 1 && (p.ldy & 1) == 0 &&
                             (reinterpret_cast<uintptr_t>(p.y) & 3) == 0 &&
                             static_cast<int64_t>(tile) * kPackRows + 32 * q + 32 <= p.N;
         for (int col = 0; col < cols; col += kEc) {
@@ -427,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             continue;
           }
           if (!nvalid) continue;
-          store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
+          emit(m0 + col, n, v, bn);
         }
       } else {
         const bool is_gate = q >= 2;

@@ -127,6 +127,14 @@ struct GemmBf16Params {
   int w_static;      // the weight is not written by any kernel of this stream (kept bf16 copy)
   int pair_stores;   // bf16 epilogue through lane pairs (4-byte stores); the host sets it when
                      // every unit runs in one round, where each unit's epilogue is exposed
+  // Implicit conv1d (stride 1): the token operand of k chunk c is the
+  // token-major input [t_in][channels] at channel offset 64 (c % conv_cpt),
+  // rows t + j conv_dil - conv_pad for output token t and tap j = c / conv_cpt
+  // (rows outside [0, t_in) read as zero).  conv_cpt = 0: a plain GEMM.
+  int conv_cpt;
+  int conv_dil;
+  int conv_pad;
+  int y_cm;          // channel-major output y[n][ldy] (NCW); no GLU, no split-K
   DevCtl ctl;
 };
 int gemm_bf16_block_t();              // default tokens per pair unit
@@ -189,6 +197,14 @@ cudaError_t launch_qtiled_quantize(const void *x, int x_dtype, int64_t ldx, int6
 cudaError_t launch_qtiled(const QtiledParams &p, cudaStream_t stream);
 
 // conv1d / conv_transpose1d glue (nq8_conv.cu).
+// Implicit conv1d operands: token-major planes hi[t][c] = bf16(leaky(x[c][t]))
+// (lo = bf16(v - hi) for f32 x; lo may be null), rows of c_in elements.
+cudaError_t launch_conv_tokens(const void *x, int x_dtype, int64_t ldx, int c_in, int t_in, float slope,
+                               __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t s);
+// Tap-major copy of a conv weight: dst[r][j c_in + ci] = src[r][ci K + j] for
+// rows r < rows (src rows ld_src elements, dst rows K c_in).
+cudaError_t launch_conv_tap_weight(const __nv_bfloat16 *src, int64_t ld_src, int rows, int c_in, int K,
+                                   __nv_bfloat16 *dst, cudaStream_t s);
 // rows[t][e] = leaky(x[e / K][t * stride - pad + (e % K) * dil]) for e < c_in * K,
 // zero up to ld; x NCW with row stride ldx; a_dtype 0 f32, 1 bf16.
 cudaError_t launch_im2col(const void *x, int x_dtype, int64_t ldx, int c_in, int t_in, int K, int stride, int pad,

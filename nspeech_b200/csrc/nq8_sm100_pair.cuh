@@ -205,6 +205,48 @@ __device__ __forceinline__ void store_pair_act(int epi, __nv_bfloat16 *pair_base
   }
 }
 
+// kEc consecutive tokens of one output feature, contiguous in y (a row of a
+// channel-major output): act(v + b), as 16-byte stores when `vec` (the run
+// starts 16-byte aligned) and all kEc tokens are valid, else per element.
+template <typename T, int EPI>
+__device__ __forceinline__ void store_run(T *base, int valid, bool vec, const float (&v)[kEc], float b) {
+  float a[kEc];
+#pragma unroll
+  for (int e = 0; e < kEc; ++e) a[e] = act_t<EPI>(v[e] + b);
+  if (vec && valid >= kEc) {
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+      for (int e = 0; e < kEc; e += 4)
+        *reinterpret_cast<float4 *>(reinterpret_cast<float *>(base) + e) = make_float4(a[e], a[e + 1], a[e + 2], a[e + 3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < kEc; e += 8)
+        *reinterpret_cast<uint4 *>(reinterpret_cast<__nv_bfloat16 *>(base) + e) =
+            make_uint4(pack_bf16x2(a[e], a[e + 1]), pack_bf16x2(a[e + 2], a[e + 3]), pack_bf16x2(a[e + 4], a[e + 5]),
+                       pack_bf16x2(a[e + 6], a[e + 7]));
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < kEc; ++e)
+      if (e < valid) put<T>(base + e, a[e]);
+  }
+}
+__device__ __forceinline__ void store_run_act(int epi, int y_dtype, void *y, int64_t off, int valid, bool vec,
+                                              const float (&v)[kEc], float b) {
+  float *yf = static_cast<float *>(y) + off;
+  __nv_bfloat16 *yb = static_cast<__nv_bfloat16 *>(y) + off;
+  switch (epi * 2 + y_dtype) {
+    case kEpiNone * 2 + 0: store_run<float, kEpiNone>(yf, valid, vec, v, b); break;
+    case kEpiNone * 2 + 1: store_run<__nv_bfloat16, kEpiNone>(yb, valid, vec, v, b); break;
+    case kEpiSilu * 2 + 0: store_run<float, kEpiSilu>(yf, valid, vec, v, b); break;
+    case kEpiSilu * 2 + 1: store_run<__nv_bfloat16, kEpiSilu>(yb, valid, vec, v, b); break;
+    case kEpiGeluErf * 2 + 0: store_run<float, kEpiGeluErf>(yf, valid, vec, v, b); break;
+    case kEpiGeluErf * 2 + 1: store_run<__nv_bfloat16, kEpiGeluErf>(yb, valid, vec, v, b); break;
+    case kEpiRelu * 2 + 0: store_run<float, kEpiRelu>(yf, valid, vec, v, b); break;
+    default: store_run<__nv_bfloat16, kEpiRelu>(yb, valid, vec, v, b); break;
+  }
+}
+
 __device__ __forceinline__ void store_glu_act(int epi, int y_dtype, void *y, int64_t off, int64_t ldy, int valid,
                                               const float (&v)[kEc], float b, const float (&g)[kEc]) {
   float *yf = static_cast<float *>(y) + off;

@@ -45,6 +45,9 @@ NQ_MODE_QTILED = 2
 NQ_ATTENTION_TCGEN05 = 0
 NQ_ATTENTION_MMA_SYNC = 1
 
+NQ_CONV_AUTO = 0
+NQ_CONV_IM2COL = 1
+
 
 class NqError(RuntimeError):
     """A non-zero status from libnq8 (carries the code and the library message)."""
@@ -122,6 +125,7 @@ SIGNATURES = {
     "nq_set_gemm_unit_tokens": (_I, [_I]),
     "nq_set_gemm_tail_split": (_I, [_I]),
     "nq_set_attention_kernel": (_I, [_I]),
+    "nq_set_conv_path": (_I, [_I]),
     "nq_set_wait_limit": (_I, [_I64]),
     "nq_debug_wait_timeout": (_I, [_P]),
 }

@@ -100,6 +100,124 @@ def test_conv1d_epilogue_bf16_out_and_strided_rows(nq, oracle):
     assert torch.isnan(ybig[:, 500:].float()).all()  # nothing written past the output length
 
 
+# Implicit-GEMM conv1d (stride 1, c_in a multiple of 64): (c_in, c_out, K,
+# padding, dilation, leaky, T_in).  Many token tiles with dilation 5; a short
+# sequence (tail split); c_out 22 (partial feature rows); no padding (T_out <
+# T_in); padding beyond the kernel's reach (rows outside the input on both
+# ends); 512 input channels.
+IMPLICIT = [(128, 128, 11, 25, 5, 0.1, 3000), (256, 256, 7, 9, 3, 0.1, 1000), (512, 256, 3, 1, 1, 1.0, 300),
+            (64, 22, 7, 3, 1, 0.01, 2000), (128, 64, 5, 0, 2, 1.0, 40), (64, 96, 3, 10, 1, 1.0, 150)]
+
+
+@pytest.mark.parametrize("cin,cout,k,pad,dil,leaky,t_in", IMPLICIT)
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_conv1d_implicit_matches_oracle_and_im2col(nq, oracle, cin, cout, k, pad, dil, leaky, t_in, dt):
+    """The implicit GEMM (default for these shapes) against the oracle and
+    against the im2col lowering (NQ_CONV_IM2COL) of the same weights; both
+    sum the same products in different orders.  Repeated calls are
+    bit-identical."""
+    from nspeech_b200 import conv as C
+    from nspeech_b200.fast_matmul import QWeight
+    L = nq.load()
+    rng = np.random.default_rng(cin + 3 * k + t_in)
+    w2 = (rng.standard_normal((cout, cin * k)) * 0.05).astype(np.float32)
+    q = oracle.quantize_q8_0(w2)
+    w = QWeight.from_q8_0(q, cout, cin * k)
+    wref = _bf16(oracle.dequant_q8_0(q, cout, cin * k)).reshape(cout, cin, k)
+    bias = (rng.standard_normal(cout) * 0.1).astype(np.float32)
+    x = rng.standard_normal((cin, t_in)).astype(np.float32)
+    tdt = torch.float32 if dt == "f32" else torch.bfloat16
+    if dt == "bf16":
+        x = _bf16(x)
+    xt = torch.from_numpy(x).cuda().to(tdt)
+    bt = torch.from_numpy(bias).cuda()
+    y = C.conv1d(xt, w, bt, k, 1, pad, dil, x_leaky=leaky, out_dtype=torch.float32)
+    y_again = C.conv1d(xt, w, bt, k, 1, pad, dil, x_leaky=leaky, out_dtype=torch.float32)
+    try:
+        nq.check(L.nq_set_conv_path(nq.NQ_CONV_IM2COL))
+        y_im2col = C.conv1d(xt, w, bt, k, 1, pad, dil, x_leaky=leaky, out_dtype=torch.float32)
+    finally:
+        nq.check(L.nq_set_conv_path(nq.NQ_CONV_AUTO))
+    torch.cuda.synchronize()
+    ref = oracle.conv1d_ref(x, wref, bias, 1, pad, dil, leaky)
+    assert y.shape == ref.shape
+    tol = 2e-3 if dt == "f32" else 1e-2
+    assert _err(oracle, y.cpu().numpy(), ref) <= tol
+    assert _err(oracle, y_im2col.cpu().numpy(), ref) <= tol
+    assert torch.equal(y, y_again)
+    # same bf16 products, f32 sums in another order
+    assert (y - y_im2col).abs().max().item() <= 1e-3 * max(1.0, y_im2col.abs().max().item())
+    assert nq.status() == 0
+
+
+@pytest.mark.parametrize("unit", [64, 128, 256])
+def test_conv1d_implicit_unit_widths_and_tail_split(nq, oracle, unit):
+    """Forced unit widths and a forced tail split give the oracle's result
+    on a short, wide conv (few token tiles)."""
+    from nspeech_b200 import conv as C
+    from nspeech_b200.fast_matmul import QWeight
+    L = nq.load()
+    rng = np.random.default_rng(unit)
+    cin, cout, k, pad, dil, t_in = 256, 512, 3, 1, 1, 300
+    w2 = (rng.standard_normal((cout, cin * k)) * 0.05).astype(np.float32)
+    q = oracle.quantize_q8_0(w2)
+    w = QWeight.from_q8_0(q, cout, cin * k)
+    wref = _bf16(oracle.dequant_q8_0(q, cout, cin * k)).reshape(cout, cin, k)
+    x = _bf16(rng.standard_normal((cin, t_in)).astype(np.float32))
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    ref = oracle.conv1d_ref(x, wref, None, 1, pad, dil)
+    outs = []
+    try:
+        nq.check(L.nq_set_gemm_unit_tokens(unit))
+        for split in (1, 4):
+            nq.check(L.nq_set_gemm_tail_split(split))
+            outs.append(C.conv1d(xt, w, None, k, 1, pad, dil, out_dtype=torch.float32))
+    finally:
+        nq.check(L.nq_set_gemm_unit_tokens(0))
+        nq.check(L.nq_set_gemm_tail_split(0))
+    torch.cuda.synchronize()
+    for y in outs:
+        assert _err(oracle, y.cpu().numpy(), ref) <= 1e-2
+    assert nq.status() == 0
+
+
+@pytest.mark.parametrize("pad_t", [0, 3])
+def test_conv1d_implicit_bf16_rows_and_graph(nq, oracle, pad_t):
+    """bf16 NCW output with 16-byte aligned rows (vector stores) and with
+    odd row padding (element stores), nothing written past the output length;
+    after a first call the conv replays inside a CUDA graph."""
+    from nspeech_b200 import conv as C
+    from nspeech_b200.fast_matmul import QWeight
+    rng = np.random.default_rng(11 + pad_t)
+    cin, cout, k, pad, dil, t_in = 128, 128, 7, 9, 3, 1200
+    w2 = (rng.standard_normal((cout, cin * k)) * 0.05).astype(np.float32)
+    q = oracle.quantize_q8_0(w2)
+    w = QWeight.from_q8_0(q, cout, cin * k)
+    wref = _bf16(oracle.dequant_q8_0(q, cout, cin * k)).reshape(cout, cin, k)
+    x = _bf16(rng.standard_normal((cin, t_in)).astype(np.float32))
+    xt = torch.from_numpy(x).cuda().to(torch.bfloat16)
+    t_out = C.conv1d_out_len(t_in, k, 1, pad, dil)
+    ybig = torch.full((cout, t_out + 8 + pad_t), float("nan"), device="cuda", dtype=torch.bfloat16)
+    y = ybig[:, :t_out]
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        C.conv1d(xt, w, None, k, 1, pad, dil, x_leaky=0.1, epilogue=nq.NQ_EPI_RELU, out=y, stream=s)
+    torch.cuda.synchronize()
+    ref = np.maximum(oracle.conv1d_ref(x, wref, None, 1, pad, dil, 0.1), 0.0)
+    assert _err(oracle, y.float().cpu().numpy(), ref) <= 1e-2
+    assert torch.isnan(ybig[:, t_out:].float()).all()
+    first = y.clone()
+    y.zero_()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        C.conv1d(xt, w, None, k, 1, pad, dil, x_leaky=0.1, epilogue=nq.NQ_EPI_RELU, out=y, stream=s)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, first)
+    del g
+    assert nq.status() == 0
+
+
 # Kokoro generator upsampling (ConvTranspose1d 512 -> 256, K 20, stride 10,
 # padding 5; 256 -> 128, K 12, stride 6, padding 3; leaky 0.1 on the input) and
 # a small one with output padding.
