@@ -110,6 +110,8 @@ def parse_args():
     ap.add_argument("--conv", action="store_true",
                     help="time the Kokoro generator's conv1d / conv_transpose1d shapes (nq_conv*) instead")
     ap.add_argument("--conv-frames", type=int, default=300, help="--conv: decoder frames (80 Hz) of the utterance")
+    ap.add_argument("--conv-only", default=None,
+                    help="--conv: time only the convs whose name contains this text (e.g. 'k11 d5')")
     ap.add_argument("--tail-split", type=int, default=0,
                     help="nq_set_gemm_tail_split mode of the GEMMs (0 cost model, 1 off, >= 2 pieces)")
     ap.add_argument("--attention", choices=["tcgen05", "mma_sync"], default="tcgen05",
@@ -751,6 +753,8 @@ def run_conv_sweep(args) -> None:
     rng = np.random.default_rng(0)
     rows = []
     for name, kind, cin, cout, k, stride, pad, dil, tmul in KOKORO_CONVS:
+        if args.conv_only and args.conv_only not in name:
+            continue
         t_in = args.conv_frames * tmul
         x = torch.randn(cin, t_in, device="cuda").to(torch.bfloat16)
         if kind == "c":

@@ -169,6 +169,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first ring stages before the dependency wait, during the previous
   // kernel's tail; the token halves of those stages follow after the wait.
   int pre = 0;
+  if (warp == 0 && lane == 0) {  // descriptors are launch parameters: fetch them before the wait
+    prefetch_tmap(&tm_a);
+    if (SPLITX) prefetch_tmap(&tm_alo);
+  }
   if (warp == 0 && lane == 0 && p.w_static) {
     prefetch_tmap(&tm_w);
     for (int u = cl; u < n_units && pre < kStages; u += ncl) {
@@ -329,15 +333,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int cols = max(0, min(kColsPerWarp, ((p.M - m0 + kEc - 1) / kEc) * kEc));
       const int tile = 2 * un.ft + static_cast<int>(rank);
       const int64_t n = static_cast<int64_t>(tile) * kPackRows + frow;  // packed row
-      // kEc tokens [tok, tok + kEc) of output feature f (bias b, epilogue
-      // applied): a token-major column, or a channel-major run.
-      auto emit = [&](int tok, int64_t f, const float (&v)[kEc], float b) {
-        const int valid = p.M - tok;
-        if (p.y_cm)
-          store_run_act(p.epi, p.y_dtype, p.y, f * p.ldy + tok, valid, y_vec, v, b);
-        else
-          store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(tok) * p.ldy + f, p.ldy, valid, v, b);
-      };
       auto fetch = [&](int col, float (&v)[kEc]) {
         uint32_t r[kEc];
         __syncwarp();  // tcgen05.ld is warp-collective: reconverge first
@@ -345,6 +340,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_ld_wait();
 #pragma unroll
         for (int x = 0; x < kEc; ++x) v[x] = __uint_as_float(r[x]);
+      };
+      // Channel-major output (y[n][ldy]) of this warp's columns; get(col, v)
+      // yields chunk col's sums of the lane's own row (warp-uniform calls).
+      // Whole, aligned groups of 64 bytes per row (16 f32 or 32 bf16 tokens)
+      // go through quad_transpose: each store writes 64 bytes of 8 rows.
+      // With 16 bf16 tokens per warp, lane pairs swap halves instead (32
+      // bytes of 16 rows per store).  Partial groups store element runs.
+      auto emit_cm = [&](auto &&get, float b, bool nvalid) {
+        const int gt = (p.y_dtype == 0 || kColsPerWarp < 2 * kEc) ? kEc : 2 * kEc;  // tokens per group
+        const int64_t row_q = static_cast<int64_t>(tile) * kPackRows + 32 * q;  // row of lane 0
+        if (row_q >= p.N) return;  // no output row in this lane quarter
+        for (int col = 0; col < cols; col += gt) {
+          const int valid = p.M - (m0 + col);
+          if (y_vec && valid >= gt && col + gt <= cols) {
+            uint4 a[4], unused0, unused1;
+            float v[kEc];
+            get(col, v);
+            act_segs(p.epi, p.y_dtype, v, b, a[0], a[1], a[2], a[3]);
+            if (gt == 2 * kEc) {
+              get(col + kEc, v);
+              act_segs(p.epi, p.y_dtype, v, b, a[2], a[3], unused0, unused1);
+            }
+            char *yb = static_cast<char *>(p.y);
+            if (p.y_dtype == 0 || gt == 2 * kEc) {
+              quad_transpose(a, lane);
+              const int64_t tok = m0 + col + (lane & 3) * (16 / esz);
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int64_t row = row_q + (lane & ~3) + j;
+                if (row < p.N) *reinterpret_cast<uint4 *>(yb + (row * p.ldy + tok) * esz) = a[j];
+              }
+            } else {
+              const bool odd = (lane & 1) != 0;
+              const uint4 r = shfl_xor_u4(odd ? a[0] : a[1], 1);
+              if (odd) a[0] = r;
+              else a[1] = r;
+              const int64_t tok = m0 + col + (lane & 1) * 8;
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const int64_t row = row_q + (lane & ~1) + j;
+                if (row < p.N) *reinterpret_cast<uint4 *>(yb + (row * p.ldy + tok) * esz) = a[j];
+              }
+            }
+          } else {
+            for (int c2 = col; c2 < cols && c2 < col + gt; c2 += kEc) {
+              float v[kEc];
+              get(c2, v);
+              if (nvalid)
+                store_run_act(p.epi, p.y_dtype, p.y, n * p.ldy + m0 + c2, p.M - (m0 + c2), y_vec, v, b);
+            }
+          }
+        }
       };
       if (un.tail >= 0) {
         // Tail piece: the raw accumulator goes to scratch and this warp
@@ -388,10 +435,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!p.glu) {
             const bool nvalid = n < p.N;
             const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
-            for (int col = 0; col < cols && nvalid; col += kEc) {
-              float v[kEc];
-              sum_pieces(e, col, v);
-              emit(m0 + col, n, v, bn);
+            if (p.y_cm) {
+              emit_cm([&](int col, float(&v)[kEc]) { sum_pieces(e, col, v); }, bn, nvalid);
+            } else {
+              for (int col = 0; col < cols && nvalid; col += kEc) {
+                float v[kEc];
+                sum_pieces(e, col, v);
+                const int valid = p.M - (m0 + col);
+                store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
+              }
             }
           } else {
             // epilogue warp index of lane quarter qq in this column group
@@ -426,6 +478,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int x = 0; x < kEc; ++x)
             if (x < valid) part[static_cast<size_t>(col + x) * p.n_rows] = v[x];
         }
+      } else if (!p.glu && p.y_cm) {
+        const bool nvalid = n < p.N;
+        emit_cm(fetch, (p.bias && nvalid) ? p.bias[n] : 0.f, nvalid);
       } else if (!p.glu) {
         const bool nvalid = n < p.N;
         const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
@@ -433,7 +488,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // stores (half the store instructions for one shuffle per token pair;
         // they pay when the epilogue is exposed, and cost ~1% of a multi-round
         // call, where it overlaps the next unit's main loop)
-        const bool paired = p.pair_stores && !p.y_cm && p.y_dtype == 1 && (p.ldy & 1) == 0 &&
+        const bool paired = p.pair_stores && p.y_dtype == 1 && (p.ldy & 1) == 0 &&
                             (reinterpret_cast<uintptr_t>(p.y) & 3) == 0 &&
                             static_cast<int64_t>(tile) * kPackRows + 32 * q + 32 <= p.N;
         for (int col = 0; col < cols; col += kEc) {
@@ -446,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             continue;
           }
           if (!nvalid) continue;
-          emit(m0 + col, n, v, bn);
+          store_act(p.epi, p.y_dtype, p.y, static_cast<int64_t>(m0 + col) * p.ldy + n, p.ldy, valid, v, bn);
         }
       } else {
         const bool is_gate = q >= 2;

@@ -247,6 +247,67 @@ __device__ __forceinline__ void store_run_act(int epi, int y_dtype, void *y, int
   }
 }
 
+// Channel-major output through lane quads.  A lane holds 64 contiguous bytes
+// of its own output row as four 16-byte segments (act(v + b) of kEc f32
+// tokens, or of 2 kEc bf16 tokens from two chunks); quad_transpose leaves lane
+// 4g + s with segment s of rows 4g .. 4g + 3, so that store j of the warp
+// writes 64 contiguous bytes of each of 8 rows (rows 4g + j) instead of 16
+// bytes of each of 32 rows: a quarter of the cache lines per store.
+template <int EPI>
+__device__ __forceinline__ void act_segs_t(int y_dtype, const float (&v)[kEc], float b, uint4 &s0, uint4 &s1,
+                                           uint4 &s2, uint4 &s3) {
+  float a[kEc];
+#pragma unroll
+  for (int e = 0; e < kEc; ++e) a[e] = act_t<EPI>(v[e] + b);
+  if (y_dtype == 0) {
+    s0 = make_uint4(__float_as_uint(a[0]), __float_as_uint(a[1]), __float_as_uint(a[2]), __float_as_uint(a[3]));
+    s1 = make_uint4(__float_as_uint(a[4]), __float_as_uint(a[5]), __float_as_uint(a[6]), __float_as_uint(a[7]));
+    s2 = make_uint4(__float_as_uint(a[8]), __float_as_uint(a[9]), __float_as_uint(a[10]), __float_as_uint(a[11]));
+    s3 = make_uint4(__float_as_uint(a[12]), __float_as_uint(a[13]), __float_as_uint(a[14]), __float_as_uint(a[15]));
+  } else {  // two segments; s2, s3 untouched
+    s0 = make_uint4(pack_bf16x2(a[0], a[1]), pack_bf16x2(a[2], a[3]), pack_bf16x2(a[4], a[5]), pack_bf16x2(a[6], a[7]));
+    s1 = make_uint4(pack_bf16x2(a[8], a[9]), pack_bf16x2(a[10], a[11]), pack_bf16x2(a[12], a[13]),
+                    pack_bf16x2(a[14], a[15]));
+  }
+}
+__device__ __forceinline__ void act_segs(int epi, int y_dtype, const float (&v)[kEc], float b, uint4 &s0, uint4 &s1,
+                                         uint4 &s2, uint4 &s3) {
+  switch (epi) {
+    case kEpiSilu: act_segs_t<kEpiSilu>(y_dtype, v, b, s0, s1, s2, s3); break;
+    case kEpiGeluErf: act_segs_t<kEpiGeluErf>(y_dtype, v, b, s0, s1, s2, s3); break;
+    case kEpiRelu: act_segs_t<kEpiRelu>(y_dtype, v, b, s0, s1, s2, s3); break;
+    default: act_segs_t<kEpiNone>(y_dtype, v, b, s0, s1, s2, s3); break;
+  }
+}
+__device__ __forceinline__ uint4 shfl_xor_u4(uint4 v, int d) {
+  return make_uint4(__shfl_xor_sync(0xffffffffu, v.x, d), __shfl_xor_sync(0xffffffffu, v.y, d),
+                    __shfl_xor_sync(0xffffffffu, v.z, d), __shfl_xor_sync(0xffffffffu, v.w, d));
+}
+// Lane s of each quad holds row s's segments a[0..3]; afterwards a[j] is
+// segment s of row j of the quad.
+__device__ __forceinline__ void quad_transpose(uint4 (&a)[4], int lane) {
+  const bool b1 = (lane & 2) != 0;
+  uint4 r0 = shfl_xor_u4(b1 ? a[0] : a[2], 2);
+  uint4 r1 = shfl_xor_u4(b1 ? a[1] : a[3], 2);
+  if (b1) {
+    a[0] = r0;
+    a[1] = r1;
+  } else {
+    a[2] = r0;
+    a[3] = r1;
+  }
+  const bool b0 = (lane & 1) != 0;
+  r0 = shfl_xor_u4(b0 ? a[0] : a[1], 1);
+  r1 = shfl_xor_u4(b0 ? a[2] : a[3], 1);
+  if (b0) {
+    a[0] = r0;
+    a[2] = r1;
+  } else {
+    a[1] = r0;
+    a[3] = r1;
+  }
+}
+
 __device__ __forceinline__ void store_glu_act(int epi, int y_dtype, void *y, int64_t off, int64_t ldy, int valid,
                                               const float (&v)[kEc], float b, const float (&g)[kEc]) {
   float *yf = static_cast<float *>(y) + off;
