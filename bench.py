@@ -941,11 +941,53 @@ def decode_step(rng, pk) -> dict:
     e1.record()
     torch.cuda.synchronize()
     us = e0.elapsed_time(e1) * 1e3 / (reps * tokens)
+    del gr
     floor_us = wbytes / pk["hbm_gbs"] / 1e3
     calls = layers * 6 + 1
+
+    # The same token as one decode-chain launch (nq_chain_*): the same calls
+    # recorded once per weight copy, then a graph of 8 chain runs.
+    from nspeech_b200.decode import DecodeChain
+    chains = []
+    for lay, head in nets:
+        c = DecodeChain(0)
+        for L in lay:
+            c.linear(L["qkv"], x[0], qkv[0])
+            c.gemv_resadd_ln(L["o"], qkv[0, :d], res[0], g, residual_out=res[0], out=h[0])
+            c.linear(L["cq"], h[0], qkv[0, :d])
+            c.gemv_resadd_ln(L["co"], qkv[0, :d], res[0], g, residual_out=res[0], out=h[0])
+            c.linear(L["fc1"], h[0], t[0], epilogue=lib.NQ_EPI_GLU_SILU)
+            c.gemv_resadd_ln(L["fc2"], t[0], res[0], g, residual_out=res[0], out=x[0])
+        c.linear(head, x[0], logits[0])
+        chains.append(c)
+    with torch.cuda.stream(s):
+        for c in chains:
+            c.run(s)  # uploads
+    torch.cuda.synchronize()
+    gc = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gc, stream=s):
+        for i in range(tokens):
+            chains[i % copies].run(s)
+    for _ in range(2):
+        gc.replay()
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        gc.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    us_chain = e0.elapsed_time(e1) * 1e3 / (reps * tokens)
+    del gc
+    for c in chains:
+        c.close()
+    if lib.status() != 0:
+        raise RuntimeError("device status bits set after the decode chain")
     return {"config": "configs[2] Moonshine decoder, M = 1, 14 layers + lm_head", "weight_mb_per_token":
-            round(wbytes / 1e6, 2), "us_per_token": round(us, 1), "hbm_floor_us": round(floor_us, 1),
-            "frac_of_floor": round(floor_us / us, 3), "gemv_calls_per_token": calls, "launches_per_token": 2 * calls}
+            round(wbytes / 1e6, 2), "hbm_floor_us": round(floor_us, 1), "gemv_calls_per_token": calls,
+            "op_by_op": {"us_per_token": round(us, 1), "frac_of_floor": round(floor_us / us, 3),
+                         "launches_per_token": 2 * calls},
+            "chain": {"us_per_token": round(us_chain, 1), "frac_of_floor": round(floor_us / us_chain, 3),
+                      "launches_per_token": 1}}
 
 
 def main():

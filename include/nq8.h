@@ -192,6 +192,43 @@ int nq_gemv_resadd_ln(const nq_weight *w, const void *x, int x_dtype, int64_t m,
                       const float *bias, const float *res_in, float *res_out, int64_t ld_res,
                       const float *ln_gamma, const float *ln_beta, float eps, void *norm_out,
                       int out_dtype, int64_t ld_out, void *stream);
+/* ---- decode chain ----------------------------------------------------------
+ * The dependent M = 1 projections of a decoder token (the calls of
+ * src/moonshine/decoder.rs through DecoderBackend::gemv and ::gemv_resadd_ln,
+ * src/moonshine/gpu_decoder.rs:67-70), recorded once and run as ONE
+ * cooperative kernel per token instead of two launches per call: a
+ * persistent grid streams every step's weights, waits on device counters
+ * between dependent steps, and computes the LayerNorm of a residual step in
+ * the CTAs of the step that reads it.  No counterpart in the reference; each
+ * step computes the corresponding nq_linear (M = 1) / nq_gemv_resadd_ln call
+ * -- the same bf16 weight products -- with f32 sums in another fixed order
+ * (deterministic; one CTA owns a whole 128-row tile).  Steps: Q8_0 weights
+ * (no QTiled, no bf16-only), K and a residual step's N at most 4096, x bf16
+ * (one row), y of a plain step
+ * f32 or bf16, a residual step's LayerNorm output bf16.  Buffers are bound by
+ * address when a step is added.  A step's input may be an external vector or
+ * any earlier step's output; inputs that equal the previous residual step's
+ * LayerNorm output are computed on load.  Rejected (NQ_ERR_UNSUPPORTED):
+ * a step whose input overlaps its outputs, two residual steps in a row, and a
+ * step that writes over the previous step's residual or LayerNorm output.
+ * The first nq_chain_run uploads the chain (allocations, not capturable);
+ * later runs are one launch each and may be captured in a CUDA graph.  Runs
+ * of one chain must not overlap.  After a device status error (a bounded wait
+ * ran out), nq_status re-arms the chain's counters. */
+typedef struct nq_chain nq_chain;
+int nq_chain_create(nq_chain **out);  /* on the current device */
+/* y = act(W x + bias), as nq_linear with M = 1. */
+int nq_chain_linear(nq_chain *c, const nq_weight *w, const void *x, const float *bias, int epilogue, void *y,
+                    int y_dtype);
+/* res_out = res_in + W x + bias; norm_out = LN(res_out) * gamma + beta (bf16),
+ * as nq_gemv_resadd_ln with M = 1 (res_out may be res_in; norm_out may be
+ * NULL when no later step or caller reads it). */
+int nq_chain_gemv_resadd_ln(nq_chain *c, const nq_weight *w, const void *x, const float *bias, const float *res_in,
+                            float *res_out, const float *ln_gamma, const float *ln_beta, float eps, void *norm_out);
+int nq_chain_steps(const nq_chain *c);
+int nq_chain_run(nq_chain *c, void *stream);
+void nq_chain_free(nq_chain *c);  /* no run of the chain may be in flight */
+
 /* No counterpart in the reference.  The GEMV of nq_linear (M <= 16 rows,
  * same arguments and result) without any allocation: its partial sums,
  * staged activations and work counter live in a static device array of this

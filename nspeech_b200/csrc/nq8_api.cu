@@ -48,6 +48,22 @@ struct nq_weight {
   mutable int tap_k = 0;
 };
 
+struct nq_chain {
+  int device = 0;
+  struct Range {
+    uintptr_t lo = 0, hi = 0;  // [lo, hi)
+    bool overlaps(const Range &o) const { return lo < o.hi && o.lo < hi; }
+  };
+  std::vector<nq::ChainStep> steps;
+  std::vector<Range> x_range, y_range, res_range;  // per step (empty ranges where absent)
+  double flops = 0, bytes = 0;
+  bool uploaded = false;
+  int ctas = 0;
+  nq::ChainStep *d_steps = nullptr;
+  int *d_counters = nullptr;  // completed tiles per step
+  size_t counter_bytes = 0;
+};
+
 namespace {
 
 constexpr int kMaxDevices = 64;
@@ -74,6 +90,9 @@ struct DeviceCtx {
   // Scratch of the conv entry points (im2col rows, GEMM outputs), separate from
   // `ws` so that the GEMM's own workspace growth cannot free it mid-call.
   std::map<cudaStream_t, Workspace> conv_ws;
+  // Counters of the decode chains on this device (re-zeroed with the
+  // workspace counters when a status bit reports a kernel that gave up).
+  std::map<int *, size_t> chain_counters;
 };
 
 DeviceCtx g_ctx[kMaxDevices];
@@ -1006,6 +1025,123 @@ int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_
 }  // namespace nq
 
 // ======================================================================= ABI
+namespace {
+int chain_add(nq_chain *c, const nq_weight *w, const void *x, const float *bias, int epilogue, void *y, int y_dtype,
+              const float *res_in, float *res_out, const float *ln_g, const float *ln_b, float eps) {
+  if (!c || !w || !x) return fail(NQ_ERR_ARG, "null argument");
+  if (c->uploaded) return fail(NQ_ERR_UNSUPPORTED, "nq_chain: steps cannot be added after the first run");
+  if (w->device != c->device) return fail(NQ_ERR_ARG, "weight lives on device %d, the chain on %d", w->device, c->device);
+  if (w->bf16_only || (w->flags & NQ_MODE_QTILED))
+    return fail(NQ_ERR_UNSUPPORTED, "nq_chain: Q8_0 weights with FbgemmBf16Op semantics only");
+  if (static_cast<int64_t>(w->kc) * nq::kPackK > nq::kChainMaxK)
+    return fail(NQ_ERR_SHAPE, "nq_chain: K = %lld exceeds %d", (long long)w->k, nq::kChainMaxK);
+  if (reinterpret_cast<uintptr_t>(x) % 2) return fail(NQ_ERR_ARG, "nq_chain: x must be 2-byte aligned bf16");
+  const bool resadd = res_out != nullptr;
+  const bool glu_w = (w->flags & NQ_PACK_GLU) != 0;
+  const bool glu_e = epilogue == NQ_EPI_GLU_SIGMOID || epilogue == NQ_EPI_GLU_SILU;
+  if (epilogue < NQ_EPI_NONE || epilogue > NQ_EPI_RELU) return fail(NQ_ERR_ARG, "unknown epilogue %d", epilogue);
+  if (glu_w != glu_e) return fail(NQ_ERR_ARG, "GLU epilogues need an NQ_PACK_GLU weight and vice versa");
+  if (y_dtype != NQ_F32 && y_dtype != NQ_BF16) return fail(NQ_ERR_DTYPE, "y dtype %d unsupported", y_dtype);
+  if (resadd) {
+    if (!res_in || !ln_g) return fail(NQ_ERR_ARG, "nq_chain_gemv_resadd_ln: null residual or gamma");
+    if (glu_w) return fail(NQ_ERR_ARG, "nq_chain_gemv_resadd_ln: GLU-packed weight");
+    if (w->n > nq::kChainMaxLnN) return fail(NQ_ERR_SHAPE, "nq_chain_gemv_resadd_ln: N exceeds %d", nq::kChainMaxLnN);
+    if (!(eps >= 0.f)) return fail(NQ_ERR_ARG, "nq_chain_gemv_resadd_ln: eps must be >= 0");
+  } else if (!y) {
+    return fail(NQ_ERR_ARG, "null output");
+  }
+  const int64_t n_out = glu_w ? w->n / 2 : w->n;
+  using R = nq_chain::Range;
+  const uintptr_t xa = reinterpret_cast<uintptr_t>(x), ya = reinterpret_cast<uintptr_t>(y);
+  const R xr{xa, xa + static_cast<uintptr_t>(w->k) * 2};
+  const R yr = y ? R{ya, ya + static_cast<uintptr_t>(n_out) * (y_dtype == NQ_F32 ? 4 : 2)} : R{};
+  const R rr = resadd ? R{reinterpret_cast<uintptr_t>(res_out), reinterpret_cast<uintptr_t>(res_out) + w->n * 4} : R{};
+  const R ri = resadd ? R{reinterpret_cast<uintptr_t>(res_in), reinterpret_cast<uintptr_t>(res_in) + w->n * 4} : R{};
+  // Hazards inside one step: its input is read while other CTAs already write its outputs.
+  if (xr.overlaps(yr) || xr.overlaps(rr)) return fail(NQ_ERR_UNSUPPORTED, "nq_chain: a step's input overlaps its output");
+  if (resadd && ri.lo != rr.lo && ri.overlaps(rr))
+    return fail(NQ_ERR_UNSUPPORTED, "nq_chain: res_in and res_out overlap without being the same row");
+  int x_ln = 0;
+  if (!c->steps.empty()) {
+    const size_t ps = c->steps.size() - 1;
+    const nq::ChainStep &pv = c->steps[ps];
+    if (pv.res_out) {
+      // The previous residual step's LayerNorm output is written while this
+      // step runs: this step reads it computed on load, and must not write it.
+      if (resadd) return fail(NQ_ERR_UNSUPPORTED, "nq_chain: two residual steps in a row");
+      const R &lr = c->y_range[ps];
+      if (pv.y && xa == lr.lo && w->k == pv.N) {
+        x_ln = 1;
+      } else if (xr.overlaps(lr)) {
+        return fail(NQ_ERR_UNSUPPORTED, "nq_chain: the input reads part of the previous step's LayerNorm output");
+      }
+      if (yr.overlaps(lr) || yr.overlaps(c->res_range[ps]))
+        return fail(NQ_ERR_UNSUPPORTED, "nq_chain: a step overwrites the previous step's residual or LayerNorm output");
+    }
+    for (size_t i = 0; i < c->steps.size(); ++i)
+      if (!x_ln && xr.overlaps(c->y_range[i]) && c->steps[i].y_dtype != NQ_BF16)
+        return fail(NQ_ERR_DTYPE, "nq_chain: the input reads an f32 output of step %zu", i);
+  }
+  nq::ChainStep st;
+  std::memset(&st, 0, sizeof(st));
+  st.w = w->dev;
+  st.n_tiles = w->n_tiles;
+  st.kc = w->kc;
+  st.N = w->n;
+  st.glu = glu_w ? 1 : 0;
+  st.n_out = n_out;
+  st.epi = epilogue;
+  st.bias = bias;
+  st.x_ln = x_ln;
+  st.x = static_cast<const __nv_bfloat16 *>(x);
+  st.K = static_cast<int>(w->k);
+  st.res_in = res_in;
+  st.res_out = res_out;
+  st.ln_g = ln_g;
+  st.ln_b = ln_b;
+  st.ln_eps = eps;
+  st.y = y;
+  st.y_dtype = y_dtype;
+  c->steps.push_back(st);
+  c->x_range.push_back(xr);
+  c->y_range.push_back(yr);
+  c->res_range.push_back(rr);
+  c->flops += 2.0 * w->n * w->k;
+  c->bytes += w->n * (w->k / 32) * 34.0 + w->k * 2.0 + n_out * (y_dtype == NQ_F32 ? 4.0 : 2.0);
+  return NQ_OK;
+}
+
+int chain_upload(nq_chain *c, DeviceCtx *ctx, cudaStream_t stream) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &cs);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(NQ_ERR_UNSUPPORTED, "nq_chain_run: the first run uploads the chain and cannot be captured");
+  e = nq::chain_max_ctas(ctx->sm_count, &c->ctas);
+  if (e != cudaSuccess) return cuda_fail(e, "chain occupancy");
+  // Tiles go round-robin over the CTAs, continuing from step to step.
+  int rot = 0;
+  for (auto &st : c->steps) {
+    st.rot = rot;
+    rot = (rot + st.n_tiles) % c->ctas;
+  }
+  const size_t n_steps = c->steps.size();
+  c->counter_bytes = n_steps * sizeof(int);
+  e = cudaMalloc(&c->d_counters, c->counter_bytes);
+  if (e == cudaSuccess) e = cudaMemset(c->d_counters, 0, c->counter_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&c->d_steps, n_steps * sizeof(nq::ChainStep));
+  if (e != cudaSuccess) return cuda_fail(e, "nq_chain_run: device buffers");
+  e = cudaMemcpy(c->d_steps, c->steps.data(), n_steps * sizeof(nq::ChainStep), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return cuda_fail(e, "nq_chain_run: upload");
+  {
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    ctx->chain_counters[c->d_counters] = c->counter_bytes;
+  }
+  c->uploaded = true;
+  return NQ_OK;
+}
+}  // namespace
+
 extern "C" {
 
 const char *nq_version(void) { return "nq8 0.1 sm_100a"; }
@@ -1445,6 +1581,75 @@ int nq_gemv_resadd_ln(const nq_weight *w, const void *x, int x_dtype, int64_t m,
   return run_gemv(ctx, &a, 1, x, x_dtype, m, ldx, NQ_EPI_NONE, out_dtype, static_cast<cudaStream_t>(stream), &rl);
 }
 
+int nq_chain_create(nq_chain **out) {
+  if (!out) return fail(NQ_ERR_ARG, "null argument");
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  int rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  nq_chain *c = new nq_chain;
+  c->device = dev;
+  *out = c;
+  return NQ_OK;
+}
+
+
+int nq_chain_linear(nq_chain *c, const nq_weight *w, const void *x, const float *bias, int epilogue, void *y,
+                    int y_dtype) {
+  return chain_add(c, w, x, bias, epilogue, y, y_dtype, nullptr, nullptr, nullptr, nullptr, 0.f);
+}
+
+int nq_chain_gemv_resadd_ln(nq_chain *c, const nq_weight *w, const void *x, const float *bias, const float *res_in,
+                            float *res_out, const float *ln_gamma, const float *ln_beta, float eps, void *norm_out) {
+  if (!res_out) return fail(NQ_ERR_ARG, "nq_chain_gemv_resadd_ln: null residual output");
+  return chain_add(c, w, x, bias, NQ_EPI_NONE, norm_out, NQ_BF16, res_in, res_out, ln_gamma, ln_beta, eps);
+}
+
+int nq_chain_steps(const nq_chain *c) { return c ? static_cast<int>(c->steps.size()) : NQ_ERR_ARG; }
+
+int nq_chain_run(nq_chain *c, void *stream) {
+  if (!c) return fail(NQ_ERR_ARG, "null chain");
+  if (c->steps.empty()) return NQ_OK;
+  DeviceCtx *ctx = nullptr;
+  int dev = 0;
+  int rc = current_ctx(&ctx, &dev);
+  if (rc) return rc;
+  if (dev != c->device) return fail(NQ_ERR_ARG, "the chain lives on device %d, current device is %d", c->device, dev);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (!c->uploaded) {
+    rc = chain_upload(c, ctx, s);
+    if (rc) return rc;
+  }
+  nq::ChainParams p;
+  p.steps = c->d_steps;
+  p.n_steps = static_cast<int>(c->steps.size());
+  p.ready = c->d_counters;
+  p.ctl.status = ctx->status;
+  p.ctl.wait_limit = g_wait_limit;
+  ProfScope ps(NQ_KCLASS_GEMV, s, c->flops, c->bytes);
+  cudaError_t e = nq::launch_chain(p, c->ctas, s);
+  if (e != cudaSuccess) return cuda_fail(e, "decode chain launch");
+  return NQ_OK;
+}
+
+void nq_chain_free(nq_chain *c) {
+  if (!c) return;
+  if (c->uploaded) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (cur != c->device) cudaSetDevice(c->device);
+    cudaDeviceSynchronize();  // no run may still read the step table or counters
+    {
+      std::lock_guard<std::mutex> lk(g_ctx[c->device].mu);
+      g_ctx[c->device].chain_counters.erase(c->d_counters);
+    }
+    cudaFree(c->d_steps);
+    cudaFree(c->d_counters);
+    if (cur != c->device) cudaSetDevice(cur);
+  }
+  delete c;
+}
+
 int nq_matmul(const nq_weight *w, const void *a, int a_dtype, void *c, int c_dtype, int64_t m, void *stream) {
   if (!w) return fail(NQ_ERR_ARG, "null weight");
   return nq_linear(w, a, a_dtype, m, w->k, nullptr, NQ_EPI_NONE, c, c_dtype, w->n, stream);
@@ -1508,6 +1713,7 @@ int nq_status(void *stream, int *bits) {
     std::lock_guard<std::mutex> lk(ctx->mu);
     for (auto &kv : ctx->ws)
       if (kv.second.counters) cudaMemset(kv.second.counters, 0, kCounterSlots * sizeof(int));
+    for (auto &kv : ctx->chain_counters) cudaMemset(kv.first, 0, kv.second);
     return fail(NQ_ERR_TIMEOUT, "device status 0x%x: a bounded wait in a kernel ran out", v);
   }
   return NQ_OK;

@@ -59,6 +59,46 @@ GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int m);
 // The GEMV (ctas CTAs) and its gemv_reduce: two launches.
 cudaError_t launch_gemv(const GemvParams &p, int ctas, cudaStream_t stream);
 
+// Decode chain (nq8_chain.cu): the dependent M = 1 GEMV steps of a decoder
+// token in one cooperative launch.  Step s reads a bf16 vector x (or, with
+// x_ln, the LayerNorm of step s - 1's residual row, computed on load) and
+// either stores y = act(W x + bias) (GLU for GLU-packed weights) or, with
+// res_out set, res_out = res_in + W x + bias; a residual step's LayerNorm
+// output (bf16, y) is stored by the CTA of the next step's tile 0, or by the
+// completer when it is the last step.  One CTA computes a whole 128-row tile.
+constexpr int kChainMaxK = 4096;  // input length a step stages in shared memory
+constexpr int kChainMaxLnN = 4096;
+struct ChainStep {
+  const uint8_t *w;  // packed Q8_0 tiles [n_tiles][kc]
+  int n_tiles, kc;
+  int64_t N;         // weight rows
+  int glu;
+  int64_t n_out;     // outputs: N, or N / 2 for GLU
+  int epi;
+  const float *bias;
+  int x_ln;          // input = LayerNorm of step s - 1's res_out
+  const __nv_bfloat16 *x;  // input vector (x_ln == 0)
+  int K;             // input length
+  const float *res_in;
+  float *res_out;    // residual step when set
+  const float *ln_g, *ln_b;
+  float ln_eps;
+  void *y;           // output, or a residual step's LayerNorm output (bf16); may be null for the latter
+  int y_dtype;
+  int rot;           // CTA of tile 0
+};
+struct ChainParams {
+  const ChainStep *steps;  // device array
+  int n_steps;
+  int *ready;              // [n_steps] completed tiles per step, zero between calls
+  DevCtl ctl;
+};
+size_t chain_smem_bytes();
+int chain_threads();
+// CTAs of one cooperative launch on this device (all resident at once).
+cudaError_t chain_max_ctas(int sm_count, int *ctas);
+cudaError_t launch_chain(const ChainParams &p, int ctas, cudaStream_t stream);
+
 // K1: fused Q8_0 GEMM (dequantizes in the kernel; best below a few thousand
 // tokens, where the weights dominate the traffic).
 struct GemmParams {

@@ -126,6 +126,12 @@ SIGNATURES = {
     "nq_set_gemm_tail_split": (_I, [_I]),
     "nq_set_attention_kernel": (_I, [_I]),
     "nq_set_conv_path": (_I, [_I]),
+    "nq_chain_create": (_I, [ctypes.POINTER(_P)]),
+    "nq_chain_linear": (_I, [_P, _P, _P, _P, _I, _P, _I]),
+    "nq_chain_gemv_resadd_ln": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_float, _P]),
+    "nq_chain_steps": (_I, [_P]),
+    "nq_chain_run": (_I, [_P, _P]),
+    "nq_chain_free": (None, [_P]),
     "nq_set_wait_limit": (_I, [_I64]),
     "nq_debug_wait_timeout": (_I, [_P]),
 }
