@@ -1119,11 +1119,20 @@ int chain_upload(nq_chain *c, DeviceCtx *ctx, cudaStream_t stream) {
     return fail(NQ_ERR_UNSUPPORTED, "nq_chain_run: the first run uploads the chain and cannot be captured");
   e = nq::chain_max_ctas(ctx->sm_count, &c->ctas);
   if (e != cudaSuccess) return cuda_fail(e, "chain occupancy");
-  // Tiles go round-robin over the CTAs, continuing from step to step.
-  int rot = 0;
+  // A step with no more tiles than clusters splits each tile's k over a
+  // cluster; larger steps give each tile to one CTA.  Owners go round-robin,
+  // continuing from step to step.
+  const int clusters = c->ctas / nq::kChainCluster;
+  int rot_cl = 0, rot_cta = 0;
   for (auto &st : c->steps) {
-    st.rot = rot;
-    rot = (rot + st.n_tiles) % c->ctas;
+    st.split = st.n_tiles <= clusters ? 1 : 0;
+    if (st.split) {
+      st.rot = rot_cl;
+      rot_cl = (rot_cl + st.n_tiles) % clusters;
+    } else {
+      st.rot = rot_cta;
+      rot_cta = (rot_cta + st.n_tiles) % c->ctas;
+    }
   }
   const size_t n_steps = c->steps.size();
   c->counter_bytes = n_steps * sizeof(int);

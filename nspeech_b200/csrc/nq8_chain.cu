@@ -38,6 +38,7 @@
 // status bit.
 #include "nq8_common.cuh"
 #include "nq8_kernels.h"
+#include "nq8_sm100_pair.cuh"
 
 namespace nq {
 namespace {
@@ -55,7 +56,9 @@ constexpr size_t kOffG = kOffX + kChainMaxK * 2;                           // f3
 constexpr size_t kOffTot = kOffG + kGroups * kPackRows * 4;               // f32 [128] tile sums
 constexpr size_t kOffRed = kOffTot + kPackRows * 4;                        // f32 [2][16] LayerNorm warp sums
 constexpr size_t kOffBars = kOffRed + 2 * kConsumerWarps * 4;              // full, empty
-constexpr size_t kOffFlags = kOffBars + 2 * kChainStages * 8;              // int [4] flags, int [16] votes
+constexpr size_t kOffPBar = kOffBars + 2 * kChainStages * 8;               // cluster partials barrier
+constexpr size_t kOffPSlot = kOffPBar + 8;                                 // f32 [kCluster - 1][128]
+constexpr size_t kOffFlags = kOffPSlot + (kChainCluster - 1) * kPackRows * 4;  // int [4] flags, int [16] votes
 constexpr size_t kChainSmem = kOffFlags + (4 + kConsumerWarps) * 4;
 constexpr int kConsumerBar = 1;  // named barrier of the consumer warps
 // Drain limit: a CTA leaves only when its bulk copies have landed, which
@@ -113,9 +116,46 @@ __device__ __forceinline__ float neg1152(uint16_t d16) {
   return c;
 }
 
+// The first tile of step st this CTA works on, and the tile stride: split
+// steps go to clusters (all ranks of a cluster on the same tile), the other
+// steps to single CTAs.
 __device__ __forceinline__ int first_tile(const ChainStep &st, int cta, int grid) {
-  int t = (cta - st.rot) % grid;
-  return t < 0 ? t + grid : t;
+  const int owner = st.split ? cta / kChainCluster : cta;
+  const int owners = st.split ? grid / kChainCluster : grid;
+  int t = (owner - st.rot) % owners;
+  return t < 0 ? t + owners : t;
+}
+__device__ __forceinline__ int tile_stride(const ChainStep &st, int grid) {
+  return st.split ? grid / kChainCluster : grid;
+}
+
+// try_wait with cluster-scope acquire: the arrivals are releases of other
+// CTAs of the cluster, after their stores to this CTA's shared memory.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ bool wait_partials(uint32_t bar, uint32_t parity, const DevCtl &ctl, volatile int *abort) {
+  long long t0 = 0;
+  for (int it = 0;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (*abort || status_set(ctl)) return false;
+    if (it == 0) {
+      t0 = clock64();
+    } else if (clock64() - t0 > ctl.wait_limit) {
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void st_cluster_f32(uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -205,6 +245,9 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
   float *tot = reinterpret_cast<float *>(smem + kOffTot);
   float *red = reinterpret_cast<float *>(smem + kOffRed);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kOffBars);
+  uint64_t *pbar = reinterpret_cast<uint64_t *>(smem + kOffPBar);  // rank 0: the other ranks' partials landed
+  float *pslot = reinterpret_cast<float *>(smem + kOffPSlot);      // rank 0: [rank - 1][128] partial tile sums
+  const uint32_t rank = cluster_ctarank();
   // [0] abort (any role of this CTA)  [1] input ready  [2] tile count
   volatile int *flags = reinterpret_cast<volatile int *>(smem + kOffFlags);
   volatile int *vote = flags + 4;  // [16] per consumer warp: its part of the tile completed
@@ -218,10 +261,12 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), kRowWarps);  // the k group's four warps
     }
+    mbar_init(smem_u32(pbar), (kChainCluster - 1) * kPackRows);  // one arrival per row of each other rank
     flags[0] = 0;
     fence_mbar_init();
   }
   __syncthreads();
+  cluster_sync_all();  // every CTA's barriers exist before a remote arrive
 
   if (warp == 0) {
     if (lane == 0) {
@@ -232,9 +277,10 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
       bool ok = true;
       for (int si = 0; si < p.n_steps && ok; ++si) {
         const ChainStep &st = p.steps[si];
-        for (int T = first_tile(st, cta, grid); T < st.n_tiles && ok; T += grid) {
-          const uint8_t *src = st.w + static_cast<size_t>(T) * st.kc * kTileBytes;
-          for (int ch = 0; ch < st.kc; ++ch, src += kTileBytes) {
+        const int c0 = st.split ? static_cast<int>(rank) : 0, cstep = st.split ? kChainCluster : 1;
+        for (int T = first_tile(st, cta, grid); T < st.n_tiles && ok; T += tile_stride(st, grid)) {
+          for (int ch = c0; ch < st.kc; ch += cstep) {
+            const uint8_t *src = st.w + (static_cast<size_t>(T) * st.kc + ch) * kTileBytes;
             if (issued >= S && !chain_wait(empty_bar(s), ph ^ 1u, p.ctl, flags)) {
               if (!flags[0]) report(p.ctl, flags, kDevTimeoutProducer);
               ok = false;
@@ -275,7 +321,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
       sofs[b][0] = scale_offset(32 * rw + 8 * b + g4, 0);
       sofs[b][1] = scale_offset(32 * rw + 8 * b + g4, 1);
     }
-    int q = 0;  // chunk sequence number of this CTA (stage q % S)
+    int q = 0;       // chunk sequence number of this CTA (stage q % S)
+    int nsplit = 0;  // split tiles this CTA has worked on (rank 0: phase of pbar)
     bool ok = true;
     for (int si = 0; si < p.n_steps && ok; ++si) {
       const ChainStep &st = p.steps[si];
@@ -300,7 +347,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
       if (st.x_ln) {
         const ChainStep &rs = p.steps[si - 1];
         // the CTA of tile 0 also stores the LayerNorm output for later readers
-        ln_stage(rs, xs, red, T == 0 ? static_cast<__nv_bfloat16 *>(rs.y) : nullptr);
+        ln_stage(rs, xs, red, T == 0 && rank == 0 ? static_cast<__nv_bfloat16 *>(rs.y) : nullptr);
         kin = static_cast<int>(rs.N);
       } else {
         x_stage(st, xs);
@@ -308,7 +355,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
       }
       for (int k = kin + ct; k < kpad; k += kConsumers) xs[k] = __float2bfloat16_rn(0.f);
       named_bar_sync(kConsumerBar, kConsumers);
-      for (; T < st.n_tiles && ok; T += grid) {
+      const int c0 = st.split ? static_cast<int>(rank) : 0, cstep = st.split ? kChainCluster : 1;
+      for (; T < st.n_tiles && ok; T += tile_stride(st, grid)) {
         float acc[2][4];
 #pragma unroll
         for (int gi = 0; gi < 2; ++gi)
@@ -318,8 +366,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
         // barrier, where the warps vote and leave together (named barriers
         // have no time limit).
         bool wok = true;
-        for (int ch = 0; ch < st.kc; ++ch, ++q) {
-          if (ch % kGroups != grp || !wok) continue;
+        for (int ch = c0, idx = 0; ch < st.kc; ch += cstep, ++idx, ++q) {
+          if (idx % kGroups != grp || !wok) continue;
           const int stg = q % S;
           bool got = chain_wait(full_bar(stg), (q / S) & 1, p.ctl, flags);
           got = __all_sync(0xffffffffu, got);
@@ -375,12 +423,40 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
         for (int w = 0; w < kConsumerWarps; ++w) all = all && vote[w] != 0;
         ok = all;
         if (!ok) break;  // every consumer warp read the same votes
-        // epilogue of tile T: thread r < 128 owns row r
+        // tile T: thread r < 128 owns row r; this CTA's sum of the row
+        float t = 0.f;
+        if (ct < kPackRows) {
+          t = gsum[ct];
+#pragma unroll
+          for (int g = 1; g < kGroups; ++g) t += gsum[g * kPackRows + ct];
+        }
+        if (st.split) {
+          const int par = nsplit & 1;
+          ++nsplit;
+          if (rank != 0) {
+            // hand the partial to rank 0 and go on; rank 0 finishes the tile
+            // (each row's thread releases its own store with its arrival)
+            if (ct < kPackRows) {
+              st_cluster_f32(map_rank(smem_u32(&pslot[(rank - 1) * kPackRows + ct]), 0), t);
+              mbar_arrive_remote(map_rank(smem_u32(pbar), 0));
+            }
+            continue;
+          }
+          if (ct < kPackRows && !wait_partials(smem_u32(pbar), par, p.ctl, flags) && !flags[0])
+            report(p.ctl, flags, kDevTimeoutConsumer);
+          named_bar_sync(kConsumerBar, kConsumers);
+          if (flags[0]) {
+            ok = false;
+            break;
+          }
+          if (ct < kPackRows) {
+#pragma unroll
+            for (int rk = 1; rk < kChainCluster; ++rk) t += pslot[(rk - 1) * kPackRows + ct];
+          }
+        }
+        // epilogue of tile T
         if (ct < kPackRows) {
           const int r = ct;
-          float t = gsum[r];
-#pragma unroll
-          for (int g = 1; g < kGroups; ++g) t += gsum[g * kPackRows + r];
           const int64_t n = static_cast<int64_t>(T) * kPackRows + r;
           if (st.res_out) {
             if (n < st.N) {
@@ -431,6 +507,7 @@ __global__ void __launch_bounds__(kChainThreads, 1) chain_kernel(const __grid_co
     }
   }
   __syncthreads();
+  cluster_sync_all();  // no CTA leaves while a peer may still signal it
 }
 
 }  // namespace
@@ -448,10 +525,22 @@ cudaError_t chain_max_ctas(int sm_count, int *ctas) {
     if (e != cudaSuccess) return e;
     if (dev < 64) attr_set[dev] = true;
   }
-  int per_sm = 0;
-  cudaError_t e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, chain_kernel, kChainThreads, kChainSmem);
+  (void)sm_count;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kChainCluster * 64);
+  cfg.blockDim = dim3(kChainThreads);
+  cfg.dynamicSmemBytes = kChainSmem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kChainCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  cudaError_t e = cudaOccupancyMaxActiveClusters(&clusters, chain_kernel, &cfg);
   if (e != cudaSuccess) return e;
-  *ctas = per_sm * sm_count;
+  *ctas = clusters * kChainCluster;
   return *ctas > 0 ? cudaSuccess : cudaErrorInvalidConfiguration;
 }
 
@@ -461,11 +550,15 @@ cudaError_t launch_chain(const ChainParams &p, int ctas, cudaStream_t stream) {
   cfg.blockDim = dim3(kChainThreads);
   cfg.dynamicSmemBytes = kChainSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: they wait on one another
   attr[0].val.cooperative = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = kChainCluster;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, chain_kernel, p);
   if (e == cudaSuccess) note_launch();
   return e;

@@ -68,6 +68,7 @@ cudaError_t launch_gemv(const GemvParams &p, int ctas, cudaStream_t stream);
 // completer when it is the last step.  One CTA computes a whole 128-row tile.
 constexpr int kChainMaxK = 4096;  // input length a step stages in shared memory
 constexpr int kChainMaxLnN = 4096;
+constexpr int kChainCluster = 4;  // CTAs that share one tile of a split step
 struct ChainStep {
   const uint8_t *w;  // packed Q8_0 tiles [n_tiles][kc]
   int n_tiles, kc;
@@ -85,7 +86,8 @@ struct ChainStep {
   float ln_eps;
   void *y;           // output, or a residual step's LayerNorm output (bf16); may be null for the latter
   int y_dtype;
-  int rot;           // CTA of tile 0
+  int split;         // tiles go to clusters (chunk c to rank c % kChainCluster), else to CTAs
+  int rot;           // cluster (split) or CTA of tile 0
 };
 struct ChainParams {
   const ChainStep *steps;  // device array
