@@ -111,7 +111,9 @@ __device__ __forceinline__ Unit decode_unit(const GemmBf16Params &p, int u) {
   return r;
 }
 
-template <bool SPLITX, int PT>
+// CONV: the implicit conv1d form (shifted token rows per tap, channel-major
+// output); compiled separately so that the plain GEMM carries none of it.
+template <bool SPLITX, int PT, bool CONV>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_sm100_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a,
                            const __grid_constant__ CUtensorMap tm_alo, const __grid_constant__ GemmBf16Params p) {
@@ -169,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first ring stages before the dependency wait, during the previous
   // kernel's tail; the token halves of those stages follow after the wait.
   int pre = 0;
-  if (warp == 0 && lane == 0) {  // descriptors are launch parameters: fetch them before the wait
+  if (CONV && warp == 0 && lane == 0) {  // descriptors are launch parameters: fetch them before the wait
     prefetch_tmap(&tm_a);
     if (SPLITX) prefetch_tmap(&tm_alo);
   }
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t bar = map_rank(full(s), 0);
           const int kx = (un.kc0 + i) * kPackK;
           int ax = kx, arow = trow0;  // token operand coordinates
-          if (p.conv_cpt) {
+          if (CONV) {
             const int c = un.kc0 + i;
             const int tap = c / p.conv_cpt;
             ax = (c - tap * p.conv_cpt) * kPackK;
@@ -310,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // channel-major runs start at token multiples of kEc: 16-byte vector
     // stores when every row start is 16-byte aligned
     const int esz = p.y_dtype == 0 ? 4 : 2;
-    const bool y_vec = p.y_cm && (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && ((p.ldy * esz) & 15) == 0;
+    const bool y_vec = CONV && (reinterpret_cast<uintptr_t>(p.y) & 15) == 0 && ((p.ldy * esz) & 15) == 0;
     int j = 0;
     for (int u = cl; u < n_units; u += ncl, ++j) {
       const Unit un = decode_unit(p, u);
@@ -435,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!p.glu) {
             const bool nvalid = n < p.N;
             const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
-            if (p.y_cm) {
+            if (CONV) {
               emit_cm([&](int col, float(&v)[kEc]) { sum_pieces(e, col, v); }, bn, nvalid);
             } else {
               for (int col = 0; col < cols && nvalid; col += kEc) {
@@ -478,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int x = 0; x < kEc; ++x)
             if (x < valid) part[static_cast<size_t>(col + x) * p.n_rows] = v[x];
         }
-      } else if (!p.glu && p.y_cm) {
+      } else if (CONV) {
         const bool nvalid = n < p.N;
         emit_cm(fetch, (p.bias && nvalid) ? p.bias[n] : 0.f, nvalid);
       } else if (!p.glu) {
@@ -547,11 +549,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool SPLITX, int PT>
+template <bool SPLITX, int PT, bool CONV>
 cudaError_t launch_t(const CUtensorMap &w, const CUtensorMap &a_hi, const CUtensorMap &a_lo, const GemmBf16Params &p,
                      int pairs, cudaStream_t stream) {
   using C = Cfg<SPLITX, PT>;
-  auto kern = gemm_bf16_sm100_kernel<SPLITX, PT>;
+  auto kern = gemm_bf16_sm100_kernel<SPLITX, PT, CONV>;
   static bool attr_set[64] = {false};  // once per device (the attribute is per-context state)
   static int max_pairs[64] = {0};
   int dev = 0;
@@ -594,13 +596,26 @@ int gemm_bf16_token_box(int unit_tokens) { return (unit_tokens < 256 ? unit_toke
 
 cudaError_t launch_gemm_bf16(bool splitx, int unit_tokens, const CUtensorMap &w, const CUtensorMap &a_hi,
                              const CUtensorMap &a_lo, const GemmBf16Params &p, int pairs, cudaStream_t stream) {
+  if (p.conv_cpt) {  // implicit conv1d: channel-major output, no GLU, no split-K
+    if (!p.y_cm || p.glu || p.splits > 1) return cudaErrorInvalidValue;
+    switch (unit_tokens * 2 + (splitx ? 1 : 0)) {
+      case 512: return launch_t<false, 256, true>(w, a_hi, a_lo, p, pairs, stream);
+      case 513: return launch_t<true, 256, true>(w, a_hi, a_lo, p, pairs, stream);
+      case 256: return launch_t<false, 128, true>(w, a_hi, a_lo, p, pairs, stream);
+      case 257: return launch_t<true, 128, true>(w, a_hi, a_lo, p, pairs, stream);
+      case 128: return launch_t<false, 64, true>(w, a_hi, a_lo, p, pairs, stream);
+      case 129: return launch_t<true, 64, true>(w, a_hi, a_lo, p, pairs, stream);
+      default: return cudaErrorInvalidValue;
+    }
+  }
+  if (p.y_cm) return cudaErrorInvalidValue;
   switch (unit_tokens * 2 + (splitx ? 1 : 0)) {
-    case 512: return launch_t<false, 256>(w, a_hi, a_lo, p, pairs, stream);
-    case 513: return launch_t<true, 256>(w, a_hi, a_lo, p, pairs, stream);
-    case 256: return launch_t<false, 128>(w, a_hi, a_lo, p, pairs, stream);
-    case 257: return launch_t<true, 128>(w, a_hi, a_lo, p, pairs, stream);
-    case 128: return launch_t<false, 64>(w, a_hi, a_lo, p, pairs, stream);
-    case 129: return launch_t<true, 64>(w, a_hi, a_lo, p, pairs, stream);
+    case 512: return launch_t<false, 256, false>(w, a_hi, a_lo, p, pairs, stream);
+    case 513: return launch_t<true, 256, false>(w, a_hi, a_lo, p, pairs, stream);
+    case 256: return launch_t<false, 128, false>(w, a_hi, a_lo, p, pairs, stream);
+    case 257: return launch_t<true, 128, false>(w, a_hi, a_lo, p, pairs, stream);
+    case 128: return launch_t<false, 64, false>(w, a_hi, a_lo, p, pairs, stream);
+    case 129: return launch_t<true, 64, false>(w, a_hi, a_lo, p, pairs, stream);
     default: return cudaErrorInvalidValue;
   }
 }
