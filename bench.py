@@ -771,7 +771,7 @@ def run_conv_sweep(args) -> None:
             flops = 2.0 * cin * cout * k * t_in
             call = lambda: C.conv_transpose1d(x, w, None, stride, pad, out=y)  # noqa: E731
         y = torch.empty(cout, t_out, device="cuda", dtype=torch.bfloat16)
-        implicit = kind == "c" and stride == 1 and cin % 64 == 0 and t_out > 16
+        implicit = (kind == "c" and stride == 1 and cin % 64 == 0 and t_out > 16) or (kind == "t" and cin % 64 == 0)
 
         def graph_us():
             s = torch.cuda.Stream()
@@ -799,10 +799,10 @@ def run_conv_sweep(args) -> None:
                "t_out": t_out, "path": "implicit" if implicit else ("im2col" if kind == "c" else "col2im"),
                "us": round(us, 2), "tflops": round(flops / us / 1e6, 1),
                "frac_bf16_peak": round(flops / us / 1e6 / pk["bf16_tflops"], 3)}
-        if implicit:  # the same call through the im2col lowering, for comparison
+        if implicit:  # the same call through the im2col / column-GEMM lowering, for comparison
             lib.check(lib.load().nq_set_conv_path(lib.NQ_CONV_IM2COL))
             try:
-                row["us_im2col"] = round(graph_us(), 2)
+                row["us_im2col" if kind == "c" else "us_col2im"] = round(graph_us(), 2)
             finally:
                 lib.check(lib.load().nq_set_conv_path(lib.NQ_CONV_AUTO))
         rows.append(row)

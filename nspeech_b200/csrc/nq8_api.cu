@@ -46,6 +46,13 @@ struct nq_weight {
   mutable __nv_bfloat16 *tap = nullptr;
   mutable int64_t tap_cin = 0;
   mutable int tap_k = 0;
+  // Polyphase copy of a conv_transpose1d weight for stride poly_s:
+  // [ceil(c_out poly_s / 128) * 128][ceil(K / poly_s) * c_in], row
+  // co * poly_s + r, column i c_in + ci = W[ci][co][r + poly_s i]; built on the
+  // first nq_conv_transpose1d call that takes the implicit path, freed with
+  // the weight.
+  mutable __nv_bfloat16 *poly = nullptr;
+  mutable int poly_s = 0;
 };
 
 struct nq_chain {
@@ -776,6 +783,141 @@ int ensure_tap_copy(const nq_weight *w, int64_t c_in, int kernel, cudaStream_t s
   return NQ_OK;
 }
 
+// The polyphase copy of a conv_transpose1d weight for `stride`, built once
+// on `stream` from the weight's bf16 form and synchronized.
+int ensure_poly_copy(const nq_weight *w, int64_t c_in, int64_t c_out, int kernel, int stride, cudaStream_t stream,
+                     const __nv_bfloat16 **out) {
+  std::lock_guard<std::mutex> lk(g_tap_mu);
+  if (w->poly && w->poly_s == stride) {
+    *out = w->poly;
+    return NQ_OK;
+  }
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(stream, &cs);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+  if (cs != cudaStreamCaptureStatusNone)
+    return fail(NQ_ERR_UNSUPPORTED,
+                "nq_conv_transpose1d: the first call with a weight builds its polyphase copy and cannot run under "
+                "stream capture; call it once before capturing");
+  const int taps = (kernel + stride - 1) / stride;
+  const int rows = static_cast<int>((c_out * stride + nq::kPackRows - 1) / nq::kPackRows) * nq::kPackRows;
+  const int64_t k_pad = static_cast<int64_t>(w->kc) * nq::kPackK;
+  __nv_bfloat16 *dst = nullptr;
+  e = cudaMalloc(&dst, static_cast<size_t>(rows) * taps * c_in * 2);
+  if (e == cudaSuccess)
+    e = nq::launch_conv_poly_weight(w->bf16, k_pad, static_cast<int>(c_out), kernel, stride, static_cast<int>(c_in),
+                                    taps, rows, dst, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) {
+    if (dst) cudaFree(dst);
+    return cuda_fail(e, "conv_transpose weight polyphase copy");
+  }
+  if (w->poly) {
+    e = cudaDeviceSynchronize();  // no launch in flight may still read it
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize(replace polyphase copy)");
+    cudaFree(w->poly);
+  }
+  w->poly = dst;
+  w->poly_s = stride;
+  *out = dst;
+  return NQ_OK;
+}
+
+// Implicit-GEMM conv_transpose1d in polyphase form.  Output frame
+// t = q s + r - padding (phase r = (t + padding) mod s) sums taps j = r + s i
+// of input position q - i, so the whole transposed conv is one stride-1
+// implicit GEMM over the token-major input: weight rows (co, r) with k =
+// (tap i, channels), token m = input position q = q0 + m reading rows
+// q - i (dilation -1), and an epilogue that scatters row (co, r) of token m
+// to frame q s + r - padding.  No column buffer and no overlap-add pass.
+int conv_transpose1d_implicit(DeviceCtx *ctx, const nq_weight *w, const void *x, int x_dtype, int64_t c_in,
+                              int64_t t_in, int64_t ldx, int kernel, int stride, int padding, float x_leaky,
+                              const float *bias, int epilogue, void *y, int y_dtype, int64_t ldy, int64_t t_out,
+                              int64_t q0, int64_t m, cudaStream_t stream) {
+  const int64_t c_out = w->n / kernel;
+  const __nv_bfloat16 *wp = nullptr;
+  int rc = ensure_poly_copy(w, c_in, c_out, kernel, stride, stream, &wp);
+  if (rc) return rc;
+  const bool splitx = x_dtype == NQ_F32;
+  const int taps = (kernel + stride - 1) / stride;
+  const int kc = static_cast<int>(taps * c_in / nq::kPackK);
+  const int n_tiles = static_cast<int>((c_out * stride + nq::kPackRows - 1) / nq::kPackRows);
+  const int ldp = n_tiles * nq::kPackRows;
+  GemmPlan g;
+  g.deq = true;
+  g.cached = true;
+  g.pairs = std::max(1, ctx->sm_count / 2);
+  g.grid_n = (n_tiles + 1) / 2;
+  const GemmPlan plan = plan_bf16(g, m, kc, ldp, false);
+  const int bt = plan.bt;
+  const size_t plane = align_up(static_cast<size_t>(t_in) * c_in * 2, 1024);
+  const size_t tail_bytes = static_cast<size_t>(plan.tail_tiles()) * plan.tail_pieces * 2 * 16 * (bt / 4) * 32 * 4;
+  if (kTailCounterBase + static_cast<size_t>(plan.tail_tiles()) * 2 * 16 > kCounterSlots)
+    return fail(NQ_ERR_SHAPE, "tail split needs more counters than the workspace holds");
+  Workspace *ws = nullptr;
+  rc = get_workspace(ctx, stream, plane * (splitx ? 2 : 1) + tail_bytes, &ws, true);
+  if (rc) return rc;
+  __nv_bfloat16 *hi = reinterpret_cast<__nv_bfloat16 *>(ws->buf);
+  __nv_bfloat16 *lo = splitx ? reinterpret_cast<__nv_bfloat16 *>(ws->buf + plane) : nullptr;
+  float *tail_part = tail_bytes ? reinterpret_cast<float *>(ws->buf + plane * (splitx ? 2 : 1)) : nullptr;
+  cudaError_t e = nq::launch_conv_tokens(x, x_dtype, ldx, static_cast<int>(c_in), static_cast<int>(t_in), x_leaky,
+                                         hi, lo, stream);
+  if (e != cudaSuccess) return cuda_fail(e, "conv_transpose input launch");
+  CUtensorMap tm_w, tm_a, tm_alo;
+  const int64_t kw = static_cast<int64_t>(kc) * nq::kPackK;
+  rc = make_tmap(ctx, &tm_w, wp, kw, ldp, kw, nq::gemm_bf16_block_w() / 2);
+  if (rc) return rc;
+  rc = make_tmap(ctx, &tm_a, hi, c_in, t_in, c_in, nq::gemm_bf16_token_box(bt));
+  if (rc) return rc;
+  if (splitx) {
+    rc = make_tmap(ctx, &tm_alo, lo, c_in, t_in, c_in, nq::gemm_bf16_token_box(bt));
+    if (rc) return rc;
+  } else {
+    tm_alo = tm_a;
+  }
+  nq::GemmBf16Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.N = c_out * stride;
+  p.n_rows = ldp;
+  p.n_out = p.N;
+  p.M = static_cast<int>(m);
+  p.kc_total = kc;
+  p.bias = bias;
+  p.epi = epilogue;
+  p.y = y;
+  p.y_dtype = y_dtype;
+  p.ldy = ldy;
+  p.splits = 1;
+  p.cps = kc;
+  p.grid_n = plan.grid_n;
+  p.grid_m = plan.grid_m;
+  p.full_units = plan.full_units;
+  p.tail_pieces = plan.tail_pieces;
+  p.tail_cps = plan.tail_cps;
+  p.tail_part = tail_part;
+  p.tail_cnt = ws->counters + kTailCounterBase;
+  p.w_static = 1;
+  p.conv_cpt = static_cast<int>(c_in / nq::kPackK);
+  p.conv_dil = -1;
+  p.conv_pad = static_cast<int>(-q0);
+  p.y_cm = 1;
+  p.poly_s = stride;
+  p.poly_q0 = static_cast<int>(q0);
+  p.poly_pad = padding;
+  p.t_out = t_out;
+  p.ctl.status = ctx->status;
+  p.ctl.wait_limit = g_wait_limit;
+  const int work_units = plan.tail_pieces > 1 ? plan.full_units + plan.tail_tiles() * plan.tail_pieces
+                                              : plan.grid_m * plan.grid_n;
+  const double flops = 2.0 * t_in * c_in * c_out * kernel;
+  const double bytes = static_cast<double>(ldp) * kw * 2 + t_in * c_in * (splitx ? 4.0 : 2.0) +
+                       c_out * t_out * (y_dtype == NQ_F32 ? 4.0 : 2.0) + (bias ? 4.0 * c_out : 0.0);
+  ProfScope ps(NQ_KCLASS_GEMM, stream, flops, bytes);
+  e = nq::launch_gemm_bf16(splitx, bt, tm_w, tm_a, tm_alo, p, std::min(work_units, plan.pairs), stream);
+  if (e != cudaSuccess) return cuda_fail(e, "implicit conv_transpose GEMM launch");
+  return NQ_OK;
+}
+
 // Implicit-GEMM conv1d (stride 1, channels in whole 64-wide k chunks): the
 // input goes to token-major bf16 planes once (leaky ReLU applied), and the
 // bf16 GEMM reads, for k chunk (tap j, channels c), the planes' rows shifted
@@ -1340,6 +1482,7 @@ void nq_weight_free(nq_weight *w) {
   if (w->bf16) cudaFree(w->bf16);
   if (w->dev) cudaFree(w->dev);
   if (w->tap) cudaFree(w->tap);
+  if (w->poly) cudaFree(w->poly);
   if (cur != w->device) cudaSetDevice(cur);
   delete w;
 }
@@ -1453,6 +1596,15 @@ int nq_conv_transpose1d(const nq_weight *w, const void *x, int x_dtype, int64_t 
   if (w->device != dev) return fail(NQ_ERR_ARG, "weight lives on device %d, current device is %d", w->device, dev);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t c_out = w->n / kernel;
+  // Polyphase implicit GEMM: input positions q in [q0, q1] reach an output
+  // frame (t = q stride + r - padding in [0, t_out) for some phase r).
+  auto floor_div = [](int64_t a, int64_t b) { return a >= 0 ? a / b : -((-a + b - 1) / b); };
+  const int64_t q0 = floor_div(padding - (stride - 1), stride);
+  const int64_t q1 = floor_div(t_out - 1 + padding, stride);
+  const int64_t mq = q1 - q0 + 1;
+  if (g_conv_path == NQ_CONV_AUTO && c_in % nq::kPackK == 0 && mq > 16 && w->bf16)
+    return conv_transpose1d_implicit(ctx, w, x, x_dtype, c_in, t_in, ldx, kernel, stride, padding, x_leaky, bias,
+                                     epilogue, y, y_dtype, ldy, t_out, q0, mq, s);
   const int64_t k_pad = static_cast<int64_t>(w->kc) * nq::kPackK;
   const size_t esz = x_dtype == NQ_F32 ? 4 : 2;
   const size_t rows_bytes = align_up(static_cast<size_t>(t_in) * k_pad * esz, 256);

@@ -154,6 +154,26 @@ __global__ void conv_tap_weight_kernel(const __nv_bfloat16 *__restrict__ src, in
   }
 }
 
+// dst[co s + r][i c_in + ci] = src[co K + r + s i][ci] (zero when the tap or
+// the row does not exist): eight consecutive destination elements per thread.
+__global__ void conv_poly_weight_kernel(const __nv_bfloat16 *__restrict__ src, int64_t ld_src, int c_out, int K,
+                                        int s, int c_in, int taps, int rows, __nv_bfloat16 *__restrict__ dst) {
+  const int64_t ld_dst = static_cast<int64_t>(taps) * c_in;
+  const int64_t groups = static_cast<int64_t>(rows) * (ld_dst / 8);
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t n = g / (ld_dst / 8);
+    const int64_t e0 = (g - n * (ld_dst / 8)) * 8;
+    const int i = static_cast<int>(e0 / c_in);
+    const int ci0 = static_cast<int>(e0 - static_cast<int64_t>(i) * c_in);
+    const int co = static_cast<int>(n / s), r = static_cast<int>(n - static_cast<int64_t>(co) * s);
+    const int j = r + s * i;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (co < c_out && j < K) v = *reinterpret_cast<const uint4 *>(src + (static_cast<int64_t>(co) * K + j) * ld_src + ci0);
+    *reinterpret_cast<uint4 *>(dst + n * ld_dst + e0) = v;
+  }
+}
+
 // y[c][t] (ldy) = src[t][c] (lds): 32 x 32 tiles through shared memory.
 __global__ void transpose_out_kernel(const void *__restrict__ src, int src_dtype, int64_t lds, int rows_t, int cols_c,
                                      void *__restrict__ y, int y_dtype, int64_t ldy) {
@@ -255,6 +275,15 @@ cudaError_t launch_conv_tap_weight(const __nv_bfloat16 *src, int64_t ld_src, int
   const int64_t groups = static_cast<int64_t>(rows) * K * c_in / 8;
   if (groups == 0) return cudaSuccess;
   conv_tap_weight_kernel<<<grid_for(groups, 256), 256, 0, s>>>(src, ld_src, rows, c_in, K, dst);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_conv_poly_weight(const __nv_bfloat16 *src, int64_t ld_src, int c_out, int K, int s, int c_in,
+                                   int taps, int rows, __nv_bfloat16 *dst, cudaStream_t stream) {
+  if (c_in % 8 || ld_src % 8) return cudaErrorInvalidValue;
+  const int64_t groups = static_cast<int64_t>(rows) * taps * c_in / 8;
+  if (groups == 0) return cudaSuccess;
+  conv_poly_weight_kernel<<<grid_for(groups, 256), 256, 0, stream>>>(src, ld_src, c_out, K, s, c_in, taps, rows, dst);
   return cudaGetLastError();
 }
 

@@ -349,6 +349,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       // go through quad_transpose: each store writes 64 bytes of 8 rows.
       // With 16 bf16 tokens per warp, lane pairs swap halves instead (32
       // bytes of 16 rows per store).  Partial groups store element runs.
+      // Polyphase conv_transpose1d output of this lane's row (co, r): token
+      // m goes to frame (poly_q0 + m) poly_s + r - poly_pad of channel co.
+      auto emit_poly = [&](auto &&get, bool nvalid) {
+        const int64_t co = n / p.poly_s;
+        const int r = static_cast<int>(n - co * p.poly_s);
+        const float b = (p.bias && nvalid) ? p.bias[co] : 0.f;
+        for (int col = 0; col < cols; col += kEc) {
+          float v[kEc];
+          get(col, v);
+          if (!nvalid) continue;
+#pragma unroll
+          for (int x = 0; x < kEc; ++x) {
+            const int tok = m0 + col + x;
+            const int64_t t = static_cast<int64_t>(p.poly_q0 + tok) * p.poly_s + r - p.poly_pad;
+            if (tok < p.M && t >= 0 && t < p.t_out) {
+              const float a = act_single(p.epi, v[x] + b);
+              if (p.y_dtype == 0) static_cast<float *>(p.y)[co * p.ldy + t] = a;
+              else static_cast<__nv_bfloat16 *>(p.y)[co * p.ldy + t] = __float2bfloat16_rn(a);
+            }
+          }
+        }
+      };
       auto emit_cm = [&](auto &&get, float b, bool nvalid) {
         const int gt = (p.y_dtype == 0 || kColsPerWarp < 2 * kEc) ? kEc : 2 * kEc;  // tokens per group
         const int64_t row_q = static_cast<int64_t>(tile) * kPackRows + 32 * q;  // row of lane 0
@@ -436,8 +458,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           };
           if (!p.glu) {
             const bool nvalid = n < p.N;
-            const float bn = (p.bias && nvalid) ? p.bias[n] : 0.f;
-            if (CONV) {
+            // (a polyphase bias is per output channel: emit_poly reads it)
+            const float bn = (p.bias && nvalid && !(CONV && p.poly_s)) ? p.bias[n] : 0.f;
+            if (CONV && p.poly_s) {
+              emit_poly([&](int col, float(&v)[kEc]) { sum_pieces(e, col, v); }, nvalid);
+            } else if (CONV) {
               emit_cm([&](int col, float(&v)[kEc]) { sum_pieces(e, col, v); }, bn, nvalid);
             } else {
               for (int col = 0; col < cols && nvalid; col += kEc) {
@@ -480,6 +505,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int x = 0; x < kEc; ++x)
             if (x < valid) part[static_cast<size_t>(col + x) * p.n_rows] = v[x];
         }
+      } else if (CONV && p.poly_s) {
+        emit_poly(fetch, n < p.N);
       } else if (CONV) {
         const bool nvalid = n < p.N;
         emit_cm(fetch, (p.bias && nvalid) ? p.bias[n] : 0.f, nvalid);

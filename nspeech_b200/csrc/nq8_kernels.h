@@ -177,6 +177,14 @@ struct GemmBf16Params {
   int conv_dil;
   int conv_pad;
   int y_cm;          // channel-major output y[n][ldy] (NCW); no GLU, no split-K
+  // Polyphase conv_transpose1d (poly_s > 0, with conv_cpt): weight row
+  // n = co * poly_s + r holds phase r of output channel co; token m is input
+  // position q = poly_q0 + m, and its value goes to y[co][q * poly_s + r -
+  // poly_pad] when that frame is in [0, t_out); bias is indexed by co.
+  int poly_s;
+  int poly_q0;
+  int poly_pad;
+  int64_t t_out;
   DevCtl ctl;
 };
 int gemm_bf16_block_t();              // default tokens per pair unit
@@ -243,6 +251,12 @@ cudaError_t launch_qtiled(const QtiledParams &p, cudaStream_t stream);
 // (lo = bf16(v - hi) for f32 x; lo may be null), rows of c_in elements.
 cudaError_t launch_conv_tokens(const void *x, int x_dtype, int64_t ldx, int c_in, int t_in, float slope,
                                __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t s);
+// Polyphase weight of a conv_transpose1d from its transposed GEMM form src
+// [c_out K][c_in] (rows (co, j), ld_src elements): dst row co * s + r, column
+// i c_in + ci = src[co K + r + s i][ci] when r + s i < K, else 0; rows up to
+// `rows` (zero past c_out * s).
+cudaError_t launch_conv_poly_weight(const __nv_bfloat16 *src, int64_t ld_src, int c_out, int K, int s, int c_in,
+                                   int taps, int rows, __nv_bfloat16 *dst, cudaStream_t stream);
 // Tap-major copy of a conv weight: dst[r][j c_in + ci] = src[r][ci K + j] for
 // rows r < rows (src rows ld_src elements, dst rows K c_in).
 cudaError_t launch_conv_tap_weight(const __nv_bfloat16 *src, int64_t ld_src, int rows, int c_in, int K,

@@ -250,6 +250,50 @@ def test_conv_transpose1d_matches_oracle(nq, oracle, cin, cout, k, stride, pad, 
     assert nq.status() == 0
 
 
+# Polyphase implicit GEMM (c_in a multiple of 64, more than 16 input
+# positions): (c_in, c_out, K, stride, padding, output_padding, leaky, T_in).
+# Kernels that are and are not multiples of the stride, output padding, no
+# padding, and c_out * stride not a multiple of 128.
+POLY = [(512, 256, 20, 10, 5, 0, 0.1, 300), (256, 128, 12, 6, 3, 0, 0.1, 700), (128, 48, 7, 3, 2, 1, 1.0, 60),
+        (64, 40, 5, 2, 0, 1, 0.2, 33), (128, 64, 4, 4, 0, 0, 1.0, 50)]
+
+
+@pytest.mark.parametrize("cin,cout,k,stride,pad,opad,leaky,t_in", POLY)
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_conv_transpose1d_implicit_matches_oracle_and_col2im(nq, oracle, cin, cout, k, stride, pad, opad, leaky,
+                                                             t_in, dt):
+    """The polyphase implicit GEMM (default for these shapes) against the
+    oracle and against the column GEMM + overlap-add (NQ_CONV_IM2COL)."""
+    from nspeech_b200 import conv as C
+    L = nq.load()
+    rng = np.random.default_rng(cin + 5 * k + t_in)
+    w = (rng.standard_normal((cin, cout, k)) * 0.05).astype(np.float32)
+    wt = C.ConvTransposeWeight.from_f32(w)
+    bias = (rng.standard_normal(cout) * 0.1).astype(np.float32)
+    x = rng.standard_normal((cin, t_in)).astype(np.float32)
+    tdt = torch.float32 if dt == "f32" else torch.bfloat16
+    if dt == "bf16":
+        x = _bf16(x)
+    xt = torch.from_numpy(x).cuda().to(tdt)
+    bt = torch.from_numpy(bias).cuda()
+    y = C.conv_transpose1d(xt, wt, bt, stride, pad, opad, x_leaky=leaky, out_dtype=torch.float32)
+    y2 = C.conv_transpose1d(xt, wt, bt, stride, pad, opad, x_leaky=leaky, out_dtype=torch.float32)
+    try:
+        nq.check(L.nq_set_conv_path(nq.NQ_CONV_IM2COL))
+        yc = C.conv_transpose1d(xt, wt, bt, stride, pad, opad, x_leaky=leaky, out_dtype=torch.float32)
+    finally:
+        nq.check(L.nq_set_conv_path(nq.NQ_CONV_AUTO))
+    torch.cuda.synchronize()
+    ref = oracle.conv_transpose1d_ref(x, _bf16(w), bias, stride, pad, opad, leaky)
+    assert y.shape == ref.shape
+    tol = 2e-3 if dt == "f32" else 1e-2
+    assert _err(oracle, y.cpu().numpy(), ref) <= tol
+    assert _err(oracle, yc.cpu().numpy(), ref) <= tol
+    assert torch.equal(y, y2)
+    assert (y - yc).abs().max().item() <= 1e-3 * max(1.0, yc.abs().max().item())
+    assert nq.status() == 0
+
+
 def test_conv_rejects_bad_shapes(nq, oracle):
     from nspeech_b200 import conv as C
     from nspeech_b200.fast_matmul import MatMulError, QWeight
