@@ -293,9 +293,14 @@ int64_t nq_conv_transpose1d_out_len(int64_t t_in, int kernel, int stride, int pa
 int nq_conv_transpose1d_weight(const float *w, int64_t c_in, int64_t c_out, int kernel, nq_weight **out);
 
 /* y[co][t] = act(bias[co] + sum over ci, j with t = ti * stride - padding + j
- * of W[ci][co][j] * leaky(x[ci][ti])): one GEMM to the columns
+ * of W[ci][co][j] * leaky(x[ci][ti])).  For c_in a multiple of 64 (and more
+ * than 16 input positions reaching the output) one polyphase implicit GEMM:
+ * output phase r = (t + padding) mod stride is a stride-1 conv over the input
+ * with taps r, r + stride, ..., computed against a polyphase bf16 copy of the
+ * weight built on the first such call (not under stream capture).  Otherwise
+ * (or with nq_set_conv_path(NQ_CONV_IM2COL)) one GEMM to the columns
  * [t_in][c_out * kernel] (f32), then an overlap-add that sums each output's
- * taps in ascending j (deterministic).  Replaces
+ * taps in ascending j.  Both are deterministic.  Replaces
  * KokoroGpuBackend::conv_transpose1d / conv_transpose1d_lrelu
  * (src/kokoro/gpu_backend.rs:72-81; decoder.rs generator.ups). */
 int nq_conv_transpose1d(const nq_weight *w, const void *x, int x_dtype, int64_t c_in, int64_t t_in, int64_t ldx,
@@ -462,14 +467,15 @@ int nq_set_gemm_tail_split(int mode);
 #define NQ_ATTENTION_MMA_SYNC 1
 int nq_set_attention_kernel(int kernel);
 
-/* How nq_conv1d lowers a convolution.  No counterpart in the reference: a
- * B200 dispatch knob.  AUTO (default): stride-1 convs whose c_in is a multiple
- * of 64 with more than 16 output frames run as an implicit GEMM (token-major
- * input planes, the weight's tap-major bf16 copy, shifted-row loads, NCW
- * output from the GEMM epilogue); other convs as im2col + nq_linear +
- * transpose.  IM2COL forces the second form (tests compare the two).
- * Results differ by f32 summation order only.  Process-wide; returns
- * NQ_ERR_ARG for other values. */
+/* How nq_conv1d and nq_conv_transpose1d lower a convolution.  No
+ * counterpart in the reference: a B200 dispatch knob.  AUTO (default):
+ * stride-1 conv1d and conv_transpose1d whose c_in is a multiple of 64 (and
+ * more than 16 output frames / input positions) run as implicit GEMMs
+ * (token-major input planes, a tap-major or polyphase bf16 copy of the
+ * weight, shifted-row loads, NCW output from the GEMM epilogue); other convs
+ * as im2col + nq_linear + transpose, or column GEMM + overlap-add.  IM2COL
+ * forces the second forms (tests compare the two).  Results differ by f32
+ * summation order only.  Process-wide; returns NQ_ERR_ARG for other values. */
 #define NQ_CONV_AUTO 0
 #define NQ_CONV_IM2COL 1
 int nq_set_conv_path(int path);
