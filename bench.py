@@ -90,6 +90,8 @@ def parse_args():
     ap.add_argument("--gemv-shapes", default="1x640x640,1x640x2560,1x2560x640,1x4096x4096,1x8192x8192,"
                     "1x640x32768,8x4096x4096,16x4096x4096,1x16384x16384")
     ap.add_argument("--gemv-plain", type=int, default=0, help="only make this many plain calls per shape")
+    ap.add_argument("--gemv-path", type=int, default=0, choices=(0, 1, 2),
+                    help="--gemv: GEMV form (nq_set_gemv_path: 0 auto, 1 split + reduce, 2 cluster where it applies)")
     ap.add_argument("--no-decode-step", action="store_true", help="--gemv without the configs[2] decode step")
     ap.add_argument("--linear", action="store_true", help="time nq_linear per shape instead of the encoder")
     ap.add_argument("--shape", action="append", default=[], help="--linear: MxKxN")
@@ -820,6 +822,7 @@ def run_gemv_sweep(args) -> None:
     from nspeech_b200.fast_matmul import QWeight
     torch.cuda.set_device(0)
     lib.init(0)
+    lib.check(lib.load().nq_set_gemv_path(args.gemv_path))
     pk = peaks()
     rng = np.random.default_rng(0)
     rows = []
@@ -925,6 +928,11 @@ def decode_step(rng, pk) -> dict:
         for net in nets:
             token(net)
     torch.cuda.synchronize()
+    lib.launch_counter(reset=True)
+    with torch.cuda.stream(s):
+        token(nets[0])
+    torch.cuda.synchronize()
+    launches_op = lib.launch_counter(reset=True)
     tokens = 8
     gr = torch.cuda.CUDAGraph()
     with torch.cuda.graph(gr, stream=s):
@@ -985,7 +993,7 @@ def decode_step(rng, pk) -> dict:
     return {"config": "configs[2] Moonshine decoder, M = 1, 14 layers + lm_head", "weight_mb_per_token":
             round(wbytes / 1e6, 2), "hbm_floor_us": round(floor_us, 1), "gemv_calls_per_token": calls,
             "op_by_op": {"us_per_token": round(us, 1), "frac_of_floor": round(floor_us / us, 3),
-                         "launches_per_token": 2 * calls},
+                         "launches_per_token": launches_op},
             "chain": {"us_per_token": round(us_chain, 1), "frac_of_floor": round(floor_us / us_chain, 3),
                       "launches_per_token": 1}}
 

@@ -467,6 +467,26 @@ int nq_set_gemm_tail_split(int mode);
 #define NQ_ATTENTION_MMA_SYNC 1
 int nq_set_attention_kernel(int kernel);
 
+/* Which form serves a GEMV call (M <= 16: nq_linear, the named GEMV entries,
+ * nq_gemv_resadd_ln, nq_gemv_noalloc).  No counterpart in the reference: a
+ * B200 dispatch knob.  SPLIT: k cut into units over all SMs (dynamic work
+ * counter), then a reduce launch -- two launches, best for large weights.
+ * CLUSTER: each 128-row tile's k over a thread-block cluster of up to 8 CTAs,
+ * the partial sums added through distributed shared memory -- one launch;
+ * a residual + LayerNorm call's LayerNorm is computed by the cluster that
+ * finishes last.  AUTO (default): CLUSTER for calls of at most 8 rows
+ * without the residual + LayerNorm epilogue whose CTAs get at most 5 k
+ * chunks, with all CTAs in one wave (the latency-bound decoder projections),
+ * else SPLIT.  CLUSTER forces
+ * the cluster form wherever it applies (at most 8 chunks per CTA), residual
+ * calls included; elsewhere SPLIT runs.  The two forms add the same products
+ * in different f32 orders.  Process-wide; returns NQ_ERR_ARG for other
+ * values. */
+#define NQ_GEMV_AUTO 0
+#define NQ_GEMV_SPLIT 1
+#define NQ_GEMV_CLUSTER 2
+int nq_set_gemv_path(int path);
+
 /* How nq_conv1d and nq_conv_transpose1d lower a convolution.  No
  * counterpart in the reference: a B200 dispatch knob.  AUTO (default):
  * stride-1 conv1d and conv_transpose1d whose c_in is a multiple of 64 (and

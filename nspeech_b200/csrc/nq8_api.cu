@@ -110,6 +110,7 @@ int g_gemm_unit_tokens = 0;  // 0: the kernel's default unit width
 int g_attention_kernel = NQ_ATTENTION_TCGEN05;
 int g_tail_split = 0;        // 0: cost model, 1: off, >= 2: that many pieces when a tail exists
 int g_conv_path = NQ_CONV_AUTO;
+int g_gemv_path = NQ_GEMV_AUTO;
 std::mutex g_tap_mu;         // builds of weights' tap-major copies
 // Token count from which a GEMM call dequantizes the weight once and runs
 // the bf16 tensor-core GEMM (measured crossover on B200).
@@ -414,7 +415,9 @@ int run_gemv(DeviceCtx *ctx, const LinearArgs *args, int nprob, const void *x, i
     pr.partials = reinterpret_cast<float *>(ws->buf + part_off);
     part_off += gemv_partial_bytes(plan, w->n_tiles, m);
   }
-  p.sched = ws->counters;  // work counter
+  p.sched = ws->counters;  // work counter, tile arrivals
+  p.sm_count = ctx->sm_count;
+  p.path = g_gemv_path;
   if (direct) {
     p.xh = static_cast<const __nv_bfloat16 *>(x);
     p.ldx = ldx;
@@ -1680,6 +1683,8 @@ int nq_gemv_noalloc(const nq_weight *w, const void *x, int x_dtype, int64_t m, i
   pr.ldy = ldy;
   pr.partials = reinterpret_cast<float *>(scratch);
   p.sched = sched;
+  p.sm_count = ctx->sm_count;
+  p.path = g_gemv_path;
   if (direct) {
     p.xh = static_cast<const __nv_bfloat16 *>(x);
     p.ldx = ldx;
@@ -1945,6 +1950,13 @@ int nq_set_gemm_unit_tokens(int tokens) {
 int nq_set_gemm_tail_split(int mode) {
   if (mode < 0 || mode > 16) return fail(NQ_ERR_ARG, "tail split mode %d (0 auto, 1 off, 2..16 pieces)", mode);
   g_tail_split = mode;
+  return NQ_OK;
+}
+
+int nq_set_gemv_path(int path) {
+  if (path != NQ_GEMV_AUTO && path != NQ_GEMV_SPLIT && path != NQ_GEMV_CLUSTER)
+    return fail(NQ_ERR_ARG, "GEMV path %d (0 auto, 1 split + reduce, 2 cluster)", path);
+  g_gemv_path = path;
   return NQ_OK;
 }
 

@@ -37,6 +37,7 @@
 
 #include "nq8_common.cuh"
 #include "nq8_kernels.h"
+#include "nq8_sm100_pair.cuh"
 
 namespace nq {
 
@@ -518,6 +519,323 @@ __global__ void __launch_bounds__(kLnThreads) gemv_reduce_resadd_ln_kernel(const
   if (m == 0 && threadIdx.x == 0) p.sched[0] = 0;
 }
 
+// ------------------------------------------------------- cluster form
+// One launch per call for latency-bound shapes.  Tile T of the call (over
+// all problems) belongs to a cluster of `cl` CTAs; rank r streams chunks
+// r, r + cl, ... of the tile (the whole tile's k, so no unit partials leave
+// the cluster) and runs the consumer above on them.  The ranks' 128-row
+// partial sums meet in rank 0's shared memory through distributed shared
+// memory, added in rank order; rank 0 applies bias / activation / GLU, or the
+// residual add.  A residual call's LayerNorm needs whole rows: each cluster
+// counts its tile on a device counter after storing its residual rows, and
+// the cluster that counts last computes the LayerNorm of every row (mean and
+// biased variance in f32, fixed-order sums) and re-arms the counter.  No
+// wait depends on another CTA's progress except the cluster barriers, which
+// every thread reaches.
+constexpr int kGcStages = 5;
+constexpr size_t kGcPartOff = static_cast<size_t>(kGcStages) * kTileBytes;  // f32 [16][128] this CTA's partial
+constexpr size_t kGcRedOff = kGcPartOff + 16 * kPackRows * 4;                // f32 [8] block sums
+constexpr size_t kGcBarOff = kGcRedOff + 32;
+constexpr size_t kGcFlagOff = kGcBarOff + 2 * kGcStages * 8;
+constexpr size_t kGcSmemBytes = kGcFlagOff + 16;
+constexpr long long kGcDrainLimit = 1LL << 31;
+static_assert(16 * kPackRows * 4 <= kGcStages * kTileBytes, "tile sums fit in the ring");
+
+__device__ __forceinline__ float ld_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Sum over the CTA's 160 threads in a fixed order (warp butterflies, then the
+// five warp sums in warp order); every thread gets the result.
+__device__ __forceinline__ float gc_block_sum(float v, float *red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();  // red is free
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kGemvThreads / 32; ++w) t += red[w];
+  return t;
+}
+
+template <int MT, bool SPLITX>
+__global__ void __launch_bounds__(kGemvThreads, gemv_min_ctas(MT, SPLITX))
+    gemv_cluster_kernel(const __grid_constant__ GemvParams p, int cl) {
+  constexpr int S = kGcStages;
+  pdl_trigger();
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t *ring = smem;
+  float *part = reinterpret_cast<float *>(smem + kGcPartOff);  // [m][128]
+  float *tot = reinterpret_cast<float *>(smem);                  // rank 0: [m][128] tile sums (ring space, free by then)
+  float *red = reinterpret_cast<float *>(smem + kGcRedOff);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + kGcBarOff);
+  volatile int *flags = reinterpret_cast<volatile int *>(smem + kGcFlagOff);  // [0] abort [1] tile count
+  const int kc = p.kc;
+  const uint32_t rank = cluster_ctarank();
+  const int T = blockIdx.x / cl;
+  const int t1 = p.prob[0].n_tiles, t2 = t1 + p.prob[1].n_tiles;
+  const int total_tiles = t2 + p.prob[2].n_tiles;
+  const int pi = (T >= t1) + (T >= t2);
+  const int tl = T - (pi == 0 ? 0 : (pi == 1 ? t1 : t2));
+  const GemvProblem &pr = p.prob[pi];
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_my = static_cast<int>(rank) < kc ? (kc - static_cast<int>(rank) + cl - 1) / cl : 0;
+  auto full_bar = [&](int s) { return smem_u32(&bars[s]); };
+  auto empty_bar = [&](int s) { return smem_u32(&bars[S + s]); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), kGemvConsumerWarps);
+    }
+    flags[0] = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // producer: this rank's chunks of the tile (weights are constant: no
+      // dependency wait before the copies)
+      const uint64_t pol = policy_evict_first();
+      int i = 0;
+      for (; i < n_my; ++i) {
+        const int s = i % S;
+        if (i >= S && !mbar_wait(empty_bar(s), ((i / S) - 1) & 1, p.ctl.wait_limit, flags)) {
+          if (!flags[0]) report(p.ctl, flags, kDevTimeoutProducer);
+          break;
+        }
+        if (flags[0]) break;
+        const int ch = static_cast<int>(rank) + i * cl;
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(full_bar(s), kTileBytes);
+        bulk_load(smem_u32(ring + s * kTileBytes), pr.w + (static_cast<size_t>(tl) * kc + ch) * kTileBytes,
+                  kTileBytes, full_bar(s), pol);
+      }
+      volatile int no_abort = 0;
+      for (int st = 0; st < S && st < i; ++st) {
+        const int last = st + S * ((i - 1 - st) / S);
+        if (!mbar_wait(full_bar(st), (last / S) & 1, kGcDrainLimit, &no_abort))
+          atomicOr(p.ctl.status, kDevTimeoutDrain);
+      }
+    }
+  } else {
+    pdl_wait();  // predecessor kernel complete, its writes visible
+    const int cw = warp - 1;
+    const int g4 = lane >> 2;
+    const int c = lane & 3;
+    const int M = p.M;
+    uint32_t lofs[4], sofs[4][2];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      lofs[b] = qs_offset(32 * cw + 8 * b + (lane & 7), lane >> 3);
+      sofs[b][0] = scale_offset(32 * cw + 8 * b + g4, 0);
+      sofs[b][1] = scale_offset(32 * cw + 8 * b + g4, 1);
+    }
+    const __nv_bfloat16 *xh[MT];
+    const __nv_bfloat16 *xl[MT];
+    bool live[MT];
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt) {
+      const int m = mt * 8 + g4;
+      live[mt] = m < M;
+      xh[mt] = p.xh + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + 4 * c;
+      xl[mt] = SPLITX ? p.xl + static_cast<int64_t>(live[mt] ? m : 0) * p.ldx + 4 * c : nullptr;
+    }
+    float acc[2][MT][4];
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi)
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[gi][mt][e] = 0.f;
+    uint2 xc[MT][4], xcl[MT][4];
+    if (n_my > 0) {
+      load_x_chunk<MT>(xc, xh, live, static_cast<int>(rank));
+      if (SPLITX) load_x_chunk<MT>(xcl, xl, live, static_cast<int>(rank));
+    }
+    for (int i = 0; i < n_my; ++i) {
+      const int s = i % S;
+      bool ok = mbar_wait(full_bar(s), (i / S) & 1, p.ctl.wait_limit, flags);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0 && !flags[0]) report(p.ctl, flags, kDevTimeoutConsumer);
+        break;
+      }
+      const uint8_t *sp = ring + s * kTileBytes;
+      const uint32_t sa = smem_u32(sp);
+      uint32_t R[4][4];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) ldsm_x4(sa + lofs[b], R[b]);
+      uint16_t dv[4][2];
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        dv[b][0] = *reinterpret_cast<const uint16_t *>(sp + sofs[b][0]);
+        dv[b][1] = *reinterpret_cast<const uint16_t *>(sp + sofs[b][1]);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(s));
+      // next chunk's activations, one chunk ahead of their use
+      uint2 xn[MT][4], xnl[MT][4];
+      const bool more = i + 1 < n_my;
+      if (more) {
+        load_x_chunk<MT>(xn, xh, live, static_cast<int>(rank) + (i + 1) * cl);
+        if (SPLITX) load_x_chunk<MT>(xnl, xl, live, static_cast<int>(rank) + (i + 1) * cl);
+      }
+#pragma unroll
+      for (int gi = 0; gi < 2; ++gi) {
+        const int ba = 2 * gi, bb = 2 * gi + 1;
+        const float ca[2] = {neg1152(dv[ba][0]), neg1152(dv[ba][1])};
+        const float cb[2] = {neg1152(dv[bb][0]), neg1152(dv[bb][1])};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t a[4];
+          dequant4_bf16_mix(R[ba][q], dv[ba][q >> 1], ca[q >> 1], a[0], a[2]);
+          dequant4_bf16_mix(R[bb][q], dv[bb][q >> 1], cb[q >> 1], a[1], a[3]);
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt) {
+            mma_16816_bf16(acc[gi][mt], a, xc[mt][q].x, xc[mt][q].y);
+            if (SPLITX) mma_16816_bf16(acc[gi][mt], a, xcl[mt][q].x, xcl[mt][q].y);
+          }
+        }
+      }
+      if (more) {
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            xc[mt][q] = xn[mt][q];
+            if (SPLITX) xcl[mt][q] = xnl[mt][q];
+          }
+      }
+    }
+    // this rank's partial: part[m][row] (m < MT * 8; rows m >= M hold zeros)
+#pragma unroll
+    for (int gi = 0; gi < 2; ++gi) {
+      const int ra = 32 * cw + 16 * gi + g4;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int m0 = mt * 8 + 2 * c;
+        part[m0 * kPackRows + ra] = acc[gi][mt][0];
+        part[m0 * kPackRows + ra + 8] = acc[gi][mt][2];
+        part[(m0 + 1) * kPackRows + ra] = acc[gi][mt][1];
+        part[(m0 + 1) * kPackRows + ra + 8] = acc[gi][mt][3];
+      }
+    }
+  }
+  pdl_wait();  // every thread: the predecessor's writes are visible before the epilogue touches outputs
+  __syncthreads();
+  cluster_sync_all();  // every rank's partial is in place
+  const int M = p.M;
+  if (rank == 0) {
+    for (int idx = threadIdx.x; idx < M * kPackRows; idx += kGemvThreads) {
+      float v = part[idx];
+      for (int k = 1; k < cl; ++k) v += ld_cluster_f32(map_rank(smem_u32(&part[idx]), static_cast<uint32_t>(k)));
+      tot[idx] = v;
+    }
+  }
+  cluster_sync_all();  // the peers' partials are read: they may leave
+  if (rank != 0) return;
+  if (!p.res_out) {
+    if (pr.glu) {
+      for (int idx = threadIdx.x; idx < M * 64; idx += kGemvThreads) {
+        const int m = idx >> 6, r = idx & 63;
+        const int64_t j = static_cast<int64_t>(tl) * 64 + r;
+        if (j >= pr.n_out) continue;
+        float v = tot[m * kPackRows + r], gt = tot[m * kPackRows + 64 + r];
+        if (pr.bias) {
+          v += pr.bias[j];
+          gt += pr.bias[pr.n_out + j];
+        }
+        store_out(pr.y, p.y_dtype, m * pr.ldy + j, act_glu(p.epi, v, gt));
+      }
+    } else {
+      for (int idx = threadIdx.x; idx < M * kPackRows; idx += kGemvThreads) {
+        const int m = idx >> 7, r = idx & 127;
+        const int64_t n = static_cast<int64_t>(tl) * kPackRows + r;
+        if (n >= pr.N) continue;
+        float v = tot[idx];
+        if (pr.bias) v += pr.bias[n];
+        store_out(pr.y, p.y_dtype, m * pr.ldy + n, act_single(p.epi, v));
+      }
+    }
+    return;
+  }
+  // residual add of this tile's rows, then the tile count
+  for (int idx = threadIdx.x; idx < M * kPackRows; idx += kGemvThreads) {
+    const int m = idx >> 7, r = idx & 127;
+    const int64_t n = static_cast<int64_t>(tl) * kPackRows + r;
+    if (n >= pr.N) continue;
+    float a = tot[idx];
+    if (pr.bias) a += pr.bias[n];
+    a += p.res_in[m * p.ld_res + n];
+    p.res_out[m * p.ld_res + n] = a;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this CTA's residual rows are visible before the count
+    flags[1] = atomicAdd(&p.sched[1], 1);
+    __threadfence();  // acquire: the other clusters' rows, when this is the last count
+  }
+  __syncthreads();
+  if (flags[1] != total_tiles - 1) return;
+  // last cluster: LayerNorm of every row (rows read once into registers in
+  // pieces of 8 values per thread, so up to 1,280 wide rows take one read)
+  const int N = static_cast<int>(pr.N);
+  constexpr int kPer = 8;
+  for (int m = 0; m < M; ++m) {
+    const float *row = p.res_out + m * p.ld_res;
+    float s = 0.f;
+    for (int n0 = 0; n0 < N; n0 += kPer * kGemvThreads) {
+      float v[kPer];
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int n = n0 + threadIdx.x + i * kGemvThreads;
+        v[i] = n < N ? __ldcg(row + n) : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) s += v[i];
+    }
+    const float mean = gc_block_sum(s, red) / static_cast<float>(N);
+    float q = 0.f;
+    for (int n0 = 0; n0 < N; n0 += kPer * kGemvThreads) {
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int n = n0 + threadIdx.x + i * kGemvThreads;
+        const float d = n < N ? __ldcg(row + n) - mean : 0.f;
+        q += d * d;
+      }
+    }
+    const float rstd = rsqrtf(gc_block_sum(q, red) / static_cast<float>(N) + p.ln_eps);
+    for (int n = threadIdx.x; n < N; n += kGemvThreads)
+      store_out(pr.y, p.y_dtype, m * pr.ldy + n,
+                (__ldcg(row + n) - mean) * rstd * p.ln_g[n] + (p.ln_b ? p.ln_b[n] : 0.f));
+  }
+  if (threadIdx.x == 0) atomicExch(&p.sched[1], 0);  // every tile has counted: re-arm
+}
+
+template <int MT, bool SPLITX>
+static cudaError_t launch_gemv_cluster_t(const GemvParams &p, int cl, cudaStream_t stream) {
+  auto kern = gemv_cluster_kernel<MT, SPLITX>;
+  static bool attr_set[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !attr_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kGcSmemBytes));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+    if (dev < 64) attr_set[dev] = true;
+  }
+  const int tiles = p.prob[0].n_tiles + p.prob[1].n_tiles + p.prob[2].n_tiles;
+  return launch_pdl(kern, dim3(tiles * cl), dim3(kGemvThreads), kGcSmemBytes, stream, static_cast<unsigned>(cl), p,
+                    cl);
+}
+
 template <int MT, bool SPLITX>
 static cudaError_t launch_gemv_t(const GemvParams &p, int ctas, cudaStream_t stream) {
   auto kern = gemv_q8_kernel<MT, SPLITX>;
@@ -533,8 +851,30 @@ static cudaError_t launch_gemv_t(const GemvParams &p, int ctas, cudaStream_t str
   return launch_pdl(kern, dim3(ctas), dim3(kGemvThreads), kGemvSmemBytes, stream, 1, p);
 }
 
+// AUTO takes the cluster form for plain calls of at most 8 rows whose CTAs
+// get at most 5 k chunks (measured on B200: 640 x 640 3.2 vs 3.9 us,
+// 640 -> 32,768 8.6 vs 9.7 us; at 8 chunks per CTA, 4096 x 4096, and with
+// 16 rows the split form's dynamic schedule is faster).  A residual +
+// LayerNorm call keeps the split form (its 1,024-thread LayerNorm launch is
+// faster than one CTA's) unless CLUSTER is forced.
+int gemv_cluster_size(int total_tiles, int kc, int sm_count, int path, bool resadd, int m) {
+  if (path == 1 || (path != 2 && (resadd || m > 8))) return 0;
+  const int slots = kGemvCtasPerSm * sm_count;
+  const int max_chunks = path == 2 ? 8 : 5;
+  for (int cl = 8; cl >= 1; cl >>= 1)
+    if (cl <= kc && total_tiles * cl <= slots && (kc + cl - 1) / cl <= max_chunks) return cl;
+  return 0;
+}
+
 cudaError_t launch_gemv(const GemvParams &p, int ctas, cudaStream_t stream) {
   const bool splitx = p.xl != nullptr;
+  const int tiles = p.prob[0].n_tiles + p.prob[1].n_tiles + p.prob[2].n_tiles;
+  const int cl = gemv_cluster_size(tiles, p.kc, p.sm_count, p.path, p.res_out != nullptr, p.M);
+  if (cl > 0) {
+    if (p.M <= 8)
+      return splitx ? launch_gemv_cluster_t<1, true>(p, cl, stream) : launch_gemv_cluster_t<1, false>(p, cl, stream);
+    return splitx ? launch_gemv_cluster_t<2, true>(p, cl, stream) : launch_gemv_cluster_t<2, false>(p, cl, stream);
+  }
   cudaError_t e;
   if (p.M <= 8)
     e = splitx ? launch_gemv_t<1, true>(p, ctas, stream) : launch_gemv_t<1, false>(p, ctas, stream);

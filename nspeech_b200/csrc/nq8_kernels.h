@@ -38,7 +38,9 @@ struct GemvParams {
   int upt;     // units per tile: ceil(kc / unit)
   int units;   // units of all problems, tile-major
   int ctas;    // CTAs launched; CTA c starts with unit c
-  int *sched;  // [0] work counter: zero between calls (gemv_reduce re-arms it)
+  int *sched;  // [0] work counter, [1] cluster form's tile arrivals: zero between calls (re-armed by the kernels)
+  int sm_count;
+  int path;    // 0: the cost rule below, 1: always the split + reduce form, 2: the cluster form where it applies
   // Decoder-step epilogue (one problem; res_out non-null selects it): the
   // row is y = W x + bias, res_out = res_in + y, prob[0].y = LN(res_out).
   const float *res_in;
@@ -56,8 +58,14 @@ struct GemvPlan {
   int unit, upt, units, ctas;
 };
 GemvPlan gemv_plan(int sm_count, int total_tiles, int kc, int m);
-// The GEMV (ctas CTAs) and its gemv_reduce: two launches.
+// The GEMV (ctas CTAs) and its gemv_reduce: two launches.  Latency-bound
+// plain calls (at most 8 rows, at most 5 k chunks per CTA with the tile's k
+// over a cluster of up to 8 CTAs, all CTAs in one wave) instead run the
+// cluster form: one launch, the partial sums meet in distributed shared
+// memory.
 cudaError_t launch_gemv(const GemvParams &p, int ctas, cudaStream_t stream);
+// Cluster size the cluster form uses for a call (0: the split + reduce form).
+int gemv_cluster_size(int total_tiles, int kc, int sm_count, int path, bool resadd, int m);
 
 // Decode chain (nq8_chain.cu): the dependent M = 1 GEMV steps of a decoder
 // token in one cooperative launch.  Step s reads a bf16 vector x (or, with

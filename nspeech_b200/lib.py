@@ -48,6 +48,10 @@ NQ_ATTENTION_MMA_SYNC = 1
 NQ_CONV_AUTO = 0
 NQ_CONV_IM2COL = 1
 
+NQ_GEMV_AUTO = 0
+NQ_GEMV_SPLIT = 1
+NQ_GEMV_CLUSTER = 2
+
 
 class NqError(RuntimeError):
     """A non-zero status from libnq8 (carries the code and the library message)."""
@@ -126,6 +130,7 @@ SIGNATURES = {
     "nq_set_gemm_tail_split": (_I, [_I]),
     "nq_set_attention_kernel": (_I, [_I]),
     "nq_set_conv_path": (_I, [_I]),
+    "nq_set_gemv_path": (_I, [_I]),
     "nq_chain_create": (_I, [ctypes.POINTER(_P)]),
     "nq_chain_linear": (_I, [_P, _P, _P, _P, _I, _P, _I]),
     "nq_chain_gemv_resadd_ln": (_I, [_P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_float, _P]),

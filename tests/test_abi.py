@@ -50,6 +50,10 @@ def test_null_arguments_are_rejected_without_device_work():
         assert lib.nq_set_attention_kernel(bad) == L.NQ_ERR_ARG, bad
     for ok in (L.NQ_ATTENTION_MMA_SYNC, L.NQ_ATTENTION_TCGEN05):
         assert lib.nq_set_attention_kernel(ok) == L.NQ_OK, ok
+    for bad in (-1, 3):
+        assert lib.nq_set_gemv_path(bad) == L.NQ_ERR_ARG, bad
+    for ok in (L.NQ_GEMV_SPLIT, L.NQ_GEMV_CLUSTER, L.NQ_GEMV_AUTO):
+        assert lib.nq_set_gemv_path(ok) == L.NQ_OK, ok
     for bad in (-1, 2):
         assert lib.nq_set_conv_path(bad) == L.NQ_ERR_ARG, bad
     for ok in (L.NQ_CONV_IM2COL, L.NQ_CONV_AUTO):

@@ -441,10 +441,56 @@ def test_wait_timeout_reports_and_recovers(nq, oracle):
     _check(oracle, _run(w, x), _ref(oracle, x, q, 256), "after timeout")
 
 
+@pytest.fixture
+def gemv_path(nq):
+    """Select the GEMV form for one test (nq_set_gemv_path), AUTO after it."""
+    L = nq.load()
+
+    def set_path(path):
+        nq.check(L.nq_set_gemv_path(path))
+
+    yield set_path
+    nq.check(L.nq_set_gemv_path(nq.NQ_GEMV_AUTO))
+
+
+# Both GEMV forms -- k split over all SMs + reduce launch, and each tile's k
+# over a cluster with the partials added in distributed shared memory -- on
+# the decoder's shapes and on shapes at the edges of the cluster rule (one k
+# chunk; the lm_head's 256 tiles; 16 rows; f32 activations; GLU).
+@pytest.mark.parametrize("m,k,n,flags,epi,dt", [
+    (1, 640, 640, 0, 0, "bf16"), (1, 640, 1920, 0, 0, "bf16"), (1, 640, 5120, 1, 4, "bf16"),
+    (1, 2560, 640, 0, 1, "bf16"), (1, 640, 32768, 0, 0, "bf16"), (8, 4096, 4096, 0, 2, "bf16"),
+    (16, 1024, 3000, 0, 0, "f32"), (4, 64, 200, 0, 5, "f32"), (3, 512, 4096, 1, 3, "f32")])
+def test_gemv_forms_match_oracle(nq, oracle, gemv_path, m, k, n, flags, epi, dt):
+    from nspeech_b200.fast_matmul import QWeight
+    q = oracle.quantize_q8_0(oracle.normal(70 + n + k, (n, k), 0.0, 0.02))
+    w = QWeight.from_q8_0(q, n, k, flags=flags)
+    x = oracle.normal(71, (m, k))
+    bias = oracle.normal(72, (n,), 0.0, 0.1)
+    if dt == "bf16":
+        x = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    ref = _ref(oracle, x, q, n, bias, epi) if not flags else None
+    outs = []
+    for path in (1, 2):
+        gemv_path(path)
+        y = _run(w, x, torch.float32 if dt == "f32" else torch.bfloat16, bias=bias, epi=epi)
+        y2 = _run(w, x, torch.float32 if dt == "f32" else torch.bfloat16, bias=bias, epi=epi)
+        assert np.array_equal(y, y2)  # deterministic
+        outs.append(y)
+    if ref is not None:
+        for got in outs:
+            _check(oracle, got, ref, f"gemv {m}x{k}x{n}")
+    # same products, f32 sums in another order
+    scale = max(1.0, float(np.abs(outs[0]).max()))
+    assert np.abs(outs[0] - outs[1]).max() <= 1e-3 * scale
+    assert nq.status() == 0
+
+
 # nq_gemv_resadd_ln: decoder-step GEMV with the fused residual add + LayerNorm
 # (DecoderBackend::gemv_resadd_ln).  Moonshine decoder shapes (640 -> 640 O
 # projections, 2560 -> 640 fc2), an odd width, and several rows; in-place
 # residual, with and without bias / beta, bf16 and f32 outputs.
+@pytest.mark.parametrize("path", [1, 2])  # NQ_GEMV_SPLIT, NQ_GEMV_CLUSTER
 @pytest.mark.parametrize("m,k,n,bias,beta,inplace,odt", [
     (1, 640, 640, False, False, False, torch.bfloat16),
     (1, 2560, 640, True, False, True, torch.bfloat16),
@@ -452,8 +498,9 @@ def test_wait_timeout_reports_and_recovers(nq, oracle):
     (16, 640, 640, True, True, True, torch.float32),
     (1, 4096, 8192, False, True, False, torch.bfloat16),
 ])
-def test_gemv_resadd_ln_matches_oracle(nq, oracle, m, k, n, bias, beta, inplace, odt):
+def test_gemv_resadd_ln_matches_oracle(nq, oracle, gemv_path, m, k, n, bias, beta, inplace, odt, path):
     from nspeech_b200.fast_matmul import QWeight
+    gemv_path(path)
     q = oracle.quantize_q8_0(oracle.normal(60 + n, (n, k), 0.0, 0.02))
     w = QWeight.from_q8_0(q, n, k)
     x = oracle.normal(61, (m, k))
