@@ -104,24 +104,67 @@ __global__ void __launch_bounds__(256) im2col_kernel(const void *__restrict__ x,
   }
 }
 
-// Token-major operand planes of the implicit conv1d: hi[t][c] =
+// Token-major operand planes of the implicit convs: hi[t][c] =
 // bf16(leaky(x[c][t])), lo[t][c] = bf16(v - hi) (f32 x only).  A block moves
-// a 64-channel x 32-frame tile through shared memory: loads coalesced along
-// time, stores of whole 128-byte channel rows per frame.
+// a 64-channel x 32-frame tile through shared memory.  Loads run along time,
+// 16 bytes per thread where the vector lies inside the row (issued before
+// their use).  Stores write whole 128-byte channel runs per frame.
+constexpr int kTokT = 32;
 __global__ void __launch_bounds__(256) conv_tokens_kernel(const void *__restrict__ x, int x_dtype, int64_t ldx, int c_in,
                                                           int t_in, float slope, __nv_bfloat16 *__restrict__ hi,
-                                                          __nv_bfloat16 *__restrict__ lo) {
+                                                          __nv_bfloat16 *__restrict__ lo, int vec) {
   pdl_wait();
   pdl_trigger();
-  __shared__ float tile[64][33];
-  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 64;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  for (int c = ty; c < 64; c += 8) {
-    const int t = t0 + tx;
-    tile[c][tx] = t < t_in ? leaky(load_x(x, x_dtype, static_cast<int64_t>(c0 + c) * ldx + t), slope) : 0.f;
+  __shared__ float tile[64][kTokT + 1];
+  const int t0 = blockIdx.x * kTokT, c0 = blockIdx.y * 64;
+  if (x_dtype != 0) {
+    // bf16: 8 frames per vector, 4 vectors per channel row of the tile, one per thread
+    const __nv_bfloat16 *xb = static_cast<const __nv_bfloat16 *>(x);
+    const int q = threadIdx.x, c = q >> 2, tl = (q & 3) * 8, t = t0 + tl;
+    const __nv_bfloat16 *src = xb + static_cast<int64_t>(c0 + c) * ldx + t;
+    uint4 v;
+    if (vec && t + 8 <= t_in) {
+      v = __ldg(reinterpret_cast<const uint4 *>(src));
+    } else {
+      uint16_t e[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) e[u] = t + u < t_in ? __bfloat16_as_ushort(src[u]) : 0;
+      v = make_uint4(e[0] | (uint32_t(e[1]) << 16), e[2] | (uint32_t(e[3]) << 16), e[4] | (uint32_t(e[5]) << 16),
+                     e[6] | (uint32_t(e[7]) << 16));
+    }
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      tile[c][tl + 2 * u] = leaky(bf16_bits_to_f32(w[u] & 0xffffu), slope);
+      tile[c][tl + 2 * u + 1] = leaky(bf16_bits_to_f32(w[u] >> 16), slope);
+    }
+  } else {
+    // f32: 4 frames per vector, 8 vectors per channel row of the tile, two per thread
+    const float *xf = static_cast<const float *>(x);
+    float4 v[2];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = threadIdx.x + i * 256, c = q >> 3, t = t0 + (q & 7) * 4;
+      const float *src = xf + static_cast<int64_t>(c0 + c) * ldx + t;
+      if (vec && t + 4 <= t_in) {
+        v[i] = __ldg(reinterpret_cast<const float4 *>(src));
+      } else {
+        v[i] = make_float4(t < t_in ? src[0] : 0.f, t + 1 < t_in ? src[1] : 0.f, t + 2 < t_in ? src[2] : 0.f,
+                           t + 3 < t_in ? src[3] : 0.f);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int q = threadIdx.x + i * 256, c = q >> 3, tl = (q & 7) * 4;
+      tile[c][tl] = leaky(v[i].x, slope);
+      tile[c][tl + 1] = leaky(v[i].y, slope);
+      tile[c][tl + 2] = leaky(v[i].z, slope);
+      tile[c][tl + 3] = leaky(v[i].w, slope);
+    }
   }
   __syncthreads();
-  for (int r = ty; r < 32; r += 8) {
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  for (int r = ty; r < kTokT; r += 8) {
     const int t = t0 + r;
     if (t >= t_in) break;
     const float v0 = tile[2 * tx][r], v1 = tile[2 * tx + 1][r];
@@ -265,8 +308,11 @@ cudaError_t launch_conv_tokens(const void *x, int x_dtype, int64_t ldx, int c_in
                                __nv_bfloat16 *hi, __nv_bfloat16 *lo, cudaStream_t s) {
   if (t_in == 0) return cudaSuccess;
   if (c_in % 64) return cudaErrorInvalidValue;
-  const dim3 grid((t_in + 31) / 32, c_in / 64);
-  return launch_pdl(conv_tokens_kernel, grid, dim3(256), 0, s, 1, x, x_dtype, ldx, c_in, t_in, slope, hi, lo);
+  // 16-byte loads need 16-byte aligned rows (base and row stride)
+  const int per_vec = x_dtype == 0 ? 4 : 8;
+  const int vec = (reinterpret_cast<uintptr_t>(x) % 16 == 0 && ldx % per_vec == 0) ? 1 : 0;
+  const dim3 grid((t_in + kTokT - 1) / kTokT, c_in / 64);
+  return launch_pdl(conv_tokens_kernel, grid, dim3(256), 0, s, 1, x, x_dtype, ldx, c_in, t_in, slope, hi, lo, vec);
 }
 
 cudaError_t launch_conv_tap_weight(const __nv_bfloat16 *src, int64_t ld_src, int rows, int c_in, int K,
