@@ -4,6 +4,8 @@
 // the glue between them.  Batches of padded segments: every kernel that mixes
 // frames (convolutions, attention) reads frames >= the segment's own length as
 // zero (keys: masked), so a padded batch reproduces per-segment results.
+#include <algorithm>
+
 #include "nq8_common.cuh"
 #include "nq8_encoder.h"
 
@@ -408,98 +410,130 @@ __global__ void flatten_cf_kernel(const __nv_bfloat16 *__restrict__ in, int rows
 // mode kLnResAdd: x = x + alpha * u (u bf16);       h1 = LN1(x)
 // mode kLnResAddOut: x = LN1(x + alpha * u) (final norm_out, stored f32);
 //                    h1 = LN2(x) if g2 != null (next layer's first norm)
+// The grid is persistent (a few blocks per SM; each warp strides over the
+// rows), and the LayerNorm parameters are staged once per block in shared
+// memory before the dependency wait -- no kernel writes them.  A row then
+// costs one global round trip (its x and u loads, issued together), not
+// three (x/u, then gamma/beta of each LayerNorm after the reductions), and a
+// warp issues the loads of its next row before the reductions of the current
+// one, so that round trip overlaps the current row's work.
+constexpr int kLnThreads = 256;
+// Resident blocks per SM: a D = 1024 row in flight takes 48 registers per
+// lane, and a warp holds one in flight beside the row it computes.
+__host__ __device__ constexpr int ln_min_blocks(int kVec) { return kVec >= 8 ? 2 : 3; }
 template <int kVec>
-__global__ void ln_row_kernel(int mode, float *__restrict__ x, const void *__restrict__ u, float alpha, int rows,
-                              const float *__restrict__ g1, const float *__restrict__ b1,
-                              const float *__restrict__ g2, const float *__restrict__ b2,
-                              __nv_bfloat16 *__restrict__ h, float eps) {
+__global__ void __launch_bounds__(kLnThreads, ln_min_blocks(kVec))
+    ln_row_kernel(int mode, float *__restrict__ x, const void *__restrict__ u, float alpha, int rows,
+                  const float *__restrict__ g1, const float *__restrict__ b1, const float *__restrict__ g2,
+                  const float *__restrict__ b2, __nv_bfloat16 *__restrict__ h, float eps) {
+  constexpr int D = 32 * 4 * kVec;
+  constexpr int kQ = D / 4;  // float4 per parameter vector
+  extern __shared__ float4 ln_par[];  // g1 | b1 | g2 | b2, kQ float4 each (g2, b2 when given)
+  {
+    const int n = (g2 ? 4 : 2) * kQ;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const int which = i / kQ;
+      const float *src = which == 0 ? g1 : which == 1 ? b1 : which == 2 ? g2 : b2;
+      ln_par[i] = reinterpret_cast<const float4 *>(src)[i - which * kQ];
+    }
+  }
+  __syncthreads();
   pdl_wait();  // predecessor kernel complete, its writes visible
   pdl_trigger();
-  constexpr int D = 32 * 4 * kVec;
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  if (warp >= rows) return;
-  float *xr = x + static_cast<int64_t>(warp) * D;
-  float v[kVec][4];
+  const int nwarps = gridDim.x * (blockDim.x >> 5);
+  float4 ra[kVec];  // the x row (kLnScale: the f32 u row)
+  uint2 rb[kVec];   // the bf16 u row (kLnResAdd, kLnResAddOut)
+  auto load = [&](int r) {
+    const int64_t off = static_cast<int64_t>(r) * D;
 #pragma unroll
-  for (int i = 0; i < kVec; ++i) {
-    const int col = (i * 32 + lane) * 4;
-    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (mode != kLnScale) a = *reinterpret_cast<const float4 *>(xr + col);
-    float uu[4];
-    if (mode == kLnScale) {
-      const float4 t = *reinterpret_cast<const float4 *>(static_cast<const float *>(u) + static_cast<int64_t>(warp) * D + col);
-      uu[0] = t.x; uu[1] = t.y; uu[2] = t.z; uu[3] = t.w;
-    } else {
-      const uint2 t = *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(u) + static_cast<int64_t>(warp) * D + col);
-      uu[0] = bf16_bits_to_f32(t.x & 0xffffu); uu[1] = bf16_bits_to_f32(t.x >> 16);
-      uu[2] = bf16_bits_to_f32(t.y & 0xffffu); uu[3] = bf16_bits_to_f32(t.y >> 16);
-    }
-    v[i][0] = a.x + alpha * uu[0];
-    v[i][1] = a.y + alpha * uu[1];
-    v[i][2] = a.z + alpha * uu[2];
-    v[i][3] = a.w + alpha * uu[3];
-  }
-  auto normalize = [&](const float *g, const float *bb) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < kVec; ++i) s += v[i][0] + v[i][1] + v[i][2] + v[i][3];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float mean = s * (1.0f / D);
-    float q = 0.f;
-#pragma unroll
-    for (int i = 0; i < kVec; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float dlt = v[i][e] - mean;
-        q += dlt * dlt;
+    for (int i = 0; i < kVec; ++i) {
+      const int col = (i * 32 + lane) * 4;
+      if (mode == kLnScale) {
+        ra[i] = *reinterpret_cast<const float4 *>(static_cast<const float *>(u) + off + col);
+      } else {
+        ra[i] = *reinterpret_cast<const float4 *>(x + off + col);
+        rb[i] = *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(u) + off + col);
       }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
-    const float rstd = rsqrtf(q * (1.0f / D) + eps);
-    float out[kVec][4];
-#pragma unroll
-    for (int i = 0; i < kVec; ++i) {
-      const int col = (i * 32 + lane) * 4;
-      const float4 gg = *reinterpret_cast<const float4 *>(g + col);
-      const float4 bv = *reinterpret_cast<const float4 *>(bb + col);
-      out[i][0] = (v[i][0] - mean) * rstd * gg.x + bv.x;
-      out[i][1] = (v[i][1] - mean) * rstd * gg.y + bv.y;
-      out[i][2] = (v[i][2] - mean) * rstd * gg.z + bv.z;
-      out[i][3] = (v[i][3] - mean) * rstd * gg.w + bv.w;
-    }
-#pragma unroll
-    for (int i = 0; i < kVec; ++i)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[i][e] = out[i][e];
-  };
-  auto store_h = [&]() {
-    __nv_bfloat16 *hr = h + static_cast<int64_t>(warp) * D;
-#pragma unroll
-    for (int i = 0; i < kVec; ++i) {
-      const int col = (i * 32 + lane) * 4;
-      *reinterpret_cast<uint2 *>(hr + col) = make_uint2(pack_bf16x2(v[i][0], v[i][1]), pack_bf16x2(v[i][2], v[i][3]));
     }
   };
-  auto store_x = [&]() {
+  int warp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (warp < rows) load(warp);
+  for (; warp < rows; warp += nwarps) {
+    float *xr = x + static_cast<int64_t>(warp) * D;
+    float v[kVec][4];
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {
-      const int col = (i * 32 + lane) * 4;
-      *reinterpret_cast<float4 *>(xr + col) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+      float uu[4];
+      if (mode == kLnScale) {
+        uu[0] = ra[i].x; uu[1] = ra[i].y; uu[2] = ra[i].z; uu[3] = ra[i].w;
+      } else {
+        a = ra[i];
+        uu[0] = bf16_bits_to_f32(rb[i].x & 0xffffu); uu[1] = bf16_bits_to_f32(rb[i].x >> 16);
+        uu[2] = bf16_bits_to_f32(rb[i].y & 0xffffu); uu[3] = bf16_bits_to_f32(rb[i].y >> 16);
+      }
+      v[i][0] = a.x + alpha * uu[0];
+      v[i][1] = a.y + alpha * uu[1];
+      v[i][2] = a.z + alpha * uu[2];
+      v[i][3] = a.w + alpha * uu[3];
     }
-  };
-  if (mode == kLnResAddOut) {
-    normalize(g1, b1);
-    store_x();
-    if (g2) {
-      normalize(g2, b2);
+    if (warp + nwarps < rows) load(warp + nwarps);  // next row: in flight during this row's work
+    auto normalize = [&](const float4 *g, const float4 *bb) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) s += v[i][0] + v[i][1] + v[i][2] + v[i][3];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float mean = s * (1.0f / D);
+      float q = 0.f;
+#pragma unroll
+      for (int i = 0; i < kVec; ++i)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float dlt = v[i][e] - mean;
+          q += dlt * dlt;
+        }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+      const float rstd = rsqrtf(q * (1.0f / D) + eps);
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) {
+        const float4 gg = g[i * 32 + lane];
+        const float4 bv = bb[i * 32 + lane];
+        v[i][0] = (v[i][0] - mean) * rstd * gg.x + bv.x;
+        v[i][1] = (v[i][1] - mean) * rstd * gg.y + bv.y;
+        v[i][2] = (v[i][2] - mean) * rstd * gg.z + bv.z;
+        v[i][3] = (v[i][3] - mean) * rstd * gg.w + bv.w;
+      }
+    };
+    auto store_h = [&]() {
+      __nv_bfloat16 *hr = h + static_cast<int64_t>(warp) * D;
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) {
+        const int col = (i * 32 + lane) * 4;
+        *reinterpret_cast<uint2 *>(hr + col) = make_uint2(pack_bf16x2(v[i][0], v[i][1]), pack_bf16x2(v[i][2], v[i][3]));
+      }
+    };
+    auto store_x = [&]() {
+#pragma unroll
+      for (int i = 0; i < kVec; ++i) {
+        const int col = (i * 32 + lane) * 4;
+        *reinterpret_cast<float4 *>(xr + col) = make_float4(v[i][0], v[i][1], v[i][2], v[i][3]);
+      }
+    };
+    if (mode == kLnResAddOut) {
+      normalize(ln_par, ln_par + kQ);
+      store_x();
+      if (g2) {
+        normalize(ln_par + 2 * kQ, ln_par + 3 * kQ);
+        store_h();
+      }
+    } else {
+      store_x();
+      normalize(ln_par, ln_par + kQ);
       store_h();
     }
-  } else {
-    store_x();
-    normalize(g1, b1);
-    store_h();
   }
 }
 
@@ -943,13 +977,25 @@ cudaError_t flatten_cf(const __nv_bfloat16 *in, int rows, int F, int C, __nv_bfl
 cudaError_t ln_rows(int mode, float *x, const void *u, float alpha, int rows, int D, const float *g1, const float *b1,
                     const float *g2, const float *b2, __nv_bfloat16 *h, float eps, cudaStream_t s) {
   if (D != 1024 && D != 512) return cudaErrorInvalidValue;
-  const int threads = 256;
-  const int blocks = (rows * 32 + threads - 1) / threads;
+  if (rows <= 0) return cudaSuccess;
+  static int sms[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 64) return cudaErrorInvalidDevice;
+  if (!sms[dev]) {
+    int n = 0;
+    const cudaError_t e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    sms[dev] = n;
+  }
+  const int per_block = kLnThreads / 32;
+  const int blocks = std::min((rows + per_block - 1) / per_block, sms[dev] * ln_min_blocks(D / 128));
+  const size_t smem = static_cast<size_t>(g2 ? 4 : 2) * D * sizeof(float);
   if (D == 1024)
-    return launch_pdl(ln_row_kernel<8>, dim3(blocks), dim3(threads), 0, s, 1, mode, x, u, alpha, rows, g1, b1, g2, b2, h,
-                      eps);
-  return launch_pdl(ln_row_kernel<4>, dim3(blocks), dim3(threads), 0, s, 1, mode, x, u, alpha, rows, g1, b1, g2, b2, h,
-                    eps);
+    return launch_pdl(ln_row_kernel<8>, dim3(blocks), dim3(kLnThreads), smem, s, 1, mode, x, u, alpha, rows, g1, b1,
+                      g2, b2, h, eps);
+  return launch_pdl(ln_row_kernel<4>, dim3(blocks), dim3(kLnThreads), smem, s, 1, mode, x, u, alpha, rows, g1, b1, g2,
+                    b2, h, eps);
 }
 
 cudaError_t dwconv1d_bn_silu(const __nv_bfloat16 *in, const int *len, int B, int Tp, int D, int K, const float *w,
