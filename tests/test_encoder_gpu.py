@@ -171,6 +171,35 @@ def test_batched_segments_equal_single(nq, oracle):
         _compare(oracle, out[i, :olens[i]], ref, f"batched seg {i} len {L}", 0.05)
 
 
+@pytest.mark.parametrize("d_model,heads,blocks_per_sm", [(512, 4, 3), (1024, 8, 2)])
+def test_layernorm_rows_beyond_one_grid_pass(nq, oracle, d_model, heads, blocks_per_sm):
+    """More token rows than the LayerNorm kernel's persistent grid has warps
+    (SMs x resident blocks x 8 warps; blocks_per_sm mirrors ln_min_blocks in
+    nq8_encoder_kernels.cu): warps take a second row, whose loads are issued
+    during the first row's work.  The segments holding those rows match their
+    own single-segment forwards, which run one row per warp."""
+    from nspeech_b200 import synthetic as S
+    from nspeech_b200.encoder import out_frames
+    spec = S.EncoderSpec(d_model=d_model, n_heads=heads, n_layers=1, sub_channels=64)
+    q = _model(oracle, spec, seed=17)
+    enc = _gpu_encoder(spec, q)
+    t_mel = 2500
+    tp = out_frames(t_mel)
+    grid_warps = torch.cuda.get_device_properties(0).multi_processor_count * blocks_per_sm * 8
+    n = grid_warps // tp + 2
+    assert (n - 1) * tp >= grid_warps  # the last segment lies wholly past the first grid pass
+    mel = oracle.normal(70, (n, t_mel, 128))
+    out, olens = enc.forward(torch.from_numpy(mel).cuda())
+    out = out.cpu().numpy()
+    for i in (n - 2, n - 1):
+        single, _ = enc.forward(torch.from_numpy(mel[i:i + 1]).cuda().contiguous())
+        single = single[0].cpu().numpy()
+        assert olens[i] == tp
+        assert np.isfinite(out[i]).all()
+        assert oracle.max_rel_err(out[i], single.astype(np.float64), 1.0) < 2e-2, i
+    assert nq.status() == 0
+
+
 def test_arena_growth_without_host_sync(nq, oracle):
     """A small bucket then larger ones on the same stream, queued without a
     host synchronize between them: the arena grows (its old buffers are freed
