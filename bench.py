@@ -63,7 +63,7 @@ sys.path.insert(0, ROOT)
 METRIC = "Parakeet encoder RTFx (audio s/s) at 1/2/4/8 B200; Q8_0 GEMM % of peak"
 UNIT = "audio s/s"
 # libnq8 kernel classes timed by its event profiler (include/nq8.h NQ_KCLASS_*).
-KCLASSES = {"gemm": 0, "gemv": 1, "dequant": 2, "reduce": 3, "attention": 4}
+KCLASSES = {"gemm": 0, "gemv": 1, "dequant": 2, "reduce": 3, "attention": 4, "layernorm": 5}
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 

@@ -403,6 +403,10 @@ void nq_encoder_free(nq_encoder *enc);
 #define NQ_KCLASS_ATTENTION 4 /* encoder relative-position attention; FLOPs
                                * 6 B Tp^2 D (QK^T, the relative band, PV over
                                * padded frames), bytes q, k, v, rel. keys, out */
+#define NQ_KCLASS_NORM 5      /* encoder residual add + LayerNorm; no FLOPs
+                               * counted, bytes per token row: the f32 residual
+                               * read and written, the added row read, the
+                               * bf16 normalized row written */
 int nq_profile_enable(int on);
 /* Synchronizes the recorded events and reports for one class: launches,
  * summed device ms, summed algorithmic FLOPs (2MNK) and bytes

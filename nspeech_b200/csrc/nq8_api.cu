@@ -1125,6 +1125,19 @@ int linear_launches(const nq_weight *w, int64_t m, int x_dtype, bool aligned) {
 
 bool attention_tc(int Tp) { return g_attention_kernel == NQ_ATTENTION_TCGEN05 && Tp <= attention_tc_max_tp(); }
 
+int layer_norm_rows(int mode, float *x, const void *u, float alpha, int rows, int D, const float *g1, const float *b1,
+                    const float *g2, const float *b2, __nv_bfloat16 *h, float eps, cudaStream_t s) {
+  // algorithmic bytes per row: x written (f32); x read unless kLnScale; u read
+  // (f32 for kLnScale, else bf16); h written (bf16) unless the final norm_out
+  // has no next LayerNorm
+  const double per_row = 4.0 * D + (mode == enc::kLnScale ? 4.0 * D : 4.0 * D + 2.0 * D) +
+                         (mode != enc::kLnResAddOut || g2 ? 2.0 * D : 0.0);
+  ProfScope ps(NQ_KCLASS_NORM, s, 0.0, per_row * rows);
+  const cudaError_t e = enc::ln_rows(mode, x, u, alpha, rows, D, g1, b1, g2, b2, h, eps, s);
+  if (e != cudaSuccess) return cuda_fail(e, "ln_rows launch");
+  return NQ_OK;
+}
+
 int relpos_bias(const __nv_bfloat16 *krel, const float *vmu, int nrel, int n_layers, int D, float *vrel,
                 cudaStream_t s) {
   const cudaError_t e = launch_relpos_bias(krel, vmu, nrel, n_layers, D, vrel, s);

@@ -47,6 +47,9 @@ cudaError_t copy_masked(const float *x, const int *len, int B, int Tp, int D, fl
 // enc::relpos_attention gets bias_u = 0 and bias_v = v - u.  Return NQ_*
 // codes.
 bool attention_tc(int Tp);
+// enc::ln_rows, timed as NQ_KCLASS_NORM when profiling; returns an NQ_* code.
+int layer_norm_rows(int mode, float *x, const void *u, float alpha, int rows, int D, const float *g1, const float *b1,
+                    const float *g2, const float *b2, __nv_bfloat16 *h, float eps, cudaStream_t s);
 int relpos_bias(const __nv_bfloat16 *krel, const float *vmu, int nrel, int n_layers, int D, float *vrel,
                 cudaStream_t s);
 int relpos_attention(const __nv_bfloat16 *qkv, const __nv_bfloat16 *krel, int64_t ldr, const float *bias_u,

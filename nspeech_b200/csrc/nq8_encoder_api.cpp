@@ -490,7 +490,7 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
                    NQ_F32, D, stv));
   const float alpha = c.scale_input ? std::sqrt(static_cast<float>(D)) : 1.0f;
   const Layer &L_0 = e->layers[0];
-  NQ_K(nq::enc::ln_rows(nq::enc::kLnScale, x, A.u32.p, alpha, M, D, L_0.ln_ff1_g, L_0.ln_ff1_b, nullptr, nullptr, h,
+  NQ_TRY(nq::layer_norm_rows(nq::enc::kLnScale, x, A.u32.p, alpha, M, D, L_0.ln_ff1_g, L_0.ln_ff1_b, nullptr, nullptr, h,
                         eps, st));
   NQ_K(nq::enc::relpos(Tp, D, A.pos.as<__nv_bfloat16>(), st));
   // relative keys of every layer: krel[p][li * D + :] = pos[p] . W_rel(li)^T
@@ -505,7 +505,7 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
     // FF1 (x0.5) -> norm_self_att
     NQ_TRY(nq_linear(L.ff1_w1, h, NQ_BF16, M, D, L.ff1_b1, NQ_EPI_SILU, t, NQ_BF16, FF, stv));
     NQ_TRY(nq_linear(L.ff1_w2, t, NQ_BF16, M, FF, L.ff1_b2, NQ_EPI_NONE, u, NQ_BF16, D, stv));
-    NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 0.5f, M, D, L.ln_mha_g, L.ln_mha_b, nullptr, nullptr, h, eps, st));
+    NQ_TRY(nq::layer_norm_rows(nq::enc::kLnResAdd, x, u, 0.5f, M, D, L.ln_mha_g, L.ln_mha_b, nullptr, nullptr, h, eps, st));
     // MHSA with relative positions -> norm_conv
     NQ_TRY(nq_linear(L.qkv, h, NQ_BF16, M, D, L.qkv_b, NQ_EPI_NONE, A.qkv.p, NQ_BF16, 3 * D, stv));
     NQ_TRY(nq::relpos_attention(A.qkv.as<__nv_bfloat16>(), A.krel.as<__nv_bfloat16>() + static_cast<size_t>(li) * D,
@@ -513,18 +513,18 @@ int forward(nq_encoder *e, const float *mel, const int32_t *lengths, int batch, 
                                 att_tc ? A.vrel.as<float>() + static_cast<size_t>(li) * H * (2 * Tp - 1) : nullptr,
                                 L3, s.B, Tp, H, D, A.att.as<__nv_bfloat16>(), st));
     NQ_TRY(nq_linear(L.o, A.att.p, NQ_BF16, M, D, L.o_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
-    NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_conv_g, L.ln_conv_b, nullptr, nullptr, h, eps, st));
+    NQ_TRY(nq::layer_norm_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_conv_g, L.ln_conv_b, nullptr, nullptr, h, eps, st));
     // Conv module -> norm_feed_forward2
     NQ_TRY(nq_linear(L.pw1, h, NQ_BF16, M, D, L.pw1_b, NQ_EPI_GLU_SIGMOID, A.g.p, NQ_BF16, D, stv));
     NQ_K(nq::enc::dwconv1d_bn_silu(A.g.as<__nv_bfloat16>(), L3, s.B, Tp, D, c.conv_kernel, L.dw_w, L.dw_b, L.bn_scale,
                                    L.bn_shift, A.c.as<__nv_bfloat16>(), st));
     NQ_TRY(nq_linear(L.pw2, A.c.p, NQ_BF16, M, D, L.pw2_b, NQ_EPI_NONE, u, NQ_BF16, D, stv));
-    NQ_K(nq::enc::ln_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_ff2_g, L.ln_ff2_b, nullptr, nullptr, h, eps, st));
+    NQ_TRY(nq::layer_norm_rows(nq::enc::kLnResAdd, x, u, 1.0f, M, D, L.ln_ff2_g, L.ln_ff2_b, nullptr, nullptr, h, eps, st));
     // FF2 (x0.5) -> norm_out (-> next layer's norm_feed_forward1)
     NQ_TRY(nq_linear(L.ff2_w1, h, NQ_BF16, M, D, L.ff2_b1, NQ_EPI_SILU, t, NQ_BF16, FF, stv));
     NQ_TRY(nq_linear(L.ff2_w2, t, NQ_BF16, M, FF, L.ff2_b2, NQ_EPI_NONE, u, NQ_BF16, D, stv));
     const Layer *nx = li + 1 < c.n_layers ? &e->layers[li + 1] : nullptr;
-    NQ_K(nq::enc::ln_rows(nq::enc::kLnResAddOut, x, u, 0.5f, M, D, L.ln_out_g, L.ln_out_b,
+    NQ_TRY(nq::layer_norm_rows(nq::enc::kLnResAddOut, x, u, 0.5f, M, D, L.ln_out_g, L.ln_out_b,
                           nx ? nx->ln_ff1_g : nullptr, nx ? nx->ln_ff1_b : nullptr, h, eps, st));
   }
   NQ_K(nq::enc::copy_masked(x, L3, s.B, Tp, D, out, st));

@@ -192,6 +192,7 @@ NQ_KCLASS_GEMV = 1
 NQ_KCLASS_DEQUANT = 2
 NQ_KCLASS_REDUCE = 3
 NQ_KCLASS_ATTENTION = 4
+NQ_KCLASS_NORM = 5
 NQ_GEMM_AUTO = 0
 NQ_GEMM_FUSED = 1
 NQ_GEMM_DEQUANT = 2
