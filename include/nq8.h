@@ -450,15 +450,15 @@ int nq_set_gemm_path(int path);
 int nq_set_gemm_unit_tokens(int tokens);
 
 /* Tail split of the dequantize-once GEMM.  No counterpart in the reference: a
- * B200 dispatch knob.  When a call's 256 x 256 output tiles leave the last
- * round of SM pairs partly idle, the tiles of that round are cut into k
- * pieces that run on the idle pairs; the last piece of each tile to finish
- * adds the pieces in piece order (deterministic) and writes the output, in
- * the same launch.  0 (default): a cost model decides per call; 1: never;
- * 2..16: that many pieces whenever a partial round exists (tests).  Results
- * differ from the unsplit sums only by f32 summation order.  A forced piece
- * count also selects 256-token units (the tail split's width) unless
- * nq_set_gemm_unit_tokens sets one.  Process-wide. */
+ * B200 dispatch knob.  When a call's output tiles (256 weight rows x the unit
+ * width in tokens) leave the last round of SM pairs partly idle, the tiles of
+ * that round are cut into k pieces that run on the idle pairs; the last piece
+ * of each tile to finish adds the pieces in piece order (deterministic) and
+ * writes the output, in the same launch.  0 (default): a cost model decides
+ * per call; 1: never; 2..16: that many pieces whenever a partial round exists
+ * (tests).  Results differ from the unsplit sums only by f32 summation order.
+ * A forced piece count runs on 256-token units unless nq_set_gemm_unit_tokens
+ * sets a width.  Process-wide. */
 int nq_set_gemm_tail_split(int mode);
 
 /* Which kernel runs the encoder's relative-position attention.  No

@@ -121,10 +121,11 @@ constexpr int64_t kDequantMinM = 128;
 constexpr double kNsPerUnitStep = 390.0;
 constexpr double kReduceBytesPerNs = 5000.0;
 constexpr double kReduceLaunchNs = 3000.0;
-// Tail split: each piece stores 128 KB of f32 accumulators per CTA and the last
-// piece reads every piece back from L2 (about 130 GB/s per SM), modelled per
-// piece; measured on B200 from 1024^3 (no split 10.5 us, 4 pieces 15.3 us)
-// and 2048 x 4096 -> 1024 (28.2 us, 2 pieces 22.8 us).
+// Tail split: each piece of a 256-token unit stores 128 KB of f32
+// accumulators per CTA and the last piece reads every piece back from L2
+// (about 130 GB/s per SM), modelled per piece; measured on B200 from 1024^3
+// (no split 10.5 us, 4 pieces 15.3 us) and 2048 x 4096 -> 1024 (28.2 us,
+// 2 pieces 22.8 us).  A narrower unit's piece moves width / 256 of it.
 constexpr double kTailFixupNsPerPiece = 2200.0;
 // Workspace counters: slot 0 is the GEMV work counter; the tail split's
 // per-(tile, CTA, warp group) counters start here.
@@ -482,7 +483,12 @@ double unit_step_ns(int bt) { return bt >= 256 ? kNsPerUnitStep : bt >= 128 ? 36
 // tiles of the last, partial round into S k pieces on S x L <= pairs pairs,
 // the last piece of each tile summing them (no extra launch).  Returns the
 // estimate.
-double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp, bool splitk = true) {
+// narrow_tail: the cost model may also tail-split 64- and 128-token units
+// (f32 activations: two MMAs per k step, so a piece saves enough; measured
+// on B200, configs[0] at M = 125 with f32 x: 81.9 -> 74.7 us, but with bf16 x
+// 54.8 -> 56.7 us).  A forced split (nq_set_gemm_tail_split) always applies.
+double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp, bool splitk = true,
+                       bool narrow_tail = false) {
   GemmPlan &g = *gp;
   g.bt = bt;
   g.grid_m = static_cast<int>((m + g.bt - 1) / g.bt);
@@ -508,14 +514,15 @@ double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp, bool sp
   g.full_units = tiles;
   g.tail_pieces = 1;
   g.tail_cps = 0;
-  if (g.bt == 256 && g_tail_split != 1 && L > 0) {
+  if (g_tail_split != 1 && L > 0 && (g.bt == 256 || narrow_tail || g_tail_split >= 2)) {
+    const double fixup = kTailFixupNsPerPiece * g.bt / 256.0;
     const int s_cap = std::min(std::min(g.pairs / L, kc / 2), 16);
     double best_tail = 1e300;
     int pick = 1, pick_cps = kc;
     for (int sp = 2; sp <= s_cap; ++sp) {
       const int cps = (kc + sp - 1) / sp;
       if ((kc + cps - 1) / cps != sp) continue;
-      const double t = (static_cast<double>(R) * kc + cps) * step + (sp + 1) * kTailFixupNsPerPiece;
+      const double t = (static_cast<double>(R) * kc + cps) * step + (sp + 1) * fixup;
       if (g_tail_split >= 2 ? sp == g_tail_split : t < best_tail) {
         best_tail = t;
         pick = sp;
@@ -538,17 +545,17 @@ double plan_bf16_width(GemmPlan *gp, int bt, int64_t m, int kc, int ldp, bool sp
 // unless a width or a tail split is forced.  Narrow units give a call with
 // few 256-token tiles more units for the SM pairs, at a k step that costs
 // nearly as much (the weight tile streams whole either way).
-GemmPlan plan_bf16(const GemmPlan &g0, int64_t m, int kc, int ldp, bool splitk) {
+GemmPlan plan_bf16(const GemmPlan &g0, int64_t m, int kc, int ldp, bool splitk, bool narrow_tail = false) {
   GemmPlan g = g0;
-  if (g_gemm_unit_tokens || g_tail_split >= 2) {  // a forced tail split runs on 256-token units
-    plan_bf16_width(&g, g_gemm_unit_tokens ? g_gemm_unit_tokens : 256, m, kc, ldp, splitk);
+  if (g_gemm_unit_tokens || g_tail_split >= 2) {  // a forced tail split without a forced width: 256
+    plan_bf16_width(&g, g_gemm_unit_tokens ? g_gemm_unit_tokens : 256, m, kc, ldp, splitk, narrow_tail);
     return g;
   }
   GemmPlan best_plan = g;
   double best_t = 1e300;
   for (int bt : {256, 128, 64}) {
     GemmPlan c = g;
-    const double t = plan_bf16_width(&c, bt, m, kc, ldp, splitk);
+    const double t = plan_bf16_width(&c, bt, m, kc, ldp, splitk, narrow_tail);
     if (t < best_t) {
       best_t = t;
       best_plan = c;
@@ -585,7 +592,7 @@ GemmPlan plan_gemm(int sm_count, const nq_weight *w, int64_t m, int x_dtype, boo
     g.splits = (kc + g.cps - 1) / g.cps;
     return g;
   }
-  return plan_bf16(g, m, kc, w->n_tiles * nq::kPackRows, true);
+  return plan_bf16(g, m, kc, w->n_tiles * nq::kPackRows, true, splitx);
 }
 
 bool direct_bf16(const void *x, int x_dtype, int64_t ldx) {

@@ -219,6 +219,19 @@ def test_unit_widths_match_oracle(nq, oracle, unit, m, k, n, epi, xdt):
                                                   (2100, 1024, 1024, 2, "f32", 2), (1000, 1024, 1000, 0, "bf16", 3)])
 @pytest.mark.parametrize("keep", [False, True])
 def test_tail_split_matches_oracle_and_unsplit(nq, oracle, m, k, n, epi, xdt, pieces, keep):
+    _tail_split_case(nq, oracle, m, k, n, epi, xdt, pieces, keep, 0)
+
+
+# The same on narrow units (64 / 128 tokens): small-M calls, where few tiles
+# leave most SM pairs idle.  pieces x tiles <= 74 in every case.
+@pytest.mark.parametrize("unit", [64, 128])
+@pytest.mark.parametrize("m,k,n,epi,xdt,pieces", [(125, 1024, 1024, 0, "bf16", 4), (125, 4096, 1024, 1, "f32", 8),
+                                                  (200, 640, 1920, 3, "bf16", 2), (100, 1024, 4096, 0, "bf16", 2)])
+def test_tail_split_narrow_units(nq, oracle, unit, m, k, n, epi, xdt, pieces):
+    _tail_split_case(nq, oracle, m, k, n, epi, xdt, pieces, True, unit)
+
+
+def _tail_split_case(nq, oracle, m, k, n, epi, xdt, pieces, keep, unit):
     from nspeech_b200.fast_matmul import QWeight
     L = nq.load()
     glu = epi in (3, 4)
@@ -235,6 +248,7 @@ def test_tail_split_matches_oracle_and_unsplit(nq, oracle, m, k, n, epi, xdt, pi
     nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_DEQUANT))
     nq.profile_enable(True)
     try:
+        nq.check(L.nq_set_gemm_unit_tokens(unit))
         nq.check(L.nq_set_gemm_tail_split(1))
         nq.profile_read(nq.NQ_KCLASS_REDUCE, True)
         ref = w.linear(xt, bias=bt, epilogue=epi, out_dtype=torch.float32).clone()
@@ -246,6 +260,7 @@ def test_tail_split_matches_oracle_and_unsplit(nq, oracle, m, k, n, epi, xdt, pi
     finally:
         nq.profile_enable(False)
         nq.check(L.nq_set_gemm_tail_split(0))
+        nq.check(L.nq_set_gemm_unit_tokens(0))
         nq.check(L.nq_set_gemm_path(nq.NQ_GEMM_AUTO))
     torch.cuda.synchronize()
     assert nq.status() == 0
@@ -253,6 +268,6 @@ def test_tail_split_matches_oracle_and_unsplit(nq, oracle, m, k, n, epi, xdt, pi
     # An unsplit sum differs from the pieces' sum in rounding; a global split-K
     # with the same cut adds the same two halves in the same order.
     assert ref_reduced or not torch.equal(a, ref), "the forced tail split did not run"
-    tag = f"tail {pieces} {m}x{k}x{n} epi={epi} {xdt} keep={keep}"
+    tag = f"tail {pieces} unit {unit} {m}x{k}x{n} epi={epi} {xdt} keep={keep}"
     _check(oracle, a.cpu().numpy(), _ref(oracle, x, q, n, bias, epi), tag)
     assert oracle.max_rel_err(a.cpu().numpy(), ref.cpu().numpy().astype(np.float64), 1.0) < 1e-4, tag
